@@ -1,0 +1,213 @@
+/*
+ * diffspec_b200.h — C ABI of the B200 (sm_100a) DiffSpec draft-context path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, NULL = legacy default stream), enqueues its kernels on
+ * that stream and returns without synchronising.  The return value is a
+ * status code; on failure dsb_last_error() returns a message for the calling
+ * thread.  Arguments are validated on the host before any launch; indices that
+ * live in device memory (plans, block tables, slots, positions) are checked by
+ * the kernels, which skip an out-of-range access and OR a bit into
+ * *error_flag (when error_flag is non-NULL) instead of faulting.
+ *
+ * Layouts (row-major, contiguous unless a stride is given):
+ *   query            [rows, num_query_heads, head_dim]
+ *   paged key cache  [num_blocks, block_size, num_kv_heads, head_dim]
+ *   raw draft KV     [num_slots, max_model_len, num_kv_heads, head_dim]
+ *   working KV       [num_slots, num_kv_heads, working_budget, head_dim]
+ *   plan row         [slot, history_len, tail_start, prefix_len, prefix_drop,
+ *                     chunk_ids..., 0 padding]   (int64, width 5 + W / C)
+ *
+ * Reference interfaces replaced (paths inside vllm-ascend-hust-diffspec 0.3.0):
+ *   see the comment above each function.
+ */
+#ifndef DIFFSPEC_B200_H_
+#define DIFFSPEC_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define DSB_OK 0
+#define DSB_ERR_INVALID 1     /* an argument failed validation               */
+#define DSB_ERR_UNSUPPORTED 2 /* valid, but no kernel for this shape/dtype   */
+#define DSB_ERR_CUDA 3        /* a CUDA launch or runtime call failed        */
+
+/* element type codes */
+#define DSB_BF16 0
+#define DSB_F16 1
+#define DSB_F32 2
+
+/* bits OR-ed into *error_flag by kernels that met a bad device-side index */
+#define DSB_FLAG_SLOT 1       /* slot outside [0, num_slots)                 */
+#define DSB_FLAG_POSITION 2   /* token position outside its cache            */
+#define DSB_FLAG_BLOCK 4      /* block-table entry outside [0, num_blocks)   */
+#define DSB_FLAG_PLAN 8       /* malformed plan row                          */
+#define DSB_FLAG_CAPACITY 16  /* selection larger than the per-slot capacity */
+
+const char *dsb_last_error(void);
+int dsb_abi_version(void);
+
+/* Per-(row, kv-head, chunk) retrieval mass with a caller-supplied softmax LSE:
+ *   head_scores[b, g, c] = sum_{h in group g} sum_{t in chunk c, t < L_b}
+ *                          exp(scale * q[b,h] . k[b,t,g] - lse[b,h])
+ * head_scores is [batch, num_kv_heads, max_chunks] fp32; chunks at or past
+ * L_b = seq_lens[b] are written as 0, so L_b = 0 marks a skipped row.
+ * query_index (nullable) maps row b to the query/LSE row it reads.
+ * Replaces the device kernel of paged_chunk_attention_scores
+ * (diffspec/kernels.py:11-92, launch at :131-149); the head mean of :150 is
+ * dsb_finalize_chunk_scores. */
+int dsb_paged_chunk_head_scores(
+    const void *query, const float *softmax_lse, const int32_t *query_index,
+    const void *key_cache, const int32_t *block_table, int64_t block_table_stride,
+    int64_t block_table_cols, const int32_t *seq_lens, int32_t batch,
+    int32_t num_query_heads, int32_t num_kv_heads, int32_t head_dim,
+    int32_t block_size, int64_t num_blocks, int32_t chunk_size, int32_t max_chunks,
+    float scale, int32_t dtype, float *head_scores, int32_t *error_flag,
+    void *stream);
+
+/* Same pass without an LSE: per (row, query head, chunk) the maximum logit
+ * and the sum of exp(logit - max) ([batch, num_query_heads, max_chunks] fp32
+ * each).  dsb_chunk_stats_to_head_scores turns them into head_scores with the
+ * sequence-wide log-sum-exp, which is the softmax_lse=None branch of
+ * chunk_attention_scores (diffspec/runtime.py:321-322). */
+int dsb_paged_chunk_stats(
+    const void *query, const int32_t *query_index, const void *key_cache,
+    const int32_t *block_table, int64_t block_table_stride, int64_t block_table_cols,
+    const int32_t *seq_lens, int32_t batch, int32_t num_query_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int64_t num_blocks,
+    int32_t chunk_size, int32_t max_chunks, float scale, int32_t dtype,
+    float *chunk_max, float *chunk_sum, int32_t *error_flag, void *stream);
+
+/* lse_out (nullable) receives the per-(row, query head) log-sum-exp. */
+int dsb_chunk_stats_to_head_scores(
+    const float *chunk_max, const float *chunk_sum, const int32_t *seq_lens,
+    int32_t batch, int32_t num_query_heads, int32_t num_kv_heads,
+    int32_t chunk_size, int32_t max_chunks, float *head_scores, float *lse_out,
+    void *stream);
+
+/* scores[b, c] = sum_p parts[b, p, c] / (n_valid(b, c) * total_query_heads),
+ * n_valid = number of tokens of chunk c below seq_lens[b] (0 -> score 0).
+ * This is the per-head normalisation and head mean of
+ * diffspec/kernels.py:81-83,150 and diffspec/runtime.py:336-345, with the
+ * per-kv-head parts summed in a fixed order. */
+int dsb_finalize_chunk_scores(
+    const float *parts, int64_t row_stride, int64_t part_stride, int32_t num_parts,
+    const int32_t *seq_lens, int32_t batch, int32_t total_query_heads,
+    int32_t chunk_size, int32_t max_chunks, float *scores, void *stream);
+
+/* Device top-k chunk selection, one CTA per row (select_context_chunks,
+ * diffspec/runtime.py:348-414, via set_chunk_scores :1554-1567).
+ * Row scores are sum_p parts[row, p, c], divided by n_valid * normalize_heads
+ * when normalize_heads > 0.  With n = ceil(L / C) chunks and
+ * S = history_budget / C: n <= S keeps every chunk, otherwise the S - 1
+ * highest-scoring chunks among 0..n-2 (ties go to the lower chunk index) plus
+ * chunk n-1, in ascending order.  Rows whose row_slots entry is < 0 are left
+ * alone; the others overwrite sel_chunks[slot, :count] / sel_count[slot].
+ * The optional outputs mirror DiffSpecSelection (-1 padded). */
+int dsb_select_context_chunks(
+    const float *parts, int64_t row_stride, int64_t part_stride, int32_t num_parts,
+    int32_t normalize_heads, const int32_t *seq_lens, const int32_t *row_slots,
+    int32_t rows, int32_t max_chunks, int32_t chunk_size, int32_t history_budget,
+    int32_t *sel_chunks, int32_t sel_stride, int32_t *sel_count, int32_t num_slots,
+    int64_t *out_chunk_indices, int64_t *out_token_indices, float *out_chunk_scores,
+    int32_t *error_flag, void *stream);
+
+/* Compact history plan rows (_history_plan_host, diffspec/runtime.py:1713-1735,
+ * equal to _history_indices :1650-1681 once expanded).  history_end =
+ * max(0, committed_lens[row] - 1); sel_count[slot] < 0 means "no retrieval
+ * yet".  plan is [rows, plan_width] int64 with plan_width = 5 + W / C.
+ * history_lens (nullable, [rows]) and working_lens (nullable, [num_slots])
+ * receive history_len. */
+int dsb_build_history_plan(
+    const int32_t *row_slots, const int32_t *committed_lens, int32_t rows,
+    const int32_t *sel_chunks, int32_t sel_stride, const int32_t *sel_count,
+    int32_t num_slots, int32_t chunk_size, int32_t history_budget,
+    int32_t plan_width, int64_t *plan, int32_t *history_lens, int32_t *working_lens,
+    int32_t *error_flag, void *stream);
+
+/* Fused gather + local-position RoPE + working-cache write
+ * (rebuild_compact_kv_from_plan, diffspec/compact_kv.py:184-242, kernel
+ * :8-133).  For p < history_len of each plan row the K row at its absolute
+ * position is rotated at local position p (fp32 math, products rounded before
+ * the sum) and stored; V and K dims >= rotary_dim are copied.  Positions at or
+ * past history_len are untouched.  cos_sin_cache rows hold [cos | sin]. */
+int dsb_rebuild_compact_kv_from_plan(
+    const void *raw_key, const void *raw_value, void *working_key, void *working_value,
+    const int64_t *plan, int32_t plan_rows, int32_t plan_width,
+    const void *cos_sin_cache, int32_t cos_sin_dtype, int64_t cos_sin_stride,
+    int64_t cos_sin_rows, int32_t num_slots, int64_t max_model_len,
+    int32_t num_heads, int32_t head_dim, int32_t working_budget, int32_t chunk_size,
+    int32_t max_width, int32_t rotary_dim, int32_t is_neox_style, int32_t dtype,
+    int32_t *error_flag, void *stream);
+
+/* Paged gather at selected token ids with RoPE at local positions 0..W-1
+ * (gather_raw_kv_with_local_rope, diffspec/kernels.py:153-210).  Ids < 0 give
+ * zero rows (which still take a local position).  Outputs are
+ * [batch, working_tokens, num_heads, head_dim]. */
+int dsb_gather_raw_kv_with_local_rope(
+    const void *raw_key_cache, const void *raw_value_cache, int64_t num_blocks,
+    int32_t block_size, int32_t num_heads, int32_t head_dim,
+    const int32_t *block_table, int64_t block_table_stride, int64_t block_table_cols,
+    const int64_t *selected_token_indices, int32_t batch, int32_t working_tokens,
+    const void *cos_sin_cache, int32_t cos_sin_dtype, int64_t cos_sin_stride,
+    int64_t cos_sin_rows, int32_t rotary_dim, int32_t is_neox_style, int32_t dtype,
+    void *out_key, void *out_value, int32_t *error_flag, void *stream);
+
+/* Draft decode attention over capacity-sized working caches
+ * (_forward_linear_attention_npu, diffspec/runtime.py:2079-2134; CPU loop
+ * :2040-2077).  With p_r = positions[r] + position_offset, row r writes
+ * key[r]/value[r] into slot slots[r] at local position p_r and attends over
+ * positions 0..p_r with a softmax of scale * q.k; rows r in [rows, out_rows)
+ * get zero output.  position_offset lets the K draft steps of one cycle share
+ * the plan's history_len vector (step j passes j).
+ * Split-KV: each (row, kv head) is cut into num_splits pieces whose partial
+ * softmax states go to `scratch` (dsb_draft_attention_scratch_floats floats);
+ * the last piece to finish merges them.  `counters` holds rows * num_kv_heads
+ * int32 that must be zero before the first call; every call leaves them
+ * zero.  Calls sharing scratch/counters must not overlap on the GPU. */
+int dsb_draft_decode_attention(
+    const void *query, const void *key, const void *value, void *working_key,
+    void *working_value, const int32_t *slots, const int32_t *positions,
+    int32_t position_offset, int32_t rows, int32_t out_rows, int32_t num_slots, int32_t num_query_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t working_budget, float scale,
+    int32_t dtype, void *output, float *scratch, int64_t scratch_floats,
+    int32_t *counters, int32_t num_splits, int32_t *error_flag, void *stream);
+
+/* Split count the library would choose and the scratch size it then needs. */
+int32_t dsb_draft_attention_default_splits(int32_t rows, int32_t num_kv_heads,
+                                           int32_t working_budget, int32_t sm_count);
+int64_t dsb_draft_attention_scratch_floats(int32_t rows, int32_t num_query_heads,
+                                           int32_t num_kv_heads, int32_t head_dim,
+                                           int32_t num_splits);
+
+/* Committed-query pick of the retrieval hook
+ * (_accept_target_queries, diffspec/runtime.py:1211-1276): for each of `rows`
+ * real requests with query span [query_ends[r-1], query_ends[r]) and count
+ * accepted tokens, query_index = start + clamp(count - 1, 0, len - 1) and
+ * retrieval_len = target_seq_len - len + min(max(count, 1), len).  Rows with
+ * count <= 0 get retrieval_len 0 and row_slots -1.  counts is int64 when
+ * counts_are_int64, else int32.  status[0] (retrievals run) or status[1]
+ * (skipped: nothing committed) is incremented when status is non-NULL. */
+int dsb_prepare_retrieval_rows(
+    const int32_t *query_ends, const int32_t *target_seq_lens, const void *counts,
+    int32_t counts_are_int64, const int32_t *active_slots, int32_t rows,
+    int32_t *query_index, int32_t *retrieval_lens, int32_t *row_slots,
+    int32_t *status, void *stream);
+
+/* Canonical pre-RoPE KV write (_write_raw, diffspec/runtime.py:1602-1618):
+ * raw[slots[i], positions[i]] = kv[i] for i < tokens; slots[i] < 0 skips. */
+int dsb_write_raw_kv(
+    const void *key, const void *value, void *raw_key, void *raw_value,
+    const int32_t *slots, const int64_t *positions, int32_t tokens,
+    int32_t num_slots, int64_t max_model_len, int32_t num_heads, int32_t head_dim,
+    int32_t dtype, int32_t *error_flag, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIFFSPEC_B200_H_ */

@@ -1,0 +1,194 @@
+// Small per-request kernels of the draft cycle: compact history plans (A5),
+// the committed-query pick of the retrieval hook (A3) and the canonical raw-KV
+// write (A9).  All of them keep the reference's host Python loops on the
+// device so a draft cycle needs no device-to-host copy.
+#include "common.cuh"
+
+namespace dsb {
+namespace {
+
+// One thread per plan row: _history_plan_host, diffspec/runtime.py:1713-1735.
+__global__ void build_plan_kernel(const int32_t *__restrict__ row_slots,
+                                  const int32_t *__restrict__ committed_lens, int rows,
+                                  const int32_t *__restrict__ sel_chunks, int sel_stride,
+                                  const int32_t *__restrict__ sel_count, int num_slots, int C,
+                                  int HB, int plan_width, int64_t *__restrict__ plan,
+                                  int32_t *__restrict__ history_lens,
+                                  int32_t *__restrict__ working_lens, int32_t *err) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  int64_t *out = plan + (int64_t)r * plan_width;
+  const int slot = (row_slots != nullptr) ? row_slots[r] : r;
+  if (slot < 0 || slot >= num_slots) {
+    flag_error(err, DSB_FLAG_SLOT);
+    for (int i = 0; i < plan_width; ++i) out[i] = 0;
+    if (history_lens != nullptr) history_lens[r] = 0;
+    return;
+  }
+  const int64_t he = max(0, committed_lens[r] - 1);  // history ends before the root
+  const int cnt = sel_count[slot];
+  int64_t hlen, tail_start, prefix_len = 0, prefix_drop = 0;
+  int n_chunks = 0;
+  const int64_t tail_len = min(he, (int64_t)min(C, HB));
+  if (cnt < 0) {  // no retrieval yet: the most recent history_budget tokens
+    hlen = min(he, (int64_t)HB);
+    tail_start = he - hlen;
+  } else if (cnt == 0) {
+    hlen = tail_len;
+    tail_start = he - tail_len;
+  } else {
+    n_chunks = min(cnt, sel_stride);
+    if (5 + n_chunks > plan_width) {
+      flag_error(err, DSB_FLAG_CAPACITY);
+      n_chunks = plan_width - 5;
+    }
+    const int32_t *ch = sel_chunks + (int64_t)slot * sel_stride;
+    tail_start = he - tail_len;
+    const int64_t prefix_end = min(tail_start, (int64_t)ch[min(cnt, sel_stride) - 1] * C);
+    int64_t prefix_tokens = 0;
+    for (int i = 0; i < min(cnt, sel_stride); ++i) {
+      const int64_t v = prefix_end - (int64_t)ch[i] * C;
+      prefix_tokens += max((int64_t)0, min((int64_t)C, v));
+    }
+    prefix_len = min(prefix_tokens, (int64_t)HB - tail_len);
+    prefix_drop = prefix_tokens - prefix_len;
+    hlen = prefix_len + tail_len;
+  }
+  out[0] = slot;
+  out[1] = hlen;
+  out[2] = tail_start;
+  out[3] = prefix_len;
+  out[4] = prefix_drop;
+  const int32_t *ch = sel_chunks + (int64_t)slot * sel_stride;
+  for (int i = 5; i < plan_width; ++i) out[i] = (i - 5 < n_chunks) ? ch[i - 5] : 0;
+  if (history_lens != nullptr) history_lens[r] = (int32_t)hlen;
+  if (working_lens != nullptr) working_lens[slot] = (int32_t)hlen;
+}
+
+// _accept_target_queries, diffspec/runtime.py:1211-1276 (linear proposals).
+__global__ void prepare_rows_kernel(const int32_t *__restrict__ query_ends,
+                                    const int32_t *__restrict__ target_seq_lens,
+                                    const void *__restrict__ counts, int counts64,
+                                    const int32_t *__restrict__ active_slots, int rows,
+                                    int32_t *__restrict__ query_index,
+                                    int32_t *__restrict__ retrieval_lens,
+                                    int32_t *__restrict__ row_slots, int32_t *status) {
+  __shared__ int any;
+  if (threadIdx.x == 0) any = 0;
+  __syncthreads();
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    const int start = (r == 0) ? 0 : query_ends[r - 1];
+    const int qlen = query_ends[r] - start;
+    const int64_t cnt = counts64 ? static_cast<const int64_t *>(counts)[r]
+                                 : (int64_t) static_cast<const int32_t *>(counts)[r];
+    if (cnt > 0 && qlen > 0) {
+      const int off = (int)min(max(cnt - 1, (int64_t)0), (int64_t)(qlen - 1));
+      const int committed = (int)min(max(cnt, (int64_t)1), (int64_t)qlen);
+      query_index[r] = start + off;
+      retrieval_lens[r] = target_seq_lens[r] - qlen + committed;
+      row_slots[r] = active_slots[r];
+      any = 1;
+    } else {
+      query_index[r] = max(start, 0);
+      retrieval_lens[r] = 0;
+      row_slots[r] = -1;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && status != nullptr) {
+    if (any) status[0] += 1;
+    else status[1] += 1;
+  }
+}
+
+// One warp per token row: raw[slot, pos] = kv[i].
+__global__ void write_raw_kernel(const uint4 *__restrict__ key, const uint4 *__restrict__ value,
+                                 uint4 *__restrict__ raw_key, uint4 *__restrict__ raw_value,
+                                 const int32_t *__restrict__ slots,
+                                 const int64_t *__restrict__ positions, int tokens,
+                                 int num_slots, int64_t max_model_len, int row_vecs,
+                                 int32_t *err) {
+  const int lane = threadIdx.x & 31;
+  const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= tokens) return;
+  const int slot = slots[i];
+  if (slot < 0) return;
+  const int64_t pos = positions[i];
+  if (slot >= num_slots || pos < 0 || pos >= max_model_len) {
+    if (lane == 0) flag_error(err, slot >= num_slots ? DSB_FLAG_SLOT : DSB_FLAG_POSITION);
+    return;
+  }
+  const int64_t dst = ((int64_t)slot * max_model_len + pos) * row_vecs;
+  const int64_t src = (int64_t)i * row_vecs;
+  for (int v = lane; v < row_vecs; v += 32) {
+    raw_key[dst + v] = key[src + v];
+    raw_value[dst + v] = value[src + v];
+  }
+}
+
+int elem_size(int dtype) { return dtype == DSB_F32 ? 4 : 2; }
+
+}  // namespace
+}  // namespace dsb
+
+using namespace dsb;
+
+extern "C" int dsb_build_history_plan(const int32_t *row_slots, const int32_t *committed_lens,
+                                      int32_t rows, const int32_t *sel_chunks,
+                                      int32_t sel_stride, const int32_t *sel_count,
+                                      int32_t num_slots, int32_t chunk_size,
+                                      int32_t history_budget, int32_t plan_width,
+                                      int64_t *plan, int32_t *history_lens,
+                                      int32_t *working_lens, int32_t *error_flag,
+                                      void *stream) {
+  if (rows < 0) return fail(DSB_ERR_INVALID, "negative rows");
+  if (rows == 0) return DSB_OK;
+  if (!committed_lens || !sel_chunks || !sel_count || !plan)
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (chunk_size <= 0 || history_budget <= 0 || plan_width < 5 || sel_stride <= 0 ||
+      num_slots <= 0)
+    return fail(DSB_ERR_INVALID, "bad chunk size, budget, plan width or selection stride");
+  build_plan_kernel<<<(rows + 127) / 128, 128, 0, as_stream(stream)>>>(
+      row_slots, committed_lens, rows, sel_chunks, sel_stride, sel_count, num_slots,
+      chunk_size, history_budget, plan_width, plan, history_lens, working_lens, error_flag);
+  return check_launch("build_plan_kernel");
+}
+
+extern "C" int dsb_prepare_retrieval_rows(const int32_t *query_ends,
+                                          const int32_t *target_seq_lens, const void *counts,
+                                          int32_t counts_are_int64,
+                                          const int32_t *active_slots, int32_t rows,
+                                          int32_t *query_index, int32_t *retrieval_lens,
+                                          int32_t *row_slots, int32_t *status, void *stream) {
+  if (rows < 0) return fail(DSB_ERR_INVALID, "negative rows");
+  if (rows == 0) return DSB_OK;
+  if (!query_ends || !target_seq_lens || !counts || !active_slots || !query_index ||
+      !retrieval_lens || !row_slots)
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  prepare_rows_kernel<<<1, 256, 0, as_stream(stream)>>>(
+      query_ends, target_seq_lens, counts, counts_are_int64, active_slots, rows, query_index,
+      retrieval_lens, row_slots, status);
+  return check_launch("prepare_rows_kernel");
+}
+
+extern "C" int dsb_write_raw_kv(const void *key, const void *value, void *raw_key,
+                                void *raw_value, const int32_t *slots,
+                                const int64_t *positions, int32_t tokens, int32_t num_slots,
+                                int64_t max_model_len, int32_t num_heads, int32_t head_dim,
+                                int32_t dtype, int32_t *error_flag, void *stream) {
+  if (tokens < 0) return fail(DSB_ERR_INVALID, "negative token count");
+  if (tokens == 0) return DSB_OK;
+  if (!key || !value || !raw_key || !raw_value || !slots || !positions)
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (dtype != DSB_BF16 && dtype != DSB_F16 && dtype != DSB_F32)
+    return fail(DSB_ERR_INVALID, "unknown dtype");
+  const int64_t row_bytes = (int64_t)num_heads * head_dim * elem_size(dtype);
+  if (num_heads <= 0 || head_dim <= 0 || row_bytes % 16)
+    return fail(DSB_ERR_UNSUPPORTED, "KV row must be a multiple of 16 bytes");
+  const int warps = 8;
+  write_raw_kernel<<<(tokens + warps - 1) / warps, warps * 32, 0, as_stream(stream)>>>(
+      static_cast<const uint4 *>(key), static_cast<const uint4 *>(value),
+      static_cast<uint4 *>(raw_key), static_cast<uint4 *>(raw_value), slots, positions, tokens,
+      num_slots, max_model_len, (int)(row_bytes / 16), error_flag);
+  return check_launch("write_raw_kernel");
+}

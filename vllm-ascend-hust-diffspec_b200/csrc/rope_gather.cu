@@ -1,0 +1,368 @@
+// Fused gather + local-position RoPE + write (DiffSpec rows A6 and A7).
+//
+// Reference: _rebuild_compact_kv_kernel / rebuild_compact_kv_from_plan,
+// diffspec/compact_kv.py:8-242 (grid (rows, heads, cdiv(width, 16)), one head
+// and 16 tokens per program, cos/sin re-read per head) and
+// gather_raw_kv_with_local_rope, diffspec/kernels.py:153-210 (index_select
+// followed by a separate in-place RoPE pass).
+//
+// B200 design: a warp owns U whole token rows (all kv heads, K and V).  The
+// raw rows are contiguous [heads * head_dim] runs, so each lane issues 16-byte
+// cp.async copies into a per-warp shared-memory stage (perfectly coalesced,
+// no register staging, U * 2 rows in flight per warp).  The warp then writes
+// V straight back out and K rotated at the local position, reading the RoPE
+// partner element from the staged row, so one HBM read and one HBM write per
+// byte is all the kernel moves.  RoPE math is fp32 with both products rounded
+// before the add, i.e. exactly "first * cos - second * sin" evaluated without
+// fused multiply-add, then rounded once to the cache dtype.
+#include "common.cuh"
+
+namespace dsb {
+namespace {
+
+constexpr int kWarpsRope = 8;
+
+struct RopeArgs {
+  const void *src_k, *src_v;
+  void *dst_k, *dst_v;
+  // rebuild (plan-driven)
+  const int64_t *plan;
+  int plan_width, num_slots;
+  int64_t max_model_len;
+  int working_budget, chunk, max_width;
+  // gather (paged, index-driven)
+  const int32_t *bt;
+  int64_t bt_stride, bt_cols, num_blocks;
+  int block_size;
+  const int64_t *sel;
+  int working_tokens;
+  // common
+  const void *cos_sin;
+  int64_t cs_stride, cs_rows;
+  int heads, head_dim, rotary_dim, neox, tokens_per_warp;
+  int32_t *err;
+};
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+template <typename CS>
+__device__ __forceinline__ float cs_load(const CS *p) {
+  return Elem<CS>::to_f(*p);
+}
+
+template <typename T, typename CS, bool GATHER>
+__global__ void __launch_bounds__(kWarpsRope * 32) rope_rows_kernel(const RopeArgs a) {
+  extern __shared__ uint4 stage[];
+  constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int U = a.tokens_per_warp;
+  const int row_elems = a.heads * a.head_dim;
+  const int row_vecs = row_elems / VE;
+  uint4 *wstage = stage + (size_t)warp * U * 2 * row_vecs;
+  const T *src_k = static_cast<const T *>(a.src_k);
+  const T *src_v = static_cast<const T *>(a.src_v);
+  T *dst_k = static_cast<T *>(a.dst_k);
+  T *dst_v = static_cast<T *>(a.dst_v);
+  const CS *cs = static_cast<const CS *>(a.cos_sin);
+  const int r = blockIdx.y;
+  const int p0 = (blockIdx.x * kWarpsRope + warp) * U;
+
+  // Row descriptor.
+  int64_t slot = 0, hlen = 0, tail_start = 0, prefix_len = 0, drop = 0;
+  const int64_t *chunks = nullptr;
+  int n_plan_chunks = 0;
+  if (!GATHER) {
+    const int64_t *pr = a.plan + (int64_t)r * a.plan_width;
+    slot = pr[0];
+    hlen = pr[1];
+    tail_start = pr[2];
+    prefix_len = pr[3];
+    drop = pr[4];
+    chunks = pr + 5;
+    n_plan_chunks = a.plan_width - 5;
+    const int64_t cap = min((int64_t)a.max_width, (int64_t)a.working_budget);
+    if (slot < 0 || slot >= a.num_slots || hlen < 0 || prefix_len < 0 || prefix_len > hlen ||
+        drop < 0 || hlen > cap) {
+      if (lane == 0 && warp == 0 && blockIdx.x == 0)
+        flag_error(a.err, (slot < 0 || slot >= a.num_slots) ? DSB_FLAG_SLOT : DSB_FLAG_PLAN);
+      if (slot < 0 || slot >= a.num_slots) return;
+      hlen = max((int64_t)0, min(hlen, cap));
+      prefix_len = max((int64_t)0, min(prefix_len, hlen));
+      drop = max((int64_t)0, drop);
+    }
+  }
+  const int64_t width = GATHER ? a.working_tokens : hlen;
+
+  // Phase 1: stage the U rows (K then V) of this warp.
+  for (int j = 0; j < U; ++j) {
+    const int64_t p = p0 + j;
+    if (p >= width) break;
+    const T *rk = nullptr, *rv = nullptr;
+    bool zero_row = false;
+    if (!GATHER) {
+      int64_t abs_pos;
+      bool ok = true;
+      if (p < prefix_len) {
+        const int64_t q = p + drop;
+        const int64_t ci = q / a.chunk;
+        if (ci >= n_plan_chunks) ok = false;
+        abs_pos = ok ? chunks[ci] * a.chunk + q % a.chunk : 0;
+      } else {
+        abs_pos = tail_start + p - prefix_len;
+      }
+      if (!ok || abs_pos < 0 || abs_pos >= a.max_model_len) {
+        if (lane == 0) flag_error(a.err, ok ? DSB_FLAG_POSITION : DSB_FLAG_PLAN);
+        continue;
+      }
+      const int64_t off = (slot * a.max_model_len + abs_pos) * row_elems;
+      rk = src_k + off;
+      rv = src_v + off;
+    } else {
+      const int64_t idx = a.sel[(int64_t)r * a.working_tokens + p];
+      if (idx < 0) {
+        zero_row = true;
+      } else {
+        const int64_t lb = idx / a.block_size;
+        const int64_t pb = (lb < a.bt_cols) ? a.bt[(int64_t)r * a.bt_stride + lb] : -1;
+        if (pb < 0 || pb >= a.num_blocks) {
+          if (lane == 0) flag_error(a.err, DSB_FLAG_BLOCK);
+          zero_row = true;
+        } else {
+          const int64_t off = (pb * a.block_size + idx % a.block_size) * row_elems;
+          rk = src_k + off;
+          rv = src_v + off;
+        }
+      }
+    }
+    uint4 *sk = wstage + (size_t)j * 2 * row_vecs;
+    uint4 *sv = sk + row_vecs;
+    for (int v = lane; v < row_vecs; v += 32) {
+      if (zero_row) {
+        sk[v] = make_uint4(0, 0, 0, 0);
+        sv[v] = make_uint4(0, 0, 0, 0);
+      } else {
+        cp_async16(sk + v, reinterpret_cast<const uint4 *>(rk) + v);
+        cp_async16(sv + v, reinterpret_cast<const uint4 *>(rv) + v);
+      }
+    }
+  }
+  cp_async_wait_all();
+  __syncwarp();
+
+  // Phase 2: write V as is and K rotated at local position p.
+  const int rot = a.rotary_dim, half = rot / 2;
+  for (int j = 0; j < U; ++j) {
+    const int64_t p = p0 + j;
+    if (p >= width) break;
+    if (!GATHER) {  // skip rows whose source was rejected above
+      bool ok = true;
+      int64_t abs_pos;
+      if (p < prefix_len) {
+        const int64_t q = p + drop;
+        const int64_t ci = q / a.chunk;
+        ok = ci < n_plan_chunks;
+        abs_pos = ok ? chunks[ci] * a.chunk + q % a.chunk : 0;
+      } else {
+        abs_pos = tail_start + p - prefix_len;
+      }
+      if (!ok || abs_pos < 0 || abs_pos >= a.max_model_len) continue;
+    }
+    const uint4 *sk = wstage + (size_t)j * 2 * row_vecs;
+    const uint4 *sv = sk + row_vecs;
+    const T *kx = reinterpret_cast<const T *>(sk);
+    for (int v = lane; v < row_vecs; v += 32) {
+      const int e0 = v * VE;
+      const int h = e0 / a.head_dim, d0 = e0 % a.head_dim;
+      int64_t dst_off;
+      if (GATHER) {
+        dst_off = ((int64_t)r * a.working_tokens + p) * row_elems + e0;
+      } else {
+        dst_off = ((slot * a.heads + h) * a.working_budget + p) * a.head_dim + d0;
+      }
+      stg_stream(dst_v + dst_off, sv[v]);
+      if (d0 >= rot) {
+        stg_stream(dst_k + dst_off, sk[v]);
+        continue;
+      }
+      const T *hx = kx + h * a.head_dim;
+      union {
+        uint4 u;
+        T e[VE];
+      } out;
+      out.u = sk[v];
+      const CS *csr = cs + p * a.cs_stride;
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        const int d = d0 + e;
+        if (d >= rot) break;
+        int i;
+        float x1, x2;
+        bool first;
+        if (a.neox) {
+          first = d < half;
+          i = first ? d : d - half;
+          x1 = Elem<T>::to_f(hx[i]);
+          x2 = Elem<T>::to_f(hx[i + half]);
+        } else {
+          first = (d & 1) == 0;
+          i = d >> 1;
+          x1 = Elem<T>::to_f(hx[2 * i]);
+          x2 = Elem<T>::to_f(hx[2 * i + 1]);
+        }
+        const float c = cs_load(csr + i), s = cs_load(csr + half + i);
+        const float y = first ? __fmul_rn(x1, c) - __fmul_rn(x2, s)
+                              : __fmul_rn(x2, c) + __fmul_rn(x1, s);
+        out.e[e] = Elem<T>::from_f(y);
+      }
+      stg_stream(dst_k + dst_off, out.u);
+    }
+  }
+}
+
+int elem_bytes(int dtype) { return dtype == DSB_F32 ? 4 : 2; }
+
+template <typename T, typename CS, bool GATHER>
+int launch_rope(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
+  const int row_bytes = a.heads * a.head_dim * (int)sizeof(T);
+  int U = row_bytes <= 2048 ? 4 : (row_bytes <= 4096 ? 2 : 1);
+  const size_t smem = (size_t)kWarpsRope * U * 2 * row_bytes;
+  if (smem > 200 * 1024) return fail(DSB_ERR_UNSUPPORTED, "KV rows too wide for staging");
+  a.tokens_per_warp = U;
+  auto kern = rope_rows_kernel<T, CS, GATHER>;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int64_t per_cta = (int64_t)kWarpsRope * U;
+  const int64_t gx = (width + per_cta - 1) / per_cta;
+  if (gx > 0x7fffffff || rows > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
+  kern<<<dim3((unsigned)gx, rows), kWarpsRope * 32, smem, st>>>(a);
+  return check_launch(GATHER ? "gather_rope_kernel" : "rebuild_rope_kernel");
+}
+
+template <bool GATHER>
+int dispatch_rope(const RopeArgs &a, int dtype, int cs_dtype, int rows, int64_t width,
+                  cudaStream_t st) {
+#define DSB_RP(TD, T, CD, CS) \
+  if (dtype == TD && cs_dtype == CD) return launch_rope<T, CS, GATHER>(a, rows, width, st);
+  DSB_RP(DSB_BF16, __nv_bfloat16, DSB_BF16, __nv_bfloat16)
+  DSB_RP(DSB_BF16, __nv_bfloat16, DSB_F32, float)
+  DSB_RP(DSB_BF16, __nv_bfloat16, DSB_F16, __half)
+  DSB_RP(DSB_F16, __half, DSB_F16, __half)
+  DSB_RP(DSB_F16, __half, DSB_F32, float)
+  DSB_RP(DSB_F16, __half, DSB_BF16, __nv_bfloat16)
+  DSB_RP(DSB_F32, float, DSB_F32, float)
+  DSB_RP(DSB_F32, float, DSB_BF16, __nv_bfloat16)
+  DSB_RP(DSB_F32, float, DSB_F16, __half)
+#undef DSB_RP
+  return fail(DSB_ERR_INVALID, "unknown dtype");
+}
+
+int common_checks(int heads, int head_dim, int rotary_dim, int dtype) {
+  if (heads <= 0 || head_dim <= 0)
+    return fail(DSB_ERR_INVALID, "raw sequence, head and head dimensions must be positive");
+  if (rotary_dim < 0 || rotary_dim > head_dim || rotary_dim % 2)
+    return fail(DSB_ERR_INVALID, "rotary_dim must be even and between zero and head_dim");
+  if (dtype != DSB_BF16 && dtype != DSB_F16 && dtype != DSB_F32)
+    return fail(DSB_ERR_INVALID, "KV caches must use BF16, FP16 or FP32");
+  if ((head_dim * elem_bytes(dtype)) % 16)
+    return fail(DSB_ERR_UNSUPPORTED, "head_dim * element size must be a multiple of 16 bytes");
+  return DSB_OK;
+}
+
+}  // namespace
+}  // namespace dsb
+
+using namespace dsb;
+
+extern "C" int dsb_rebuild_compact_kv_from_plan(
+    const void *raw_key, const void *raw_value, void *working_key, void *working_value,
+    const int64_t *plan, int32_t plan_rows, int32_t plan_width, const void *cos_sin_cache,
+    int32_t cos_sin_dtype, int64_t cos_sin_stride, int64_t cos_sin_rows, int32_t num_slots,
+    int64_t max_model_len, int32_t num_heads, int32_t head_dim, int32_t working_budget,
+    int32_t chunk_size, int32_t max_width, int32_t rotary_dim, int32_t is_neox_style,
+    int32_t dtype, int32_t *error_flag, void *stream) {
+  int c = common_checks(num_heads, head_dim, rotary_dim, dtype);
+  if (c != DSB_OK) return c;
+  if (max_model_len <= 0 || num_slots <= 0)
+    return fail(DSB_ERR_INVALID, "raw sequence, head and head dimensions must be positive");
+  if (plan_rows < 0 || plan_rows > num_slots || max_width < 0 || max_width > working_budget)
+    return fail(DSB_ERR_INVALID, "KV plan exceeds the working cache batch or token capacity");
+  if (chunk_size <= 0 || plan_width != 5 + working_budget / chunk_size)
+    return fail(DSB_ERR_INVALID, "plan width must be 5 + working_budget // chunk_size");
+  if (rotary_dim > 0 && (cos_sin_rows < max_width || cos_sin_stride < rotary_dim))
+    return fail(DSB_ERR_INVALID, "cos/sin cache must contain all local positions and rotary dimensions");
+  if (plan_rows == 0 || max_width == 0) return DSB_OK;
+  if (!raw_key || !raw_value || !working_key || !working_value || !plan ||
+      (rotary_dim > 0 && !cos_sin_cache))
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  RopeArgs a{};
+  a.src_k = raw_key;
+  a.src_v = raw_value;
+  a.dst_k = working_key;
+  a.dst_v = working_value;
+  a.plan = plan;
+  a.plan_width = plan_width;
+  a.num_slots = num_slots;
+  a.max_model_len = max_model_len;
+  a.working_budget = working_budget;
+  a.chunk = chunk_size;
+  a.max_width = max_width;
+  a.cos_sin = cos_sin_cache;
+  a.cs_stride = cos_sin_stride;
+  a.cs_rows = cos_sin_rows;
+  a.heads = num_heads;
+  a.head_dim = head_dim;
+  a.rotary_dim = rotary_dim;
+  a.neox = is_neox_style ? 1 : 0;
+  a.err = error_flag;
+  return dispatch_rope<false>(a, dtype, rotary_dim > 0 ? cos_sin_dtype : DSB_F32, plan_rows,
+                              max_width, as_stream(stream));
+}
+
+extern "C" int dsb_gather_raw_kv_with_local_rope(
+    const void *raw_key_cache, const void *raw_value_cache, int64_t num_blocks,
+    int32_t block_size, int32_t num_heads, int32_t head_dim, const int32_t *block_table,
+    int64_t block_table_stride, int64_t block_table_cols,
+    const int64_t *selected_token_indices, int32_t batch, int32_t working_tokens,
+    const void *cos_sin_cache, int32_t cos_sin_dtype, int64_t cos_sin_stride,
+    int64_t cos_sin_rows, int32_t rotary_dim, int32_t is_neox_style, int32_t dtype,
+    void *out_key, void *out_value, int32_t *error_flag, void *stream) {
+  int c = common_checks(num_heads, head_dim, rotary_dim, dtype);
+  if (c != DSB_OK) return c;
+  if (batch < 0 || working_tokens < 0) return fail(DSB_ERR_INVALID, "negative sizes");
+  if (batch == 0 || working_tokens == 0) return DSB_OK;
+  if (num_blocks <= 0 || block_size <= 0 || block_table_cols <= 0)
+    return fail(DSB_ERR_INVALID, "block table and cache must be non-empty");
+  if (rotary_dim > 0 && (cos_sin_rows < working_tokens || cos_sin_stride < rotary_dim))
+    return fail(DSB_ERR_INVALID, "cos/sin cache must contain all local positions and rotary dimensions");
+  if (!raw_key_cache || !raw_value_cache || !block_table || !selected_token_indices ||
+      !out_key || !out_value || (rotary_dim > 0 && !cos_sin_cache))
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  RopeArgs a{};
+  a.src_k = raw_key_cache;
+  a.src_v = raw_value_cache;
+  a.dst_k = out_key;
+  a.dst_v = out_value;
+  a.bt = block_table;
+  a.bt_stride = block_table_stride;
+  a.bt_cols = block_table_cols;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.sel = selected_token_indices;
+  a.working_tokens = working_tokens;
+  a.cos_sin = cos_sin_cache;
+  a.cs_stride = cos_sin_stride;
+  a.cs_rows = cos_sin_rows;
+  a.heads = num_heads;
+  a.head_dim = head_dim;
+  a.rotary_dim = rotary_dim;
+  a.neox = is_neox_style ? 1 : 0;
+  a.err = error_flag;
+  return dispatch_rope<true>(a, dtype, rotary_dim > 0 ? cos_sin_dtype : DSB_F32, batch,
+                             working_tokens, as_stream(stream));
+}

@@ -1,0 +1,506 @@
+"""DiffSpec draft-context runtime on B200: the retrieval hook, the per-cycle
+compact-cache rebuild and the draft attention, with device-resident state.
+
+Mirrors the hot-path subset of ``DiffSpecDraftCache``
+(diffspec/runtime.py:596-2134) for linear (non-tree) Eagle3 proposals:
+
+* ``accept_target_queries`` — the retrieval hook (:1170-1334): committed-query
+  pick, rejected-suffix exclusion, chunk scores over the target's paged K,
+  the head-sharded exchange and the top-k selection, all on the device.  The
+  reference's ``counts.to("cpu")`` sync (:1248) and per-request Python loop
+  (:1298-1308) are gone: rows with nothing committed are masked in-kernel.
+* ``prepare_compact_prefill`` / ``rebuild`` — ``_history_plan_host`` +
+  ``rebuild_compact_kv_from_plan`` (:1683-1765) with the plan built on the
+  device (no D2H of selections, no host plan upload).
+* ``forward_attention`` — the draft attention (:2024-2134) over the working
+  cache through a slot vector (no copy for reordered slots).
+* ``write_raw`` / ``populate_prefill`` — canonical pre-RoPE KV (:1336-1347,
+  :1602-1618).
+
+Host-visible counters that depend on device data (retrievals run, rows with
+nothing committed) live on the device and are read only by
+``retrieval_status()``.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from . import _lib
+from .attention import AttentionWorkspace, draft_decode_attention
+from .compact_kv import rebuild_compact_kv_from_plan
+from .kernels import paged_chunk_head_scores
+from .parallel import gather_head_scores
+from .selection import (
+    DiffSpecSelection,
+    build_history_plan,
+    select_context_chunks,
+    select_rows,
+)
+
+__all__ = [
+    "DiffSpecSettings",
+    "DiffSpecSelection",
+    "DiffSpecRuntimeMetrics",
+    "DiffSpecDraftCache",
+    "chunk_attention_scores",
+    "select_context_chunks",
+]
+
+
+@dataclass(frozen=True)
+class DiffSpecSettings:
+    """Same fields and order as diffspec/runtime.py:18-41."""
+
+    chunk_size: int
+    token_budget: int
+    retrieval_interval: int
+    max_tree_nodes: int
+    max_tree_depth: int
+    tree_threshold: float
+    adaptive_profile: bool
+
+
+@dataclass
+class DiffSpecRuntimeMetrics:
+    """Host counters of diffspec/runtime.py:66-116 that need no device data."""
+
+    retrieval_attempts: int = 0
+    retrieval_skipped_prefill: int = 0
+    retrieval_skipped_no_snapshot: int = 0
+    retrieval_skipped_interval: int = 0
+    retrieval_launches: int = 0
+    retrieval_seconds: float = 0.0
+
+
+def chunk_attention_scores(
+    query: torch.Tensor,
+    keys: torch.Tensor,
+    chunk_size: int,
+    softmax_lse: torch.Tensor | None = None,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Dense form of the retrieval scores (diffspec/runtime.py:281-345).
+
+    ``query [Hq, D]``, ``keys [T, Hk, D]`` (CUDA) -> ``[ceil(T / C)]`` fp32.
+    Runs the paged kernel with the dense keys as one page.
+    """
+    from .kernels import paged_chunk_attention_scores
+
+    if query.ndim != 2 or keys.ndim != 3:
+        raise ValueError("query must be 2-D and keys must be 3-D")
+    num_query_heads, head_dim = query.shape
+    num_tokens, num_kv_heads, key_head_dim = keys.shape
+    if head_dim != key_head_dim:
+        raise ValueError("query and key head dimensions must match")
+    if num_query_heads % num_kv_heads != 0:
+        raise ValueError("query heads must be divisible by KV heads")
+    if chunk_size <= 0:
+        raise ValueError("chunk_size must be positive")
+    device = _lib.require_cuda(query, keys)
+    if num_tokens == 0:
+        return torch.empty(0, dtype=torch.float32, device=device)
+    lse = None if softmax_lse is None else softmax_lse.reshape(1, -1)
+    if lse is not None and lse.numel() != num_query_heads:
+        raise ValueError("softmax_lse must contain one value per query head")
+    scores = paged_chunk_attention_scores(
+        query.to(keys.dtype).unsqueeze(0),
+        keys.unsqueeze(0),
+        lse,
+        torch.zeros((1, 1), dtype=torch.int32, device=device),
+        torch.tensor([num_tokens], dtype=torch.int32).to(device),
+        chunk_size=chunk_size,
+        max_seq_len=num_tokens,
+        scale=scale if scale is not None else head_dim**-0.5,
+    )
+    return scores[0]
+
+
+class _Staging:
+    """Device buffer for small per-call int32 vectors from host lists.
+
+    Each upload goes through a fresh pinned tensor from PyTorch's caching
+    host allocator, which keeps the block alive until its asynchronous copy
+    has run, so no host synchronisation is needed.
+    """
+
+    def __init__(self, device: torch.device, capacity: int):
+        self.dev = torch.empty(capacity, dtype=torch.int32, device=device)
+
+    def upload(self, *lists: list[int]) -> list[torch.Tensor]:
+        flat = [v for x in lists for v in x]
+        if len(flat) > self.dev.numel():
+            self.dev = torch.empty(2 * len(flat), dtype=torch.int32, device=self.dev.device)
+        host = torch.tensor(flat, dtype=torch.int32).pin_memory()
+        self.dev[: len(flat)].copy_(host, non_blocking=True)
+        views, off = [], 0
+        for x in lists:
+            views.append(self.dev[off:off + len(x)])
+            off += len(x)
+        return views
+
+
+class DiffSpecDraftCache:
+    """Canonical raw KV and compact attention state for one-layer Eagle3 drafts."""
+
+    def __init__(
+        self,
+        settings: DiffSpecSettings,
+        *,
+        max_num_reqs: int,
+        max_model_len: int,
+        num_kv_heads: int,
+        head_dim: int,
+        target_num_layers: int,
+        dtype: torch.dtype,
+        device: torch.device,
+        rotary_embedding: Any = None,
+        cos_sin_cache: torch.Tensor | None = None,
+        rotary_dim: int | None = None,
+        is_neox_style: bool = True,
+        target_tensor_parallel_size: int = 1,
+        process_group: Any = None,
+    ) -> None:
+        if target_tensor_parallel_size < 1:
+            raise ValueError("Target tensor parallel size must be positive")
+        self.settings = settings
+        self.max_num_reqs = max_num_reqs
+        self.max_model_len = max_model_len
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.target_last_layer = target_num_layers - 1
+        self.target_tensor_parallel_size = target_tensor_parallel_size
+        self.process_group = process_group
+        self.dtype = dtype
+        self.device = torch.device(device)
+        # diffspec/runtime.py:627-637
+        self.history_budget = (
+            (settings.token_budget - settings.max_tree_depth - 1)
+            // settings.chunk_size
+            * settings.chunk_size
+        )
+        if self.history_budget <= 0:
+            raise ValueError("DiffSpec token budget is too small for tree tokens")
+        if rotary_embedding is not None:
+            cos_sin_cache = rotary_embedding.cos_sin_cache
+            rotary_dim = rotary_embedding.rotary_dim
+            is_neox_style = rotary_embedding.is_neox_style
+        if cos_sin_cache is None:
+            raise ValueError("a RoPE cos/sin cache (or rotary embedding) is required")
+        self.cos_sin_cache = cos_sin_cache.to(self.device).contiguous()
+        self.rotary_dim = head_dim if rotary_dim is None else rotary_dim
+        self.is_neox_style = is_neox_style
+
+        cache_shape = (max_num_reqs, max_model_len, num_kv_heads, head_dim)
+        self.raw_key = torch.empty(cache_shape, dtype=dtype, device=self.device)
+        self.raw_value = torch.empty_like(self.raw_key)
+        working_shape = (max_num_reqs, num_kv_heads, settings.token_budget, head_dim)
+        self.working_key = torch.empty(working_shape, dtype=dtype, device=self.device)
+        self.working_value = torch.empty_like(self.working_key)
+
+        self.max_selected_chunks = self.history_budget // settings.chunk_size
+        self.sel_chunks = torch.zeros(
+            (max_num_reqs, self.max_selected_chunks), dtype=torch.int32, device=self.device
+        )
+        self.sel_count = torch.full((max_num_reqs,), -1, dtype=torch.int32, device=self.device)
+        self.working_lens = torch.zeros(max_num_reqs, dtype=torch.int32, device=self.device)
+        self._status = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self._plan = torch.zeros(
+            (max_num_reqs, 5 + settings.token_budget // settings.chunk_size),
+            dtype=torch.int64, device=self.device,
+        )
+        self._history_lens = torch.zeros(max_num_reqs, dtype=torch.int32, device=self.device)
+        self._staging = _Staging(self.device, 4 * max_num_reqs + 16)
+        self._attn_workspace = AttentionWorkspace(self.device)
+        self.metrics = DiffSpecRuntimeMetrics()
+
+        self._request_slots: dict[str, int] = {}
+        self._active_slots: list[int] = []
+        self._active_slots_dev: torch.Tensor | None = None
+        self._retrieval_cycle = 0
+        self._cycle_open = False
+        self._draft_step = 0
+        self._pending_rows = 0
+        self._target: dict[str, Any] | None = None
+        self.target_is_prefill = True
+
+    # ------------------------------------------------------------ slots
+    def set_active_requests(self, request_ids: list[str]) -> None:
+        """Keep canonical rows stable across batch reorder and cancellation
+        (diffspec/runtime.py:755-778)."""
+        active = set(request_ids)
+        released = []
+        for request_id in list(self._request_slots):
+            if request_id not in active:
+                released.append(self._request_slots.pop(request_id))
+        if released:
+            idx = torch.tensor(released, dtype=torch.long).to(self.device, non_blocking=True)
+            self.sel_count.index_fill_(0, idx, -1)
+            self.working_lens.index_fill_(0, idx, 0)
+        used = set(self._request_slots.values())
+        free = iter(sorted(set(range(self.max_num_reqs)) - used))
+        for request_id in request_ids:
+            if request_id not in self._request_slots:
+                try:
+                    self._request_slots[request_id] = next(free)
+                except StopIteration as error:
+                    raise RuntimeError("DiffSpec canonical request slots are exhausted") from error
+        slots = [self._request_slots[r] for r in request_ids]
+        if slots != self._active_slots or self._active_slots_dev is None:
+            self._active_slots = slots
+            self._active_slots_dev = (
+                torch.tensor(slots, dtype=torch.int32).to(self.device, non_blocking=True)
+                if slots else torch.empty(0, dtype=torch.int32, device=self.device)
+            )
+
+    def begin_cycle(self, request_ids: list[str]) -> None:
+        self.set_active_requests(request_ids)
+        self._cycle_open = True
+        self._draft_step = 0
+
+    def end_cycle(self) -> None:
+        self._cycle_open = False
+        self._pending_rows = 0
+
+    # ------------------------------------------------------------ retrieval
+    def begin_target_forward(self, request_ids: list[str]) -> None:
+        """Discard a stale target snapshot before a new verifier pass."""
+        self.set_active_requests(request_ids)
+        self._target = None
+        self.target_is_prefill = True
+
+    def capture_target_attention(
+        self,
+        query: torch.Tensor,
+        softmax_lse: torch.Tensor | None,
+        key_cache: torch.Tensor | None,
+        metadata: Any,
+        scale: float,
+    ) -> None:
+        """Save the last target layer's attention inputs (runtime.py:841-878).
+
+        ``metadata`` provides ``actual_seq_lengths_q`` (cumulative query ends),
+        ``seq_lens_list`` and ``block_tables`` as in vLLM-Ascend.
+        """
+        if softmax_lse is None or key_cache is None:
+            return
+        query_ends = list(getattr(metadata, "actual_seq_lengths_q", ()))
+        seq_lens = list(getattr(metadata, "seq_lens_list", ()))
+        block_tables = getattr(metadata, "block_tables", None)
+        if not query_ends or not seq_lens or block_tables is None:
+            return
+        is_prefill = bool(getattr(metadata, "num_prefills", 1))
+        lse = softmax_lse.reshape(query.shape[0], query.shape[1])
+        if is_prefill:  # keep only each request's last query (runtime.py:862-872)
+            idx = torch.tensor([e - 1 for e in query_ends], dtype=torch.long).to(query.device)
+            query = query.index_select(0, idx)
+            lse = lse.index_select(0, idx)
+            query_ends = list(range(1, len(query_ends) + 1))
+        self._target = dict(
+            query=query.detach(), lse=lse.detach(), key_cache=key_cache,
+            block_tables=block_tables[: len(seq_lens)], query_ends=query_ends,
+            seq_lens=seq_lens, scale=scale,
+        )
+        self.target_is_prefill = is_prefill
+
+    def accept_target_queries(self, valid_sampled_token_count: torch.Tensor, *, is_prefill: bool) -> None:
+        """Retrieve context with the last committed target query per request
+        (diffspec/runtime.py:1170-1334)."""
+        self.metrics.retrieval_attempts += 1
+        if self._target is None:
+            self.metrics.retrieval_skipped_no_snapshot += 1
+            return
+        if is_prefill:
+            self.metrics.retrieval_skipped_prefill += 1
+            return
+        self._retrieval_cycle += 1
+        if self._retrieval_cycle % self.settings.retrieval_interval:
+            self.metrics.retrieval_skipped_interval += 1
+            return
+        batch = len(self._active_slots)
+        t = self._target
+        if (
+            valid_sampled_token_count.numel() < batch
+            or len(t["query_ends"]) < batch
+            or len(t["seq_lens"]) < batch
+            or t["block_tables"].shape[0] < batch
+        ):
+            self.metrics.retrieval_skipped_no_snapshot += 1
+            return
+        self.retrieve(
+            t["query"], t["lse"], t["key_cache"], t["block_tables"][:batch],
+            t["query_ends"][:batch], t["seq_lens"][:batch],
+            valid_sampled_token_count[:batch], t["scale"],
+        )
+
+    def retrieve(
+        self,
+        query: torch.Tensor,
+        softmax_lse: torch.Tensor,
+        key_cache: torch.Tensor,
+        block_tables: torch.Tensor,
+        query_ends: list[int],
+        target_seq_lens: list[int],
+        counts: torch.Tensor,
+        scale: float,
+    ) -> None:
+        """Device retrieval for the active batch: pick -> score -> exchange -> select."""
+        started = time.perf_counter()
+        rows = len(self._active_slots)
+        if rows == 0:
+            return
+        ends_d, seqs_d = self._staging.upload(query_ends, target_seq_lens)
+        q_index = torch.empty(rows, dtype=torch.int32, device=self.device)
+        r_len = torch.empty_like(q_index)
+        r_slot = torch.empty_like(q_index)
+        counts = counts.reshape(-1)
+        if counts.dtype not in (torch.int32, torch.int64):
+            counts = counts.to(torch.int64)
+        counts = counts.contiguous()
+        _lib.call(
+            "dsb_prepare_retrieval_rows",
+            _lib.ptr(ends_d), _lib.ptr(seqs_d), _lib.ptr(counts),
+            int(counts.dtype == torch.int64), _lib.ptr(self._active_slots_dev), rows,
+            _lib.ptr(q_index), _lib.ptr(r_len), _lib.ptr(r_slot), _lib.ptr(self._status),
+            _lib.stream_ptr(self.device),
+        )
+        max_len = max(target_seq_lens)
+        parts = paged_chunk_head_scores(
+            query, key_cache, softmax_lse, block_tables, r_len,
+            chunk_size=self.settings.chunk_size, max_seq_len=max_len, scale=scale,
+            query_index=q_index,
+        )
+        total_heads = query.shape[1]
+        if self.target_tensor_parallel_size > 1:
+            parts = gather_head_scores(parts, self.process_group)
+            total_heads *= self.target_tensor_parallel_size
+        select_rows(
+            parts, r_len, chunk_size=self.settings.chunk_size, token_budget=self.history_budget,
+            normalize_heads=total_heads, row_slots=r_slot, sel_chunks=self.sel_chunks,
+            sel_count=self.sel_count,
+        )
+        self.metrics.retrieval_launches += 1
+        self.metrics.retrieval_seconds += time.perf_counter() - started
+
+    def set_chunk_scores(self, slot: int, chunk_scores: torch.Tensor, seq_len: int) -> DiffSpecSelection:
+        """Select from a score vector and store it for ``slot`` (runtime.py:1554-1567)."""
+        selection = select_context_chunks(chunk_scores, seq_len, self.settings.chunk_size, self.history_budget)
+        n = selection.chunk_indices.numel()
+        if n:
+            self.sel_chunks[slot, :n].copy_(selection.chunk_indices.to(torch.int32))
+        self.sel_count[slot] = n
+        return selection
+
+    def clear_selection(self, slot: int) -> None:
+        self.sel_count[slot] = -1
+
+    def retrieval_status(self) -> dict[str, float | int]:
+        """Counters of diffspec/runtime.py:1184-1190 (reads two device ints)."""
+        done, no_commit = (int(v) for v in self._status.tolist())
+        m = self.metrics
+        return dict(
+            retrieval_count=done,
+            retrieval_attempts=m.retrieval_attempts,
+            retrieval_skipped_prefill=m.retrieval_skipped_prefill,
+            retrieval_skipped_no_snapshot=m.retrieval_skipped_no_snapshot,
+            retrieval_skipped_interval=m.retrieval_skipped_interval,
+            retrieval_skipped_no_committed_tokens=no_commit,
+            retrieval_ms=m.retrieval_seconds / max(m.retrieval_launches, 1) * 1e3,
+            retrieval_cycle=self._retrieval_cycle,
+            selected_slots=int((self.sel_count >= 0).sum().item()),
+            target_tensor_parallel_size=self.target_tensor_parallel_size,
+        )
+
+    # ------------------------------------------------------------ draft cycle
+    def write_raw(self, slots: torch.Tensor, positions: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> None:
+        """raw[slots[i], positions[i]] = key/value[i] (runtime.py:1602-1618)."""
+        n = key.shape[0]
+        key = key.reshape(n, -1).contiguous()
+        value = value.reshape(n, -1).contiguous()
+        _lib.call(
+            "dsb_write_raw_kv",
+            _lib.ptr(key), _lib.ptr(value), _lib.ptr(self.raw_key), _lib.ptr(self.raw_value),
+            _lib.ptr(slots.to(torch.int32).contiguous()),
+            _lib.ptr(positions.to(torch.int64).contiguous()), n, self.max_num_reqs,
+            self.max_model_len, self.num_kv_heads, self.head_dim, _lib.dtype_code(self.dtype),
+            _lib.ptr(_lib.error_flag(self.device)), _lib.stream_ptr(self.device),
+        )
+
+    def populate_prefill(self, request_rows: list[int], absolute_positions: torch.Tensor,
+                         key: torch.Tensor, value: torch.Tensor) -> None:
+        """Write projected pre-RoPE KV of batch rows ``request_rows`` (runtime.py:1336-1347)."""
+        slots = torch.tensor([self._active_slots[r] for r in request_rows], dtype=torch.int32)
+        self.write_raw(slots.to(self.device, non_blocking=True), absolute_positions, key, value)
+
+    def rebuild(self, committed_seq_lens: list[int] | torch.Tensor) -> torch.Tensor:
+        """Plan + fused gather/RoPE rebuild of every active row's working cache.
+
+        ``committed_seq_lens`` (host list or device tensor) are the committed
+        lengths including the root; history ends just before the root.
+        Returns the device int32 ``history_len`` per row, which is also the
+        root's local position.
+        """
+        rows = len(self._active_slots)
+        if rows == 0:
+            return self._history_lens[:0]
+        if isinstance(committed_seq_lens, torch.Tensor):
+            committed = committed_seq_lens.to(device=self.device, dtype=torch.int32).reshape(-1)[:rows]
+        else:
+            (committed,) = self._staging.upload(list(committed_seq_lens)[:rows])
+        plan = self._plan[:rows]
+        hl = self._history_lens[:rows]
+        build_history_plan(
+            self._active_slots_dev, committed, self.sel_chunks, self.sel_count,
+            chunk_size=self.settings.chunk_size, history_budget=self.history_budget,
+            working_budget=self.settings.token_budget, plan=plan, history_lens=hl,
+            working_lens=self.working_lens,
+        )
+        rebuild_compact_kv_from_plan(
+            self.raw_key, self.raw_value, self.working_key, self.working_value, plan,
+            self._cos_sin(), chunk_size=self.settings.chunk_size,
+            max_width=self.history_budget, rotary_dim=self.rotary_dim,
+            is_neox_style=self.is_neox_style,
+        )
+        self._pending_rows = rows
+        self._draft_step = 0
+        return hl
+
+    def prepare_compact_prefill(self, metadata: Any, num_tokens: int, *,
+                                committed_seq_lens: list[int] | None = None) -> None:
+        """runtime.py:1349-1371: rebuild history at the committed roots."""
+        seq_lens = committed_seq_lens if committed_seq_lens is not None else list(
+            getattr(metadata, "seq_lens_list", ()))
+        if seq_lens is None or len(seq_lens) == 0:
+            raise RuntimeError("DiffSpec compact prefill requires sequence lengths")
+        self.rebuild(list(seq_lens)[:num_tokens])
+
+    def local_positions(self) -> torch.Tensor:
+        """Device local RoPE positions of the current draft step."""
+        return self._history_lens[: self._pending_rows] + self._draft_step
+
+    def forward_attention(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                          scale: float, output: torch.Tensor) -> torch.Tensor:
+        """One draft step: store K/V at each row's local position and attend
+        (runtime.py:2024-2134).  Output rows past the batch are zeroed."""
+        rows = self._pending_rows
+        if rows == 0:
+            raise RuntimeError("DiffSpec attention called without prepared state")
+        if self._draft_step + 1 > self.settings.token_budget - self.history_budget:
+            raise RuntimeError("DiffSpec working cache exhausted")
+        draft_decode_attention(
+            query, key, value, self.working_key, self.working_value,
+            self._active_slots_dev, self._history_lens[:rows], scale, output,
+            rows=rows, position_offset=self._draft_step, workspace=self._attn_workspace,
+        )
+        self._draft_step += 1
+        return output
+
+    def _cos_sin(self) -> torch.Tensor:
+        cs = self.cos_sin_cache
+        if cs.dtype != self.dtype and cs.dtype != torch.float32:
+            cs = cs.to(self.dtype)
+        return cs
