@@ -56,12 +56,14 @@ int dsb_abi_version(void);
  *                          exp(scale * q[b,h] . k[b,t,g] - lse[b,h])
  * head_scores is [batch, num_kv_heads, max_chunks] fp32; chunks at or past
  * L_b = seq_lens[b] are written as 0, so L_b = 0 marks a skipped row.
- * query_index (nullable) maps row b to the query/LSE row it reads.
+ * query_index (nullable) maps row b to the query/LSE row it reads; rows
+ * mapped outside [0, query_rows) are flagged (DSB_FLAG_POSITION) and scored 0.
  * Replaces the device kernel of paged_chunk_attention_scores
  * (diffspec/kernels.py:11-92, launch at :131-149); the head mean of :150 is
  * dsb_finalize_chunk_scores. */
 int dsb_paged_chunk_head_scores(
     const void *query, const float *softmax_lse, const int32_t *query_index,
+    int32_t query_rows,
     const void *key_cache, const int32_t *block_table, int64_t block_table_stride,
     int64_t block_table_cols, const int32_t *seq_lens, int32_t batch,
     int32_t num_query_heads, int32_t num_kv_heads, int32_t head_dim,
@@ -70,12 +72,13 @@ int dsb_paged_chunk_head_scores(
     void *stream);
 
 /* Same pass without an LSE: per (row, query head, chunk) the maximum logit
- * and the sum of exp(logit - max) ([batch, num_query_heads, max_chunks] fp32
- * each).  dsb_chunk_stats_to_head_scores turns them into head_scores with the
+ * in log2 units (log2(e) * scale * q.k) and the sum of exp(logit - max_logit)
+ * ([batch, num_query_heads, max_chunks] fp32 each).  dsb_chunk_stats_to_head_scores turns them into head_scores with the
  * sequence-wide log-sum-exp, which is the softmax_lse=None branch of
  * chunk_attention_scores (diffspec/runtime.py:321-322). */
 int dsb_paged_chunk_stats(
-    const void *query, const int32_t *query_index, const void *key_cache,
+    const void *query, const int32_t *query_index, int32_t query_rows,
+    const void *key_cache,
     const int32_t *block_table, int64_t block_table_stride, int64_t block_table_cols,
     const int32_t *seq_lens, int32_t batch, int32_t num_query_heads,
     int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int64_t num_blocks,

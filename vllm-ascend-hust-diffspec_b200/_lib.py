@@ -50,12 +50,12 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dsb_abi_version": (ctypes.c_int, []),
     "dsb_paged_chunk_head_scores": (
         ctypes.c_int,
-        [_P, _P, _P, _P, _P, _I64, _I64, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I32, _I32,
+        [_P, _P, _P, _I32, _P, _P, _I64, _I64, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I32, _I32,
          _F32, _I32, _P, _P, _P],
     ),
     "dsb_paged_chunk_stats": (
         ctypes.c_int,
-        [_P, _P, _P, _P, _I64, _I64, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I32, _I32, _F32,
+        [_P, _P, _I32, _P, _P, _I64, _I64, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I32, _I32, _F32,
          _I32, _P, _P, _P, _P],
     ),
     "dsb_chunk_stats_to_head_scores": (

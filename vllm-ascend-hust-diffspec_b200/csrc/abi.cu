@@ -1,6 +1,9 @@
 // Status reporting shared by every C-ABI entry point.
 #include <cstdio>
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 
 #include "common.cuh"
 
@@ -28,6 +31,23 @@ int sm_count() {
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
   return n > 0 ? n : 148;
+}
+
+int ensure_smem(const void *kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return DSB_OK;
+  static std::mutex mu;
+  static std::map<std::pair<int, const void *>, size_t> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(DSB_ERR_CUDA, "cudaGetDevice failed");
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(dev, kernel);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return DSB_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess)
+    return fail(DSB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  done[key] = bytes;
+  return DSB_OK;
 }
 
 }  // namespace dsb

@@ -408,8 +408,7 @@ extern "C" int dsb_draft_decode_attention(
     const size_t smem = sizeof(float) * (kAttnWarps * GP * DD + 2 * kAttnWarps * GP) +  \
                         sizeof(TT) * kAttnWarps * 16 * GP;                              \
     auto kern = draft_attention_kernel<TT, DD, NN>;                                     \
-    if (smem > 48 * 1024)                                                               \
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;    \
     kern<<<dim3(splits, num_kv_heads, out_rows), kAttnWarps * 32, smem, st>>>(a);      \
     return check_launch("draft_attention_kernel");                                      \
   }

@@ -21,6 +21,10 @@ inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s
 
 int sm_count();
 
+// Raise a kernel's dynamic shared-memory limit once per (device, kernel), so
+// repeated launches (and launches during CUDA-graph capture) only enqueue.
+int ensure_smem(const void *kernel, size_t bytes);
+
 // ------------------------------------------------------------ element types
 template <typename T> struct Elem;
 template <> struct Elem<__nv_bfloat16> {

@@ -235,8 +235,7 @@ int launch_rope(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
   if (smem > 200 * 1024) return fail(DSB_ERR_UNSUPPORTED, "KV rows too wide for staging");
   a.tokens_per_warp = U;
   auto kern = rope_rows_kernel<T, CS, GATHER>;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;
   const int64_t per_cta = (int64_t)kWarpsRope * U;
   const int64_t gx = (width + per_cta - 1) / per_cta;
   if (gx > 0x7fffffff || rows > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");

@@ -70,7 +70,7 @@ __device__ __forceinline__ void load_token(uint4 (&dst)[D / 32], const T *row, i
 template <typename T, int D, int NT, bool STATS>
 __global__ void __launch_bounds__(kWarps * 32)
 chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ lse,
-                        const int32_t *__restrict__ query_index,
+                        const int32_t *__restrict__ query_index, int query_rows,
                         const T *__restrict__ key_cache, const int32_t *__restrict__ block_table,
                         int64_t bt_stride, int64_t bt_cols, const int32_t *__restrict__ seq_lens,
                         int Hq, int Hk, int block_size, int64_t num_blocks, int chunk,
@@ -81,7 +81,11 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int group = Hq / Hk;
-  const int L = seq_lens[b];
+  const int qrow = (query_index != nullptr) ? query_index[b] : b;
+  const bool qrow_ok = qrow >= 0 && qrow < query_rows;
+  if (!qrow_ok && threadIdx.x == 0 && blockIdx.x == 0 && seq_lens[b] > 0)
+    flag_error(err, DSB_FLAG_POSITION);
+  const int L = qrow_ok ? seq_lens[b] : 0;
   const int c_begin = blockIdx.x * kChunksPerCta;
   const int n_ch = min(kChunksPerCta, max_chunks - c_begin);
   if (n_ch <= 0) return;
@@ -91,7 +95,6 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
   const int i_end = min(total, i_begin + per_warp);
   const int tiles_per_chunk = chunk / 16;
   const int32_t *bt_row = block_table + (int64_t)b * bt_stride;
-  const int qrow = (query_index != nullptr) ? query_index[b] : b;
 
   uint32_t qf[NT][KS][2];
   float lse2[NT][2];
@@ -254,7 +257,7 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
 template <typename T, bool STATS>
 __global__ void __launch_bounds__(128)
 chunk_scores_generic_kernel(const T *__restrict__ query, const float *__restrict__ lse,
-                            const int32_t *__restrict__ query_index,
+                            const int32_t *__restrict__ query_index, int query_rows,
                             const T *__restrict__ key_cache,
                             const int32_t *__restrict__ block_table, int64_t bt_stride,
                             int64_t bt_cols, const int32_t *__restrict__ seq_lens, int Hq,
@@ -266,8 +269,10 @@ chunk_scores_generic_kernel(const T *__restrict__ query, const float *__restrict
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int group = Hq / Hk;
   float *qs = qs_all + warp * group * D;
-  const int L = seq_lens[b];
   const int qrow = (query_index != nullptr) ? query_index[b] : b;
+  const bool qrow_ok = qrow >= 0 && qrow < query_rows;
+  if (!qrow_ok && threadIdx.x == 0 && c == 0 && seq_lens[b] > 0) flag_error(err, DSB_FLAG_POSITION);
+  const int L = qrow_ok ? seq_lens[b] : 0;
   const int32_t *bt_row = block_table + (int64_t)b * bt_stride;
   const int tok0 = c * chunk;
   for (int kvh = warp; kvh < Hk; kvh += 4) {
@@ -397,6 +402,7 @@ struct ScoreArgs {
   const void *query;
   const float *lse;
   const int32_t *qidx;
+  int qrows;
   const void *kc;
   const int32_t *bt;
   int64_t bt_stride, bt_cols;
@@ -417,6 +423,11 @@ int validate(const ScoreArgs &a, bool stats) {
   if (!a.query || !a.kc || !a.bt || !a.seq || !a.out || (stats && !a.out_sum) ||
       (!stats && !a.lse))
     return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (a.qidx == nullptr) {
+    if (a.qrows < a.B) return fail(DSB_ERR_INVALID, "query_rows is smaller than the batch");
+  } else if (a.qrows <= 0) {
+    return fail(DSB_ERR_INVALID, "query_rows must be positive");
+  }
   if (a.Hq <= 0 || a.Hk <= 0 || a.Hq % a.Hk)
     return fail(DSB_ERR_INVALID, "query heads must be divisible by KV heads");
   if (a.D <= 0 || a.bs <= 0 || a.C <= 0 || a.nblocks <= 0 || a.bt_cols <= 0)
@@ -430,7 +441,7 @@ template <typename T, int D, int NT, bool STATS>
 void launch_mma(const ScoreArgs &a) {
   dim3 grid((a.max_chunks + kChunksPerCta - 1) / kChunksPerCta, a.B);
   chunk_scores_mma_kernel<T, D, NT, STATS><<<grid, kWarps * 32, 0, a.st>>>(
-      static_cast<const T *>(a.query), a.lse, a.qidx, static_cast<const T *>(a.kc), a.bt,
+      static_cast<const T *>(a.query), a.lse, a.qidx, a.qrows, static_cast<const T *>(a.kc), a.bt,
       a.bt_stride, a.bt_cols, a.seq, a.Hq, a.Hk, a.bs, a.nblocks, a.C, a.max_chunks,
       a.scale * kLog2e, a.out, a.out_sum, a.err);
 }
@@ -455,10 +466,9 @@ int dispatch_typed(const ScoreArgs &a) {
   const size_t smem = sizeof(float) * 4 * (size_t)group * a.D;
   if (smem > 200 * 1024) return fail(DSB_ERR_UNSUPPORTED, "group * head_dim too large");
   auto kern = chunk_scores_generic_kernel<T, STATS>;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;
   dim3 grid(a.max_chunks, a.B);
-  kern<<<grid, 128, smem, a.st>>>(static_cast<const T *>(a.query), a.lse, a.qidx,
+  kern<<<grid, 128, smem, a.st>>>(static_cast<const T *>(a.query), a.lse, a.qidx, a.qrows,
                                   static_cast<const T *>(a.kc), a.bt, a.bt_stride, a.bt_cols,
                                   a.seq, a.Hq, a.Hk, a.D, a.bs, a.nblocks, a.C, a.max_chunks,
                                   a.scale * kLog2e, a.out, a.out_sum, a.err);
@@ -484,13 +494,13 @@ int run_scores(const ScoreArgs &a) {
 using namespace dsb;
 
 extern "C" int dsb_paged_chunk_head_scores(
-    const void *query, const float *softmax_lse, const int32_t *query_index,
+    const void *query, const float *softmax_lse, const int32_t *query_index, int32_t query_rows,
     const void *key_cache, const int32_t *block_table, int64_t block_table_stride,
     int64_t block_table_cols, const int32_t *seq_lens, int32_t batch,
     int32_t num_query_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
     int64_t num_blocks, int32_t chunk_size, int32_t max_chunks, float scale, int32_t dtype,
     float *head_scores, int32_t *error_flag, void *stream) {
-  ScoreArgs a{query, softmax_lse, query_index, key_cache, block_table, block_table_stride,
+  ScoreArgs a{query, softmax_lse, query_index, query_rows, key_cache, block_table, block_table_stride,
               block_table_cols, seq_lens, batch, num_query_heads, num_kv_heads, head_dim,
               block_size, num_blocks, chunk_size, max_chunks, scale, dtype, head_scores,
               nullptr, error_flag, as_stream(stream)};
@@ -498,13 +508,13 @@ extern "C" int dsb_paged_chunk_head_scores(
 }
 
 extern "C" int dsb_paged_chunk_stats(
-    const void *query, const int32_t *query_index, const void *key_cache,
+    const void *query, const int32_t *query_index, int32_t query_rows, const void *key_cache,
     const int32_t *block_table, int64_t block_table_stride, int64_t block_table_cols,
     const int32_t *seq_lens, int32_t batch, int32_t num_query_heads, int32_t num_kv_heads,
     int32_t head_dim, int32_t block_size, int64_t num_blocks, int32_t chunk_size,
     int32_t max_chunks, float scale, int32_t dtype, float *chunk_max, float *chunk_sum,
     int32_t *error_flag, void *stream) {
-  ScoreArgs a{query, nullptr, query_index, key_cache, block_table, block_table_stride,
+  ScoreArgs a{query, nullptr, query_index, query_rows, key_cache, block_table, block_table_stride,
               block_table_cols, seq_lens, batch, num_query_heads, num_kv_heads, head_dim,
               block_size, num_blocks, chunk_size, max_chunks, scale, dtype, chunk_max,
               chunk_sum, error_flag, as_stream(stream)};

@@ -235,9 +235,7 @@ extern "C" int dsb_select_context_chunks(
     return fail(DSB_ERR_INVALID, "selection state narrower than token_budget / chunk_size");
   const size_t smem = sizeof(uint32_t) * ((size_t)max_chunks + (size_t)S);
   if (smem > 220 * 1024) return fail(DSB_ERR_UNSUPPORTED, "too many chunks for one CTA");
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(select_chunks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+  if (int st_ = ensure_smem((const void *)select_chunks_kernel, smem); st_ != DSB_OK) return st_;
   select_chunks_kernel<<<rows, kThreads, smem, as_stream(stream)>>>(
       parts, row_stride, part_stride, num_parts, normalize_heads, seq_lens, row_slots,
       max_chunks, chunk_size, S, sel_chunks, sel_stride, sel_count, num_slots,

@@ -117,6 +117,7 @@ def paged_chunk_head_scores(
             _lib.ptr(query),
             _lib.ptr(lse),
             _lib.ptr(query_index),
+            query.shape[0],
             _lib.ptr(key_cache),
             *common,
             _lib.ptr(out),
@@ -169,6 +170,7 @@ def paged_chunk_stats(
         "dsb_paged_chunk_stats",
         _lib.ptr(query),
         _lib.ptr(query_index),
+        query.shape[0],
         _lib.ptr(key_cache),
         _lib.ptr(block_table),
         block_table.stride(0),

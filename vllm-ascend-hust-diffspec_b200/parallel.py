@@ -42,7 +42,10 @@ def gather_head_scores(
         return local
     rows, hk_local, n = local.shape
     stacked = torch.empty((world, rows, hk_local, n), dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(stacked, local.contiguous(), group=group)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(stacked, local.contiguous(), group=group)
+    else:  # gloo (CPU tests) has no all_gather_into_tensor
+        dist.all_gather(list(stacked.unbind(0)), local.contiguous(), group=group)
     if out is None:
         out = torch.empty((rows, world * hk_local, n), dtype=local.dtype, device=local.device)
     out.view(rows, world, hk_local, n).copy_(stacked.permute(1, 0, 2, 3))
