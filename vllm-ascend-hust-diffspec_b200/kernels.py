@@ -21,19 +21,21 @@ __all__ = [
 ]
 
 
-def _validate_scores(query, key_cache, softmax_lse, block_table, seq_lens):
-    # diffspec/kernels.py:107-120
+def _validate_scores(query, key_cache, softmax_lse, block_table, seq_lens, query_index=None):
+    """diffspec/kernels.py:107-120; with ``query_index`` the batch is the
+    number of mapped rows and query/LSE may hold more token rows."""
     if query.ndim != 3:
         raise ValueError("query must have shape [batch, query_heads, head_dim]")
     if key_cache.ndim != 4:
         raise ValueError("key_cache must have shape [blocks, block_size, kv_heads, head_dim]")
-    batch_size, num_query_heads, head_dim = query.shape
+    query_rows, num_query_heads, head_dim = query.shape
+    batch_size = query_rows if query_index is None else query_index.numel()
     _, block_size, num_kv_heads, key_head_dim = key_cache.shape
     if head_dim != key_head_dim:
         raise ValueError("query and key head dimensions must match")
     if num_query_heads % num_kv_heads != 0:
         raise ValueError("query heads must be divisible by KV heads")
-    if softmax_lse is not None and softmax_lse.numel() != batch_size * num_query_heads:
+    if softmax_lse is not None and softmax_lse.numel() != query_rows * num_query_heads:
         raise ValueError("softmax_lse must contain one value per query head")
     if query.dtype != key_cache.dtype:
         raise ValueError("query and key_cache must share a dtype")
@@ -47,6 +49,10 @@ def _prep_index(t: torch.Tensor) -> torch.Tensor:
     if t.dtype != torch.int32:
         t = t.to(torch.int32)
     return t
+
+
+def _batch(query, query_index):
+    return query.shape[0] if query_index is None else query_index.numel()
 
 
 def paged_chunk_head_scores(
@@ -70,11 +76,12 @@ def paged_chunk_head_scores(
     ``softmax_lse=None`` the log-sum-exp over each request's whole sequence is
     computed on the device first (diffspec/runtime.py:321-322).
     """
-    _validate_scores(query, key_cache, softmax_lse, block_table, seq_lens)
+    _validate_scores(query, key_cache, softmax_lse, block_table, seq_lens, query_index)
     if chunk_size <= 0:
         raise ValueError("chunk_size must be positive")
     device = _lib.require_cuda(query, key_cache, block_table, seq_lens)
-    batch_size, num_query_heads, head_dim = query.shape
+    _, num_query_heads, head_dim = query.shape
+    batch_size = _batch(query, query_index)
     num_blocks, block_size, num_kv_heads, _ = key_cache.shape
     max_chunks = (max_seq_len + chunk_size - 1) // chunk_size
     if out is None:
@@ -149,9 +156,10 @@ def paged_chunk_stats(
     ``max`` is in log2 units (``log2(e) * scale * q.k``); ``sum`` is the sum of
     ``exp(logit - max_logit)`` over the chunk's valid tokens.
     """
-    _validate_scores(query, key_cache, None, block_table, seq_lens)
+    _validate_scores(query, key_cache, None, block_table, seq_lens, query_index)
     device = _lib.require_cuda(query, key_cache, block_table, seq_lens)
-    batch_size, num_query_heads, head_dim = query.shape
+    _, num_query_heads, head_dim = query.shape
+    batch_size = _batch(query, query_index)
     num_blocks, block_size, num_kv_heads, _ = key_cache.shape
     max_chunks = (max_seq_len + chunk_size - 1) // chunk_size
     cmax = torch.empty((batch_size, num_query_heads, max_chunks), dtype=torch.float32, device=device)
