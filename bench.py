@@ -463,6 +463,12 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     with ClockSampler(local) as clocks:
+        # keep the GPU loaded for >= 0.6 s before the timed region so the
+        # 100 ms clock sampler sees the clocks under this load
+        t_end = time.perf_counter() + 0.6
+        while time.perf_counter() < t_end:
+            step()
+            torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(device)
@@ -472,6 +478,10 @@ def run_ours(args):
             step()
         end.record()
         torch.cuda.synchronize(device)
+        t_end = time.perf_counter() + 0.3  # a few samples after the timed region too
+        while time.perf_counter() < t_end:
+            step()
+            torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier()
     ms = start.elapsed_time(end) / args.steps
@@ -596,7 +606,7 @@ def emit_ours(args):
                         avg_launch_us=round(avg_ms * 1e3, 3),
                         per_kind_us={k: round(v[1] / v[0] * 1e3, 3) for k, v in kernel_t.items()},
                         per_kind_launches={k: v[0] for k, v in kernel_t.items()})
-    e2e = run_e2e(res, args)
+    e2e = None if args.no_e2e else run_e2e(res, args)
     cpu = None
     if world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
@@ -658,6 +668,30 @@ def emit_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_only(args):
+    """One kernel kind of the config-2 period, launched eagerly `--steps`
+    times after `--warmup` launches (the command the ncu captures run)."""
+    import torch
+
+    dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    w = Workload(torch, dsb, device, B_GROUP, HK, HQ, seed=1234)
+    launches = period_launches(w)
+    for kind, fn in launches:  # one full period so selection/plan state is real
+        fn()
+    picked = [fn for kind, fn in launches if kind == args.only]
+    if not picked:
+        raise SystemExit(f"no launch of kind {args.only}")
+    for i in range(args.warmup + args.steps):
+        picked[i % len(picked)]()
+    torch.cuda.synchronize(device)
+    flag = dsb._lib.read_and_clear_error_flag(device)
+    print(json.dumps({"only": args.only, "launches": args.warmup + args.steps, "error_flag": flag}))
+    if flag:
+        raise SystemExit(1)
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -666,10 +700,15 @@ def main():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end API leg")
+    p.add_argument("--only", choices=["prepare", "scores", "select", "plan", "rebuild", "attention"],
+                   help="launch one kernel kind eagerly (for profiler captures)")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         emit_reference(args)
     else:
         emit_ours(args)

@@ -15,8 +15,9 @@
 //      O^T[D x 8 heads]     += V^T[D x 16 tok] P^T[16 x 8]    (A = V from HBM)
 //    K and V go from HBM straight into A-fragment registers with 16-byte
 //    loads: lane (g, t) loads K tokens g, g+8 at head-dim slab t, and V tokens
-//    2t, 2t+1, 2t+8, 2t+9 at head-dim run [D/8 * g, D/8 * (g+1)); the V pairs
-//    are formed with one byte-permute per register.  P goes C-layout ->
+//    2t, 2t+1, 2t+8, 2t+9 at head-dim runs {8 * (8j + g) .. +8 : j < D/64}
+//    (each load instruction covers contiguous 128-byte runs); the V pairs are
+//    formed with one byte-permute per register.  P goes C-layout ->
 //    B-layout through a 256-byte per-warp shared tile and ldmatrix.trans.
 //  * the online softmax runs in base 2 in fp32; splits publish (m, l, O)
 //    partials and the last split of each (row, kv head) to finish merges them
@@ -166,7 +167,7 @@ draft_attention_kernel(const AttnArgs a) {
         const T *rv = (tv == pos) ? nv : wv + (int64_t)tv * D;
 #pragma unroll
         for (int j = 0; j < VPL; ++j)
-          vv[q][j] = (tv < te) ? ldg_stream(rv + (D / 8) * g + 8 * j) : make_uint4(0, 0, 0, 0);
+          vv[q][j] = (tv < te) ? ldg_stream(rv + 8 * (8 * j + g)) : make_uint4(0, 0, 0, 0);
       }
     }
     const bool va = base + g < te, vb = base + g + 8 < te;
@@ -258,7 +259,8 @@ draft_attention_kernel(const AttnArgs a) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int h = nt * 8 + 2 * t + (c & 1);
-        const int d = (D / 8) * g + ((c < 2) ? i : NM + i);
+        const int e = (c < 2) ? i : NM + i;  // element of the lane's V run list
+        const int d = 64 * (e / 8) + 8 * g + e % 8;
         s_o[(warp * GP + h) * D + d] = o[nt][i][c];
       }
   }
@@ -321,19 +323,48 @@ draft_attention_kernel(const AttnArgs a) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int idx = threadIdx.x; idx < n_out; idx += blockDim.x) {
-    const int h = idx / D, d = idx % D;
+  // Merge: stage every split's (m, l) in shared memory (one independent load
+  // per thread), fold them into per-split weights exp2(m_s - M) / L, then
+  // each output float4 sums `active` independent float4 loads.
+  float *w_s = s_o;  // [active][GP]; the CTA's own O staging is no longer needed
+  float *l_s = s_o + (size_t)active * GP;
+  for (int i = threadIdx.x; i < active * GP; i += blockDim.x) {
+    const float *ps = part_base + (int64_t)(i / GP) * part_floats;
+    w_s[i] = __ldcg(ps + i % GP);
+    l_s[i] = __ldcg(ps + GP + i % GP);
+  }
+  __syncthreads();
+  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
     float M = -INFINITY;
-    for (int s = 0; s < active; ++s) M = fmaxf(M, __ldcg(part_base + s * part_floats + h));
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < active; ++s) {
-      const float *ps = part_base + s * part_floats;
-      const float ms = __ldcg(ps + h);
+    for (int s2 = 0; s2 < active; ++s2) M = fmaxf(M, w_s[s2 * GP + h]);
+    float L = 0.f;
+    for (int s2 = 0; s2 < active; ++s2) {
+      const float ms = w_s[s2 * GP + h];
       const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
-      L += __ldcg(ps + GP + h) * f;
-      O += __ldcg(ps + 2 * GP + h * D + d) * f;
+      w_s[s2 * GP + h] = f;
+      L += l_s[s2 * GP + h] * f;
     }
-    orow[idx] = Elem<T>::from_f(O / L);
+    const float inv = 1.f / L;
+    for (int s2 = 0; s2 < active; ++s2) w_s[s2 * GP + h] *= inv;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < n_out / 4; idx += blockDim.x) {
+    const int h = (4 * idx) / D, d = (4 * idx) % D;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int s2 = 0; s2 < active; ++s2) {
+      const float4 o = __ldcg(reinterpret_cast<const float4 *>(
+          part_base + (int64_t)s2 * part_floats + 2 * GP + h * D + d));
+      const float f = w_s[s2 * GP + h];
+      acc.x += o.x * f;
+      acc.y += o.y * f;
+      acc.z += o.z * f;
+      acc.w += o.w * f;
+    }
+    orow[4 * idx] = Elem<T>::from_f(acc.x);
+    orow[4 * idx + 1] = Elem<T>::from_f(acc.y);
+    orow[4 * idx + 2] = Elem<T>::from_f(acc.z);
+    orow[4 * idx + 3] = Elem<T>::from_f(acc.w);
   }
   if (threadIdx.x == 0) a.counters[row * a.Hk + kvh] = 0;
 }
@@ -349,7 +380,8 @@ extern "C" int32_t dsb_draft_attention_default_splits(int32_t rows, int32_t num_
   if (sm_count <= 0) sm_count = 148;
   const int64_t pairs = (int64_t)rows * num_kv_heads;
   int64_t splits = (4LL * sm_count + pairs - 1) / pairs;
-  const int64_t max_splits = (working_budget + 63) / 64;
+  int64_t max_splits = (working_budget + 31) / 32;
+  if (max_splits > 64) max_splits = 64;
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
   return (int32_t)splits;
@@ -388,7 +420,12 @@ extern "C" int dsb_draft_decode_attention(
   if (num_splits <= 0) return fail(DSB_ERR_INVALID, "num_splits must be positive");
   if (out_rows > 65535 || num_kv_heads > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
   int split_tokens = (working_budget + num_splits - 1) / num_splits;
-  split_tokens = (split_tokens + 63) / 64 * 64;
+  split_tokens = (split_tokens + 31) / 32 * 32;
+  // the last split stages (m, l) of every split in the CTA's shared memory,
+  // which holds 2 * head_dim floats per padded head
+  const int max_splits = 2 * head_dim;
+  if ((working_budget + split_tokens - 1) / split_tokens > max_splits)
+    split_tokens = ((working_budget + max_splits - 1) / max_splits + 31) / 32 * 32;
   const int splits = (working_budget + split_tokens - 1) / split_tokens;
   if (splits > 1 && rows > 0) {
     const int64_t need = dsb_draft_attention_scratch_floats(rows, num_query_heads, num_kv_heads,

@@ -7,7 +7,9 @@
 namespace dsb {
 namespace {
 
-// One thread per plan row: _history_plan_host, diffspec/runtime.py:1713-1735.
+// One warp per plan row: _history_plan_host, diffspec/runtime.py:1713-1735.
+// Lanes read the slot's selected chunks in parallel and a warp reduction
+// forms prefix_tokens, so a row costs one round of loads.
 __global__ void build_plan_kernel(const int32_t *__restrict__ row_slots,
                                   const int32_t *__restrict__ committed_lens, int rows,
                                   const int32_t *__restrict__ sel_chunks, int sel_stride,
@@ -15,21 +17,28 @@ __global__ void build_plan_kernel(const int32_t *__restrict__ row_slots,
                                   int HB, int plan_width, int64_t *__restrict__ plan,
                                   int32_t *__restrict__ history_lens,
                                   int32_t *__restrict__ working_lens, int32_t *err) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= rows) return;
   int64_t *out = plan + (int64_t)r * plan_width;
   const int slot = (row_slots != nullptr) ? row_slots[r] : r;
   if (slot < 0 || slot >= num_slots) {
-    flag_error(err, DSB_FLAG_SLOT);
-    for (int i = 0; i < plan_width; ++i) out[i] = 0;
-    if (history_lens != nullptr) history_lens[r] = 0;
+    if (lane == 0) flag_error(err, DSB_FLAG_SLOT);
+    for (int i = lane; i < plan_width; i += 32) out[i] = 0;
+    if (lane == 0 && history_lens != nullptr) history_lens[r] = 0;
     return;
   }
   const int64_t he = max(0, committed_lens[r] - 1);  // history ends before the root
   const int cnt = sel_count[slot];
-  int64_t hlen, tail_start, prefix_len = 0, prefix_drop = 0;
-  int n_chunks = 0;
+  const int32_t *ch = sel_chunks + (int64_t)slot * sel_stride;
+  const int n_sel = min(max(cnt, 0), sel_stride);
+  int n_chunks = n_sel;
+  if (5 + n_chunks > plan_width) {
+    if (lane == 0) flag_error(err, DSB_FLAG_CAPACITY);
+    n_chunks = plan_width - 5;
+  }
   const int64_t tail_len = min(he, (int64_t)min(C, HB));
+  int64_t hlen, tail_start, prefix_len = 0, prefix_drop = 0;
   if (cnt < 0) {  // no retrieval yet: the most recent history_budget tokens
     hlen = min(he, (int64_t)HB);
     tail_start = he - hlen;
@@ -37,32 +46,31 @@ __global__ void build_plan_kernel(const int32_t *__restrict__ row_slots,
     hlen = tail_len;
     tail_start = he - tail_len;
   } else {
-    n_chunks = min(cnt, sel_stride);
-    if (5 + n_chunks > plan_width) {
-      flag_error(err, DSB_FLAG_CAPACITY);
-      n_chunks = plan_width - 5;
-    }
-    const int32_t *ch = sel_chunks + (int64_t)slot * sel_stride;
     tail_start = he - tail_len;
-    const int64_t prefix_end = min(tail_start, (int64_t)ch[min(cnt, sel_stride) - 1] * C);
-    int64_t prefix_tokens = 0;
-    for (int i = 0; i < min(cnt, sel_stride); ++i) {
-      const int64_t v = prefix_end - (int64_t)ch[i] * C;
-      prefix_tokens += max((int64_t)0, min((int64_t)C, v));
-    }
-    prefix_len = min(prefix_tokens, (int64_t)HB - tail_len);
-    prefix_drop = prefix_tokens - prefix_len;
+    const int64_t prefix_end = min(tail_start, (int64_t)ch[n_sel - 1] * C);
+    int64_t part = 0;
+    for (int i = lane; i < n_sel; i += 32)
+      part += max((int64_t)0, min((int64_t)C, prefix_end - (int64_t)ch[i] * C));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    prefix_len = min(part, (int64_t)HB - tail_len);
+    prefix_drop = part - prefix_len;
     hlen = prefix_len + tail_len;
   }
-  out[0] = slot;
-  out[1] = hlen;
-  out[2] = tail_start;
-  out[3] = prefix_len;
-  out[4] = prefix_drop;
-  const int32_t *ch = sel_chunks + (int64_t)slot * sel_stride;
-  for (int i = 5; i < plan_width; ++i) out[i] = (i - 5 < n_chunks) ? ch[i - 5] : 0;
-  if (history_lens != nullptr) history_lens[r] = (int32_t)hlen;
-  if (working_lens != nullptr) working_lens[slot] = (int32_t)hlen;
+  for (int i = lane; i < plan_width; i += 32) {
+    int64_t v;
+    if (i == 0) v = slot;
+    else if (i == 1) v = hlen;
+    else if (i == 2) v = tail_start;
+    else if (i == 3) v = prefix_len;
+    else if (i == 4) v = prefix_drop;
+    else v = (i - 5 < n_chunks) ? ch[i - 5] : 0;
+    out[i] = v;
+  }
+  if (lane == 0) {
+    if (history_lens != nullptr) history_lens[r] = (int32_t)hlen;
+    if (working_lens != nullptr) working_lens[slot] = (int32_t)hlen;
+  }
 }
 
 // _accept_target_queries, diffspec/runtime.py:1211-1276 (linear proposals).
@@ -148,7 +156,7 @@ extern "C" int dsb_build_history_plan(const int32_t *row_slots, const int32_t *c
   if (chunk_size <= 0 || history_budget <= 0 || plan_width < 5 || sel_stride <= 0 ||
       num_slots <= 0)
     return fail(DSB_ERR_INVALID, "bad chunk size, budget, plan width or selection stride");
-  build_plan_kernel<<<(rows + 127) / 128, 128, 0, as_stream(stream)>>>(
+  build_plan_kernel<<<(rows + 3) / 4, 128, 0, as_stream(stream)>>>(
       row_slots, committed_lens, rows, sel_chunks, sel_stride, sel_count, num_slots,
       chunk_size, history_budget, plan_width, plan, history_lens, working_lens, error_flag);
   return check_launch("build_plan_kernel");

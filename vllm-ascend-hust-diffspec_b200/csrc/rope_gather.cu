@@ -40,6 +40,7 @@ struct RopeArgs {
   const void *cos_sin;
   int64_t cs_stride, cs_rows;
   int heads, head_dim, rotary_dim, neox, tokens_per_warp;
+  int vec_rope;  // NeoX with 16-byte-aligned halves and cos/sin rows: vector path
   int32_t *err;
 };
 
@@ -54,6 +55,26 @@ __device__ __forceinline__ void cp_async_wait_all() {
 template <typename CS>
 __device__ __forceinline__ float cs_load(const CS *p) {
   return Elem<CS>::to_f(*p);
+}
+
+// N consecutive table entries as floats (aligned vector loads; N * sizeof(CS)
+// is 8, 16 or 32 bytes).
+template <typename CS, int N>
+__device__ __forceinline__ void cs_load_vec(const CS *p, float (&out)[N]) {
+  constexpr int bytes = N * (int)sizeof(CS);
+  union {
+    uint4 q[bytes >= 16 ? bytes / 16 : 1];
+    uint2 d;
+    CS e[N];
+  } u;
+  if constexpr (bytes >= 16) {
+#pragma unroll
+    for (int i = 0; i < bytes / 16; ++i) u.q[i] = __ldg(reinterpret_cast<const uint4 *>(p) + i);
+  } else {
+    u.d = __ldg(reinterpret_cast<const uint2 *>(p));
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = Elem<CS>::to_f(u.e[i]);
 }
 
 template <typename T, typename CS, bool GATHER>
@@ -197,6 +218,27 @@ __global__ void __launch_bounds__(kWarpsRope * 32) rope_rows_kernel(const RopeAr
       } out;
       out.u = sk[v];
       const CS *csr = cs + p * a.cs_stride;
+      if (a.vec_rope) {  // whole vector rotary; partner is the vector half away
+        const bool first = d0 < half;
+        const int i0 = first ? d0 : d0 - half;
+        union {
+          uint4 u;
+          T e[VE];
+        } par;
+        par.u = sk[first ? v + half / VE : v - half / VE];
+        float c[VE], sn[VE];
+        cs_load_vec<CS, VE>(csr + i0, c);
+        cs_load_vec<CS, VE>(csr + half + i0, sn);
+#pragma unroll
+        for (int e = 0; e < VE; ++e) {
+          const float x = Elem<T>::to_f(out.e[e]), y = Elem<T>::to_f(par.e[e]);
+          const float r = first ? __fmul_rn(x, c[e]) - __fmul_rn(y, sn[e])
+                                : __fmul_rn(x, c[e]) + __fmul_rn(y, sn[e]);
+          out.e[e] = Elem<T>::from_f(r);
+        }
+        stg_stream(dst_k + dst_off, out.u);
+        continue;
+      }
 #pragma unroll
       for (int e = 0; e < VE; ++e) {
         const int d = d0 + e;
@@ -234,6 +276,10 @@ int launch_rope(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
   const size_t smem = (size_t)kWarpsRope * U * 2 * row_bytes;
   if (smem > 200 * 1024) return fail(DSB_ERR_UNSUPPORTED, "KV rows too wide for staging");
   a.tokens_per_warp = U;
+  constexpr int VE = 16 / (int)sizeof(T);
+  a.vec_rope = a.neox && a.rotary_dim > 0 && (a.rotary_dim / 2) % VE == 0 &&
+               reinterpret_cast<uintptr_t>(a.cos_sin) % 16 == 0 &&
+               (a.cs_stride * (int64_t)sizeof(CS)) % 16 == 0;
   auto kern = rope_rows_kernel<T, CS, GATHER>;
   if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;
   const int64_t per_cta = (int64_t)kWarpsRope * U;
