@@ -180,6 +180,31 @@ int dsb_draft_decode_attention(
     int32_t dtype, void *output, float *scratch, int64_t scratch_floats,
     int32_t *counters, int32_t num_splits, int32_t *error_flag, void *stream);
 
+/* dsb_draft_decode_attention for callers that cannot allocate device memory
+ * (no counterpart in the reference).  A serving engine that reserves almost
+ * all free memory for its KV cache up front, a step recorded during CUDA
+ * stream capture, or a latency-bound caller that cannot absorb a possibly
+ * device-synchronising cudaMalloc/cudaFree cannot provide the split scratch
+ * and tickets that dsb_draft_decode_attention takes.  This variant uses the
+ * library's own file-scope device arrays instead: 1048576 floats (4 MiB) of
+ * split partials and 4096 tickets, held by every GPU that loads the library
+ * until the process exits, and calls no allocating routine.  Calls needing
+ * more scratch (rows * kv_heads * splits * padded heads * (2 + head_dim)
+ * floats) or more than 4096 rows * kv_heads are rejected with
+ * DSB_ERR_INVALID.  num_splits <= 0 picks the library default.  The first
+ * call on a device looks the arrays' device addresses up (cudaGetSymbolAddress,
+ * with that device current); make that first call before any stream capture.
+ * Every call shares the arrays and clears the tickets it uses with a
+ * memset on `stream`, so calls that overlap on the GPU (other streams,
+ * concurrent graphs) race and must be serialised by the caller. */
+int dsb_draft_decode_attention_static(
+    const void *query, const void *key, const void *value, void *working_key,
+    void *working_value, const int32_t *slots, const int32_t *positions,
+    int32_t position_offset, int32_t rows, int32_t out_rows, int32_t num_slots,
+    int32_t num_query_heads, int32_t num_kv_heads, int32_t head_dim,
+    int32_t working_budget, float scale, int32_t dtype, void *output,
+    int32_t num_splits, int32_t *error_flag, void *stream);
+
 /* Split count the library would choose and the scratch size it then needs. */
 int32_t dsb_draft_attention_default_splits(int32_t rows, int32_t num_kv_heads,
                                            int32_t working_budget, int32_t sm_count);

@@ -90,6 +90,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F32, _I32, _P,
          _P, _I64, _P, _I32, _P, _P],
     ),
+    "dsb_draft_decode_attention_static": (
+        ctypes.c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F32, _I32,
+         _P, _I32, _P, _P],
+    ),
     "dsb_draft_attention_default_splits": (_I32, [_I32, _I32, _I32, _I32]),
     "dsb_draft_attention_scratch_floats": (_I64, [_I32, _I32, _I32, _I32, _I32]),
     "dsb_prepare_retrieval_rows": (

@@ -23,6 +23,9 @@
 //    partials and the last split of each (row, kv head) to finish merges them
 //    (an atomic ticket, no spin wait).
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <string>
 
 #include "common.cuh"
 
@@ -459,5 +462,136 @@ extern "C" int dsb_draft_decode_attention(
     DSB_AT(__half, 256, 1) DSB_AT(__half, 256, 2)
   }
 #undef DSB_AT
+  return fail(DSB_ERR_UNSUPPORTED, "no draft attention kernel for this shape");
+}
+
+// ---------------------------------------------------------------------------
+// Draft attention without any allocation by the caller or the library.
+//
+// Some callers cannot call cudaMalloc when they run the draft step: a serving
+// engine that reserves nearly all free device memory for its KV cache at start
+// and then forbids ad-hoc allocations, a host that records the step into a
+// CUDA graph (allocation is not allowed during stream capture), or a caller
+// whose latency budget cannot absorb cudaMalloc/cudaFree, which may
+// synchronise the device.  For them the split-KV partials and merge tickets
+// live in the fixed arrays below, which every GPU that loads this library
+// holds until the process exits (4 MiB + 16 KiB per device).
+//
+// In host code the array names are host-side stand-ins, not device
+// addresses; their device addresses are looked up with cudaGetSymbolAddress
+// once per device, with that device current, on the first call made on it.
+namespace dsb {
+namespace {
+
+constexpr int64_t kStaticScratchFloats = 1 << 20;  // 4 MiB of split partials
+constexpr int kStaticTickets = 4096;                 // rows * kv_heads limit
+
+static __device__ __align__(256) float g_static_scratch[kStaticScratchFloats];
+static __device__ __align__(256) int32_t g_static_tickets[kStaticTickets];
+
+struct StaticScratch {
+  float *scratch = nullptr;
+  int32_t *tickets = nullptr;
+};
+
+int static_scratch_for_current_device(StaticScratch &out) {
+  static std::mutex mu;
+  static std::map<int, StaticScratch> per_device;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(DSB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = per_device.find(dev);
+  if (it != per_device.end()) {
+    out = it->second;
+    return DSB_OK;
+  }
+  StaticScratch s;
+  e = cudaGetSymbolAddress(reinterpret_cast<void **>(&s.scratch), g_static_scratch);
+  if (e != cudaSuccess)
+    return fail(DSB_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+  e = cudaGetSymbolAddress(reinterpret_cast<void **>(&s.tickets), g_static_tickets);
+  if (e != cudaSuccess)
+    return fail(DSB_ERR_CUDA, std::string("cudaGetSymbolAddress(tickets): ") + cudaGetErrorString(e));
+  per_device[dev] = s;
+  out = s;
+  return DSB_OK;
+}
+
+}  // namespace
+}  // namespace dsb
+
+extern "C" int dsb_draft_decode_attention_static(
+    const void *query, const void *key, const void *value, void *working_key,
+    void *working_value, const int32_t *slots, const int32_t *positions,
+    int32_t position_offset, int32_t rows, int32_t out_rows, int32_t num_slots,
+    int32_t num_query_heads, int32_t num_kv_heads, int32_t head_dim, int32_t working_budget,
+    float scale, int32_t dtype, void *output, int32_t num_splits, int32_t *error_flag,
+    void *stream) {
+  if (rows < 0 || out_rows < rows) return fail(DSB_ERR_INVALID, "out_rows must be >= rows >= 0");
+  if (out_rows == 0) return DSB_OK;
+  if (num_query_heads <= 0 || num_kv_heads <= 0 || num_query_heads % num_kv_heads)
+    return fail(DSB_ERR_INVALID, "query heads must be divisible by KV heads");
+  if (num_slots <= 0 || working_budget <= 0) return fail(DSB_ERR_INVALID, "empty working cache");
+  if (dtype != DSB_BF16 && dtype != DSB_F16)
+    return fail(DSB_ERR_UNSUPPORTED, "draft attention runs on BF16 or FP16 caches");
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(DSB_ERR_UNSUPPORTED, "draft attention supports head_dim 64, 128 or 256");
+  const int group = num_query_heads / num_kv_heads;
+  if (group > 16) return fail(DSB_ERR_UNSUPPORTED, "draft attention supports GQA groups up to 16");
+  if (!query || !key || !value || !working_key || !working_value || !slots || !positions || !output)
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (out_rows > 65535 || num_kv_heads > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
+  if ((int64_t)rows * num_kv_heads > kStaticTickets)
+    return fail(DSB_ERR_INVALID, "rows * num_kv_heads exceeds the static ticket array (4096)");
+  if (num_splits <= 0)
+    num_splits = dsb_draft_attention_default_splits(rows, num_kv_heads, working_budget, sm_count());
+  int split_tokens = (working_budget + num_splits - 1) / num_splits;
+  split_tokens = (split_tokens + 31) / 32 * 32;
+  const int max_splits = 2 * head_dim;
+  if ((working_budget + split_tokens - 1) / split_tokens > max_splits)
+    split_tokens = ((working_budget + max_splits - 1) / max_splits + 31) / 32 * 32;
+  const int splits = (working_budget + split_tokens - 1) / split_tokens;
+  const int64_t need =
+      dsb_draft_attention_scratch_floats(rows, num_query_heads, num_kv_heads, head_dim, splits);
+  if (splits > 1 && need > kStaticScratchFloats)
+    return fail(DSB_ERR_INVALID,
+                "split partials need " + std::to_string(need) +
+                    " floats, more than the static scratch (1048576 floats = 4 MiB); "
+                    "pass fewer splits or use dsb_draft_decode_attention");
+  StaticScratch st_mem;
+  if (int st = static_scratch_for_current_device(st_mem); st != DSB_OK) return st;
+  cudaStream_t st = as_stream(stream);
+  // The arrays are shared by every call: tickets must start at zero, so
+  // clear the ones this call uses (a plain memset, no allocation).
+  if (rows > 0) {
+    cudaError_t e = cudaMemsetAsync(st_mem.tickets, 0, sizeof(int32_t) * rows * num_kv_heads, st);
+    if (e != cudaSuccess) return fail(DSB_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  }
+  AttnArgs a{query, key, value, working_key, working_value, slots, positions, position_offset,
+             rows, out_rows, num_slots, num_query_heads, num_kv_heads, working_budget,
+             scale * kLog2e, output, st_mem.scratch, st_mem.tickets, splits, split_tokens,
+             error_flag};
+  const int nt = group <= 8 ? 1 : 2;
+#define DSB_ATS(TT, DD, NN)                                                            \
+  if (head_dim == DD && nt == NN) {                                                    \
+    constexpr int GP = NN * 8;                                                         \
+    const size_t smem = sizeof(float) * (kAttnWarps * GP * DD + 2 * kAttnWarps * GP) + \
+                        sizeof(TT) * kAttnWarps * 16 * GP;                             \
+    auto kern = draft_attention_kernel<TT, DD, NN>;                                    \
+    if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;   \
+    kern<<<dim3(splits, num_kv_heads, out_rows), kAttnWarps * 32, smem, st>>>(a);     \
+    return check_launch("draft_attention_kernel (static scratch)");                    \
+  }
+  if (dtype == DSB_BF16) {
+    DSB_ATS(__nv_bfloat16, 64, 1) DSB_ATS(__nv_bfloat16, 64, 2)
+    DSB_ATS(__nv_bfloat16, 128, 1) DSB_ATS(__nv_bfloat16, 128, 2)
+    DSB_ATS(__nv_bfloat16, 256, 1) DSB_ATS(__nv_bfloat16, 256, 2)
+  } else {
+    DSB_ATS(__half, 64, 1) DSB_ATS(__half, 64, 2)
+    DSB_ATS(__half, 128, 1) DSB_ATS(__half, 128, 2)
+    DSB_ATS(__half, 256, 1) DSB_ATS(__half, 256, 2)
+  }
+#undef DSB_ATS
   return fail(DSB_ERR_UNSUPPORTED, "no draft attention kernel for this shape");
 }
