@@ -47,6 +47,7 @@ extern "C" {
 #define DSB_FLAG_BLOCK 4      /* block-table entry outside [0, num_blocks)   */
 #define DSB_FLAG_PLAN 8       /* malformed plan row                          */
 #define DSB_FLAG_CAPACITY 16  /* selection larger than the per-slot capacity */
+#define DSB_FLAG_TIMEOUT 32   /* a bounded wait for an asynchronous copy ran out */
 
 const char *dsb_last_error(void);
 int dsb_abi_version(void);

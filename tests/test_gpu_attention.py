@@ -24,7 +24,10 @@ def bf16(a, device):
 
 @pytest.mark.parametrize("i", range(len(R.attention_cases())))
 @pytest.mark.parametrize("splits", [None, 1])
-def test_attention_matches_reference(dsb, cuda, i, splits):
+@pytest.mark.parametrize("kernel", ["tma", "legacy"])
+def test_attention_matches_reference(dsb, cuda, i, splits, kernel, monkeypatch):
+    if kernel == "legacy":  # the register-fed kernel the library falls back to
+        monkeypatch.setenv("DSB_ATTENTION_LEGACY", "1")
     d = golden("attention")
     inp = R.attention_inputs(i)
     n = len(inp["slots"])
@@ -49,9 +52,13 @@ def test_attention_matches_reference(dsb, cuda, i, splits):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-@pytest.mark.parametrize("hq,hk,d", [(32, 4, 128), (64, 8, 128), (16, 1, 128), (8, 2, 64)])
-def test_long_history_split_kv_vs_oracle(dsb, cuda, dtype, hq, hk, d):
+@pytest.mark.parametrize("hq,hk,d", [(32, 4, 128), (64, 8, 128), (16, 1, 128), (8, 2, 64),
+                                     (16, 2, 256), (32, 2, 128)])
+@pytest.mark.parametrize("kernel", ["tma", "legacy"])
+def test_long_history_split_kv_vs_oracle(dsb, cuda, dtype, hq, hk, d, kernel, monkeypatch):
     """Config-2 lengths (history 1984 + draft step) with reordered slots."""
+    if kernel == "legacy":
+        monkeypatch.setenv("DSB_ATTENTION_LEGACY", "1")
     tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
     g = R.rng(hq * 131 + hk + d)
     slots_n, w = 6, 2048

@@ -31,6 +31,7 @@ FLAG_NAMES = {
     4: "block-table entry out of range",
     8: "malformed plan row",
     16: "selection exceeds per-slot capacity",
+    32: "bounded wait for an asynchronous copy ran out",
 }
 
 _DTYPE_CODES = {

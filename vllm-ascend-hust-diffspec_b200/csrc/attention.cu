@@ -23,9 +23,14 @@
 //    partials and the last split of each (row, kv head) to finish merges them
 //    (an atomic ticket, no spin wait).
 #include <cmath>
+#include <cstdlib>
+#include <type_traits>
 #include <map>
 #include <mutex>
 #include <string>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 
@@ -52,11 +57,146 @@ __device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
 
+template <int D> struct AttnStages { static constexpr int value = D >= 256 ? 2 : 3; };
+
+// 16-byte cp.async global -> shared; when !valid nothing is read and the
+// destination is zero-filled.
+__device__ __forceinline__ void cp_async16_zfill(void *smem_dst, const void *gmem_src, bool valid) {
+  if (valid) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+  } else {
+    *reinterpret_cast<uint4 *>(smem_dst) = make_uint4(0, 0, 0, 0);
+  }
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename T, int D, int NT>
+constexpr size_t attn_smem_bytes() {
+  return sizeof(uint4) * kAttnWarps * AttnStages<D>::value * (D / 8) * 32 +
+         sizeof(float) * 2 * kAttnWarps * NT * 8 + sizeof(T) * kAttnWarps * 16 * NT * 8;
+}
+
 template <typename T, int D>
 __device__ __forceinline__ void zero_heads(T *out, int row, int Hq, int h0, int n) {
   uint4 *o = reinterpret_cast<uint4 *>(out + ((int64_t)row * Hq + h0) * D);
   for (int i = threadIdx.x; i < n * D * (int)sizeof(T) / 16; i += blockDim.x)
     o[i] = make_uint4(0, 0, 0, 0);
+}
+
+// Combine the CTA's warps (staged in s_o/s_m/s_l) and either store the
+// normalised output (single split) or publish a partial; the last split of a
+// (row, kv head) to finish merges all partials.
+template <typename T, int D, int GP, int WARPS>
+__device__ __forceinline__ void merge_and_store(const AttnArgs &a, float *s_o, const float *s_m,
+                                                const float *s_l, T *out, int row, int kvh,
+                                                int split, int active, int group, int *s_last) {
+  const int n_out = group * D;
+  T *orow = out + ((int64_t)row * a.Hq + kvh * group) * D;
+  if (active == 1) {
+    for (int idx = threadIdx.x; idx < n_out; idx += blockDim.x) {
+      const int h = idx / D, d = idx % D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) M = fmaxf(M, s_m[w * GP + h]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) {
+        const float f = (s_m[w * GP + h] == -INFINITY) ? 0.f : exp2f(s_m[w * GP + h] - M);
+        L += s_l[w * GP + h] * f;
+        O += s_o[(w * GP + h) * D + d] * f;
+      }
+      orow[idx] = Elem<T>::from_f(O / L);
+    }
+    return;
+  }
+
+  // ---- publish this split's partial state
+  const int64_t part_floats = (int64_t)GP * (2 + D);
+  float *part_base = a.scratch + ((int64_t)row * a.Hk + kvh) * a.num_splits * part_floats;
+  float *part = part_base + (int64_t)split * part_floats;
+  for (int idx = threadIdx.x; idx < GP * (D + 1); idx += blockDim.x) {
+    if (idx < GP) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) M = fmaxf(M, s_m[w * GP + idx]);
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w)
+        L += (s_m[w * GP + idx] == -INFINITY) ? 0.f : s_l[w * GP + idx] * exp2f(s_m[w * GP + idx] - M);
+      part[idx] = M;
+      part[GP + idx] = L;
+    } else {
+      const int k = idx - GP, h = k / D, d = k % D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) M = fmaxf(M, s_m[w * GP + h]);
+      float O = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w)
+        O += (s_m[w * GP + h] == -INFINITY) ? 0.f
+                                            : s_o[(w * GP + h) * D + d] * exp2f(s_m[w * GP + h] - M);
+      part[2 * GP + k] = O;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&a.counters[row * a.Hk + kvh], 1);
+    (*s_last) = (prev == active - 1);
+  }
+  __syncthreads();
+  if (!(*s_last)) return;
+  __threadfence();
+  // Merge: stage every split's (m, l) in shared memory (one independent load
+  // per thread), fold them into per-split weights exp2(m_s - M) / L, then
+  // each output float4 sums `active` independent float4 loads.
+  float *w_s = s_o;  // [active][GP]; the CTA's own O staging is no longer needed
+  float *l_s = s_o + (size_t)active * GP;
+  for (int i = threadIdx.x; i < active * GP; i += blockDim.x) {
+    const float *ps = part_base + (int64_t)(i / GP) * part_floats;
+    w_s[i] = __ldcg(ps + i % GP);
+    l_s[i] = __ldcg(ps + GP + i % GP);
+  }
+  __syncthreads();
+  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < active; ++s2) M = fmaxf(M, w_s[s2 * GP + h]);
+    float L = 0.f;
+    for (int s2 = 0; s2 < active; ++s2) {
+      const float ms = w_s[s2 * GP + h];
+      const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+      w_s[s2 * GP + h] = f;
+      L += l_s[s2 * GP + h] * f;
+    }
+    const float inv = 1.f / L;
+    for (int s2 = 0; s2 < active; ++s2) w_s[s2 * GP + h] *= inv;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < n_out / 4; idx += blockDim.x) {
+    const int h = (4 * idx) / D, d = (4 * idx) % D;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int s2 = 0; s2 < active; ++s2) {
+      const float4 o = __ldcg(reinterpret_cast<const float4 *>(
+          part_base + (int64_t)s2 * part_floats + 2 * GP + h * D + d));
+      const float f = w_s[s2 * GP + h];
+      acc.x += o.x * f;
+      acc.y += o.y * f;
+      acc.z += o.z * f;
+      acc.w += o.w * f;
+    }
+    orow[4 * idx] = Elem<T>::from_f(acc.x);
+    orow[4 * idx + 1] = Elem<T>::from_f(acc.y);
+    orow[4 * idx + 2] = Elem<T>::from_f(acc.z);
+    orow[4 * idx + 3] = Elem<T>::from_f(acc.w);
+  }
+  if (threadIdx.x == 0) a.counters[row * a.Hk + kvh] = 0;
 }
 
 template <typename T, int D, int NT>
@@ -66,9 +206,13 @@ draft_attention_kernel(const AttnArgs a) {
   constexpr int NM = D / 16;   // M-tiles of O^T over head_dim
   constexpr int GP = NT * 8;   // padded heads per group
   constexpr int VPL = D / 64;  // 16-byte V vectors per token per lane
+  constexpr int NS = AttnStages<D>::value;  // cp.async ring depth per warp
+  constexpr int VPT = D / 8;   // 16-byte vectors per lane per 16-token tile (K + V)
   extern __shared__ float smem[];
-  float *s_o = smem;                                    // [warps][GP][D]
-  float *s_m = s_o + kAttnWarps * GP * D;               // [warps][GP]
+  // [warps][NS][VPT][32 lanes] uint4: every lane reads back only what it copied
+  uint4 *ring = reinterpret_cast<uint4 *>(smem);
+  float *s_o = smem;                                    // [warps][GP][D], aliases the ring
+  float *s_m = smem + kAttnWarps * NS * VPT * 32 * 4;   // [warps][GP]
   float *s_l = s_m + kAttnWarps * GP;                   // [warps][GP]
   T *s_p = reinterpret_cast<T *>(s_l + kAttnWarps * GP);  // [warps][16][GP]
   __shared__ int s_last;
@@ -152,26 +296,55 @@ draft_attention_kernel(const AttnArgs a) {
   }
   T *pw = s_p + warp * 16 * GP;
 
-  for (int base = ts + warp * 16; base < te; base += kAttnWarps * 16) {
-    // ---- loads (masked tokens read nothing and contribute zeros)
+  // This warp's tiles are ts + (warp + kAttnWarps * k) * 16, k < n_my.  Each
+  // is copied with cp.async into ring stage k % NS, NS - 1 tiles ahead of the
+  // one being computed; masked tokens are zero-filled without a read.
+  const int first = ts + warp * 16;
+  const int n_my = (first < te) ? (te - first + kAttnWarps * 16 - 1) / (kAttnWarps * 16) : 0;
+  uint4 *wring = ring + (size_t)warp * NS * VPT * 32 + lane;
+  auto issue = [&](int k) {
+    const int base = first + k * kAttnWarps * 16;
+    uint4 *st = wring + (size_t)(k % NS) * VPT * 32;
+    const int ta = base + g, tb = base + g + 8;
+    const T *ra = (ta == pos) ? nk : ((ta < te) ? wk + (int64_t)ta * D : nk);
+    const T *rb = (tb == pos) ? nk : ((tb < te) ? wk + (int64_t)tb * D : nk);
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+      cp_async16_zfill(st + j * 32, ra + 8 * (4 * j + t), ta < te);
+      cp_async16_zfill(st + (D / 32 + j) * 32, rb + 8 * (4 * j + t), tb < te);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int tv = base + 2 * t + (q & 1) + (q >> 1) * 8;
+      const T *rv = (tv == pos) ? nv : ((tv < te) ? wv + (int64_t)tv * D : nv);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        cp_async16_zfill(st + (D / 16 + q * VPL + j) * 32, rv + 8 * (8 * j + g), tv < te);
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < NS - 1; ++k) {
+    if (k < n_my) issue(k);
+    cp_async_commit();
+  }
+
+  for (int k = 0; k < n_my; ++k) {
+    if (k + NS - 1 < n_my) issue(k + NS - 1);
+    cp_async_commit();
+    cp_async_wait<NS - 1>();
+    const int base = first + k * kAttnWarps * 16;
     uint4 ka[D / 32], kb[D / 32], vv[4][VPL];
     {
-      const int ta = base + g, tb = base + g + 8;
-      const T *ra = (ta == pos) ? nk : wk + (int64_t)ta * D;
-      const T *rb = (tb == pos) ? nk : wk + (int64_t)tb * D;
+      const uint4 *st = wring + (size_t)(k % NS) * VPT * 32;
 #pragma unroll
       for (int j = 0; j < D / 32; ++j) {
-        ka[j] = (ta < te) ? ldg_stream(ra + 8 * (4 * j + t)) : make_uint4(0, 0, 0, 0);
-        kb[j] = (tb < te) ? ldg_stream(rb + 8 * (4 * j + t)) : make_uint4(0, 0, 0, 0);
+        ka[j] = st[j * 32];
+        kb[j] = st[(D / 32 + j) * 32];
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int tv = base + 2 * t + (q & 1) + (q >> 1) * 8;
-        const T *rv = (tv == pos) ? nv : wv + (int64_t)tv * D;
+      for (int q = 0; q < 4; ++q)
 #pragma unroll
-        for (int j = 0; j < VPL; ++j)
-          vv[q][j] = (tv < te) ? ldg_stream(rv + 8 * (8 * j + g)) : make_uint4(0, 0, 0, 0);
-      }
+        for (int j = 0; j < VPL; ++j) vv[q][j] = st[(D / 16 + q * VPL + j) * 32];
     }
     const bool va = base + g < te, vb = base + g + 8 < te;
 
@@ -244,7 +417,9 @@ draft_attention_kernel(const AttnArgs a) {
     }
   }
 
-  // ---- merge the warps of this CTA
+  // ---- merge the warps of this CTA (the O staging reuses the ring)
+  cp_async_wait<0>();
+  __syncthreads();
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -269,107 +444,418 @@ draft_attention_kernel(const AttnArgs a) {
   }
   __syncthreads();
 
-  const int n_out = group * D;
-  T *orow = out + ((int64_t)row * a.Hq + kvh * group) * D;
-  if (active == 1) {
-    for (int idx = threadIdx.x; idx < n_out; idx += blockDim.x) {
-      const int h = idx / D, d = idx % D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w * GP + h]);
-      float L = 0.f, O = 0.f;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) {
-        const float f = (s_m[w * GP + h] == -INFINITY) ? 0.f : exp2f(s_m[w * GP + h] - M);
-        L += s_l[w * GP + h] * f;
-        O += s_o[(w * GP + h) * D + d] * f;
-      }
-      orow[idx] = Elem<T>::from_f(O / L);
+  merge_and_store<T, D, GP, kAttnWarps>(a, s_o, s_m, s_l, out, row, kvh, split, active, group,
+                                        &s_last);
+}
+
+
+// ===========================================================================
+// TMA-fed variant (the default on sm_100a): 64-token K/V tiles are copied by
+// cp.async.bulk.tensor with 128-byte swizzle into a CTA-wide ring of NS
+// stages, completion tracked by mbarriers; one thread issues all copies.
+// Fragments come from the swizzled tiles with ldmatrix (conflict-free; V^T
+// directly via ldmatrix.trans).  Each of the 4 warps owns 16 tokens of every
+// stage.  The online softmax rescales O only when a running max grows by more
+// than 2^8, so steady-state tiles skip the rescale.  All mbarrier waits are
+// bounded: a wait that runs out sets DSB_FLAG_TIMEOUT and the CTA drains the
+// copies it issued (bounded again) before returning.
+// ===========================================================================
+constexpr float kLazyRescale = 8.0f;  // log2 headroom before O is rescaled
+constexpr int kWaitSpins = 1 << 22;
+
+// W warps each own 16 tokens of a stage: stages are 16 * W tokens, copied as
+// D/64 boxes of [16 W rows x 128 bytes] for K and for V.
+template <int D, int NS, int W> struct TmaCfg {
+  static constexpr int kStageTok = 16 * W;
+  static constexpr int kBoxBytes = 128 * kStageTok;
+  static constexpr int kBoxes = D / 64;                       // boxes per K (or V) row
+  static constexpr int kStageBytes = 2 * kBoxes * kBoxBytes;  // K + V
+  static constexpr int kRingBytes = NS * kStageBytes;
+  static constexpr int kBarBytes = (8 * NS + 15) / 16 * 16;  // mbarriers, padded to 16 bytes
+};
+
+template <typename T, int D, int NT, int NS, int W>
+constexpr size_t tma_smem_bytes() {
+  return 1024 /* alignment slack */ + TmaCfg<D, NS, W>::kRingBytes + TmaCfg<D, NS, W>::kBarBytes +
+         sizeof(float) * 2 * W * NT * 8 + sizeof(T) * W * 16 * NT * 8;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+// Bounded wait on an mbarrier phase; false when the bound ran out.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (int i = 0; i < kWaitSpins; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// Byte address of (row, column) inside a stage half (K or V) stored as D/64
+// boxes of [rows x 128 bytes] (box_bytes apart) with the 128-byte TMA swizzle.
+__device__ __forceinline__ uint32_t swz(uint32_t base, int box_bytes, int row, int col) {
+  const int box = col >> 6, chunk = (col & 63) >> 3;
+  return base + box * box_bytes + row * 128 + (((chunk ^ (row & 7)) << 4) | ((col & 7) << 1));
+}
+
+template <typename T, int D, int NT, int NS, int kTmaWarps>
+__global__ void __launch_bounds__(kTmaWarps * 32)
+draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
+                           const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
+  using Cfg = TmaCfg<D, NS, kTmaWarps>;
+  constexpr int KS = D / 16, NM = D / 16, GP = NT * 8;
+  constexpr int kStageTok = Cfg::kStageTok, kBoxBytes = Cfg::kBoxBytes;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *ring = smem;  // [NS][K boxes | V boxes], 1024-byte aligned
+  uint64_t *bars = reinterpret_cast<uint64_t *>(ring + Cfg::kRingBytes);
+  float *s_m = reinterpret_cast<float *>(ring + Cfg::kRingBytes + Cfg::kBarBytes);
+  float *s_l = s_m + kTmaWarps * GP;                     // [warps][GP]
+  T *s_p = reinterpret_cast<T *>(s_l + kTmaWarps * GP);  // [warps][16][GP], 16-byte aligned
+  float *s_o = reinterpret_cast<float *>(ring);          // [warps][GP][D], after the loop
+  __shared__ int s_last, s_abort;
+
+  const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int group = a.Hq / a.Hk;
+  T *out = static_cast<T *>(a.out);
+  if (row >= a.rows) {
+    if (split == 0) zero_heads<T, D>(out, row, a.Hq, kvh * group, group);
+    return;
+  }
+  const int slot = a.slots[row];
+  const int pos = a.positions[row] + a.position_offset;
+  if (slot < 0 || slot >= a.num_slots || pos < 0 || pos >= a.W) {
+    if (split == 0) {
+      if (threadIdx.x == 0)
+        flag_error(a.err, (slot < 0 || slot >= a.num_slots) ? DSB_FLAG_SLOT : DSB_FLAG_POSITION);
+      zero_heads<T, D>(out, row, a.Hq, kvh * group, group);
     }
     return;
   }
+  const int len = pos + 1;
+  const int active = (len + a.split_tokens - 1) / a.split_tokens;
+  if (split >= active) return;
+  const int ts = split * a.split_tokens;
+  const int te = min(len, ts + a.split_tokens);
+  const int64_t head_row0 = ((int64_t)slot * a.Hk + kvh) * a.W;  // tensor-map row of token 0
 
-  // ---- publish this split's partial state
-  const int64_t part_floats = (int64_t)GP * (2 + D);
-  float *part_base = a.scratch + ((int64_t)row * a.Hk + kvh) * a.num_splits * part_floats;
-  float *part = part_base + (int64_t)split * part_floats;
-  for (int idx = threadIdx.x; idx < GP * (D + 1); idx += blockDim.x) {
-    if (idx < GP) {
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w * GP + idx]);
-      float L = 0.f;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w)
-        L += (s_m[w * GP + idx] == -INFINITY) ? 0.f : s_l[w * GP + idx] * exp2f(s_m[w * GP + idx] - M);
-      part[idx] = M;
-      part[GP + idx] = L;
-    } else {
-      const int k = idx - GP, h = k / D, d = k % D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w * GP + h]);
-      float O = 0.f;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w)
-        O += (s_m[w * GP + h] == -INFINITY) ? 0.f
-                                            : s_o[(w * GP + h) * D + d] * exp2f(s_m[w * GP + h] - M);
-      part[2 * GP + k] = O;
+  // The split owning the new token stores it first; the copy engine reads it
+  // back through the tensor map after the proxy fence.
+  if (pos >= ts && pos < te) {
+    constexpr int VE = 16 / sizeof(T);
+    const uint4 *nk = reinterpret_cast<const uint4 *>(static_cast<const T *>(a.key) +
+                                                      ((int64_t)row * a.Hk + kvh) * D);
+    const uint4 *nv = reinterpret_cast<const uint4 *>(static_cast<const T *>(a.value) +
+                                                      ((int64_t)row * a.Hk + kvh) * D);
+    uint4 *dk = reinterpret_cast<uint4 *>(static_cast<T *>(a.wk) + (head_row0 + pos) * D);
+    uint4 *dv = reinterpret_cast<uint4 *>(static_cast<T *>(a.wv) + (head_row0 + pos) * D);
+    for (int i = threadIdx.x; i < D / VE; i += blockDim.x) {
+      dk[i] = nk[i];
+      dv[i] = nv[i];
     }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
   }
-  __syncthreads();
+  const int n_stages = (te - ts + kStageTok - 1) / kStageTok;
+  const uint32_t ring_u32 = smem_u32(ring);
+  const uint32_t bar_u32 = smem_u32(bars);
   if (threadIdx.x == 0) {
-    __threadfence();
-    const int prev = atomicAdd(&a.counters[row * a.Hk + kvh], 1);
-    s_last = (prev == active - 1);
+    for (int s = 0; s < NS; ++s) mbar_init(bar_u32 + 8 * s);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_abort = 0;
   }
   __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // Merge: stage every split's (m, l) in shared memory (one independent load
-  // per thread), fold them into per-split weights exp2(m_s - M) / L, then
-  // each output float4 sums `active` independent float4 loads.
-  float *w_s = s_o;  // [active][GP]; the CTA's own O staging is no longer needed
-  float *l_s = s_o + (size_t)active * GP;
-  for (int i = threadIdx.x; i < active * GP; i += blockDim.x) {
-    const float *ps = part_base + (int64_t)(i / GP) * part_floats;
-    w_s[i] = __ldcg(ps + i % GP);
-    l_s[i] = __ldcg(ps + GP + i % GP);
-  }
-  __syncthreads();
-  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < active; ++s2) M = fmaxf(M, w_s[s2 * GP + h]);
-    float L = 0.f;
-    for (int s2 = 0; s2 < active; ++s2) {
-      const float ms = w_s[s2 * GP + h];
-      const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
-      w_s[s2 * GP + h] = f;
-      L += l_s[s2 * GP + h] * f;
+  auto issue = [&](int k) {  // thread 0 only
+    const int s = k % NS;
+    const uint32_t kb = ring_u32 + s * Cfg::kStageBytes;
+    const uint32_t vb = kb + Cfg::kBoxes * kBoxBytes;
+    const int y = (int)(head_row0 + ts + k * kStageTok);
+    mbar_expect_tx(bar_u32 + 8 * s, Cfg::kStageBytes);
+#pragma unroll
+    for (int b = 0; b < Cfg::kBoxes; ++b) {
+      tma_load_2d(kb + b * kBoxBytes, &tmk, 64 * b, y, bar_u32 + 8 * s);
+      tma_load_2d(vb + b * kBoxBytes, &tmv, 64 * b, y, bar_u32 + 8 * s);
     }
-    const float inv = 1.f / L;
-    for (int s2 = 0; s2 < active; ++s2) w_s[s2 * GP + h] *= inv;
+  };
+  if (threadIdx.x == 0)
+    for (int k = 0; k < NS && k < n_stages; ++k) issue(k);
+
+  // Q^T B-fragments in natural head-dim order: lane (g, t) holds head
+  // nt*8+g, dims 16s + 2t, 2t+1 and 16s + 8 + 2t, 2t+1.
+  uint32_t qf[NT][KS][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int h = nt * 8 + g;
+    const uint32_t *qp = reinterpret_cast<const uint32_t *>(
+        static_cast<const T *>(a.query) + ((int64_t)row * a.Hq + kvh * group + min(h, group - 1)) * D);
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      qf[nt][s][0] = (h < group) ? qp[8 * s + t] : 0u;
+      qf[nt][s][1] = (h < group) ? qp[8 * s + 4 + t] : 0u;
+    }
+  }
+
+  float o[NT][NM][4];
+  float m_run[NT][2], l_run[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int i = 0; i < NM; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o[nt][i][c] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      m_run[nt][j] = -INFINITY;
+      l_run[nt][j] = 0.f;
+    }
+  }
+  T *pw = s_p + warp * 16 * GP;
+  bool ok = true;
+  int issued = min(NS, n_stages);
+
+  for (int k = 0; k < n_stages; ++k) {
+    const int s = k % NS;
+    // after a timed-out wait no further stage is issued: skip the waits too
+    if (s_abort || !mbar_wait(bar_u32 + 8 * s, (k / NS) & 1)) {
+      ok = false;
+      s_abort = 1;
+    }
+    const int base = ts + k * kStageTok + warp * 16;  // this warp's first token
+    if (ok && base < te) {
+      const uint32_t kb = ring_u32 + s * Cfg::kStageBytes;
+      const uint32_t vb = kb + Cfg::kBoxes * kBoxBytes;
+      const int r0 = warp * 16;
+      if (base + 16 > te) {  // zero V rows past the split so 0 * stale data stays 0
+        uint8_t *vgen = ring + s * Cfg::kStageBytes + Cfg::kBoxes * kBoxBytes;
+        for (int i = lane; i < 16 * (D / 8); i += 32) {
+          const int r = i / (D / 8), col = (i % (D / 8)) * 8;
+          if (base + r >= te)
+            *reinterpret_cast<uint4 *>(vgen + (swz(0, kBoxBytes, r0 + r, col))) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      // S^T = K Q^T with two accumulators per n-tile to halve the mma chain
+      float cacc[NT][2][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) cacc[nt][h][c] = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < KS; ++s2) {
+        uint32_t af[4];
+        ldsm_x4(af, swz(kb, kBoxBytes, r0 + (lane & 7) + (((lane >> 3) & 1) << 3), 16 * s2 + ((lane >> 4) << 3)));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(cacc[nt][s2 & 1], af, qf[nt][s2]);
+      }
+      const bool va = base + g < te, vb_ok = base + g + 8 < te;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float x[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const bool valid = (c < 2) ? va : vb_ok;
+          x[c] = valid ? (cacc[nt][0][c] + cacc[nt][1][c]) * a.scale_log2 : -INFINITY;
+        }
+        float p[4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float mx = fmaxf(x[j], x[j + 2]);
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          const float m_old = m_run[nt][j];
+          if (mx > m_old + kLazyRescale) {  // rescale only when the max grew a lot
+            const float alpha = (m_old == -INFINITY) ? 0.f : exp2f(m_old - mx);
+            l_run[nt][j] *= alpha;
+#pragma unroll
+            for (int i = 0; i < NM; ++i) {
+              o[nt][i][j] *= alpha;
+              o[nt][i][j + 2] *= alpha;
+            }
+            m_run[nt][j] = mx;
+          }
+          p[j] = exp2f(x[j] - m_run[nt][j]);
+          p[j + 2] = exp2f(x[j + 2] - m_run[nt][j]);
+          l_run[nt][j] += p[j] + p[j + 2];
+        }
+        uint32_t *prow = reinterpret_cast<uint32_t *>(pw);
+        prow[(g * GP + nt * 8 + 2 * t) / 2] = pack2<T>(p[0], p[1]);
+        prow[((g + 8) * GP + nt * 8 + 2 * t) / 2] = pack2<T>(p[2], p[3]);
+      }
+      __syncwarp();
+      uint32_t pb[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) ldsm_x2_trans(pb[nt], pw + (lane & 15) * GP + nt * 8);
+      __syncwarp();
+      // O^T += V^T P^T, V^T fragments straight from the swizzled tile
+#pragma unroll
+      for (int i = 0; i < NM; ++i) {
+        uint32_t vf[4];
+        ldsm_x4_t(vf, swz(vb, kBoxBytes, r0 + (lane & 7) + ((lane >> 4) << 3), 16 * i + (((lane >> 3) & 1) << 3)));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(o[nt][i], vf, pb[nt]);
+      }
+    }
+    __syncthreads();  // every warp is done with stage s
+    if (threadIdx.x == 0 && !s_abort && k + NS < n_stages) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(k + NS);
+      ++issued;
+    }
+  }
+  if (!ok && lane == 0) flag_error(a.err, DSB_FLAG_TIMEOUT);
+
+  // ---- merge the warps of this CTA (O staging reuses the ring)
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float l = l_run[nt][j];
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+      if (g == 0) {
+        s_m[warp * GP + nt * 8 + 2 * t + j] = m_run[nt][j];
+        s_l[warp * GP + nt * 8 + 2 * t + j] = l;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NM; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int h = nt * 8 + 2 * t + (c & 1);
+        const int d = 16 * i + g + ((c >= 2) ? 8 : 0);
+        s_o[(warp * GP + h) * D + d] = o[nt][i][c];
+      }
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < n_out / 4; idx += blockDim.x) {
-    const int h = (4 * idx) / D, d = (4 * idx) % D;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int s2 = 0; s2 < active; ++s2) {
-      const float4 o = __ldcg(reinterpret_cast<const float4 *>(
-          part_base + (int64_t)s2 * part_floats + 2 * GP + h * D + d));
-      const float f = w_s[s2 * GP + h];
-      acc.x += o.x * f;
-      acc.y += o.y * f;
-      acc.z += o.z * f;
-      acc.w += o.w * f;
-    }
-    orow[4 * idx] = Elem<T>::from_f(acc.x);
-    orow[4 * idx + 1] = Elem<T>::from_f(acc.y);
-    orow[4 * idx + 2] = Elem<T>::from_f(acc.z);
-    orow[4 * idx + 3] = Elem<T>::from_f(acc.w);
+  (void)issued;
+  merge_and_store<T, D, GP, kTmaWarps>(a, s_o, s_m, s_l, out, row, kvh, split, active, group,
+                                       &s_last);
+}
+
+
+// ---- host: tensor maps and the kernel choice shared by both entry points
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D map over a working cache viewed as [slots * kv_heads * W rows, D]:
+// 64-column x box_rows boxes with the 128-byte swizzle.
+bool encode_kv_map(CUtensorMap *map, const void *base, int64_t rows, int head_dim, int dtype,
+                   int box_rows) {
+  auto fn = tensor_map_encoder();
+  if (fn == nullptr || reinterpret_cast<uintptr_t>(base) % 16 || rows <= 0 || rows > 0x7fffffff)
+    return false;
+  cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, dtype == DSB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool legacy_attention_requested() {
+  const char *v = getenv("DSB_ATTENTION_LEGACY");
+  return v != nullptr && v[0] == '1';
+}
+
+template <typename T, int D, int NT, int NS, int W>
+int launch_tma(const AttnArgs &a, int splits, cudaStream_t st) {
+  CUtensorMap tmk, tmv;
+  const int64_t rows_total = (int64_t)a.num_slots * a.Hk * a.W;
+  const int dt = std::is_same<T, __half>::value ? DSB_F16 : DSB_BF16;
+  if (!encode_kv_map(&tmk, a.wk, rows_total, D, dt, 16 * W) ||
+      !encode_kv_map(&tmv, a.wv, rows_total, D, dt, 16 * W))
+    return -1;  // no tensor map: the caller uses the register-fed kernel
+  const size_t smem = tma_smem_bytes<T, D, NT, NS, W>();
+  auto kern = draft_attention_tma_kernel<T, D, NT, NS, W>;
+  if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
+  kern<<<dim3(splits, a.Hk, a.out_rows), W * 32, smem, st>>>(tmk, tmv, a);
+  return check_launch("draft_attention_tma_kernel");
+}
+
+// Geometry of the TMA kernel: 8 warps and 128-token stages up to head_dim
+// 128 (a ~192 KB ring, one CTA per SM), 4 warps and 64-token stages at 256.
+template <int D> struct TmaGeom {
+  static constexpr int W = D >= 256 ? 4 : 8;
+  static constexpr int NS = D >= 256 ? 2 : (D >= 128 ? 3 : 4);
+};
+
+template <typename T, int D, int NT>
+int launch_attention_typed(const AttnArgs &a, int splits, cudaStream_t st) {
+  if (!legacy_attention_requested()) {
+    const int e = launch_tma<T, D, NT, TmaGeom<D>::NS, TmaGeom<D>::W>(a, splits, st);
+    if (e != -1) return e;
   }
-  if (threadIdx.x == 0) a.counters[row * a.Hk + kvh] = 0;
+  const size_t smem = attn_smem_bytes<T, D, NT>();
+  auto kern = draft_attention_kernel<T, D, NT>;
+  if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
+  kern<<<dim3(splits, a.Hk, a.out_rows), kAttnWarps * 32, smem, st>>>(a);
+  return check_launch("draft_attention_kernel");
+}
+
+int launch_attention(const AttnArgs &a, int dtype, int head_dim, int group, int splits,
+                     cudaStream_t st) {
+  const int nt = group <= 8 ? 1 : 2;
+#define DSB_LA(TT, DD, NN) \
+  if (head_dim == DD && nt == NN) return launch_attention_typed<TT, DD, NN>(a, splits, st);
+  if (dtype == DSB_BF16) {
+    DSB_LA(__nv_bfloat16, 64, 1) DSB_LA(__nv_bfloat16, 64, 2)
+    DSB_LA(__nv_bfloat16, 128, 1) DSB_LA(__nv_bfloat16, 128, 2)
+    DSB_LA(__nv_bfloat16, 256, 1) DSB_LA(__nv_bfloat16, 256, 2)
+  } else {
+    DSB_LA(__half, 64, 1) DSB_LA(__half, 64, 2)
+    DSB_LA(__half, 128, 1) DSB_LA(__half, 128, 2)
+    DSB_LA(__half, 256, 1) DSB_LA(__half, 256, 2)
+  }
+#undef DSB_LA
+  return fail(DSB_ERR_UNSUPPORTED, "no draft attention kernel for this shape");
 }
 
 }  // namespace
@@ -382,7 +868,7 @@ extern "C" int32_t dsb_draft_attention_default_splits(int32_t rows, int32_t num_
   if (rows <= 0 || num_kv_heads <= 0 || working_budget <= 0) return 1;
   if (sm_count <= 0) sm_count = 148;
   const int64_t pairs = (int64_t)rows * num_kv_heads;
-  int64_t splits = (4LL * sm_count + pairs - 1) / pairs;
+  int64_t splits = (int64_t)sm_count / pairs;  // about one resident CTA per SM
   int64_t max_splits = (working_budget + 31) / 32;
   if (max_splits > 64) max_splits = 64;
   if (splits > max_splits) splits = max_splits;
@@ -441,28 +927,7 @@ extern "C" int dsb_draft_decode_attention(
              num_slots, num_query_heads, num_kv_heads, working_budget, scale * kLog2e, output,
              scratch, counters, splits, split_tokens, error_flag};
   cudaStream_t st = as_stream(stream);
-  const int nt = group <= 8 ? 1 : 2;
-#define DSB_AT(TT, DD, NN)                                                              \
-  if (head_dim == DD && nt == NN) {                                                     \
-    constexpr int GP = NN * 8;                                                          \
-    const size_t smem = sizeof(float) * (kAttnWarps * GP * DD + 2 * kAttnWarps * GP) +  \
-                        sizeof(TT) * kAttnWarps * 16 * GP;                              \
-    auto kern = draft_attention_kernel<TT, DD, NN>;                                     \
-    if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;    \
-    kern<<<dim3(splits, num_kv_heads, out_rows), kAttnWarps * 32, smem, st>>>(a);      \
-    return check_launch("draft_attention_kernel");                                      \
-  }
-  if (dtype == DSB_BF16) {
-    DSB_AT(__nv_bfloat16, 64, 1) DSB_AT(__nv_bfloat16, 64, 2)
-    DSB_AT(__nv_bfloat16, 128, 1) DSB_AT(__nv_bfloat16, 128, 2)
-    DSB_AT(__nv_bfloat16, 256, 1) DSB_AT(__nv_bfloat16, 256, 2)
-  } else {
-    DSB_AT(__half, 64, 1) DSB_AT(__half, 64, 2)
-    DSB_AT(__half, 128, 1) DSB_AT(__half, 128, 2)
-    DSB_AT(__half, 256, 1) DSB_AT(__half, 256, 2)
-  }
-#undef DSB_AT
-  return fail(DSB_ERR_UNSUPPORTED, "no draft attention kernel for this shape");
+  return launch_attention(a, dtype, head_dim, group, splits, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -572,26 +1037,5 @@ extern "C" int dsb_draft_decode_attention_static(
              rows, out_rows, num_slots, num_query_heads, num_kv_heads, working_budget,
              scale * kLog2e, output, st_mem.scratch, st_mem.tickets, splits, split_tokens,
              error_flag};
-  const int nt = group <= 8 ? 1 : 2;
-#define DSB_ATS(TT, DD, NN)                                                            \
-  if (head_dim == DD && nt == NN) {                                                    \
-    constexpr int GP = NN * 8;                                                         \
-    const size_t smem = sizeof(float) * (kAttnWarps * GP * DD + 2 * kAttnWarps * GP) + \
-                        sizeof(TT) * kAttnWarps * 16 * GP;                             \
-    auto kern = draft_attention_kernel<TT, DD, NN>;                                    \
-    if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;   \
-    kern<<<dim3(splits, num_kv_heads, out_rows), kAttnWarps * 32, smem, st>>>(a);     \
-    return check_launch("draft_attention_kernel (static scratch)");                    \
-  }
-  if (dtype == DSB_BF16) {
-    DSB_ATS(__nv_bfloat16, 64, 1) DSB_ATS(__nv_bfloat16, 64, 2)
-    DSB_ATS(__nv_bfloat16, 128, 1) DSB_ATS(__nv_bfloat16, 128, 2)
-    DSB_ATS(__nv_bfloat16, 256, 1) DSB_ATS(__nv_bfloat16, 256, 2)
-  } else {
-    DSB_ATS(__half, 64, 1) DSB_ATS(__half, 64, 2)
-    DSB_ATS(__half, 128, 1) DSB_ATS(__half, 128, 2)
-    DSB_ATS(__half, 256, 1) DSB_ATS(__half, 256, 2)
-  }
-#undef DSB_ATS
-  return fail(DSB_ERR_UNSUPPORTED, "no draft attention kernel for this shape");
+  return launch_attention(a, dtype, head_dim, group, splits, st);
 }

@@ -15,6 +15,8 @@
 // byte is all the kernel moves.  RoPE math is fp32 with both products rounded
 // before the add, i.e. exactly "first * cos - second * sin" evaluated without
 // fused multiply-add, then rounded once to the cache dtype.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace dsb {
@@ -41,6 +43,7 @@ struct RopeArgs {
   int64_t cs_stride, cs_rows;
   int heads, head_dim, rotary_dim, neox, tokens_per_warp;
   int vec_rope;  // NeoX with 16-byte-aligned halves and cos/sin rows: vector path
+  int chunk_shift, block_shift;  // log2 of chunk / block_size when powers of two, else -1
   int32_t *err;
 };
 
@@ -77,22 +80,65 @@ __device__ __forceinline__ void cs_load_vec(const CS *p, float (&out)[N]) {
   for (int i = 0; i < N; ++i) out[i] = Elem<CS>::to_f(u.e[i]);
 }
 
-template <typename T, typename CS, bool GATHER>
-__global__ void __launch_bounds__(kWarpsRope * 32) rope_rows_kernel(const RopeArgs a) {
+
+// Two 16-bit elements of a 32-bit word as floats, and back with one
+// round-to-nearest-even conversion per pair.
+template <typename T> struct Pair;
+template <> struct Pair<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+};
+template <> struct Pair<__half> {
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+};
+
+// out = x * c + y * s_signed, element-wise over 8 packed 16-bit values; the
+// caller passes s_signed = -sin for the first rotary half, so this equals
+// x*cos - y*sin there and x*cos + y*sin in the second half (products rounded
+// before the add, as in the unfused reference arithmetic).
+template <typename T>
+__device__ __forceinline__ uint4 rotate8(const uint4 &x, const uint4 &y, const float (&c)[8],
+                                         const float (&s)[8]) {
+  const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float2 xf = Pair<T>::unpack(xs[w]), yf = Pair<T>::unpack(ys[w]);
+    const float r0 = __fmul_rn(xf.x, c[2 * w]) + __fmul_rn(yf.x, s[2 * w]);
+    const float r1 = __fmul_rn(xf.y, c[2 * w + 1]) + __fmul_rn(yf.y, s[2 * w + 1]);
+    o[w] = Pair<T>::pack(r0, r1);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <typename T, typename CS, bool GATHER, int DH>
+__global__ void __launch_bounds__(kWarpsRope * 32, 3) rope_rows_kernel(const RopeArgs a) {
+  // DH: head_dim known at compile time (64, 128, 256), or 0 for any other.
+  const int head_dim = DH ? DH : a.head_dim;
   extern __shared__ uint4 stage[];
   constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int U = a.tokens_per_warp;
-  const int row_elems = a.heads * a.head_dim;
+  const int row_elems = a.heads * head_dim;
   const int row_vecs = row_elems / VE;
-  uint4 *wstage = stage + (size_t)warp * U * 2 * row_vecs;
+  uint4 *wstage = stage + (size_t)warp * 2 * U * 2 * row_vecs;  // two batches per warp
   const T *src_k = static_cast<const T *>(a.src_k);
   const T *src_v = static_cast<const T *>(a.src_v);
   T *dst_k = static_cast<T *>(a.dst_k);
   T *dst_v = static_cast<T *>(a.dst_v);
   const CS *cs = static_cast<const CS *>(a.cos_sin);
   const int r = blockIdx.y;
-  const int p0 = (blockIdx.x * kWarpsRope + warp) * U;
 
   // Row descriptor.
   int64_t slot = 0, hlen = 0, tail_start = 0, prefix_len = 0, drop = 0;
@@ -120,170 +166,240 @@ __global__ void __launch_bounds__(kWarpsRope * 32) rope_rows_kernel(const RopeAr
   }
   const int64_t width = GATHER ? a.working_tokens : hlen;
 
-  // Phase 1: stage the U rows (K then V) of this warp.
-  for (int j = 0; j < U; ++j) {
-    const int64_t p = p0 + j;
-    if (p >= width) break;
-    const T *rk = nullptr, *rv = nullptr;
-    bool zero_row = false;
+  // Source rows of local position p: 1 = copy, 2 = zero row (gather
+  // padding), 0 = skip (bad plan data, flagged).
+  auto source = [&](int64_t p, const T *&rk, const T *&rv) -> int {
     if (!GATHER) {
       int64_t abs_pos;
       bool ok = true;
       if (p < prefix_len) {
-        const int64_t q = p + drop;
-        const int64_t ci = q / a.chunk;
+        const int q = (int)(p + drop);
+        const int ci = a.chunk_shift >= 0 ? q >> a.chunk_shift : q / a.chunk;
         if (ci >= n_plan_chunks) ok = false;
-        abs_pos = ok ? chunks[ci] * a.chunk + q % a.chunk : 0;
+        abs_pos = ok ? chunks[ci] * a.chunk + (q - ci * a.chunk) : 0;
       } else {
         abs_pos = tail_start + p - prefix_len;
       }
       if (!ok || abs_pos < 0 || abs_pos >= a.max_model_len) {
         if (lane == 0) flag_error(a.err, ok ? DSB_FLAG_POSITION : DSB_FLAG_PLAN);
-        continue;
+        return 0;
       }
       const int64_t off = (slot * a.max_model_len + abs_pos) * row_elems;
       rk = src_k + off;
       rv = src_v + off;
+      return 1;
+    }
+    const int64_t idx = a.sel[(int64_t)r * a.working_tokens + p];
+    if (idx < 0) return 2;
+    int64_t lb, in_block;
+    if (a.block_shift >= 0) {
+      lb = idx >> a.block_shift;
+      in_block = idx & ((1LL << a.block_shift) - 1);
     } else {
-      const int64_t idx = a.sel[(int64_t)r * a.working_tokens + p];
-      if (idx < 0) {
-        zero_row = true;
-      } else {
-        const int64_t lb = idx / a.block_size;
-        const int64_t pb = (lb < a.bt_cols) ? a.bt[(int64_t)r * a.bt_stride + lb] : -1;
-        if (pb < 0 || pb >= a.num_blocks) {
-          if (lane == 0) flag_error(a.err, DSB_FLAG_BLOCK);
-          zero_row = true;
+      lb = idx / a.block_size;
+      in_block = idx - lb * a.block_size;
+    }
+    const int64_t pb = (lb < a.bt_cols) ? a.bt[(int64_t)r * a.bt_stride + lb] : -1;
+    if (pb < 0 || pb >= a.num_blocks) {
+      if (lane == 0) flag_error(a.err, DSB_FLAG_BLOCK);
+      return 2;
+    }
+    const int64_t off = (pb * a.block_size + in_block) * row_elems;
+    rk = src_k + off;
+    rv = src_v + off;
+    return 1;
+  };
+  // Stage the U rows (K then V) of one batch with 16-byte cp.async.
+  auto stage_batch = [&](int64_t pb, uint4 *buf) {
+    for (int j = 0; j < U; ++j) {
+      const int64_t p = pb + j;
+      if (p >= width) break;
+      const T *rk = nullptr, *rv = nullptr;
+      const int kind = source(p, rk, rv);
+      if (kind == 0) continue;
+      uint4 *sk = buf + (size_t)j * 2 * row_vecs;
+      uint4 *sv = sk + row_vecs;
+      for (int v = lane; v < row_vecs; v += 32) {
+        if (kind == 2) {
+          sk[v] = make_uint4(0, 0, 0, 0);
+          sv[v] = make_uint4(0, 0, 0, 0);
         } else {
-          const int64_t off = (pb * a.block_size + idx % a.block_size) * row_elems;
-          rk = src_k + off;
-          rv = src_v + off;
+          cp_async16(sk + v, reinterpret_cast<const uint4 *>(rk) + v);
+          cp_async16(sv + v, reinterpret_cast<const uint4 *>(rv) + v);
         }
       }
     }
-    uint4 *sk = wstage + (size_t)j * 2 * row_vecs;
-    uint4 *sv = sk + row_vecs;
-    for (int v = lane; v < row_vecs; v += 32) {
-      if (zero_row) {
-        sk[v] = make_uint4(0, 0, 0, 0);
-        sv[v] = make_uint4(0, 0, 0, 0);
-      } else {
-        cp_async16(sk + v, reinterpret_cast<const uint4 *>(rk) + v);
-        cp_async16(sv + v, reinterpret_cast<const uint4 *>(rv) + v);
-      }
-    }
-  }
-  cp_async_wait_all();
-  __syncwarp();
-
-  // Phase 2: write V as is and K rotated at local position p.
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
   const int rot = a.rotary_dim, half = rot / 2;
-  for (int j = 0; j < U; ++j) {
-    const int64_t p = p0 + j;
-    if (p >= width) break;
-    if (!GATHER) {  // skip rows whose source was rejected above
-      bool ok = true;
-      int64_t abs_pos;
-      if (p < prefix_len) {
-        const int64_t q = p + drop;
-        const int64_t ci = q / a.chunk;
-        ok = ci < n_plan_chunks;
-        abs_pos = ok ? chunks[ci] * a.chunk + q % a.chunk : 0;
-      } else {
-        abs_pos = tail_start + p - prefix_len;
+  // Write V as is and K rotated at local position p.
+  auto write_batch = [&](int64_t pb, const uint4 *buf) {
+    for (int j = 0; j < U; ++j) {
+      const int64_t p = pb + j;
+      if (p >= width) break;
+      if (!GATHER) {  // skip rows whose source was rejected when staging
+        bool ok = true;
+        int64_t abs_pos;
+        if (p < prefix_len) {
+          const int q = (int)(p + drop);
+          const int ci = a.chunk_shift >= 0 ? q >> a.chunk_shift : q / a.chunk;
+          ok = ci < n_plan_chunks;
+          abs_pos = ok ? chunks[ci] * a.chunk + (q - ci * a.chunk) : 0;
+        } else {
+          abs_pos = tail_start + p - prefix_len;
+        }
+        if (!ok || abs_pos < 0 || abs_pos >= a.max_model_len) continue;
       }
-      if (!ok || abs_pos < 0 || abs_pos >= a.max_model_len) continue;
-    }
-    const uint4 *sk = wstage + (size_t)j * 2 * row_vecs;
-    const uint4 *sv = sk + row_vecs;
-    const T *kx = reinterpret_cast<const T *>(sk);
-    for (int v = lane; v < row_vecs; v += 32) {
-      const int e0 = v * VE;
-      const int h = e0 / a.head_dim, d0 = e0 % a.head_dim;
-      int64_t dst_off;
-      if (GATHER) {
-        dst_off = ((int64_t)r * a.working_tokens + p) * row_elems + e0;
-      } else {
-        dst_off = ((slot * a.heads + h) * a.working_budget + p) * a.head_dim + d0;
-      }
-      stg_stream(dst_v + dst_off, sv[v]);
-      if (d0 >= rot) {
-        stg_stream(dst_k + dst_off, sk[v]);
-        continue;
-      }
-      const T *hx = kx + h * a.head_dim;
-      union {
-        uint4 u;
-        T e[VE];
-      } out;
-      out.u = sk[v];
+      const uint4 *sk = buf + (size_t)j * 2 * row_vecs;
+      const uint4 *sv = sk + row_vecs;
+      const T *kx = reinterpret_cast<const T *>(sk);
       const CS *csr = cs + p * a.cs_stride;
-      if (a.vec_rope) {  // whole vector rotary; partner is the vector half away
-        const bool first = d0 < half;
-        const int i0 = first ? d0 : d0 - half;
+      // With a compile-time head_dim whose vectors-per-head divide 32, every
+      // vector of this lane sits at the same head offset: one cos/sin load.
+      constexpr bool kSameOffset = DH != 0 && (32 % (DH / VE)) == 0;
+      float cvec[VE], svec[VE];  // svec holds -sin in the first rotary half
+      if (kSameOffset && a.vec_rope) {
+        const int d0 = (lane % (DH / VE)) * VE;
+        if (d0 < rot) {
+          const int i0 = d0 < half ? d0 : d0 - half;
+          cs_load_vec<CS, VE>(csr + i0, cvec);
+          cs_load_vec<CS, VE>(csr + half + i0, svec);
+          if (d0 < half) {
+#pragma unroll
+            for (int e = 0; e < VE; ++e) svec[e] = -svec[e];
+          }
+        }
+      }
+      const int64_t dst_tok = GATHER ? ((int64_t)r * a.working_tokens + p) * row_elems
+                                     : (slot * a.heads * (int64_t)a.working_budget + p) * head_dim;
+      for (int v = lane; v < row_vecs; v += 32) {
+        const int e0 = v * VE;
+        const int h = e0 / head_dim, d0 = e0 - h * head_dim;
+        const int64_t dst_off =
+            GATHER ? dst_tok + e0 : dst_tok + (int64_t)h * a.working_budget * head_dim + d0;
+        stg_stream(dst_v + dst_off, sv[v]);
+        if (d0 >= rot) {
+          stg_stream(dst_k + dst_off, sk[v]);
+          continue;
+        }
+        const T *hx = kx + h * head_dim;
         union {
           uint4 u;
           T e[VE];
-        } par;
-        par.u = sk[first ? v + half / VE : v - half / VE];
-        float c[VE], sn[VE];
-        cs_load_vec<CS, VE>(csr + i0, c);
-        cs_load_vec<CS, VE>(csr + half + i0, sn);
+        } out;
+        out.u = sk[v];
+        if constexpr (kSameOffset && sizeof(T) == 2) {
+          if (a.vec_rope) {  // packed path with the per-token cos / signed sin
+            const bool first = d0 < half;
+            const uint4 par = sk[first ? v + half / VE : v - half / VE];
+            stg_stream(dst_k + dst_off, rotate8<T>(out.u, par, cvec, svec));
+            continue;
+          }
+        }
+        if (a.vec_rope) {  // whole vector rotary; partner is the vector half away
+          const bool first = d0 < half;
+          const int i0 = first ? d0 : d0 - half;
+          union {
+            uint4 u;
+            T e[VE];
+          } par;
+          par.u = sk[first ? v + half / VE : v - half / VE];
+          float c[VE], sn[VE];
+          cs_load_vec<CS, VE>(csr + i0, c);
+          cs_load_vec<CS, VE>(csr + half + i0, sn);
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            const float x = Elem<T>::to_f(out.e[e]), y = Elem<T>::to_f(par.e[e]);
+            const float rr = first ? __fmul_rn(x, c[e]) - __fmul_rn(y, sn[e])
+                                   : __fmul_rn(x, c[e]) + __fmul_rn(y, sn[e]);
+            out.e[e] = Elem<T>::from_f(rr);
+          }
+          stg_stream(dst_k + dst_off, out.u);
+          continue;
+        }
 #pragma unroll
         for (int e = 0; e < VE; ++e) {
-          const float x = Elem<T>::to_f(out.e[e]), y = Elem<T>::to_f(par.e[e]);
-          const float r = first ? __fmul_rn(x, c[e]) - __fmul_rn(y, sn[e])
-                                : __fmul_rn(x, c[e]) + __fmul_rn(y, sn[e]);
-          out.e[e] = Elem<T>::from_f(r);
+          const int d = d0 + e;
+          if (d >= rot) break;
+          int i;
+          float x1, x2;
+          bool first;
+          if (a.neox) {
+            first = d < half;
+            i = first ? d : d - half;
+            x1 = Elem<T>::to_f(hx[i]);
+            x2 = Elem<T>::to_f(hx[i + half]);
+          } else {
+            first = (d & 1) == 0;
+            i = d >> 1;
+            x1 = Elem<T>::to_f(hx[2 * i]);
+            x2 = Elem<T>::to_f(hx[2 * i + 1]);
+          }
+          const float c = cs_load(csr + i), sn = cs_load(csr + half + i);
+          const float y = first ? __fmul_rn(x1, c) - __fmul_rn(x2, sn)
+                                : __fmul_rn(x2, c) + __fmul_rn(x1, sn);
+          out.e[e] = Elem<T>::from_f(y);
         }
         stg_stream(dst_k + dst_off, out.u);
-        continue;
       }
-#pragma unroll
-      for (int e = 0; e < VE; ++e) {
-        const int d = d0 + e;
-        if (d >= rot) break;
-        int i;
-        float x1, x2;
-        bool first;
-        if (a.neox) {
-          first = d < half;
-          i = first ? d : d - half;
-          x1 = Elem<T>::to_f(hx[i]);
-          x2 = Elem<T>::to_f(hx[i + half]);
-        } else {
-          first = (d & 1) == 0;
-          i = d >> 1;
-          x1 = Elem<T>::to_f(hx[2 * i]);
-          x2 = Elem<T>::to_f(hx[2 * i + 1]);
-        }
-        const float c = cs_load(csr + i), s = cs_load(csr + half + i);
-        const float y = first ? __fmul_rn(x1, c) - __fmul_rn(x2, s)
-                              : __fmul_rn(x2, c) + __fmul_rn(x1, s);
-        out.e[e] = Elem<T>::from_f(y);
-      }
-      stg_stream(dst_k + dst_off, out.u);
+    }
+  };
+
+  // Grid-stride over batches of U positions, double-buffered: batch b + 1 is
+  // copied while batch b is rotated and written.
+  auto batch_start = [&](int b) {
+    return ((int64_t)b * gridDim.x + blockIdx.x) * kWarpsRope * U + (int64_t)warp * U;
+  };
+  uint4 *bufs[2] = {wstage, wstage + (size_t)U * 2 * row_vecs};
+  if (batch_start(0) < width) {
+    stage_batch(batch_start(0), bufs[0]);
+    for (int b = 0; batch_start(b) < width; ++b) {
+      const bool more = batch_start(b + 1) < width;
+      if (more) stage_batch(batch_start(b + 1), bufs[(b + 1) & 1]);
+      if (more) asm volatile("cp.async.wait_group 1;" ::: "memory");
+      else asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncwarp();
+      write_batch(batch_start(b), bufs[b & 1]);
+      __syncwarp();
     }
   }
 }
 
 int elem_bytes(int dtype) { return dtype == DSB_F32 ? 4 : 2; }
 
+int log2_exact(int64_t v) {
+  if (v <= 0 || (v & (v - 1))) return -1;
+  int s = 0;
+  while ((1LL << s) < v) ++s;
+  return s;
+}
+
 template <typename T, typename CS, bool GATHER>
 int launch_rope(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
   const int row_bytes = a.heads * a.head_dim * (int)sizeof(T);
-  int U = row_bytes <= 2048 ? 4 : (row_bytes <= 4096 ? 2 : 1);
-  const size_t smem = (size_t)kWarpsRope * U * 2 * row_bytes;
+  int U = row_bytes <= 1024 ? 2 : 1;
+  const size_t smem = (size_t)kWarpsRope * 2 * U * 2 * row_bytes;  // double-buffered K+V rows
   if (smem > 200 * 1024) return fail(DSB_ERR_UNSUPPORTED, "KV rows too wide for staging");
   a.tokens_per_warp = U;
   constexpr int VE = 16 / (int)sizeof(T);
   a.vec_rope = a.neox && a.rotary_dim > 0 && (a.rotary_dim / 2) % VE == 0 &&
                reinterpret_cast<uintptr_t>(a.cos_sin) % 16 == 0 &&
                (a.cs_stride * (int64_t)sizeof(CS)) % 16 == 0;
-  auto kern = rope_rows_kernel<T, CS, GATHER>;
+  a.chunk_shift = log2_exact(a.chunk);
+  a.block_shift = log2_exact(a.block_size);
+  auto kern = a.head_dim == 128   ? rope_rows_kernel<T, CS, GATHER, 128>
+              : a.head_dim == 64  ? rope_rows_kernel<T, CS, GATHER, 64>
+              : a.head_dim == 256 ? rope_rows_kernel<T, CS, GATHER, 256>
+                                  : rope_rows_kernel<T, CS, GATHER, 0>;
   if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;
   const int64_t per_cta = (int64_t)kWarpsRope * U;
-  const int64_t gx = (width + per_cta - 1) / per_cta;
+  // enough CTAs to fill the GPU once; each warp then loops over its batches
+  int resident = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, kWarpsRope * 32, smem) !=
+          cudaSuccess || resident <= 0)
+    resident = 1;
+  const int64_t fill = ((int64_t)resident * sm_count() + rows - 1) / rows;
+  const int64_t gx = std::max<int64_t>(1, std::min<int64_t>((width + per_cta - 1) / per_cta, fill));
   if (gx > 0x7fffffff || rows > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
   kern<<<dim3((unsigned)gx, rows), kWarpsRope * 32, smem, st>>>(a);
   return check_launch(GATHER ? "gather_rope_kernel" : "rebuild_rope_kernel");
