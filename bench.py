@@ -570,17 +570,16 @@ def run_e2e(res, args):
 
 
 def period_bytes(res):
-    """Algorithmic bytes of one period and per launch kind, from the actual plans."""
-    from oracle import diffspec_oracle as O  # plan arithmetic only (host ints)
-
+    """Algorithmic bytes of one period and per launch kind, from the history
+    lengths the device plan kernel produces for each cycle of the period."""
     w = res["w"]
-    sel_count = w.sel_count.cpu().tolist()
-    sel = w.sel_chunks.cpu().tolist()
     hls = []
     for c in range(INTERVAL):
-        he = CTX - REJECTED + ACCEPT_PER_CYCLE * c - 1
-        hls.append([O.history_plan(0, sel[r][: sel_count[r]], he, CHUNK, HISTORY_BUDGET)[1]
-                    for r in range(res["rows"])])
+        w.dsb.selection.build_history_plan(
+            w.active, w.committed[c], w.sel_chunks, w.sel_count, chunk_size=CHUNK,
+            history_budget=HISTORY_BUDGET, working_budget=TOKEN_BUDGET, plan=w.plan,
+            history_lens=w.hist)
+        hls.append(w.hist[: res["rows"]].cpu().tolist())
     b = algorithmic_bytes([CTX - REJECTED] * res["rows"], hls, w.hk, res["rows"])
     per_launch = dict(scores=b["retrieval"], rebuild=b["rebuild"] / INTERVAL,
                       attention=b["attention"] / (INTERVAL * DEPTH))

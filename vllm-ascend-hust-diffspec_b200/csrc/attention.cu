@@ -450,18 +450,20 @@ draft_attention_kernel(const AttnArgs a) {
 
 
 // ===========================================================================
-// TMA-fed variant (the default on sm_100a): 64-token K/V tiles are copied by
-// cp.async.bulk.tensor with 128-byte swizzle into a CTA-wide ring of NS
-// stages, completion tracked by mbarriers; one thread issues all copies.
-// Fragments come from the swizzled tiles with ldmatrix (conflict-free; V^T
-// directly via ldmatrix.trans).  Each of the 4 warps owns 16 tokens of every
-// stage.  The online softmax rescales O only when a running max grows by more
-// than 2^8, so steady-state tiles skip the rescale.  All mbarrier waits are
-// bounded: a wait that runs out sets DSB_FLAG_TIMEOUT and the CTA drains the
-// copies it issued (bounded again) before returning.
+// TMA-fed variant (the default on sm_100a): K/V stages of 16 * W tokens (W
+// warps) are copied by cp.async.bulk.tensor as 64-column boxes with 128-byte
+// swizzle into a CTA-wide ring of NS stages, completion tracked by mbarriers;
+// one thread issues all copies.  Fragments come from the swizzled tiles with
+// ldmatrix (conflict-free; V^T directly via ldmatrix.trans).  Each warp owns
+// 16 tokens of every stage.  The online softmax rescales O only when a
+// running max grows by more than 2^8, so steady-state tiles skip the rescale.
+// All mbarrier waits are bounded: a wait that runs out sets DSB_FLAG_TIMEOUT,
+// no further stage is issued, and thread 0 waits (bounded again) for the
+// copies already issued before the ring is reused or the CTA exits.
 // ===========================================================================
 constexpr float kLazyRescale = 8.0f;  // log2 headroom before O is rescaled
-constexpr int kWaitSpins = 1 << 22;
+constexpr int kWaitSpins = 1 << 26;          // poll backstop
+constexpr uint64_t kWaitNs = 200000000ull;  // 0.2 s per wait
 
 // W warps each own 16 tokens of a stage: stages are 16 * W tokens, copied as
 // D/64 boxes of [16 W rows x 128 bytes] for K and for V.
@@ -490,8 +492,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
 }
-// Bounded wait on an mbarrier phase; false when the bound ran out.
+// Bounded wait on an mbarrier phase; false when the bound ran out.  The bound
+// is wall-clock (kWaitNs on %globaltimer, checked every 64 polls) with a poll
+// count as a backstop, so a lost copy costs a fraction of a second, not a hang.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  uint64_t t0 = 0;
   for (int i = 0; i < kWaitSpins; ++i) {
     uint32_t done;
     asm volatile(
@@ -501,6 +511,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         : "r"(bar), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 63) == 0) {
+      const uint64_t now = global_ns();
+      if (i == 0) t0 = now;
+      else if (now - t0 > kWaitNs) return false;
+    }
   }
   return false;
 }
@@ -644,12 +659,16 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   }
   T *pw = s_p + warp * 16 * GP;
   bool ok = true;
-  int issued = min(NS, n_stages);
+  int issued = min(NS, n_stages);  // stages 0 .. issued-1 have copies in flight or landed
+  int first_unwaited = n_stages;   // thread 0: first stage it did not see complete
 
   for (int k = 0; k < n_stages; ++k) {
     const int s = k % NS;
-    // after a timed-out wait no further stage is issued: skip the waits too
-    if (s_abort || !mbar_wait(bar_u32 + 8 * s, (k / NS) & 1)) {
+    // after a timed-out wait no further stage is issued: skip the waits too.
+    // The vote keeps the warp converged for the mma/ldmatrix that follow.
+    const bool got = __all_sync(0xffffffffu, !s_abort && mbar_wait(bar_u32 + 8 * s, (k / NS) & 1));
+    if (!got) {
+      if (threadIdx.x == 0 && ok) first_unwaited = k;
       ok = false;
       s_abort = 1;
     }
@@ -738,6 +757,13 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
     }
   }
   if (!ok && lane == 0) flag_error(a.err, DSB_FLAG_TIMEOUT);
+  if (s_abort) {  // CTA-uniform after the loop's last barrier
+    // Let every issued copy land (bounded again) before the ring is reused
+    // for the O staging below or released with the CTA.
+    if (threadIdx.x == 0)
+      for (int k = first_unwaited; k < issued; ++k) mbar_wait(bar_u32 + 8 * (k % NS), (k / NS) & 1);
+    __syncthreads();
+  }
 
   // ---- merge the warps of this CTA (O staging reuses the ring)
 #pragma unroll
@@ -762,7 +788,6 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
       }
   }
   __syncthreads();
-  (void)issued;
   merge_and_store<T, D, GP, kTmaWarps>(a, s_o, s_m, s_l, out, row, kvh, split, active, group,
                                        &s_last);
 }
