@@ -13,6 +13,15 @@ from oracle import diffspec_oracle as O
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=["bulk", "legacy"])
+def kernel(request, monkeypatch):
+    """Run every case on the bulk-copy kernel (default) and on the cp.async
+    row kernel the library falls back to."""
+    if request.param == "legacy":
+        monkeypatch.setenv("DSB_REBUILD_LEGACY", "1")
+    return request.param
+
+
 def bf16(a, device):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device).bfloat16()
 
@@ -84,6 +93,39 @@ def test_config2_rebuild_rows_vs_oracle(dsb, cuda):
     ok, ov = np.zeros((slots_n, hk, w, d), np.float32), np.zeros((slots_n, hk, w, d), np.float32)
     O.rebuild_compact_kv_from_plan(raw_k, raw_v, ok, ov, plan, table, c, hb, d, True, "bf16")
     np.testing.assert_array_equal(f32(wk), ok)
+    np.testing.assert_array_equal(f32(wv), ov)
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("hk,d,rot,neox", [(8, 128, 128, True), (1, 64, 64, True), (2, 256, 256, True),
+                                           (4, 128, 64, True), (4, 64, 64, False)])
+def test_rebuild_geometries_vs_oracle(dsb, cuda, dtype, hk, d, rot, neox):
+    """Chunk 64 plans with a dropped prefix head, partial last chunks and a
+    rolling tail, over head counts that change the positions per CTA."""
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    slots_n, length, w, c, hb = 3, 4096, 512, 64, 448
+    g = R.rng(hk * 1000 + d + rot + int(neox))
+    raw_k = R.normal(g, (slots_n, length, hk, d), dtype)
+    raw_v = R.normal(g, (slots_n, length, hk, d), dtype)
+    table = R.round_to(R.cos_sin_table(w, rot), dtype)
+    rows = []
+    for slot, n_sel, he in ((2, 7, 3001), (0, 3, 1000), (1, 0, 200)):
+        n = (he + c) // c
+        chunks = sorted(g.choice(n - 1, n_sel, replace=False).tolist()) + [n - 1] if n_sel else []
+        rows.append(O.history_plan(slot, chunks, he, c, hb))
+    plan = np.zeros((3, 5 + w // c), np.int64)
+    for r, pl in enumerate(rows):
+        plan[r, : len(pl)] = pl
+    wk = torch.full((slots_n, hk, w, d), float("nan"), device=cuda).to(tdt)
+    wv = wk.clone()
+    dsb.compact_kv.rebuild_compact_kv_from_plan(
+        torch.from_numpy(raw_k).to(cuda, tdt), torch.from_numpy(raw_v).to(cuda, tdt), wk, wv,
+        torch.from_numpy(plan).to(cuda), torch.from_numpy(table).to(cuda, tdt), chunk_size=c,
+        max_width=hb, rotary_dim=rot, is_neox_style=neox)
+    ok, ov = (np.full((slots_n, hk, w, d), np.nan, np.float32) for _ in range(2))
+    O.rebuild_compact_kv_from_plan(raw_k, raw_v, ok, ov, plan, table, c, hb, rot, neox, dtype)
+    np.testing.assert_array_equal(f32(wk), ok)  # NaN where the plan leaves rows untouched
     np.testing.assert_array_equal(f32(wv), ov)
     assert dsb._lib.read_and_clear_error_flag(cuda) == 0
 

@@ -462,8 +462,6 @@ draft_attention_kernel(const AttnArgs a) {
 // copies already issued before the ring is reused or the CTA exits.
 // ===========================================================================
 constexpr float kLazyRescale = 8.0f;  // log2 headroom before O is rescaled
-constexpr int kWaitSpins = 1 << 26;          // poll backstop
-constexpr uint64_t kWaitNs = 200000000ull;  // 0.2 s per wait
 
 // W warps each own 16 tokens of a stage: stages are 16 * W tokens, copied as
 // D/64 boxes of [16 W rows x 128 bytes] for K and for V.
@@ -482,43 +480,6 @@ constexpr size_t tma_smem_bytes() {
          sizeof(float) * 2 * W * NT * 8 + sizeof(T) * W * 16 * NT * 8;
 }
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-// Bounded wait on an mbarrier phase; false when the bound ran out.  The bound
-// is wall-clock (kWaitNs on %globaltimer, checked every 64 polls) with a poll
-// count as a backstop, so a lost copy costs a fraction of a second, not a hang.
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  uint64_t t0 = 0;
-  for (int i = 0; i < kWaitSpins; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((i & 63) == 0) {
-      const uint64_t now = global_ns();
-      if (i == 0) t0 = now;
-      else if (now - t0 > kWaitNs) return false;
-    }
-  }
-  return false;
-}
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
                                             uint32_t bar) {
   asm volatile(

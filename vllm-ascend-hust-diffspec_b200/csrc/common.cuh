@@ -111,4 +111,57 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// ------------------------------------------------- mbarriers (async copies)
+constexpr int kWaitSpins = 1 << 26;          // poll backstop
+constexpr uint64_t kWaitNs = 200000000ull;  // 0.2 s per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+// Bounded wait on an mbarrier phase; false when the bound ran out.  The bound
+// is wall-clock (kWaitNs on %globaltimer, checked every 64 polls) with a poll
+// count as a backstop, so a lost copy costs a fraction of a second, not a hang.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  uint64_t t0 = 0;
+  for (int i = 0; i < kWaitSpins; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 63) == 0) {
+      const uint64_t now = global_ns();
+      if (i == 0) t0 = now;
+      else if (now - t0 > kWaitNs) return false;
+    }
+  }
+  return false;
+}
+// 1-D bulk copy (TMA, no tensor map) of `bytes` from global memory into this
+// CTA's shared memory, completion counted on `bar`.  Both addresses 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 }  // namespace dsb

@@ -16,6 +16,7 @@
 // before the add, i.e. exactly "first * cos - second * sin" evaluated without
 // fused multiply-add, then rounded once to the cache dtype.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -42,6 +43,7 @@ struct RopeArgs {
   const void *cos_sin;
   int64_t cs_stride, cs_rows;
   int heads, head_dim, rotary_dim, neox, tokens_per_warp;
+  int pt_shift;  // bulk kernel: log2 of the positions per CTA
   int vec_rope;  // NeoX with 16-byte-aligned halves and cos/sin rows: vector path
   int chunk_shift, block_shift;  // log2 of chunk / block_size when powers of two, else -1
   int32_t *err;
@@ -50,9 +52,6 @@ struct RopeArgs {
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
   const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
 template <typename CS>
@@ -256,10 +255,11 @@ __global__ void __launch_bounds__(kWarpsRope * 32, 3) rope_rows_kernel(const Rop
       const CS *csr = cs + p * a.cs_stride;
       // With a compile-time head_dim whose vectors-per-head divide 32, every
       // vector of this lane sits at the same head offset: one cos/sin load.
-      constexpr bool kSameOffset = DH != 0 && (32 % (DH / VE)) == 0;
+      constexpr int kHeadVecs = DH ? DH / VE : 1;
+      constexpr bool kSameOffset = DH != 0 && (32 % kHeadVecs) == 0;
       float cvec[VE], svec[VE];  // svec holds -sin in the first rotary half
       if (kSameOffset && a.vec_rope) {
-        const int d0 = (lane % (DH / VE)) * VE;
+        const int d0 = (lane % kHeadVecs) * VE;
         if (d0 < rot) {
           const int i0 = d0 < half ? d0 : d0 - half;
           cs_load_vec<CS, VE>(csr + i0, cvec);
@@ -365,6 +365,245 @@ __global__ void __launch_bounds__(kWarpsRope * 32, 3) rope_rows_kernel(const Rop
   }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy variant (the default for 16-bit caches with head_dim 64/128/256).
+// One CTA owns PT = 1 << pt_shift consecutive local positions of one row.
+// Lane t of warp 0 decodes the source of position p0 + t once and issues two
+// 1-D bulk copies (TMA) of that token's whole K row and V row (all kv heads)
+// into shared memory; all copies complete on one mbarrier.  The block then
+// writes V out unchanged and K rotated: for NeoX with 16-byte halves a thread
+// owns one (position, 8-element pair of vectors) item, loads its cos/sin
+// vectors once and reuses them for every kv head.  No thread touches a byte
+// twice, and the loads need no per-lane address arithmetic.
+constexpr int kBulkThreads = 256;
+
+template <typename T, typename CS, bool GATHER, int DH>
+__global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs a) {
+  static_assert(sizeof(T) == 2 && DH > 0, "16-bit caches with a compile-time head_dim");
+  constexpr int VE = 8;           // elements per 16-byte vector
+  constexpr int DV = DH / VE;     // vectors per head row
+  extern __shared__ __align__(16) uint8_t bulk_smem[];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int PT = 1 << a.pt_shift;
+  const int heads = a.heads;
+  const int row_elems = heads * DH;
+  const uint32_t row_bytes = (uint32_t)row_elems * 2u;
+  // [PT][row] K, then [PT][row] V, then the mbarrier and the per-token kinds
+  uint8_t *sk = bulk_smem;
+  uint8_t *sv = bulk_smem + (size_t)PT * row_bytes;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(bulk_smem + 2 * (size_t)PT * row_bytes);
+  int *s_kind = reinterpret_cast<int *>(bar + 1);
+  const int r = blockIdx.y;
+  const int64_t p0 = (int64_t)blockIdx.x << a.pt_shift;
+
+  // Row descriptor (rebuild: plan row; gather: the row's index vector).
+  int64_t slot = 0, hlen = 0, tail_start = 0, prefix_len = 0, drop = 0;
+  const int64_t *chunks = nullptr;
+  int n_plan_chunks = 0;
+  if (!GATHER) {
+    const int64_t *pr = a.plan + (int64_t)r * a.plan_width;
+    slot = pr[0];
+    hlen = pr[1];
+    tail_start = pr[2];
+    prefix_len = pr[3];
+    drop = pr[4];
+    chunks = pr + 5;
+    n_plan_chunks = a.plan_width - 5;
+    const int64_t cap = min((int64_t)a.max_width, (int64_t)a.working_budget);
+    if (slot < 0 || slot >= a.num_slots || hlen < 0 || prefix_len < 0 || prefix_len > hlen ||
+        drop < 0 || hlen > cap) {
+      if (tid == 0 && blockIdx.x == 0)
+        flag_error(a.err, (slot < 0 || slot >= a.num_slots) ? DSB_FLAG_SLOT : DSB_FLAG_PLAN);
+      if (slot < 0 || slot >= a.num_slots) return;
+      hlen = max((int64_t)0, min(hlen, cap));
+      prefix_len = max((int64_t)0, min(prefix_len, hlen));
+      drop = max((int64_t)0, drop);
+    }
+  }
+  const int64_t width = GATHER ? a.working_tokens : hlen;
+  if (p0 >= width) return;  // CTA-uniform
+  const int n_tok = (int)min((int64_t)PT, width - p0);
+  const uint32_t bar_u32 = smem_u32(bar);
+
+  if (tid < 32) {
+    if (lane == 0) {
+      mbar_init(bar_u32);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    // kind: 1 = copy the row, 2 = zero row (gather padding / bad block), 0 = skip
+    int kind = 0;
+    const T *rk = nullptr, *rv = nullptr;
+    if (lane < n_tok) {
+      const int64_t p = p0 + lane;
+      if (!GATHER) {
+        int64_t abs_pos = 0;
+        bool ok = true;
+        if (p < prefix_len) {
+          const int q = (int)(p + drop);
+          const int ci = a.chunk_shift >= 0 ? q >> a.chunk_shift : q / a.chunk;
+          ok = ci < n_plan_chunks;
+          if (ok) abs_pos = chunks[ci] * a.chunk + (q - ci * a.chunk);
+        } else {
+          abs_pos = tail_start + p - prefix_len;
+        }
+        if (!ok || abs_pos < 0 || abs_pos >= a.max_model_len) {
+          flag_error(a.err, ok ? DSB_FLAG_POSITION : DSB_FLAG_PLAN);
+        } else {
+          const int64_t off = (slot * a.max_model_len + abs_pos) * row_elems;
+          rk = static_cast<const T *>(a.src_k) + off;
+          rv = static_cast<const T *>(a.src_v) + off;
+          kind = 1;
+        }
+      } else {
+        const int64_t idx = a.sel[(int64_t)r * a.working_tokens + p];
+        kind = 2;
+        if (idx >= 0) {
+          int64_t lb, in_block;
+          if (a.block_shift >= 0) {
+            lb = idx >> a.block_shift;
+            in_block = idx & ((1LL << a.block_shift) - 1);
+          } else {
+            lb = idx / a.block_size;
+            in_block = idx - lb * a.block_size;
+          }
+          const int64_t pb = (lb < a.bt_cols) ? a.bt[(int64_t)r * a.bt_stride + lb] : -1;
+          if (pb < 0 || pb >= a.num_blocks) {
+            flag_error(a.err, DSB_FLAG_BLOCK);
+          } else {
+            const int64_t off = (pb * a.block_size + in_block) * row_elems;
+            rk = static_cast<const T *>(a.src_k) + off;
+            rv = static_cast<const T *>(a.src_v) + off;
+            kind = 1;
+          }
+        }
+      }
+    }
+    const uint32_t loads = __ballot_sync(0xffffffffu, kind == 1);
+    if (lane == 0) mbar_expect_tx(bar_u32, (uint32_t)__popc(loads) * 2u * row_bytes);
+    __syncwarp();
+    if (kind == 1) {
+      bulk_load(smem_u32(sk + (size_t)lane * row_bytes), rk, row_bytes, bar_u32);
+      bulk_load(smem_u32(sv + (size_t)lane * row_bytes), rv, row_bytes, bar_u32);
+    }
+    if (lane < PT) s_kind[lane] = kind;
+  }
+  __syncthreads();
+  if (!mbar_wait(bar_u32, 0)) {
+    if (tid == 0) {
+      flag_error(a.err, DSB_FLAG_TIMEOUT);
+      mbar_wait(bar_u32, 0);  // let the copies land before the CTA releases its memory
+    }
+    return;
+  }
+
+  T *dst_k = static_cast<T *>(a.dst_k);
+  T *dst_v = static_cast<T *>(a.dst_v);
+  // element offset of (token t, head h, dim 0) in the destination
+  const int64_t dst_base =
+      GATHER ? ((int64_t)r * a.working_tokens + p0) * row_elems
+             : (slot * heads * (int64_t)a.working_budget + p0) * DH;
+  auto dst_off = [&](int t, int h) -> int64_t {
+    return GATHER ? dst_base + (int64_t)t * row_elems + h * DH
+                  : dst_base + ((int64_t)h * a.working_budget + t) * DH;
+  };
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+
+  // V, and the K dims past the rotary part: straight copies.  Items run
+  // dim-vector fastest, then token, then head (shifts only: PT and DV are
+  // powers of two).
+  const int rot = a.rotary_dim, half = rot / 2;
+  const int krot_vecs = a.vec_rope ? rot / VE : 0;  // K vectors handled by the rotary pass
+  const bool copy_k = a.vec_rope || rot == 0;
+  constexpr int kDvShift = DV == 8 ? 3 : DV == 16 ? 4 : 5;
+  static_assert((1 << kDvShift) == DV, "head_dim / 8 must be 8, 16 or 32");
+  const int n_items = heads << (a.pt_shift + kDvShift);
+  for (int i = tid; i < n_items; i += kBulkThreads) {
+    const int dv = i & (DV - 1);
+    const int t = (i >> kDvShift) & (PT - 1);
+    const int h = i >> (kDvShift + a.pt_shift);
+    if (t >= n_tok) continue;
+    const int kind = s_kind[t];
+    if (kind == 0) continue;
+    const int64_t o = dst_off(t, h) + dv * VE;
+    const size_t so = (size_t)t * row_bytes + ((size_t)h * DH + dv * VE) * 2;
+    stg_stream(dst_v + o, kind == 1 ? *reinterpret_cast<const uint4 *>(sv + so) : zero);
+    if (copy_k && dv >= krot_vecs)
+      stg_stream(dst_k + o, kind == 1 ? *reinterpret_cast<const uint4 *>(sk + so) : zero);
+  }
+
+  const CS *cs = static_cast<const CS *>(a.cos_sin);
+  if (a.vec_rope) {
+    // NeoX, half % 8 == 0: item (token, j) rotates vectors j and j + half/8 of
+    // every head with one cos/sin load.
+    const int hv = half / VE;
+    const int hv_shift = (hv & (hv - 1)) == 0 ? __ffs(hv) - 1 : -1;
+    const int k_items = n_tok * hv;
+    for (int i = tid; i < k_items; i += kBulkThreads) {
+      const int j = hv_shift >= 0 ? i & (hv - 1) : i % hv;
+      const int t = hv_shift >= 0 ? i >> hv_shift : i / hv;
+      const int kind = s_kind[t];
+      if (kind == 0) continue;
+      float c[VE], s[VE];
+      const CS *csr = cs + (p0 + t) * a.cs_stride;
+      cs_load_vec<CS, VE>(csr + j * VE, c);
+      cs_load_vec<CS, VE>(csr + half + j * VE, s);
+      float sneg[VE];
+#pragma unroll
+      for (int e = 0; e < VE; ++e) sneg[e] = -s[e];
+      for (int h = 0; h < heads; ++h) {
+        const int64_t o = dst_off(t, h);
+        if (kind == 2) {
+          stg_stream(dst_k + o + j * VE, zero);
+          stg_stream(dst_k + o + half + j * VE, zero);
+          continue;
+        }
+        const uint8_t *hrow = sk + (size_t)t * row_bytes + (size_t)h * DH * 2;
+        const uint4 lo = *reinterpret_cast<const uint4 *>(hrow + j * VE * 2);
+        const uint4 hi = *reinterpret_cast<const uint4 *>(hrow + (half + j * VE) * 2);
+        stg_stream(dst_k + o + j * VE, rotate8<T>(lo, hi, c, sneg));
+        stg_stream(dst_k + o + half + j * VE, rotate8<T>(hi, lo, c, s));
+      }
+    }
+  } else if (rot > 0) {
+    // Any other rotary layout: one thread per (token, head, element), the
+    // partner element read from the staged row.
+    const int n_el = n_tok * heads * DH;
+    for (int i = tid; i < n_el; i += kBulkThreads) {
+      const int d = i % DH, h = (i / DH) % heads, t = i / (DH * heads);
+      const int kind = s_kind[t];
+      if (kind == 0) continue;
+      T out = Elem<T>::from_f(0.f);
+      if (kind == 1) {
+        const T *hx = reinterpret_cast<const T *>(sk + (size_t)t * row_bytes) + h * DH;
+        if (d >= rot) {
+          out = hx[d];
+        } else {
+          const CS *csr = cs + (p0 + t) * a.cs_stride;
+          int ii;
+          float x1, x2;
+          bool first;
+          if (a.neox) {
+            first = d < half;
+            ii = first ? d : d - half;
+            x1 = Elem<T>::to_f(hx[ii]);
+            x2 = Elem<T>::to_f(hx[ii + half]);
+          } else {
+            first = (d & 1) == 0;
+            ii = d >> 1;
+            x1 = Elem<T>::to_f(hx[2 * ii]);
+            x2 = Elem<T>::to_f(hx[2 * ii + 1]);
+          }
+          const float cc = cs_load(csr + ii), sn = cs_load(csr + half + ii);
+          out = Elem<T>::from_f(first ? __fmul_rn(x1, cc) - __fmul_rn(x2, sn)
+                                      : __fmul_rn(x2, cc) + __fmul_rn(x1, sn));
+        }
+      }
+      dst_k[dst_off(t, h) + d] = out;
+    }
+  }
+}
+
 int elem_bytes(int dtype) { return dtype == DSB_F32 ? 4 : 2; }
 
 int log2_exact(int64_t v) {
@@ -374,8 +613,58 @@ int log2_exact(int64_t v) {
   return s;
 }
 
+// DSB_REBUILD_LEGACY=1 selects the cp.async row kernel (kept as the fallback
+// for shapes the bulk kernel does not take, and parity-tested on its own).
+bool legacy_rope_requested() {
+  const char *e = std::getenv("DSB_REBUILD_LEGACY");
+  return e != nullptr && e[0] == '1';
+}
+
+#ifndef DSB_BULK_STAGE_BYTES
+#define DSB_BULK_STAGE_BYTES (64 * 1024)  // K + V rows staged per bulk-kernel CTA
+#endif
+
+bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// The bulk kernel when its preconditions hold: 16-bit caches, head_dim 64,
+// 128 or 256, 16-byte aligned bases and at least one K+V row pair per stage.
+template <typename T, typename CS, bool GATHER>
+int launch_rope_bulk(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
+  if constexpr (sizeof(T) != 2) {
+    return -1;
+  } else {
+    if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return -1;
+    if (!aligned16(a.src_k) || !aligned16(a.src_v) || !aligned16(a.dst_k) || !aligned16(a.dst_v))
+      return -1;
+    const int64_t row_bytes = (int64_t)a.heads * a.head_dim * 2;
+    int pt = 32;
+    while (pt > 1 && 2 * pt * row_bytes > DSB_BULK_STAGE_BYTES) pt >>= 1;
+    if (2 * pt * row_bytes > DSB_BULK_STAGE_BYTES) return -1;
+    a.pt_shift = log2_exact(pt);
+    a.chunk_shift = log2_exact(a.chunk);
+    a.block_shift = log2_exact(a.block_size);
+    constexpr int VE = 8;
+    a.vec_rope = a.neox && a.rotary_dim > 0 && (a.rotary_dim / 2) % VE == 0 &&
+                 reinterpret_cast<uintptr_t>(a.cos_sin) % 16 == 0 &&
+                 (a.cs_stride * (int64_t)sizeof(CS)) % 16 == 0;
+    const size_t smem = 2 * (size_t)pt * row_bytes + 8 + 4 * (size_t)pt;
+    auto kern = a.head_dim == 128  ? rope_bulk_kernel<T, CS, GATHER, 128>
+                : a.head_dim == 64 ? rope_bulk_kernel<T, CS, GATHER, 64>
+                                   : rope_bulk_kernel<T, CS, GATHER, 256>;
+    if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
+    const int64_t gx = (width + pt - 1) / pt;
+    if (gx > 0x7fffffff || rows > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
+    kern<<<dim3((unsigned)gx, rows), kBulkThreads, smem, st>>>(a);
+    return check_launch(GATHER ? "gather_rope_bulk_kernel" : "rebuild_rope_bulk_kernel");
+  }
+}
+
 template <typename T, typename CS, bool GATHER>
 int launch_rope(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
+  if (!legacy_rope_requested()) {
+    const int e = launch_rope_bulk<T, CS, GATHER>(a, rows, width, st);
+    if (e >= 0) return e;
+  }
   const int row_bytes = a.heads * a.head_dim * (int)sizeof(T);
   int U = row_bytes <= 1024 ? 2 : 1;
   const size_t smem = (size_t)kWarpsRope * 2 * U * 2 * row_bytes;  // double-buffered K+V rows
