@@ -22,12 +22,25 @@ def bf16(a, device):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device).bfloat16()
 
 
-@pytest.mark.parametrize("i", range(len(R.attention_cases())))
-@pytest.mark.parametrize("splits", [None, 1])
-@pytest.mark.parametrize("kernel", ["tma", "legacy"])
-def test_attention_matches_reference(dsb, cuda, i, splits, kernel, monkeypatch):
-    if kernel == "legacy":  # the register-fed kernel the library falls back to
+KERNELS = ["tma", "tma-ticket", "legacy"]
+
+
+def use_kernel(kernel, monkeypatch):
+    """tma: TMA-fed kernel, splits merged inside a thread-block cluster (2..8
+    splits); tma-ticket: same kernel, splits merged through global partials
+    and an atomic ticket; legacy: the register-fed kernel the library falls
+    back to."""
+    if kernel == "legacy":
         monkeypatch.setenv("DSB_ATTENTION_LEGACY", "1")
+    if kernel == "tma-ticket":
+        monkeypatch.setenv("DSB_ATTENTION_TICKET_MERGE", "1")
+
+
+@pytest.mark.parametrize("i", range(len(R.attention_cases())))
+@pytest.mark.parametrize("splits", [None, 1, 2, 3])
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_attention_matches_reference(dsb, cuda, i, splits, kernel, monkeypatch):
+    use_kernel(kernel, monkeypatch)
     d = golden("attention")
     inp = R.attention_inputs(i)
     n = len(inp["slots"])
@@ -54,11 +67,12 @@ def test_attention_matches_reference(dsb, cuda, i, splits, kernel, monkeypatch):
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 @pytest.mark.parametrize("hq,hk,d", [(32, 4, 128), (64, 8, 128), (16, 1, 128), (8, 2, 64),
                                      (16, 2, 256), (32, 2, 128)])
-@pytest.mark.parametrize("kernel", ["tma", "legacy"])
-def test_long_history_split_kv_vs_oracle(dsb, cuda, dtype, hq, hk, d, kernel, monkeypatch):
-    """Config-2 lengths (history 1984 + draft step) with reordered slots."""
-    if kernel == "legacy":
-        monkeypatch.setenv("DSB_ATTENTION_LEGACY", "1")
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("splits", [None, 2, 5, 8, 12])
+def test_long_history_split_kv_vs_oracle(dsb, cuda, dtype, hq, hk, d, kernel, splits, monkeypatch):
+    """Config-2 lengths (history 1984 + draft step) with reordered slots; rows
+    whose history ends before the last splits leave those splits empty."""
+    use_kernel(kernel, monkeypatch)
     tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
     g = R.rng(hq * 131 + hk + d)
     slots_n, w = 6, 2048
@@ -75,7 +89,7 @@ def test_long_history_split_kv_vs_oracle(dsb, cuda, dtype, hq, hk, d, kernel, mo
         torch.from_numpy(q).to(cuda, tdt), torch.from_numpy(k).to(cuda, tdt),
         torch.from_numpy(v).to(cuda, tdt), twk, twv,
         torch.tensor(slots, dtype=torch.int32, device=cuda),
-        torch.tensor(positions, dtype=torch.int32, device=cuda), d ** -0.5)
+        torch.tensor(positions, dtype=torch.int32, device=cuda), d ** -0.5, num_splits=splits)
     ref = O.draft_decode_attention(q, k, v, wk, wv, slots, positions, d ** -0.5, dtype=None)
     close_bf16(out.float().cpu().numpy(), ref)
     assert dsb._lib.read_and_clear_error_flag(cuda) == 0

@@ -3,6 +3,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <utility>
 
 #include "common.cuh"
@@ -48,6 +49,33 @@ int ensure_smem(const void *kernel, size_t bytes) {
     return fail(DSB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   done[key] = bytes;
   return DSB_OK;
+}
+
+bool cluster_fits(const void *kernel, int cluster_x, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void *, int, size_t>, bool> known;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(dev, kernel, cluster_x, smem);
+  auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster_x, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  const bool ok = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && n > 0;
+  if (!ok) (void)cudaGetLastError();  // a refused query is an answer, not an error
+  known[key] = ok;
+  return ok;
 }
 
 }  // namespace dsb

@@ -89,6 +89,62 @@ __device__ __forceinline__ void zero_heads(T *out, int row, int Hq, int h0, int 
     o[i] = make_uint4(0, 0, 0, 0);
 }
 
+// Four outputs as one 8-byte store (16-bit element types).
+template <typename T>
+__device__ __forceinline__ void store4(T *p, const float4 &v) {
+  *reinterpret_cast<uint2 *>(p) = make_uint2(pack2<T>(v.x, v.y), pack2<T>(v.z, v.w));
+}
+
+// The elected last CTA of a (row, kv head) merges the `active` published
+// partials [GP m | GP l | GP x D o]: stage every split's (m, l) in shared
+// memory (one independent load per thread), fold them into per-split weights
+// exp2(m_s - M) / L, then each output float4 sums `active` independent
+// float4 loads.  s_buf holds 2 * active * GP floats.
+template <typename T, int D, int GP>
+__device__ __forceinline__ void merge_published(const float *part_base, int64_t part_floats,
+                                                int active, T *orow, int n_out, float *s_buf) {
+  // Merge: stage every split's (m, l) in shared memory (one independent load
+  // per thread), fold them into per-split weights exp2(m_s - M) / L, then
+  // each output float4 sums `active` independent float4 loads.
+  float *w_s = s_buf;  // [active][GP]
+  float *l_s = s_buf + (size_t)active * GP;
+  for (int i = threadIdx.x; i < active * GP; i += blockDim.x) {
+    const float *ps = part_base + (int64_t)(i / GP) * part_floats;
+    w_s[i] = __ldcg(ps + i % GP);
+    l_s[i] = __ldcg(ps + GP + i % GP);
+  }
+  __syncthreads();
+  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < active; ++s2) M = fmaxf(M, w_s[s2 * GP + h]);
+    float L = 0.f;
+    for (int s2 = 0; s2 < active; ++s2) {
+      const float ms = w_s[s2 * GP + h];
+      const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+      w_s[s2 * GP + h] = f;
+      L += l_s[s2 * GP + h] * f;
+    }
+    const float inv = 1.f / L;
+    for (int s2 = 0; s2 < active; ++s2) w_s[s2 * GP + h] *= inv;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < n_out / 4; idx += blockDim.x) {
+    const int h = (4 * idx) / D, d = (4 * idx) % D;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int s2 = 0; s2 < active; ++s2) {
+      const float4 o = __ldcg(reinterpret_cast<const float4 *>(
+          part_base + (int64_t)s2 * part_floats + 2 * GP + h * D + d));
+      const float f = w_s[s2 * GP + h];
+      acc.x += o.x * f;
+      acc.y += o.y * f;
+      acc.z += o.z * f;
+      acc.w += o.w * f;
+    }
+    store4<T>(orow + 4 * idx, acc);
+  }
+}
+
 // Combine the CTA's warps (staged in s_o/s_m/s_l) and either store the
 // normalised output (single split) or publish a partial; the last split of a
 // (row, kv head) to finish merges all partials.
@@ -153,55 +209,14 @@ __device__ __forceinline__ void merge_and_store(const AttnArgs &a, float *s_o, c
   __syncthreads();
   if (!(*s_last)) return;
   __threadfence();
-  // Merge: stage every split's (m, l) in shared memory (one independent load
-  // per thread), fold them into per-split weights exp2(m_s - M) / L, then
-  // each output float4 sums `active` independent float4 loads.
-  float *w_s = s_o;  // [active][GP]; the CTA's own O staging is no longer needed
-  float *l_s = s_o + (size_t)active * GP;
-  for (int i = threadIdx.x; i < active * GP; i += blockDim.x) {
-    const float *ps = part_base + (int64_t)(i / GP) * part_floats;
-    w_s[i] = __ldcg(ps + i % GP);
-    l_s[i] = __ldcg(ps + GP + i % GP);
-  }
-  __syncthreads();
-  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < active; ++s2) M = fmaxf(M, w_s[s2 * GP + h]);
-    float L = 0.f;
-    for (int s2 = 0; s2 < active; ++s2) {
-      const float ms = w_s[s2 * GP + h];
-      const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
-      w_s[s2 * GP + h] = f;
-      L += l_s[s2 * GP + h] * f;
-    }
-    const float inv = 1.f / L;
-    for (int s2 = 0; s2 < active; ++s2) w_s[s2 * GP + h] *= inv;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < n_out / 4; idx += blockDim.x) {
-    const int h = (4 * idx) / D, d = (4 * idx) % D;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int s2 = 0; s2 < active; ++s2) {
-      const float4 o = __ldcg(reinterpret_cast<const float4 *>(
-          part_base + (int64_t)s2 * part_floats + 2 * GP + h * D + d));
-      const float f = w_s[s2 * GP + h];
-      acc.x += o.x * f;
-      acc.y += o.y * f;
-      acc.z += o.z * f;
-      acc.w += o.w * f;
-    }
-    orow[4 * idx] = Elem<T>::from_f(acc.x);
-    orow[4 * idx + 1] = Elem<T>::from_f(acc.y);
-    orow[4 * idx + 2] = Elem<T>::from_f(acc.z);
-    orow[4 * idx + 3] = Elem<T>::from_f(acc.w);
-  }
+  merge_published<T, D, GP>(part_base, part_floats, active, orow, n_out, s_o);
   if (threadIdx.x == 0) a.counters[row * a.Hk + kvh] = 0;
 }
 
 template <typename T, int D, int NT>
 __global__ void __launch_bounds__(kAttnWarps * 32)
 draft_attention_kernel(const AttnArgs a) {
+  pdl_begin();
   constexpr int KS = D / 16;   // k-steps of Q.K over head_dim
   constexpr int NM = D / 16;   // M-tiles of O^T over head_dim
   constexpr int GP = NT * 8;   // padded heads per group
@@ -505,10 +520,54 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int box_bytes, int row, i
   return base + box * box_bytes + row * 128 + (((chunk ^ (row & 7)) << 4) | ((col & 7) << 1));
 }
 
-template <typename T, int D, int NT, int NS, int kTmaWarps>
+// Thread-block-cluster primitives for the split merge: the CTAs of one
+// (row, kv head) form a cluster along x; rank r writes its partial into the
+// shared memory of rank 0 (distributed shared memory), ordered by the
+// cluster barrier.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster(uint32_t addr, const float4 &v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// Every thread of every CTA in the cluster arrives (release) and waits
+// (acquire).  Only called on paths that all CTAs of a cluster take.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Shared-memory layout of the TMA kernel's epilogue, inside the (then idle)
+// ring: per-warp O rows padded to D + 4 floats (conflict-free fragment
+// stores), per-warp weights, the CTA's (M, L) per head, and - cluster merge
+// only, used in rank 0 - one (m, l, O) slot per cluster rank.
+template <int D, int GP, int W> struct TmaEpi {
+  static constexpr int DP = D + 4;
+  static constexpr int kO = 0;                        // [W][GP][DP]
+  static constexpr int kF = kO + W * GP * DP;         // [W][GP]
+  static constexpr int kML = kF + W * GP;             // [2][GP]
+  static constexpr int kX = (kML + 2 * GP + 3) / 4 * 4;  // [ranks][GP][D], then [ranks][2][GP]
+  static constexpr size_t bytes(int ranks) {
+    return sizeof(float) * ((size_t)kX + (size_t)ranks * GP * (D + 2));
+  }
+};
+
+template <typename T, int D, int NT, int NS, int kTmaWarps, bool CL>
 __global__ void __launch_bounds__(kTmaWarps * 32)
 draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
+  pdl_begin();
   using Cfg = TmaCfg<D, NS, kTmaWarps>;
   constexpr int KS = D / 16, NM = D / 16, GP = NT * 8;
   constexpr int kStageTok = Cfg::kStageTok, kBoxBytes = Cfg::kBoxBytes;
@@ -520,7 +579,6 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   float *s_m = reinterpret_cast<float *>(ring + Cfg::kRingBytes + Cfg::kBarBytes);
   float *s_l = s_m + kTmaWarps * GP;                     // [warps][GP]
   T *s_p = reinterpret_cast<T *>(s_l + kTmaWarps * GP);  // [warps][16][GP], 16-byte aligned
-  float *s_o = reinterpret_cast<float *>(ring);          // [warps][GP][D], after the loop
   __shared__ int s_last, s_abort;
 
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
@@ -544,9 +602,12 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   }
   const int len = pos + 1;
   const int active = (len + a.split_tokens - 1) / a.split_tokens;
-  if (split >= active) return;
-  const int ts = split * a.split_tokens;
-  const int te = min(len, ts + a.split_tokens);
+  // With the cluster merge every CTA of the cluster must reach the cluster
+  // barriers, so splits past the sequence stay and contribute nothing.
+  if (!CL && split >= active) return;
+  const bool live = split < active;
+  const int ts = live ? split * a.split_tokens : 0;
+  const int te = live ? min(len, ts + a.split_tokens) : 0;
   const int64_t head_row0 = ((int64_t)slot * a.Hk + kvh) * a.W;  // tensor-map row of token 0
 
   // The split owning the new token stores it first; the copy engine reads it
@@ -726,9 +787,13 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
     __syncthreads();
   }
 
-  // ---- merge the warps of this CTA (O staging reuses the ring)
+  // ---- combine the warps of this CTA (the ring is idle from here on)
+  using Epi = TmaEpi<D, GP, kTmaWarps>;
+  float *e_o = reinterpret_cast<float *>(ring) + Epi::kO;
+  float *e_f = reinterpret_cast<float *>(ring) + Epi::kF;
+  float *e_ml = reinterpret_cast<float *>(ring) + Epi::kML;
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       float l = l_run[nt][j];
@@ -739,18 +804,132 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
         s_l[warp * GP + nt * 8 + 2 * t + j] = l;
       }
     }
+  __syncthreads();
+  // per head: the CTA max, each warp's weight exp2(m_w - M) and the CTA sum
+  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kTmaWarps; ++w) M = fmaxf(M, s_m[w * GP + h]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kTmaWarps; ++w) {
+      const float mw = s_m[w * GP + h];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      e_f[w * GP + h] = f;
+      L += s_l[w * GP + h] * f;
+    }
+    e_ml[h] = M;
+    e_ml[GP + h] = L;
+  }
+  __syncthreads();
+  // each warp stores its O^T fragments pre-weighted
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const float f0 = e_f[warp * GP + nt * 8 + 2 * t], f1 = e_f[warp * GP + nt * 8 + 2 * t + 1];
 #pragma unroll
     for (int i = 0; i < NM; ++i)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int h = nt * 8 + 2 * t + (c & 1);
         const int d = 16 * i + g + ((c >= 2) ? 8 : 0);
-        s_o[(warp * GP + h) * D + d] = o[nt][i][c];
+        e_o[(warp * GP + h) * Epi::DP + d] = o[nt][i][c] * ((c & 1) ? f1 : f0);
       }
   }
   __syncthreads();
-  merge_and_store<T, D, GP, kTmaWarps>(a, s_o, s_m, s_l, out, row, kvh, split, active, group,
-                                       &s_last);
+
+  T *orow = out + ((int64_t)row * a.Hq + kvh * group) * D;
+  constexpr int kItems = GP * D / 4;  // float4 items of the CTA's [GP][D] output
+  if (CL) {
+    // Cluster merge: every rank sums its warps and writes (m, l, O) into its
+    // slot in rank 0's ring; rank 0 merges the slots and stores.
+    const uint32_t rank = cluster_rank(), ranks = gridDim.x;
+    float *x_o = reinterpret_cast<float *>(ring) + Epi::kX;  // [ranks][GP][D]
+    float *x_ml = x_o + (size_t)ranks * GP * D;               // [ranks][2][GP]
+    const uint32_t x_o0 = cluster_map(smem_u32(x_o), 0), x_ml0 = cluster_map(smem_u32(x_ml), 0);
+    cluster_sync_all();  // all ranks started; rank 0's ring is free
+    for (int it = threadIdx.x; it < kItems; it += blockDim.x) {
+      const int h = it / (D / 4), d = (it % (D / 4)) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < kTmaWarps; ++w) {
+        const float4 v = *reinterpret_cast<const float4 *>(e_o + (w * GP + h) * Epi::DP + d);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      st_cluster(x_o0 + 4u * (uint32_t)((rank * GP + h) * D + d), acc);
+    }
+    for (int h = threadIdx.x; h < GP; h += blockDim.x) {
+      st_cluster(x_ml0 + 4u * (rank * 2 * GP + h), e_ml[h]);
+      st_cluster(x_ml0 + 4u * (rank * 2 * GP + GP + h), e_ml[GP + h]);
+    }
+    cluster_sync_all();  // every slot written
+    if (rank != 0) return;
+    for (int it = threadIdx.x; it < kItems; it += blockDim.x) {
+      const int h = it / (D / 4), d = (it % (D / 4)) * 4;
+      if (h >= group) continue;
+      float M = -INFINITY;
+      for (uint32_t r = 0; r < ranks; ++r) M = fmaxf(M, x_ml[r * 2 * GP + h]);
+      float L = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (uint32_t r = 0; r < ranks; ++r) {
+        const float mr = x_ml[r * 2 * GP + h];
+        const float f = (mr == -INFINITY) ? 0.f : exp2f(mr - M);
+        L += x_ml[r * 2 * GP + GP + h] * f;
+        const float4 v = *reinterpret_cast<const float4 *>(x_o + (r * GP + h) * D + d);
+        acc.x += v.x * f;
+        acc.y += v.y * f;
+        acc.z += v.z * f;
+        acc.w += v.w * f;
+      }
+      const float inv = 1.f / L;
+      store4<T>(orow + h * D + d, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+    }
+    return;
+  }
+
+  const int64_t part_floats = (int64_t)GP * (2 + D);
+  float *part_base = a.scratch + ((int64_t)row * a.Hk + kvh) * a.num_splits * part_floats;
+  float *part = part_base + (int64_t)split * part_floats;
+  for (int it = threadIdx.x; it < kItems; it += blockDim.x) {
+    const int h = it / (D / 4), d = (it % (D / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kTmaWarps; ++w) {
+      const float4 v = *reinterpret_cast<const float4 *>(e_o + (w * GP + h) * Epi::DP + d);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (active == 1) {
+      if (h < group) {
+        const float inv = 1.f / e_ml[GP + h];
+        store4<T>(orow + h * D + d, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+      }
+    } else {
+      *reinterpret_cast<float4 *>(part + 2 * GP + h * D + d) = acc;
+    }
+  }
+  if (active == 1) return;
+  // Publish (m, l) and take a ticket; the last split of the (row, kv head)
+  // merges every partial.
+  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
+    part[h] = e_ml[h];
+    part[GP + h] = e_ml[GP + h];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&a.counters[row * a.Hk + kvh], 1);
+    s_last = (prev == active - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  merge_published<T, D, GP>(part_base, part_floats, active, orow, group * D, e_o);
+  if (threadIdx.x == 0) a.counters[row * a.Hk + kvh] = 0;
 }
 
 
@@ -791,6 +970,13 @@ bool legacy_attention_requested() {
   return v != nullptr && v[0] == '1';
 }
 
+// DSB_ATTENTION_TICKET_MERGE=1 keeps the TMA kernel but merges splits through
+// global partials (the path used above 8 splits), so tests cover both merges.
+bool legacy_merge_requested() {
+  const char *v = getenv("DSB_ATTENTION_TICKET_MERGE");
+  return v != nullptr && v[0] == '1';
+}
+
 template <typename T, int D, int NT, int NS, int W>
 int launch_tma(const AttnArgs &a, int splits, cudaStream_t st) {
   CUtensorMap tmk, tmv;
@@ -800,9 +986,24 @@ int launch_tma(const AttnArgs &a, int splits, cudaStream_t st) {
       !encode_kv_map(&tmv, a.wv, rows_total, D, dt, 16 * W))
     return -1;  // no tensor map: the caller uses the register-fed kernel
   const size_t smem = tma_smem_bytes<T, D, NT, NS, W>();
-  auto kern = draft_attention_tma_kernel<T, D, NT, NS, W>;
+  using Epi = TmaEpi<D, NT * 8, W>;
+  constexpr size_t ring = TmaCfg<D, NS, W>::kRingBytes;
+  static_assert(Epi::bytes(0) <= ring, "the epilogue staging must fit in the ring");
+  const dim3 grid(splits, a.Hk, a.out_rows);
+  // 2..8 splits: merge through distributed shared memory inside a cluster of
+  // the (row, kv head)'s splits; otherwise (or if such a cluster cannot be
+  // scheduled) through global partials and an atomic ticket.
+  if (splits >= 2 && splits <= 8 && Epi::bytes(splits) <= ring && !legacy_merge_requested()) {
+    auto kern = draft_attention_tma_kernel<T, D, NT, NS, W, true>;
+    if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
+    if (cluster_fits((const void *)kern, splits, W * 32, smem)) {
+      launch_kernel_cluster(kern, grid, dim3(W * 32), smem, st, splits, tmk, tmv, a);
+      return check_launch("draft_attention_tma_kernel (cluster merge)");
+    }
+  }
+  auto kern = draft_attention_tma_kernel<T, D, NT, NS, W, false>;
   if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
-  kern<<<dim3(splits, a.Hk, a.out_rows), W * 32, smem, st>>>(tmk, tmv, a);
+  launch_kernel(kern, grid, dim3(W * 32), smem, st, tmk, tmv, a);
   return check_launch("draft_attention_tma_kernel");
 }
 
@@ -822,7 +1023,7 @@ int launch_attention_typed(const AttnArgs &a, int splits, cudaStream_t st) {
   const size_t smem = attn_smem_bytes<T, D, NT>();
   auto kern = draft_attention_kernel<T, D, NT>;
   if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
-  kern<<<dim3(splits, a.Hk, a.out_rows), kAttnWarps * 32, smem, st>>>(a);
+  launch_kernel(kern, dim3(splits, a.Hk, a.out_rows), dim3(kAttnWarps * 32), smem, st, a);
   return check_launch("draft_attention_kernel");
 }
 

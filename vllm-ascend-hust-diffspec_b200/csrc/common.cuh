@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "diffspec_b200.h"
 
@@ -25,6 +26,53 @@ int sm_count();
 // repeated launches (and launches during CUDA-graph capture) only enqueue.
 int ensure_smem(const void *kernel, size_t bytes);
 
+// Launch with programmatic dependent launch allowed: the kernel's CTAs may be
+// scheduled while the previous kernel in the stream is finishing, and block in
+// pdl_begin() (griddepcontrol.wait) until that kernel has completed and its
+// memory is visible.  Every kernel of this library calls pdl_begin() before
+// its first global memory access, so the overlap only hides launch latency.
+// Errors surface through cudaGetLastError (check_launch).
+template <typename... Params, typename... Args>
+void launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t st, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Same, with thread-block clusters of `cluster_x` CTAs along x.
+template <typename... Params, typename... Args>
+void launch_kernel_cluster(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                           cudaStream_t st, int cluster_x, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Whether at least one cluster of `cluster_x` CTAs with this shared memory
+// fits on the device (cached per device, kernel, cluster size and smem).
+bool cluster_fits(const void *kernel, int cluster_x, int threads, size_t smem);
+
 // ------------------------------------------------------------ element types
 template <typename T> struct Elem;
 template <> struct Elem<__nv_bfloat16> {
@@ -39,6 +87,14 @@ template <> struct Elem<float> {
   static __device__ __forceinline__ float to_f(float v) { return v; }
   static __device__ __forceinline__ float from_f(float v) { return v; }
 };
+
+// Programmatic dependent launch: wait for the previous kernel in the stream
+// (a no-op when the launch had no programmatic dependency), then let the next
+// kernel's CTAs start launching.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 __device__ __forceinline__ void flag_error(int32_t *flag, int32_t bit) {
   if (flag != nullptr) atomicOr(flag, bit);

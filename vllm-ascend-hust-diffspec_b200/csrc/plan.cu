@@ -17,6 +17,7 @@ __global__ void build_plan_kernel(const int32_t *__restrict__ row_slots,
                                   int HB, int plan_width, int64_t *__restrict__ plan,
                                   int32_t *__restrict__ history_lens,
                                   int32_t *__restrict__ working_lens, int32_t *err) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= rows) return;
@@ -81,6 +82,7 @@ __global__ void prepare_rows_kernel(const int32_t *__restrict__ query_ends,
                                     int32_t *__restrict__ query_index,
                                     int32_t *__restrict__ retrieval_lens,
                                     int32_t *__restrict__ row_slots, int32_t *status) {
+  pdl_begin();
   __shared__ int any;
   if (threadIdx.x == 0) any = 0;
   __syncthreads();
@@ -116,6 +118,7 @@ __global__ void write_raw_kernel(const uint4 *__restrict__ key, const uint4 *__r
                                  const int64_t *__restrict__ positions, int tokens,
                                  int num_slots, int64_t max_model_len, int row_vecs,
                                  int32_t *err) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (i >= tokens) return;
@@ -156,7 +159,7 @@ extern "C" int dsb_build_history_plan(const int32_t *row_slots, const int32_t *c
   if (chunk_size <= 0 || history_budget <= 0 || plan_width < 5 || sel_stride <= 0 ||
       num_slots <= 0)
     return fail(DSB_ERR_INVALID, "bad chunk size, budget, plan width or selection stride");
-  build_plan_kernel<<<(rows + 3) / 4, 128, 0, as_stream(stream)>>>(
+  launch_kernel(build_plan_kernel, dim3((rows + 3) / 4), dim3(128), 0, as_stream(stream),
       row_slots, committed_lens, rows, sel_chunks, sel_stride, sel_count, num_slots,
       chunk_size, history_budget, plan_width, plan, history_lens, working_lens, error_flag);
   return check_launch("build_plan_kernel");
@@ -173,7 +176,7 @@ extern "C" int dsb_prepare_retrieval_rows(const int32_t *query_ends,
   if (!query_ends || !target_seq_lens || !counts || !active_slots || !query_index ||
       !retrieval_lens || !row_slots)
     return fail(DSB_ERR_INVALID, "null pointer argument");
-  prepare_rows_kernel<<<1, 256, 0, as_stream(stream)>>>(
+  launch_kernel(prepare_rows_kernel, dim3(1), dim3(256), 0, as_stream(stream),
       query_ends, target_seq_lens, counts, counts_are_int64, active_slots, rows, query_index,
       retrieval_lens, row_slots, status);
   return check_launch("prepare_rows_kernel");
@@ -194,7 +197,7 @@ extern "C" int dsb_write_raw_kv(const void *key, const void *value, void *raw_ke
   if (num_heads <= 0 || head_dim <= 0 || row_bytes % 16)
     return fail(DSB_ERR_UNSUPPORTED, "KV row must be a multiple of 16 bytes");
   const int warps = 8;
-  write_raw_kernel<<<(tokens + warps - 1) / warps, warps * 32, 0, as_stream(stream)>>>(
+  launch_kernel(write_raw_kernel, dim3((tokens + warps - 1) / warps), dim3(warps * 32), 0, as_stream(stream),
       static_cast<const uint4 *>(key), static_cast<const uint4 *>(value),
       static_cast<uint4 *>(raw_key), static_cast<uint4 *>(raw_value), slots, positions, tokens,
       num_slots, max_model_len, (int)(row_bytes / 16), error_flag);

@@ -123,6 +123,7 @@ __device__ __forceinline__ uint4 rotate8(const uint4 &x, const uint4 &y, const f
 
 template <typename T, typename CS, bool GATHER, int DH>
 __global__ void __launch_bounds__(kWarpsRope * 32, 3) rope_rows_kernel(const RopeArgs a) {
+  pdl_begin();
   // DH: head_dim known at compile time (64, 128, 256), or 0 for any other.
   const int head_dim = DH ? DH : a.head_dim;
   extern __shared__ uint4 stage[];
@@ -379,6 +380,7 @@ constexpr int kBulkThreads = 256;
 
 template <typename T, typename CS, bool GATHER, int DH>
 __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs a) {
+  pdl_begin();
   static_assert(sizeof(T) == 2 && DH > 0, "16-bit caches with a compile-time head_dim");
   constexpr int VE = 8;           // elements per 16-byte vector
   constexpr int DV = DH / VE;     // vectors per head row
@@ -621,7 +623,7 @@ bool legacy_rope_requested() {
 }
 
 #ifndef DSB_BULK_STAGE_BYTES
-#define DSB_BULK_STAGE_BYTES (64 * 1024)  // K + V rows staged per bulk-kernel CTA
+#define DSB_BULK_STAGE_BYTES (32 * 1024)  // K + V rows staged per bulk-kernel CTA
 #endif
 
 bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
@@ -654,7 +656,7 @@ int launch_rope_bulk(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
     if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
     const int64_t gx = (width + pt - 1) / pt;
     if (gx > 0x7fffffff || rows > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
-    kern<<<dim3((unsigned)gx, rows), kBulkThreads, smem, st>>>(a);
+    launch_kernel(kern, dim3((unsigned)gx, rows), dim3(kBulkThreads), smem, st, a);
     return check_launch(GATHER ? "gather_rope_bulk_kernel" : "rebuild_rope_bulk_kernel");
   }
 }
@@ -690,7 +692,7 @@ int launch_rope(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
   const int64_t fill = ((int64_t)resident * sm_count() + rows - 1) / rows;
   const int64_t gx = std::max<int64_t>(1, std::min<int64_t>((width + per_cta - 1) / per_cta, fill));
   if (gx > 0x7fffffff || rows > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
-  kern<<<dim3((unsigned)gx, rows), kWarpsRope * 32, smem, st>>>(a);
+  launch_kernel(kern, dim3((unsigned)gx, rows), dim3(kWarpsRope * 32), smem, st, a);
   return check_launch(GATHER ? "gather_rope_kernel" : "rebuild_rope_kernel");
 }
 

@@ -76,6 +76,7 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
                         int Hq, int Hk, int block_size, int64_t num_blocks, int chunk,
                         int max_chunks, float scale_log2, float *__restrict__ out,
                         float *__restrict__ out_sum, int32_t *err) {
+  pdl_begin();
   constexpr int KS = D / 16;  // mma k-steps over head_dim
   const int b = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -264,6 +265,7 @@ chunk_scores_generic_kernel(const T *__restrict__ query, const float *__restrict
                             int Hk, int D, int block_size, int64_t num_blocks, int chunk,
                             int max_chunks, float scale_log2, float *__restrict__ out,
                             float *__restrict__ out_sum, int32_t *err) {
+  pdl_begin();
   extern __shared__ float qs_all[];
   const int b = blockIdx.y, c = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -341,6 +343,7 @@ stats_to_head_scores_kernel(const float *__restrict__ cmax, const float *__restr
                             const int32_t *__restrict__ seq_lens, int Hq, int Hk, int chunk,
                             int max_chunks, float *__restrict__ head_scores,
                             float *__restrict__ lse_out) {
+  pdl_begin();
   extern __shared__ float lse2[];
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -384,6 +387,7 @@ finalize_scores_kernel(const float *__restrict__ parts, int64_t row_stride,
                        int64_t part_stride, int num_parts,
                        const int32_t *__restrict__ seq_lens, int total_heads, int chunk,
                        int max_chunks, float *__restrict__ scores) {
+  pdl_begin();
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= max_chunks) return;
@@ -440,7 +444,7 @@ int validate(const ScoreArgs &a, bool stats) {
 template <typename T, int D, int NT, bool STATS>
 void launch_mma(const ScoreArgs &a) {
   dim3 grid((a.max_chunks + kChunksPerCta - 1) / kChunksPerCta, a.B);
-  chunk_scores_mma_kernel<T, D, NT, STATS><<<grid, kWarps * 32, 0, a.st>>>(
+  launch_kernel(chunk_scores_mma_kernel<T, D, NT, STATS>, dim3(grid), dim3(kWarps * 32), 0, a.st,
       static_cast<const T *>(a.query), a.lse, a.qidx, a.qrows, static_cast<const T *>(a.kc), a.bt,
       a.bt_stride, a.bt_cols, a.seq, a.Hq, a.Hk, a.bs, a.nblocks, a.C, a.max_chunks,
       a.scale * kLog2e, a.out, a.out_sum, a.err);
@@ -468,10 +472,10 @@ int dispatch_typed(const ScoreArgs &a) {
   auto kern = chunk_scores_generic_kernel<T, STATS>;
   if (int st_ = ensure_smem((const void *)kern, smem); st_ != DSB_OK) return st_;
   dim3 grid(a.max_chunks, a.B);
-  kern<<<grid, 128, smem, a.st>>>(static_cast<const T *>(a.query), a.lse, a.qidx, a.qrows,
-                                  static_cast<const T *>(a.kc), a.bt, a.bt_stride, a.bt_cols,
-                                  a.seq, a.Hq, a.Hk, a.D, a.bs, a.nblocks, a.C, a.max_chunks,
-                                  a.scale * kLog2e, a.out, a.out_sum, a.err);
+  launch_kernel(kern, dim3(grid), dim3(128), smem, a.st, static_cast<const T *>(a.query), a.lse,
+                a.qidx, a.qrows, static_cast<const T *>(a.kc), a.bt, a.bt_stride, a.bt_cols, a.seq,
+                a.Hq, a.Hk, a.D, a.bs, a.nblocks, a.C, a.max_chunks, a.scale * kLog2e, a.out,
+                a.out_sum, a.err);
   return check_launch("chunk_scores_generic_kernel");
 }
 
@@ -535,7 +539,7 @@ extern "C" int dsb_chunk_stats_to_head_scores(const float *chunk_max, const floa
       chunk_size <= 0)
     return fail(DSB_ERR_INVALID, "bad head counts or chunk size");
   const size_t smem = sizeof(float) * num_query_heads;
-  stats_to_head_scores_kernel<<<batch, 256, smem, as_stream(stream)>>>(
+  launch_kernel(stats_to_head_scores_kernel, dim3(batch), dim3(256), smem, as_stream(stream),
       chunk_max, chunk_sum, seq_lens, num_query_heads, num_kv_heads, chunk_size, max_chunks,
       head_scores, lse_out);
   return check_launch("stats_to_head_scores_kernel");
@@ -552,7 +556,7 @@ extern "C" int dsb_finalize_chunk_scores(const float *parts, int64_t row_stride,
   if (total_query_heads <= 0 || chunk_size <= 0)
     return fail(DSB_ERR_INVALID, "bad head count or chunk size");
   dim3 grid((max_chunks + 255) / 256, batch);
-  finalize_scores_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+  launch_kernel(finalize_scores_kernel, dim3(grid), dim3(256), 0, as_stream(stream),
       parts, row_stride, part_stride, num_parts, seq_lens, total_query_heads, chunk_size,
       max_chunks, scores);
   return check_launch("finalize_scores_kernel");

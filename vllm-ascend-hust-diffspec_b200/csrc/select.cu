@@ -76,6 +76,7 @@ select_chunks_kernel(const float *__restrict__ parts, int64_t row_stride, int64_
                      int32_t *__restrict__ sel_count, int num_slots,
                      int64_t *__restrict__ out_ci, int64_t *__restrict__ out_ti,
                      float *__restrict__ out_cs, int32_t *err) {
+  pdl_begin();
   extern __shared__ uint32_t keys[];  // [max_chunks] order keys, then [S] chosen ids
   int32_t *chosen = reinterpret_cast<int32_t *>(keys + max_chunks);
   __shared__ int hist[256];
@@ -236,7 +237,7 @@ extern "C" int dsb_select_context_chunks(
   const size_t smem = sizeof(uint32_t) * ((size_t)max_chunks + (size_t)S);
   if (smem > 220 * 1024) return fail(DSB_ERR_UNSUPPORTED, "too many chunks for one CTA");
   if (int st_ = ensure_smem((const void *)select_chunks_kernel, smem); st_ != DSB_OK) return st_;
-  select_chunks_kernel<<<rows, kThreads, smem, as_stream(stream)>>>(
+  launch_kernel(select_chunks_kernel, dim3(rows), dim3(kThreads), smem, as_stream(stream),
       parts, row_stride, part_stride, num_parts, normalize_heads, seq_lens, row_slots,
       max_chunks, chunk_size, S, sel_chunks, sel_stride, sel_count, num_slots,
       out_chunk_indices, out_token_indices, out_chunk_scores, error_flag);
