@@ -12,11 +12,21 @@
 // lane (g, t) = (lane / 4, lane % 4) owns tokens g and g + 8 of the tile and
 // the head-dim slab {8 * (4j + t) .. +8 : j < D/32}.  The contraction order
 // over head_dim is permuted consistently for Q and K, which leaves the dot
-// product unchanged.  The chunk sum over tokens and the sum over the group's
-// query heads are reduced in registers with a fixed shuffle tree, so the
-// per-(row, kv head, chunk) mass is deterministic and independent of how kv
-// heads are sharded across GPUs.
+// product unchanged; the k-steps alternate between two accumulators to halve
+// the dependent mma chain.  Each 16-token tile's sum over tokens and query
+// heads is reduced by a fixed shuffle tree and a chunk adds its tiles in tile
+// order, so the per-(row, kv head, chunk) mass is deterministic and
+// independent of how kv heads are sharded across GPUs.
+//
+// Measured alternative, not kept: a persistent TMA-fed variant (a producer
+// warp bulk-copying 16 KB pages into a 3 x 64 KB shared-memory ring, eight
+// consumer warps scoring from it) ran at 148 us against this kernel's 133 us
+// on the config-2 retrieval (671 MB): with ~128 KB in flight per SM the bulk
+// copies saw 2-4 us of latency under full load, while 16 register-fed warps
+// per SM keep more, smaller requests in flight.
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -64,6 +74,112 @@ __device__ __forceinline__ void load_token(uint4 (&dst)[D / 32], const T *row, i
   } else {
 #pragma unroll
     for (int j = 0; j < D / 32; ++j) dst[j] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// (M, S) <- (M, S) merged with (m, s): running max and sum of exp2 in base 2.
+__device__ __forceinline__ void merge_ms(float &M, float &S, float m, float s) {
+  const float mn = fmaxf(M, m);
+  S = (mn == -INFINITY) ? 0.f : S * exp2f(M - mn) + s * exp2f(m - mn);
+  M = mn;
+}
+
+// One 16-token tile of one kv head.  lo / hi: this lane's head-dim words of
+// tokens g and g + 8 (A fragments in the permuted order); va / vb: whether
+// those tokens count.  !STATS: `mass` = the tile's sum over valid tokens and
+// heads of exp2(s * scale_log2 - lse2), reduced over the warp by a fixed xor
+// tree (every lane holds it).  STATS: per (n-tile, head 2t + j) the tile's
+// (max, sum) merged over its 16 tokens (every lane of a column holds it).
+// Both kernels below score tiles with this one function and combine tiles in
+// tile order, so a chunk's value does not depend on which warp scored it.
+template <typename T, int D, int NT, bool STATS>
+__device__ __forceinline__ void eval_tile(const uint4 (&lo)[D / 32], const uint4 (&hi)[D / 32],
+                                          bool va, bool vb, const uint32_t (&qf)[NT][D / 16][2],
+                                          const float (&lse2)[NT][2], int group, float scale_log2,
+                                          int t, float &mass, float (&tm)[NT][2],
+                                          float (&ts)[NT][2]) {
+  constexpr int KS = D / 16;
+  float acc = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      tm[nt][j] = -INFINITY;
+      ts[nt][j] = 0.f;
+    }
+    // two accumulators (even / odd k-steps) halve the dependent mma chain
+    float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      const uint32_t a[4] = {word_of(lo[(2 * s) / 4], (2 * s) % 4),
+                             word_of(hi[(2 * s) / 4], (2 * s) % 4),
+                             word_of(lo[(2 * s + 1) / 4], (2 * s + 1) % 4),
+                             word_of(hi[(2 * s + 1) / 4], (2 * s + 1) % 4)};
+      Mma<T>::run((s & 1) ? co : ce, a, qf[nt][s]);
+    }
+    const float cf[4] = {ce[0] + co[0], ce[1] + co[1], ce[2] + co[2], ce[3] + co[3]};
+    // cf: (token g, head 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int hj = j & 1;
+      const bool tv = (j < 2) ? va : vb;
+      const bool hv = nt * 8 + 2 * t + hj < group;
+      if (!STATS) {
+        if (tv && hv) acc += exp2f(fmaf(cf[j], scale_log2, -lse2[nt][hj]));
+      } else if (tv && hv) {
+        const float x = cf[j] * scale_log2;
+        const float mn = fmaxf(tm[nt][hj], x);
+        ts[nt][hj] = ts[nt][hj] * exp2f(tm[nt][hj] - mn) + exp2f(x - mn);
+        tm[nt][hj] = mn;
+      }
+    }
+  }
+  if (!STATS) {
+    mass = warp_sum(acc);
+  } else {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {  // merge over the 8 token groups
+          const float mo = __shfl_xor_sync(0xffffffffu, tm[nt][j], o);
+          const float so = __shfl_xor_sync(0xffffffffu, ts[nt][j], o);
+          merge_ms(tm[nt][j], ts[nt][j], mo, so);
+        }
+  }
+}
+
+// Q^T B fragments for one kv head (lane (g, t) holds query head g of each
+// n-tile, head-dim words in the permuted order of the K A-fragments) and the
+// heads' LSE in base 2.
+template <typename T, int D, int NT, bool STATS>
+__device__ __forceinline__ void load_query(const T *query, const float *lse, int qrow, int Hq,
+                                           int group, int kvh, int g, int t,
+                                           uint32_t (&qf)[NT][D / 16][2], float (&lse2)[NT][2]) {
+  constexpr int KS = D / 16;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int h = nt * 8 + g;
+    uint4 qv[D / 32];
+    if (h < group) {
+      const T *qp = query + ((int64_t)qrow * Hq + kvh * group + h) * D;
+#pragma unroll
+      for (int j = 0; j < D / 32; ++j) qv[j] = *reinterpret_cast<const uint4 *>(qp + 8 * (4 * j + t));
+    } else {
+#pragma unroll
+      for (int j = 0; j < D / 32; ++j) qv[j] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      qf[nt][s][0] = word_of(qv[(2 * s) / 4], (2 * s) % 4);
+      qf[nt][s][1] = word_of(qv[(2 * s + 1) / 4], (2 * s + 1) % 4);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int hh = nt * 8 + 2 * t + j;
+      lse2[nt][j] = (!STATS && hh < group) ? lse[(int64_t)qrow * Hq + kvh * group + hh] * kLog2e : 0.f;
+    }
   }
 }
 
@@ -123,47 +239,19 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
       continue;
     }
     if (kvh != loaded_kvh) {
-      // B fragments of Q^T: lane (g, t) holds query head g of this n-tile,
-      // head-dim words in the same permuted order as the K A-fragments.
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int h = nt * 8 + g;
-        uint4 qv[D / 32];
-        if (h < group) {
-          const T *qp = query + ((int64_t)qrow * Hq + kvh * group + h) * D;
-#pragma unroll
-          for (int j = 0; j < D / 32; ++j)
-            qv[j] = *reinterpret_cast<const uint4 *>(qp + 8 * (4 * j + t));
-        } else {
-#pragma unroll
-          for (int j = 0; j < D / 32; ++j) qv[j] = make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int s = 0; s < KS; ++s) {
-          qf[nt][s][0] = word_of(qv[(2 * s) / 4], (2 * s) % 4);
-          qf[nt][s][1] = word_of(qv[(2 * s + 1) / 4], (2 * s + 1) % 4);
-        }
-        if (!STATS) {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int hh = nt * 8 + 2 * t + j;
-            lse2[nt][j] = (hh < group)
-                              ? lse[(int64_t)qrow * Hq + kvh * group + hh] * kLog2e
-                              : 0.f;
-          }
-        }
-      }
+      load_query<T, D, NT, STATS>(query, lse, qrow, Hq, group, kvh, g, t, qf, lse2);
       loaded_kvh = kvh;
     }
 
-    float acc = 0.f;                       // !STATS: mass of this lane's values
-    float m[NT][2], ssum[NT][2];           // STATS: running max / sum per head
+    // Tiles are scored one by one and combined in tile order.
+    float mass = 0.f;
+    float M[NT][2], S[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        m[nt][j] = -INFINITY;
-        ssum[nt][j] = 0.f;
+        M[nt][j] = -INFINITY;
+        S[nt][j] = 0.f;
       }
 
     // Register double buffer over the chunk's 16-token tiles.
@@ -182,32 +270,16 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
     auto consume = [&](const KTile<D> &src, int mt) {
       const bool va = tok0 + mt * 16 + g < L;
       const bool vb = tok0 + mt * 16 + g + 8 < L;
+      float tmass, tm[NT][2], ts[NT][2];
+      eval_tile<T, D, NT, STATS>(src.lo, src.hi, va, vb, qf, lse2, group, scale_log2, t, tmass,
+                                 tm, ts);
+      if (!STATS) {
+        mass += tmass;
+      } else {
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        float cf[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int s = 0; s < KS; ++s) {
-          const uint32_t a[4] = {word_of(src.lo[(2 * s) / 4], (2 * s) % 4),
-                                 word_of(src.hi[(2 * s) / 4], (2 * s) % 4),
-                                 word_of(src.lo[(2 * s + 1) / 4], (2 * s + 1) % 4),
-                                 word_of(src.hi[(2 * s + 1) / 4], (2 * s + 1) % 4)};
-          Mma<T>::run(cf, a, qf[nt][s]);
-        }
-        // cf: (token g, head 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int hj = j & 1;
-          const bool tv = (j < 2) ? va : vb;
-          const bool hv = nt * 8 + 2 * t + hj < group;
-          if (!STATS) {
-            if (tv && hv) acc += exp2f(fmaf(cf[j], scale_log2, -lse2[nt][hj]));
-          } else if (tv && hv) {
-            const float x = cf[j] * scale_log2;
-            const float mn = fmaxf(m[nt][hj], x);
-            ssum[nt][hj] = ssum[nt][hj] * exp2f(m[nt][hj] - mn) + exp2f(x - mn);
-            m[nt][hj] = mn;
-          }
-        }
+          for (int j = 0; j < 2; ++j) merge_ms(M[nt][j], S[nt][j], tm[nt][j], ts[nt][j]);
       }
     };
 
@@ -221,31 +293,17 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
     }
 
     if (!STATS) {
-      acc = warp_sum(acc);
-      if (lane == 0) out[((int64_t)b * Hk + kvh) * max_chunks + c] = acc;
+      if (lane == 0) out[((int64_t)b * Hk + kvh) * max_chunks + c] = mass;
     } else {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          float mm = m[nt][j], ss = ssum[nt][j];
-#pragma unroll
-          for (int o = 4; o < 32; o <<= 1) {  // merge over the 8 token groups
-            const float mo = __shfl_xor_sync(0xffffffffu, mm, o);
-            const float so = __shfl_xor_sync(0xffffffffu, ss, o);
-            const float mn = fmaxf(mm, mo);
-            if (mn == -INFINITY) {
-              ss = 0.f;
-            } else {
-              ss = ss * exp2f(mm - mn) + so * exp2f(mo - mn);
-            }
-            mm = mn;
-          }
           const int h = nt * 8 + 2 * t + j;
           if (g == 0 && h < group) {
             const int64_t o = ((int64_t)b * Hq + kvh * group + h) * max_chunks + c;
-            out[o] = mm;
-            out_sum[o] = ss;
+            out[o] = M[nt][j];
+            out_sum[o] = S[nt][j];
           }
         }
     }
