@@ -548,18 +548,16 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
-// Shared-memory layout of the TMA kernel's epilogue, inside the (then idle)
-// ring: per-warp O rows padded to D + 4 floats (conflict-free fragment
-// stores), per-warp weights, the CTA's (M, L) per head, and - cluster merge
-// only, used in rank 0 - one (m, l, O) slot per cluster rank.
+// Shared-memory layout of the TMA kernel's epilogue: the per-warp O rows,
+// padded to D + 4 floats (conflict-free fragment stores), reuse the then idle
+// ring.  The cluster merge adds an exchange area after the kernel's other
+// shared memory, used in rank 0: one (O, m, l) slot per cluster rank.
 template <int D, int GP, int W> struct TmaEpi {
   static constexpr int DP = D + 4;
-  static constexpr int kO = 0;                        // [W][GP][DP]
-  static constexpr int kF = kO + W * GP * DP;         // [W][GP]
-  static constexpr int kML = kF + W * GP;             // [2][GP]
-  static constexpr int kX = (kML + 2 * GP + 3) / 4 * 4;  // [ranks][GP][D], then [ranks][2][GP]
-  static constexpr size_t bytes(int ranks) {
-    return sizeof(float) * ((size_t)kX + (size_t)ranks * GP * (D + 2));
+  static constexpr int kO = 0;  // [W][GP][DP] floats at the ring's start
+  static constexpr size_t ring_bytes() { return sizeof(float) * (size_t)W * GP * DP; }
+  static constexpr size_t exchange_bytes(int ranks) {
+    return sizeof(float) * (size_t)ranks * GP * (D + 2);
   }
 };
 
@@ -567,7 +565,14 @@ template <typename T, int D, int NT, int NS, int kTmaWarps, bool CL>
 __global__ void __launch_bounds__(kTmaWarps * 32)
 draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
+  if (threadIdx.x == 0) {  // descriptor fetch overlaps the wait for the previous kernel
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+  }
   pdl_begin();
+  // Cluster merge: arrive on the "all ranks started" phase right away; the
+  // matching wait comes just before the first remote shared-memory store.
+  if (CL) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   using Cfg = TmaCfg<D, NS, kTmaWarps>;
   constexpr int KS = D / 16, NM = D / 16, GP = NT * 8;
   constexpr int kStageTok = Cfg::kStageTok, kBoxBytes = Cfg::kBoxBytes;
@@ -586,9 +591,44 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   const int g = lane >> 2, t = lane & 3;
   const int group = a.Hq / a.Hk;
   T *out = static_cast<T *>(a.out);
+  const uint32_t ring_u32 = smem_u32(ring);
+  const uint32_t bar_u32 = smem_u32(bars);
+  if (threadIdx.x == 0) {  // independent of any global data: first
+    for (int s = 0; s < NS; ++s) mbar_init(bar_u32 + 8 * s);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_abort = 0;
+  }
   if (row >= a.rows) {
     if (split == 0) zero_heads<T, D>(out, row, a.Hq, kvh * group, group);
     return;
+  }
+  // Q^T B-fragments in natural head-dim order: lane (g, t) holds head
+  // nt*8+g, dims 16s + 2t, 2t+1 and 16s + 8 + 2t, 2t+1.  Loaded before the
+  // slot is known so their latency overlaps the slot / position reads.
+  uint32_t qf[NT][KS][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int h = nt * 8 + g;
+    const uint32_t *qp = reinterpret_cast<const uint32_t *>(
+        static_cast<const T *>(a.query) + ((int64_t)row * a.Hq + kvh * group + min(h, group - 1)) * D);
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      qf[nt][s][0] = (h < group) ? qp[8 * s + t] : 0u;
+      qf[nt][s][1] = (h < group) ? qp[8 * s + 4 + t] : 0u;
+    }
+  }
+  // warp 0 also fetches the step's new K / V rows (written below if this
+  // split owns the new position)
+  constexpr int VE = 16 / sizeof(T), kNewVecs = 2 * (D / VE), kNewPerLane = (kNewVecs + 31) / 32;
+  uint4 new_kv[kNewPerLane];
+  if (warp == 0) {
+#pragma unroll
+    for (int j = 0; j < kNewPerLane; ++j) {
+      const int i = lane + 32 * j;
+      const T *src = static_cast<const T *>(i < D / VE ? a.key : a.value) +
+                     ((int64_t)row * a.Hk + kvh) * D + (i % (D / VE)) * VE;
+      new_kv[j] = (i < kNewVecs) ? *reinterpret_cast<const uint4 *>(src) : make_uint4(0, 0, 0, 0);
+    }
   }
   const int slot = a.slots[row];
   const int pos = a.positions[row] + a.position_offset;
@@ -609,32 +649,8 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   const int ts = live ? split * a.split_tokens : 0;
   const int te = live ? min(len, ts + a.split_tokens) : 0;
   const int64_t head_row0 = ((int64_t)slot * a.Hk + kvh) * a.W;  // tensor-map row of token 0
-
-  // The split owning the new token stores it first; the copy engine reads it
-  // back through the tensor map after the proxy fence.
-  if (pos >= ts && pos < te) {
-    constexpr int VE = 16 / sizeof(T);
-    const uint4 *nk = reinterpret_cast<const uint4 *>(static_cast<const T *>(a.key) +
-                                                      ((int64_t)row * a.Hk + kvh) * D);
-    const uint4 *nv = reinterpret_cast<const uint4 *>(static_cast<const T *>(a.value) +
-                                                      ((int64_t)row * a.Hk + kvh) * D);
-    uint4 *dk = reinterpret_cast<uint4 *>(static_cast<T *>(a.wk) + (head_row0 + pos) * D);
-    uint4 *dv = reinterpret_cast<uint4 *>(static_cast<T *>(a.wv) + (head_row0 + pos) * D);
-    for (int i = threadIdx.x; i < D / VE; i += blockDim.x) {
-      dk[i] = nk[i];
-      dv[i] = nv[i];
-    }
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-  }
   const int n_stages = (te - ts + kStageTok - 1) / kStageTok;
-  const uint32_t ring_u32 = smem_u32(ring);
-  const uint32_t bar_u32 = smem_u32(bars);
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) mbar_init(bar_u32 + 8 * s);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    s_abort = 0;
-  }
-  __syncthreads();
+
   auto issue = [&](int k) {  // thread 0 only
     const int s = k % NS;
     const uint32_t kb = ring_u32 + s * Cfg::kStageBytes;
@@ -647,23 +663,31 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
       tma_load_2d(vb + b * kBoxBytes, &tmv, 64 * b, y, bar_u32 + 8 * s);
     }
   };
-  if (threadIdx.x == 0)
-    for (int k = 0; k < NS && k < n_stages; ++k) issue(k);
-
-  // Q^T B-fragments in natural head-dim order: lane (g, t) holds head
-  // nt*8+g, dims 16s + 2t, 2t+1 and 16s + 8 + 2t, 2t+1.
-  uint32_t qf[NT][KS][2];
+  if (warp == 0) {
+    // Stages before the one holding the new position are issued at once; the
+    // owner split then stores the new token (each lane fences its stores for
+    // the async proxy) before the stage that reads it back is issued.
+    const bool owner = pos >= ts && pos < te;
+    const int n_first = min(NS, n_stages);
+    const int k_pos = owner ? (pos - ts) / kStageTok : n_first;
+    if (lane == 0)
+      for (int k = 0; k < min(n_first, k_pos); ++k) issue(k);
+    if (owner) {
+      T *dst = static_cast<T *>(a.wk) + (head_row0 + pos) * D;
+      T *dsv = static_cast<T *>(a.wv) + (head_row0 + pos) * D;
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int h = nt * 8 + g;
-    const uint32_t *qp = reinterpret_cast<const uint32_t *>(
-        static_cast<const T *>(a.query) + ((int64_t)row * a.Hq + kvh * group + min(h, group - 1)) * D);
-#pragma unroll
-    for (int s = 0; s < KS; ++s) {
-      qf[nt][s][0] = (h < group) ? qp[8 * s + t] : 0u;
-      qf[nt][s][1] = (h < group) ? qp[8 * s + 4 + t] : 0u;
+      for (int j = 0; j < kNewPerLane; ++j) {
+        const int i = lane + 32 * j;
+        if (i < kNewVecs)
+          *reinterpret_cast<uint4 *>((i < D / VE ? dst : dsv) + (i % (D / VE)) * VE) = new_kv[j];
+      }
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __syncwarp();
     }
+    if (lane == 0)
+      for (int k = min(n_first, k_pos); k < n_first; ++k) issue(k);
   }
+  __syncthreads();  // barrier initialisation and s_abort visible to every warp
 
   float o[NT][NM][4];
   float m_run[NT][2], l_run[NT][2];
@@ -789,11 +813,9 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
 
   // ---- combine the warps of this CTA (the ring is idle from here on)
   using Epi = TmaEpi<D, GP, kTmaWarps>;
-  float *e_o = reinterpret_cast<float *>(ring) + Epi::kO;
-  float *e_f = reinterpret_cast<float *>(ring) + Epi::kF;
-  float *e_ml = reinterpret_cast<float *>(ring) + Epi::kML;
+  float *e_o = reinterpret_cast<float *>(ring) + Epi::kO;  // [warps][GP][DP], unscaled
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+  for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       float l = l_run[nt][j];
@@ -804,65 +826,60 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
         s_l[warp * GP + nt * 8 + 2 * t + j] = l;
       }
     }
-  __syncthreads();
-  // per head: the CTA max, each warp's weight exp2(m_w - M) and the CTA sum
-  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kTmaWarps; ++w) M = fmaxf(M, s_m[w * GP + h]);
-    float L = 0.f;
-#pragma unroll
-    for (int w = 0; w < kTmaWarps; ++w) {
-      const float mw = s_m[w * GP + h];
-      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-      e_f[w * GP + h] = f;
-      L += s_l[w * GP + h] * f;
-    }
-    e_ml[h] = M;
-    e_ml[GP + h] = L;
-  }
-  __syncthreads();
-  // each warp stores its O^T fragments pre-weighted
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const float f0 = e_f[warp * GP + nt * 8 + 2 * t], f1 = e_f[warp * GP + nt * 8 + 2 * t + 1];
 #pragma unroll
     for (int i = 0; i < NM; ++i)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int h = nt * 8 + 2 * t + (c & 1);
         const int d = 16 * i + g + ((c >= 2) ? 8 : 0);
-        e_o[(warp * GP + h) * Epi::DP + d] = o[nt][i][c] * ((c & 1) ? f1 : f0);
+        e_o[(warp * GP + h) * Epi::DP + d] = o[nt][i][c];
       }
   }
   __syncthreads();
+  // Item `it` (head h, dims d..d+3): fold the warps with weights
+  // exp2(m_w - M) into the CTA's partial (acc, M, L).
+  auto fold = [&](int it, int &h, int &d, float4 &acc, float &M, float &L) {
+    h = it / (D / 4);
+    d = (it % (D / 4)) * 4;
+    M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kTmaWarps; ++w) M = fmaxf(M, s_m[w * GP + h]);
+    L = 0.f;
+    acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kTmaWarps; ++w) {
+      const float mw = s_m[w * GP + h];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      L += s_l[w * GP + h] * f;
+      const float4 v = *reinterpret_cast<const float4 *>(e_o + (w * GP + h) * Epi::DP + d);
+      acc.x += v.x * f;
+      acc.y += v.y * f;
+      acc.z += v.z * f;
+      acc.w += v.w * f;
+    }
+  };
 
   T *orow = out + ((int64_t)row * a.Hq + kvh * group) * D;
   constexpr int kItems = GP * D / 4;  // float4 items of the CTA's [GP][D] output
   if (CL) {
-    // Cluster merge: every rank sums its warps and writes (m, l, O) into its
-    // slot in rank 0's ring; rank 0 merges the slots and stores.
+    // Cluster merge: every rank writes (M, L, O) into its slot of rank 0's
+    // exchange area (outside the ring, so no rank waits for another's loop
+    // before writing); rank 0 merges the slots and stores.
     const uint32_t rank = cluster_rank(), ranks = gridDim.x;
-    float *x_o = reinterpret_cast<float *>(ring) + Epi::kX;  // [ranks][GP][D]
-    float *x_ml = x_o + (size_t)ranks * GP * D;               // [ranks][2][GP]
+    float *x_o = reinterpret_cast<float *>(s_p + kTmaWarps * 16 * GP);  // [ranks][GP][D]
+    float *x_ml = x_o + (size_t)ranks * GP * D;                        // [ranks][2][GP]
     const uint32_t x_o0 = cluster_map(smem_u32(x_o), 0), x_ml0 = cluster_map(smem_u32(x_ml), 0);
-    cluster_sync_all();  // all ranks started; rank 0's ring is free
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");  // every rank is running
     for (int it = threadIdx.x; it < kItems; it += blockDim.x) {
-      const int h = it / (D / 4), d = (it % (D / 4)) * 4;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int w = 0; w < kTmaWarps; ++w) {
-        const float4 v = *reinterpret_cast<const float4 *>(e_o + (w * GP + h) * Epi::DP + d);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
+      int h, d;
+      float4 acc;
+      float M, L;
+      fold(it, h, d, acc, M, L);
       st_cluster(x_o0 + 4u * (uint32_t)((rank * GP + h) * D + d), acc);
-    }
-    for (int h = threadIdx.x; h < GP; h += blockDim.x) {
-      st_cluster(x_ml0 + 4u * (rank * 2 * GP + h), e_ml[h]);
-      st_cluster(x_ml0 + 4u * (rank * 2 * GP + GP + h), e_ml[GP + h]);
+      if (d == 0) {
+        st_cluster(x_ml0 + 4u * (rank * 2 * GP + h), M);
+        st_cluster(x_ml0 + 4u * (rank * 2 * GP + GP + h), L);
+      }
     }
     cluster_sync_all();  // every slot written
     if (rank != 0) return;
@@ -893,32 +910,26 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   float *part_base = a.scratch + ((int64_t)row * a.Hk + kvh) * a.num_splits * part_floats;
   float *part = part_base + (int64_t)split * part_floats;
   for (int it = threadIdx.x; it < kItems; it += blockDim.x) {
-    const int h = it / (D / 4), d = (it % (D / 4)) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int w = 0; w < kTmaWarps; ++w) {
-      const float4 v = *reinterpret_cast<const float4 *>(e_o + (w * GP + h) * Epi::DP + d);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
-    }
+    int h, d;
+    float4 acc;
+    float M, L;
+    fold(it, h, d, acc, M, L);
     if (active == 1) {
       if (h < group) {
-        const float inv = 1.f / e_ml[GP + h];
+        const float inv = 1.f / L;
         store4<T>(orow + h * D + d, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
       }
     } else {
       *reinterpret_cast<float4 *>(part + 2 * GP + h * D + d) = acc;
+      if (d == 0) {
+        part[h] = M;
+        part[GP + h] = L;
+      }
     }
   }
   if (active == 1) return;
-  // Publish (m, l) and take a ticket; the last split of the (row, kv head)
-  // merges every partial.
-  for (int h = threadIdx.x; h < GP; h += blockDim.x) {
-    part[h] = e_ml[h];
-    part[GP + h] = e_ml[GP + h];
-  }
+  // Publish and take a ticket; the last split of the (row, kv head) merges
+  // every partial.
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -987,17 +998,19 @@ int launch_tma(const AttnArgs &a, int splits, cudaStream_t st) {
     return -1;  // no tensor map: the caller uses the register-fed kernel
   const size_t smem = tma_smem_bytes<T, D, NT, NS, W>();
   using Epi = TmaEpi<D, NT * 8, W>;
-  constexpr size_t ring = TmaCfg<D, NS, W>::kRingBytes;
-  static_assert(Epi::bytes(0) <= ring, "the epilogue staging must fit in the ring");
+  static_assert(Epi::ring_bytes() <= TmaCfg<D, NS, W>::kRingBytes,
+                "the epilogue staging must fit in the ring");
   const dim3 grid(splits, a.Hk, a.out_rows);
   // 2..8 splits: merge through distributed shared memory inside a cluster of
   // the (row, kv head)'s splits; otherwise (or if such a cluster cannot be
   // scheduled) through global partials and an atomic ticket.
-  if (splits >= 2 && splits <= 8 && Epi::bytes(splits) <= ring && !legacy_merge_requested()) {
+  constexpr size_t kMaxSmem = 227 * 1024;
+  const size_t smem_cl = smem + Epi::exchange_bytes(splits);
+  if (splits >= 2 && splits <= 8 && smem_cl <= kMaxSmem && !legacy_merge_requested()) {
     auto kern = draft_attention_tma_kernel<T, D, NT, NS, W, true>;
-    if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
-    if (cluster_fits((const void *)kern, splits, W * 32, smem)) {
-      launch_kernel_cluster(kern, grid, dim3(W * 32), smem, st, splits, tmk, tmv, a);
+    if (int e = ensure_smem((const void *)kern, smem_cl); e != DSB_OK) return e;
+    if (cluster_fits((const void *)kern, splits, W * 32, smem_cl)) {
+      launch_kernel_cluster(kern, grid, dim3(W * 32), smem_cl, st, splits, tmk, tmv, a);
       return check_launch("draft_attention_tma_kernel (cluster merge)");
     }
   }
