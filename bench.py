@@ -63,6 +63,14 @@ UNIT = "draft steps/s"
 STEPS_PER_PERIOD = INTERVAL * DEPTH
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch per
+# kind, from one ncu capture of the current kernels on a B200:
+# `ncu --set full --clock-control none -k regex:<kernel> -s 2 -c 1
+#  python bench.py --only <kind> --steps 3 --warmup 2`.
+PROFILED_TRAFFIC = {"attention": 67_276_032 + 883_968, "rebuild": 65_614_848 + 17_102,
+                    "scores": 671_360_256 + 6_041}
+
+
 def _peaks() -> tuple[float, str]:
     try:
         data = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -170,11 +178,12 @@ class Workload:
         return lse
 
 
-def period_launches(w: "Workload", exchange=None, total_hq=None):
+def period_launches(w: "Workload", exchange=None, total_hq=None, gathered=None):
     """The kernels of one retrieval period as (kind, callable) in stream order.
 
-    `exchange` (multi-GPU) maps the local [rows, hk, N] mass to the request
-    group's [rows, hk_total, N]; it is inserted between scoring and selection.
+    `exchange` (multi-GPU) gathers the local [rows, hk, N] mass into the
+    request group's fixed [rows, hk_total, N] buffer `gathered`, which the
+    selection then reads; it is inserted between scoring and selection.
     """
     dsb, lib = w.dsb, w.dsb._lib
     total_hq = total_hq or w.hq
@@ -198,9 +207,8 @@ def period_launches(w: "Workload", exchange=None, total_hq=None):
 
     seq = [("prepare", prepare), ("scores", scores)]
     if exchange is not None:
-        holder = {}
-        seq.append(("exchange", lambda: holder.__setitem__("p", exchange(w.parts))))
-        seq.append(("select", lambda: select(lambda: holder["p"])))
+        seq.append(("exchange", lambda: exchange(w.parts)))
+        seq.append(("select", lambda: select(lambda: gathered)))
     else:
         seq.append(("select", select))
     for c in range(INTERVAL):
@@ -465,7 +473,8 @@ def run_ours(args):
     if hg > 1:
         gathered = torch.empty((rows, HK, w.max_chunks), dtype=torch.float32, device=device)
         exchange = lambda parts: dsb.parallel.gather_head_scores(parts, group, out=gathered)  # noqa: E731
-    launches = period_launches(w, exchange, total_hq=HQ)
+    launches = period_launches(w, exchange, total_hq=HQ,
+                               gathered=gathered if exchange is not None else None)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
     if exchange is None:
@@ -482,19 +491,27 @@ def run_ours(args):
             ex()
             second.replay()
 
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record()
     for _ in range(args.warmup):
         step()
+    w1.record()
     torch.cuda.synchronize(device)
     assert dsb._lib.read_and_clear_error_flag(device) == 0, "kernel index check tripped"
+    # Steps that keep the GPU loaded for ~0.6 s before and ~0.3 s after the
+    # timed region, so the clock sampler sees clocks under this load.  The
+    # counts come from the slowest rank's warm-up, so every rank issues the
+    # same collectives.
+    est_ms = torch.tensor([max(w0.elapsed_time(w1) / max(1, args.warmup), 1e-3)], device=device)
     if world > 1:
+        dist.all_reduce(est_ms, op=dist.ReduceOp.MAX)
         dist.barrier()
+    n_pre = max(1, math.ceil(600.0 / float(est_ms.item())))
+    n_post = max(1, math.ceil(300.0 / float(est_ms.item())))
     with ClockSampler(local) as clocks:
-        # keep the GPU loaded for >= 0.6 s before the timed region so the
-        # 100 ms clock sampler sees the clocks under this load
-        t_end = time.perf_counter() + 0.6
-        while time.perf_counter() < t_end:
+        for _ in range(n_pre):
             step()
-            torch.cuda.synchronize(device)
+        torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(device)
@@ -504,10 +521,9 @@ def run_ours(args):
             step()
         end.record()
         torch.cuda.synchronize(device)
-        t_end = time.perf_counter() + 0.3  # a few samples after the timed region too
-        while time.perf_counter() < t_end:
+        for _ in range(n_post):
             step()
-            torch.cuda.synchronize(device)
+        torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier()
     ms = start.elapsed_time(end) / args.steps
@@ -628,7 +644,8 @@ def emit_ours(args):
         achieved = per_launch[dominant] / (avg_ms / 1e3) / 1e9
         roofline = dict(bound="hbm", kernel=dominant, achieved=round(achieved, 1), peak=peak,
                         peak_kind=peak_kind, unit="GB/s", frac=round(achieved / peak, 4),
-                        traffic=None, algorithmic_bytes_per_launch=int(per_launch[dominant]),
+                        traffic=PROFILED_TRAFFIC.get(dominant),
+                        algorithmic_bytes_per_launch=int(per_launch[dominant]),
                         avg_launch_us=round(avg_ms * 1e3, 3),
                         timing="avg_launch_us: the kind's launches of one period back to back "
                                "in a CUDA graph; per_kind_us: each launch bracketed by events "
