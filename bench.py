@@ -43,6 +43,9 @@ sys.path.insert(0, str(ROOT))
 # the CPU baseline runs one numpy worker per core; keep BLAS single-threaded
 os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
 os.environ.setdefault("OMP_NUM_THREADS", "1")
+# stdout carries exactly one JSON line: keep NCCL's version banner off it
+if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+    os.environ["NCCL_DEBUG"] = "WARN"
 
 # ---------------------------------------------------------------- config 2
 B_GROUP = 16          # requests per request group
@@ -292,6 +295,13 @@ class ClockSampler:
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: wait (bounded) for its first sample
+        t_end = time.perf_counter() + 5.0
+        while time.perf_counter() < t_end and self.proc.poll() is None:
+            if Path(self.path).stat().st_size > 0:
+                break
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):
@@ -491,18 +501,20 @@ def run_ours(args):
             ex()
             second.replay()
 
-    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0.record()
+    step_ms = []
     for _ in range(args.warmup):
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0.record()
         step()
-    w1.record()
-    torch.cuda.synchronize(device)
+        w1.record()
+        torch.cuda.synchronize(device)
+        step_ms.append(w0.elapsed_time(w1))
     assert dsb._lib.read_and_clear_error_flag(device) == 0, "kernel index check tripped"
     # Steps that keep the GPU loaded for ~0.6 s before and ~0.3 s after the
     # timed region, so the clock sampler sees clocks under this load.  The
-    # counts come from the slowest rank's warm-up, so every rank issues the
-    # same collectives.
-    est_ms = torch.tensor([max(w0.elapsed_time(w1) / max(1, args.warmup), 1e-3)], device=device)
+    # counts come from the slowest rank's fastest warm-up step, so every rank
+    # issues the same collectives.
+    est_ms = torch.tensor([max(min(step_ms, default=1.0), 1e-3)], device=device)
     if world > 1:
         dist.all_reduce(est_ms, op=dist.ReduceOp.MAX)
         dist.barrier()
