@@ -79,7 +79,7 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
 template <typename T, int D, int NT>
 constexpr size_t attn_smem_bytes() {
   return sizeof(uint4) * kAttnWarps * AttnStages<D>::value * (D / 8) * 32 +
-         sizeof(float) * 2 * kAttnWarps * NT * 8 + sizeof(T) * kAttnWarps * 16 * NT * 8;
+         sizeof(float) * 2 * kAttnWarps * NT * 8 + sizeof(T) * kAttnWarps * 2 * 16 * NT * 8;
 }
 
 template <typename T, int D>
@@ -229,7 +229,7 @@ draft_attention_kernel(const AttnArgs a) {
   float *s_o = smem;                                    // [warps][GP][D], aliases the ring
   float *s_m = smem + kAttnWarps * NS * VPT * 32 * 4;   // [warps][GP]
   float *s_l = s_m + kAttnWarps * GP;                   // [warps][GP]
-  T *s_p = reinterpret_cast<T *>(s_l + kAttnWarps * GP);  // [warps][16][GP]
+  T *s_p = reinterpret_cast<T *>(s_l + kAttnWarps * GP);  // [warps][hi, lo][16][GP]
   __shared__ int s_last;
 
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
@@ -309,7 +309,7 @@ draft_attention_kernel(const AttnArgs a) {
       l_run[nt][j] = 0.f;
     }
   }
-  T *pw = s_p + warp * 16 * GP;
+  T *pw = s_p + warp * 2 * 16 * GP;  // hi tile; the lo tile follows
 
   // This warp's tiles are ts + (warp + kAttnWarps * k) * 16, k < n_my.  Each
   // is copied with cp.async into ring stage k % NS, NS - 1 tiles ahead of the
@@ -406,13 +406,19 @@ draft_attention_kernel(const AttnArgs a) {
         }
       }
       uint32_t *prow = reinterpret_cast<uint32_t *>(pw);
-      prow[(g * GP + nt * 8 + 2 * t) / 2] = pack2<T>(p[0], p[1]);
-      prow[((g + 8) * GP + nt * 8 + 2 * t) / 2] = pack2<T>(p[2], p[3]);
+      uint32_t *prow_lo = prow + 16 * GP / 2;
+      pack2_split<T>(p[0], p[1], prow[(g * GP + nt * 8 + 2 * t) / 2],
+                     prow_lo[(g * GP + nt * 8 + 2 * t) / 2]);
+      pack2_split<T>(p[2], p[3], prow[((g + 8) * GP + nt * 8 + 2 * t) / 2],
+                     prow_lo[((g + 8) * GP + nt * 8 + 2 * t) / 2]);
     }
     __syncwarp();
-    uint32_t pb[NT][2];
+    uint32_t pb[NT][2], pl[NT][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) ldsm_x2_trans(pb[nt], pw + (lane & 15) * GP + nt * 8);
+    for (int nt = 0; nt < NT; ++nt) {
+      ldsm_x2_trans(pb[nt], pw + (lane & 15) * GP + nt * 8);
+      ldsm_x2_trans(pl[nt], pw + 16 * GP + (lane & 15) * GP + nt * 8);
+    }
     __syncwarp();
 
     // ---- O^T += V^T P^T
@@ -428,7 +434,10 @@ draft_attention_kernel(const AttnArgs a) {
           __byte_perm(word_of(vv[2][wl / 4], wl % 4), word_of(vv[3][wl / 4], wl % 4), sel_lo),
           __byte_perm(word_of(vv[2][wh / 4], wh % 4), word_of(vv[3][wh / 4], wh % 4), sel_hi)};
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) Mma<T>::run(o[nt][i], af, pb[nt]);
+      for (int nt = 0; nt < NT; ++nt) {
+        Mma<T>::run(o[nt][i], af, pb[nt]);
+        Mma<T>::run(o[nt][i], af, pl[nt]);
+      }
     }
   }
 
@@ -492,7 +501,7 @@ template <int D, int NS, int W> struct TmaCfg {
 template <typename T, int D, int NT, int NS, int W>
 constexpr size_t tma_smem_bytes() {
   return 1024 /* alignment slack */ + TmaCfg<D, NS, W>::kRingBytes + TmaCfg<D, NS, W>::kBarBytes +
-         sizeof(float) * 2 * W * NT * 8 + sizeof(T) * W * 16 * NT * 8;
+         sizeof(float) * 2 * W * NT * 8 + sizeof(T) * W * 2 * 16 * NT * 8;
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
@@ -583,7 +592,7 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   uint64_t *bars = reinterpret_cast<uint64_t *>(ring + Cfg::kRingBytes);
   float *s_m = reinterpret_cast<float *>(ring + Cfg::kRingBytes + Cfg::kBarBytes);
   float *s_l = s_m + kTmaWarps * GP;                     // [warps][GP]
-  T *s_p = reinterpret_cast<T *>(s_l + kTmaWarps * GP);  // [warps][16][GP], 16-byte aligned
+  T *s_p = reinterpret_cast<T *>(s_l + kTmaWarps * GP);  // [warps][hi, lo][16][GP], 16-B aligned
   __shared__ int s_last, s_abort;
 
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
@@ -703,7 +712,7 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
       l_run[nt][j] = 0.f;
     }
   }
-  T *pw = s_p + warp * 16 * GP;
+  T *pw = s_p + warp * 2 * 16 * GP;  // hi tile; the lo tile follows
   bool ok = true;
   int issued = min(NS, n_stages);  // stages 0 .. issued-1 have copies in flight or landed
   int first_unwaited = n_stages;   // thread 0: first stage it did not see complete
@@ -778,13 +787,19 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
           l_run[nt][j] += p[j] + p[j + 2];
         }
         uint32_t *prow = reinterpret_cast<uint32_t *>(pw);
-        prow[(g * GP + nt * 8 + 2 * t) / 2] = pack2<T>(p[0], p[1]);
-        prow[((g + 8) * GP + nt * 8 + 2 * t) / 2] = pack2<T>(p[2], p[3]);
+        uint32_t *prow_lo = prow + 16 * GP / 2;
+        pack2_split<T>(p[0], p[1], prow[(g * GP + nt * 8 + 2 * t) / 2],
+                       prow_lo[(g * GP + nt * 8 + 2 * t) / 2]);
+        pack2_split<T>(p[2], p[3], prow[((g + 8) * GP + nt * 8 + 2 * t) / 2],
+                       prow_lo[((g + 8) * GP + nt * 8 + 2 * t) / 2]);
       }
       __syncwarp();
-      uint32_t pb[NT][2];
+      uint32_t pb[NT][2], pl[NT][2];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) ldsm_x2_trans(pb[nt], pw + (lane & 15) * GP + nt * 8);
+      for (int nt = 0; nt < NT; ++nt) {
+        ldsm_x2_trans(pb[nt], pw + (lane & 15) * GP + nt * 8);
+        ldsm_x2_trans(pl[nt], pw + 16 * GP + (lane & 15) * GP + nt * 8);
+      }
       __syncwarp();
       // O^T += V^T P^T, V^T fragments straight from the swizzled tile
 #pragma unroll
@@ -792,7 +807,10 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
         uint32_t vf[4];
         ldsm_x4_t(vf, swz(vb, kBoxBytes, r0 + (lane & 7) + ((lane >> 4) << 3), 16 * i + (((lane >> 3) & 1) << 3)));
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(o[nt][i], vf, pb[nt]);
+        for (int nt = 0; nt < NT; ++nt) {
+          Mma<T>::run(o[nt][i], vf, pb[nt]);
+          Mma<T>::run(o[nt][i], vf, pl[nt]);
+        }
       }
     }
     __syncthreads();  // every warp is done with stage s
@@ -866,7 +884,7 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
     // exchange area (outside the ring, so no rank waits for another's loop
     // before writing); rank 0 merges the slots and stores.
     const uint32_t rank = cluster_rank(), ranks = gridDim.x;
-    float *x_o = reinterpret_cast<float *>(s_p + kTmaWarps * 16 * GP);  // [ranks][GP][D]
+    float *x_o = reinterpret_cast<float *>(s_p + kTmaWarps * 2 * 16 * GP);  // [ranks][GP][D]
     float *x_ml = x_o + (size_t)ranks * GP * D;                        // [ranks][2][GP]
     const uint32_t x_o0 = cluster_map(smem_u32(x_o), 0), x_ml0 = cluster_map(smem_u32(x_ml), 0);
     asm volatile("barrier.cluster.wait.acquire;" ::: "memory");  // every rank is running

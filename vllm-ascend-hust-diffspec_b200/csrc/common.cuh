@@ -151,6 +151,26 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
+// The two floats of a packed 16-bit pair (low half first).
+template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t w);
+template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+}
+
+// Softmax weights for a 16-bit P.V product as two 16-bit terms, hi + lo:
+// hi = round(p), lo = round(p - hi).  Both feed the tensor cores, so the
+// weights carry ~16 mantissa bits instead of 8 (bf16) and the output error
+// stays at the output's own rounding even for sums over thousands of tokens.
+template <typename T>
+__device__ __forceinline__ void pack2_split(float a, float b, uint32_t &hi, uint32_t &lo) {
+  hi = pack2<T>(a, b);
+  const float2 h = unpack2<T>(hi);
+  lo = pack2<T>(a - h.x, b - h.y);
+}
+
 // ldmatrix .x2 .trans of two 8x8 16-bit matrices.
 __device__ __forceinline__ void ldsm_x2_trans(uint32_t (&r)[2], const void *smem_row) {
   uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
