@@ -368,14 +368,14 @@ __global__ void __launch_bounds__(kWarpsRope * 32, 3) rope_rows_kernel(const Rop
 
 // ---------------------------------------------------------------------------
 // Bulk-copy variant (the default for 16-bit caches with head_dim 64/128/256).
-// One CTA owns PT = 1 << pt_shift consecutive local positions of one row.
-// Lane t of warp 0 decodes the source of position p0 + t once and issues two
-// 1-D bulk copies (TMA) of that token's whole K row and V row (all kv heads)
-// into shared memory; all copies complete on one mbarrier.  The block then
-// writes V out unchanged and K rotated: for NeoX with 16-byte halves a thread
-// owns one (position, 8-element pair of vectors) item, loads its cos/sin
-// vectors once and reuses them for every kv head.  No thread touches a byte
-// twice, and the loads need no per-lane address arithmetic.
+// One CTA owns PT = 1 << pt_shift (<= 64) consecutive local positions of one
+// row.  Warp 0 decodes the source of each position once (lane t: positions t
+// and t + 32) and issues 1-D bulk copies (TMA) of the K rows and V rows (all
+// kv heads) into shared memory, one copy per run of consecutive source rows
+// (a selected chunk or the rolling tail is one run), all completing on one
+// mbarrier.  The block then writes V out unchanged and K rotated: for NeoX
+// with 16-byte halves a thread owns one (position, 8-element pair of vectors)
+// item, loads its cos/sin vectors once and reuses them for every kv head.
 constexpr int kBulkThreads = 256;
 
 template <typename T, typename CS, bool GATHER, int DH>
@@ -433,11 +433,11 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncwarp();
-    // kind: 1 = copy the row, 2 = zero row (gather padding / bad block), 0 = skip
-    int kind = 0;
-    const T *rk = nullptr, *rv = nullptr;
-    if (lane < n_tok) {
-      const int64_t p = p0 + lane;
+    // Source row of local position p0 + t; kind: 1 = copy the row, 2 = zero
+    // row (gather padding / bad block), 0 = skip.
+    auto resolve = [&](int t, int64_t &off) -> int {
+      if (t >= n_tok) return 0;
+      const int64_t p = p0 + t;
       if (!GATHER) {
         int64_t abs_pos = 0;
         bool ok = true;
@@ -451,44 +451,60 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
         }
         if (!ok || abs_pos < 0 || abs_pos >= a.max_model_len) {
           flag_error(a.err, ok ? DSB_FLAG_POSITION : DSB_FLAG_PLAN);
-        } else {
-          const int64_t off = (slot * a.max_model_len + abs_pos) * row_elems;
-          rk = static_cast<const T *>(a.src_k) + off;
-          rv = static_cast<const T *>(a.src_v) + off;
-          kind = 1;
+          return 0;
         }
-      } else {
-        const int64_t idx = a.sel[(int64_t)r * a.working_tokens + p];
-        kind = 2;
-        if (idx >= 0) {
-          int64_t lb, in_block;
-          if (a.block_shift >= 0) {
-            lb = idx >> a.block_shift;
-            in_block = idx & ((1LL << a.block_shift) - 1);
-          } else {
-            lb = idx / a.block_size;
-            in_block = idx - lb * a.block_size;
-          }
-          const int64_t pb = (lb < a.bt_cols) ? a.bt[(int64_t)r * a.bt_stride + lb] : -1;
-          if (pb < 0 || pb >= a.num_blocks) {
-            flag_error(a.err, DSB_FLAG_BLOCK);
-          } else {
-            const int64_t off = (pb * a.block_size + in_block) * row_elems;
-            rk = static_cast<const T *>(a.src_k) + off;
-            rv = static_cast<const T *>(a.src_v) + off;
-            kind = 1;
-          }
-        }
+        off = (slot * a.max_model_len + abs_pos) * row_elems;
+        return 1;
       }
+      const int64_t idx = a.sel[(int64_t)r * a.working_tokens + p];
+      if (idx < 0) return 2;
+      int64_t lb, in_block;
+      if (a.block_shift >= 0) {
+        lb = idx >> a.block_shift;
+        in_block = idx & ((1LL << a.block_shift) - 1);
+      } else {
+        lb = idx / a.block_size;
+        in_block = idx - lb * a.block_size;
+      }
+      const int64_t pb = (lb < a.bt_cols) ? a.bt[(int64_t)r * a.bt_stride + lb] : -1;
+      if (pb < 0 || pb >= a.num_blocks) {
+        flag_error(a.err, DSB_FLAG_BLOCK);
+        return 2;
+      }
+      off = (pb * a.block_size + in_block) * row_elems;
+      return 1;
+    };
+    // Tokens lane, lane + 32: consecutive source rows form runs, and each run
+    // is one bulk copy of K and one of V (the rows of a run are contiguous
+    // in the raw cache and in the stage).
+    int kinds[2];
+    int64_t offs[2] = {0, 0};
+    uint32_t n_loads = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      kinds[j] = (32 * j < PT) ? resolve(lane + 32 * j, offs[j]) : 0;
+      n_loads += __popc(__ballot_sync(0xffffffffu, kinds[j] == 1));
     }
-    const uint32_t loads = __ballot_sync(0xffffffffu, kind == 1);
-    if (lane == 0) mbar_expect_tx(bar_u32, (uint32_t)__popc(loads) * 2u * row_bytes);
+    if (lane == 0) mbar_expect_tx(bar_u32, n_loads * 2u * row_bytes);
     __syncwarp();
-    if (kind == 1) {
-      bulk_load(smem_u32(sk + (size_t)lane * row_bytes), rk, row_bytes, bar_u32);
-      bulk_load(smem_u32(sv + (size_t)lane * row_bytes), rv, row_bytes, bar_u32);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int t = lane + 32 * j;
+      const int prev_kind = __shfl_up_sync(0xffffffffu, kinds[j], 1);
+      const int64_t prev_off = __shfl_up_sync(0xffffffffu, offs[j], 1);
+      const bool cont = lane > 0 && kinds[j] == 1 && prev_kind == 1 && offs[j] == prev_off + row_elems;
+      const uint32_t breaks = __ballot_sync(0xffffffffu, !cont);
+      if (kinds[j] == 1 && !cont) {
+        const uint32_t later = breaks & ~((2u << lane) - 1u);  // 2u << 31 wraps to 0: no later break
+        const int end = later ? __ffs(later) - 1 : 32;
+        const uint32_t bytes = (uint32_t)(end - lane) * row_bytes;
+        bulk_load(smem_u32(sk + (size_t)t * row_bytes), static_cast<const T *>(a.src_k) + offs[j],
+                  bytes, bar_u32);
+        bulk_load(smem_u32(sv + (size_t)t * row_bytes), static_cast<const T *>(a.src_v) + offs[j],
+                  bytes, bar_u32);
+      }
+      if (t < PT) s_kind[t] = kinds[j];
     }
-    if (lane < PT) s_kind[lane] = kind;
   }
   __syncthreads();
   if (!mbar_wait(bar_u32, 0)) {
@@ -639,7 +655,7 @@ int launch_rope_bulk(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
     if (!aligned16(a.src_k) || !aligned16(a.src_v) || !aligned16(a.dst_k) || !aligned16(a.dst_v))
       return -1;
     const int64_t row_bytes = (int64_t)a.heads * a.head_dim * 2;
-    int pt = 32;
+    int pt = 64;  // two positions per lane of the issuing warp at most
     while (pt > 1 && 2 * pt * row_bytes > DSB_BULK_STAGE_BYTES) pt >>= 1;
     if (2 * pt * row_bytes > DSB_BULK_STAGE_BYTES) return -1;
     a.pt_shift = log2_exact(pt);
