@@ -487,19 +487,32 @@ def run_ours(args):
                                gathered=gathered if exchange is not None else None)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
+    graphs = []
+    res_mode = "one CUDA graph per bench step"
     if exchange is None:
-        period = Graph(torch, launches, device)
-        step = period.replay
-    else:  # the NCCL exchange runs eagerly between two captured halves
+        graphs.append(Graph(torch, launches, device))
+        step = graphs[0].replay
+    else:
+        # The NCCL all-gather is captured inside the period's graph (after one
+        # eager call has set up the communicator); if this build of PyTorch /
+        # NCCL refuses, it runs eagerly between two captured halves.
         cut = [k for k, _ in launches].index("exchange")
-        first = Graph(torch, launches[:cut], device)
-        second = Graph(torch, launches[cut + 1:], device)
         ex = launches[cut][1]
+        ex()
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        try:
+            graphs.append(Graph(torch, launches, device))
+            step = graphs[0].replay
+            res_mode = "one CUDA graph per bench step, NCCL exchange captured in it"
+        except Exception:  # noqa: BLE001 - fall back to the split graph
+            graphs = [Graph(torch, launches[:cut], device), Graph(torch, launches[cut + 1:], device)]
 
-        def step():
-            first.replay()
-            ex()
-            second.replay()
+            def step():
+                graphs[0].replay()
+                ex()
+                graphs[1].replay()
+            res_mode = "two CUDA graphs per bench step, NCCL exchange eager between them"
 
     step_ms = []
     for _ in range(args.warmup):
@@ -544,7 +557,12 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     value = STEPS_PER_PERIOD * (B_GROUP * world // B_GROUP) / (ms / 1e3)
+    # graphs holding NCCL work must be released before the process group
+    del step
+    graphs.clear()
+    torch.cuda.synchronize(device)
     result = dict(ms=ms, value=value, clocks=clocks.summary(), w=w, launches=launches, rows=rows,
+                  graph_mode=res_mode,
                   hk_local=hk_local, world=world, rank=rank, device=device, torch=torch, dsb=dsb,
                   dist=dist if world > 1 else None, flush=flush, group=group, hg=hg)
     return result
@@ -687,7 +705,7 @@ def emit_ours(args):
                     l2="inputs larger than L2 (target K 671 MB, raw KV 1.3 GB per group)",
                     bytes_per_step=int(b["total"]),
                     hbm_frac_whole_step=round(b["total"] / (period_ms / 1e3) / 1e9 / peak, 4),
-                    graph="CUDA graph per bench step"),
+                    graph=res["graph_mode"]),
         roofline=roofline, cpu_baseline=cpu, e2e=e2e,
         gpu_launches=sum(1 for k, _ in res["launches"] if k != "exchange") * args.steps,
         clocks=res["clocks"])
