@@ -123,25 +123,60 @@ def chunk_attention_scores(
 class _Staging:
     """Device buffer for small per-call int32 vectors from host lists.
 
-    Each upload goes through a fresh pinned tensor from PyTorch's caching
-    host allocator, which keeps the block alive until its asynchronous copy
-    has run, so no host synchronisation is needed.
+    Uploads go through a ring of preallocated pinned host buffers; each slot
+    records an event after its asynchronous copy and is reused only once that
+    event has completed, so no host synchronisation happens in steady state
+    and no pinned memory is allocated per call.
     """
 
+    SLOTS = 8
+
     def __init__(self, device: torch.device, capacity: int):
+        self.device = device
         self.dev = torch.empty(capacity, dtype=torch.int32, device=device)
+        self._alloc_host(capacity)
+
+    def _alloc_host(self, capacity: int) -> None:
+        self.host = [torch.empty(capacity, dtype=torch.int32).pin_memory() for _ in range(self.SLOTS)]
+        self.events: list[torch.cuda.Event | None] = [None] * self.SLOTS
+        self.next = 0
 
     def upload(self, *lists: list[int]) -> list[torch.Tensor]:
         flat = [v for x in lists for v in x]
-        if len(flat) > self.dev.numel():
-            self.dev = torch.empty(2 * len(flat), dtype=torch.int32, device=self.dev.device)
-        host = torch.tensor(flat, dtype=torch.int32).pin_memory()
-        self.dev[: len(flat)].copy_(host, non_blocking=True)
+        n = len(flat)
+        if n > self.dev.numel():
+            for ev in self.events:
+                if ev is not None:
+                    ev.synchronize()
+            self.dev = torch.empty(2 * n, dtype=torch.int32, device=self.device)
+            self._alloc_host(2 * n)
+        slot = self.next
+        self.next = (slot + 1) % self.SLOTS
+        ev = self.events[slot]
+        if ev is not None:
+            ev.synchronize()  # the copy that last used this slot has run
+        host = self.host[slot]
+        if n:
+            host[:n] = torch.tensor(flat, dtype=torch.int32)
+        # each upload gets its own device region of the staging buffer too:
+        # earlier kernels may still read the previous region
+        dev = self._dev_region(slot, n)
+        dev.copy_(host[:n], non_blocking=True)
+        if ev is None:
+            ev = torch.cuda.Event()
+            self.events[slot] = ev
+        ev.record(torch.cuda.current_stream(self.device))
         views, off = [], 0
         for x in lists:
-            views.append(self.dev[off:off + len(x)])
+            views.append(dev[off:off + len(x)])
             off += len(x)
         return views
+
+    def _dev_region(self, slot: int, n: int) -> torch.Tensor:
+        per = self.dev.numel() // self.SLOTS
+        if n <= per:
+            return self.dev[slot * per: slot * per + n]
+        return self.dev[:n]
 
 
 class DiffSpecDraftCache:
@@ -214,7 +249,7 @@ class DiffSpecDraftCache:
             dtype=torch.int64, device=self.device,
         )
         self._history_lens = torch.zeros(max_num_reqs, dtype=torch.int32, device=self.device)
-        self._staging = _Staging(self.device, 4 * max_num_reqs + 16)
+        self._staging = _Staging(self.device, _Staging.SLOTS * (4 * max_num_reqs + 16))
         self._attn_workspace = AttentionWorkspace(self.device)
         self.metrics = DiffSpecRuntimeMetrics()
 
