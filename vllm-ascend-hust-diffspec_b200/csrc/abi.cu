@@ -51,9 +51,9 @@ int ensure_smem(const void *kernel, size_t bytes) {
   return DSB_OK;
 }
 
-bool cluster_fits(const void *kernel, int cluster_x, int threads, size_t smem) {
+int max_active_clusters(const void *kernel, int cluster_x, int threads, size_t smem) {
   static std::mutex mu;
-  static std::map<std::tuple<int, const void *, int, size_t>, bool> known;
+  static std::map<std::tuple<int, const void *, int, size_t>, int> known;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   std::lock_guard<std::mutex> lock(mu);
@@ -72,10 +72,12 @@ bool cluster_fits(const void *kernel, int cluster_x, int threads, size_t smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  const bool ok = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && n > 0;
-  if (!ok) (void)cudaGetLastError();  // a refused query is an answer, not an error
-  known[key] = ok;
-  return ok;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();  // a refused query is an answer, not an error
+    n = 0;
+  }
+  known[key] = n;
+  return n;
 }
 
 }  // namespace dsb

@@ -495,7 +495,7 @@ template <int D, int NS, int W> struct TmaCfg {
   static constexpr int kBoxes = D / 64;                       // boxes per K (or V) row
   static constexpr int kStageBytes = 2 * kBoxes * kBoxBytes;  // K + V
   static constexpr int kRingBytes = NS * kStageBytes;
-  static constexpr int kBarBytes = (8 * NS + 15) / 16 * 16;  // mbarriers, padded to 16 bytes
+  static constexpr int kBarBytes = (16 * NS + 15) / 16 * 16;  // full + empty mbarriers, padded
 };
 
 template <typename T, int D, int NT, int NS, int W>
@@ -665,11 +665,21 @@ __device__ __forceinline__ void finish_split(const AttnArgs &a, Fold &fold, T *o
   if (threadIdx.x == 0) a.counters[row * a.Hk + kvh] = 0;
 }
 
+// Warp roles: kTmaWarps consumer warps each own 16 tokens of every stage; the
+// last warp (the producer) issues every copy.  Consumers release a stage on
+// its "empty" mbarrier instead of a CTA barrier, so they never wait for one
+// another inside the loop: warps sharing a scheduler drift into different
+// phases (one in the products while the other is in the softmax), which keeps
+// the mma pipe busy.  The producer refills a slot as soon as every consumer
+// has released it.
 template <typename T, int D, int NT, int NS, int kTmaWarps, bool CL>
-__global__ void __launch_bounds__(kTmaWarps * 32)
+__global__ void __launch_bounds__((kTmaWarps + 1) * 32)
 draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
-  if (threadIdx.x == 0) {  // descriptor fetch overlaps the wait for the previous kernel
+  constexpr int kProducer = kTmaWarps;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool producer = warp == kProducer;
+  if (producer && lane == 0) {  // descriptor fetch overlaps the wait for the previous kernel
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
   }
@@ -684,21 +694,23 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *ring = smem;  // [NS][K boxes | V boxes], 1024-byte aligned
-  uint64_t *bars = reinterpret_cast<uint64_t *>(ring + Cfg::kRingBytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(ring + Cfg::kRingBytes);  // full[NS], empty[NS]
   float *s_m = reinterpret_cast<float *>(ring + Cfg::kRingBytes + Cfg::kBarBytes);
   float *s_l = s_m + kTmaWarps * GP;                     // [warps][GP]
   T *s_p = reinterpret_cast<T *>(s_l + kTmaWarps * GP);  // [warps][hi, lo][16][GP], 16-B aligned
-  __shared__ int s_last, s_abort;
+  __shared__ int s_last, s_abort, s_first_unwaited;
 
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int group = a.Hq / a.Hk;
   T *out = static_cast<T *>(a.out);
   const uint32_t ring_u32 = smem_u32(ring);
-  const uint32_t bar_u32 = smem_u32(bars);
-  if (threadIdx.x == 0) {  // independent of any global data: first
-    for (int s = 0; s < NS; ++s) mbar_init(bar_u32 + 8 * s);
+  const uint32_t full_u32 = smem_u32(bars), empty_u32 = full_u32 + 8 * NS;
+  if (producer && lane == 0) {  // independent of any global data: first
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(full_u32 + 8 * s);                    // one expect_tx arrival + the bytes
+      mbar_init_count(empty_u32 + 8 * s, kTmaWarps);  // one arrival per consumer warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
   }
@@ -717,15 +729,15 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
         static_cast<const T *>(a.query) + ((int64_t)row * a.Hq + kvh * group + min(h, group - 1)) * D);
 #pragma unroll
     for (int s = 0; s < KS; ++s) {
-      qf[nt][s][0] = (h < group) ? qp[8 * s + t] : 0u;
-      qf[nt][s][1] = (h < group) ? qp[8 * s + 4 + t] : 0u;
+      qf[nt][s][0] = (!producer && h < group) ? qp[8 * s + t] : 0u;
+      qf[nt][s][1] = (!producer && h < group) ? qp[8 * s + 4 + t] : 0u;
     }
   }
-  // warp 0 also fetches the step's new K / V rows (written below if this
-  // split owns the new position)
+  // the producer also fetches the step's new K / V rows (written below if
+  // this split owns the new position)
   constexpr int VE = 16 / sizeof(T), kNewVecs = 2 * (D / VE), kNewPerLane = (kNewVecs + 31) / 32;
   uint4 new_kv[kNewPerLane];
-  if (warp == 0) {
+  if (producer) {
 #pragma unroll
     for (int j = 0; j < kNewPerLane; ++j) {
       const int i = lane + 32 * j;
@@ -755,19 +767,20 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   const int64_t head_row0 = ((int64_t)slot * a.Hk + kvh) * a.W;  // tensor-map row of token 0
   const int n_stages = (te - ts + kStageTok - 1) / kStageTok;
 
-  auto issue = [&](int k) {  // thread 0 only
+  auto issue = [&](int k) {  // producer lane 0 only
     const int s = k % NS;
     const uint32_t kb = ring_u32 + s * Cfg::kStageBytes;
     const uint32_t vb = kb + Cfg::kBoxes * kBoxBytes;
     const int y = (int)(head_row0 + ts + k * kStageTok);
-    mbar_expect_tx(bar_u32 + 8 * s, Cfg::kStageBytes);
+    mbar_expect_tx(full_u32 + 8 * s, Cfg::kStageBytes);
 #pragma unroll
     for (int b = 0; b < Cfg::kBoxes; ++b) {
-      tma_load_2d(kb + b * kBoxBytes, &tmk, 64 * b, y, bar_u32 + 8 * s);
-      tma_load_2d(vb + b * kBoxBytes, &tmv, 64 * b, y, bar_u32 + 8 * s);
+      tma_load_2d(kb + b * kBoxBytes, &tmk, 64 * b, y, full_u32 + 8 * s);
+      tma_load_2d(vb + b * kBoxBytes, &tmv, 64 * b, y, full_u32 + 8 * s);
     }
   };
-  if (warp == 0) {
+  int issued = 0;  // producer lane 0: stages 0 .. issued-1 have copies in flight or landed
+  if (producer) {
     // Stages before the one holding the new position are issued at once; the
     // owner split then stores the new token (each lane fences its stores for
     // the async proxy) before the stage that reads it back is issued.
@@ -788,10 +801,13 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
       asm volatile("fence.proxy.async.global;" ::: "memory");
       __syncwarp();
     }
-    if (lane == 0)
+    if (lane == 0) {
       for (int k = min(n_first, k_pos); k < n_first; ++k) issue(k);
+      s_first_unwaited = n_stages;
+    }
+    issued = n_first;
   }
-  __syncthreads();  // barrier initialisation and s_abort visible to every warp
+  __syncthreads();  // barrier initialisation, s_abort and s_first_unwaited visible to every warp
 
   float o[NT][NM][4];
   float m_run[NT][2], l_run[NT][2];
@@ -807,146 +823,173 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
       l_run[nt][j] = 0.f;
     }
   }
-  T *pw = s_p + warp * 2 * 16 * GP;  // hi tile; the lo tile follows
   bool ok = true;
-  int issued = min(NS, n_stages);  // stages 0 .. issued-1 have copies in flight or landed
-  int first_unwaited = n_stages;   // thread 0: first stage it did not see complete
-
-  for (int k = 0; k < n_stages; ++k) {
-    const int s = k % NS;
-    // after a timed-out wait no further stage is issued: skip the waits too.
-    // The vote keeps the warp converged for the mma/ldmatrix that follow.
-    const bool got = __all_sync(0xffffffffu, !s_abort && mbar_wait(bar_u32 + 8 * s, (k / NS) & 1));
-    if (!got) {
-      if (threadIdx.x == 0 && ok) first_unwaited = k;
-      ok = false;
-      s_abort = 1;
-    }
-    const int base = ts + k * kStageTok + warp * 16;  // this warp's first token
-    if (ok && base < te) {
-      const uint32_t kb = ring_u32 + s * Cfg::kStageBytes;
-      const uint32_t vb = kb + Cfg::kBoxes * kBoxBytes;
-      const int r0 = warp * 16;
-      if (base + 16 > te) {  // zero V rows past the split so 0 * stale data stays 0
-        uint8_t *vgen = ring + s * Cfg::kStageBytes + Cfg::kBoxes * kBoxBytes;
-        for (int i = lane; i < 16 * (D / 8); i += 32) {
-          const int r = i / (D / 8), col = (i % (D / 8)) * 8;
-          if (base + r >= te)
-            *reinterpret_cast<uint4 *>(vgen + (swz(0, kBoxBytes, r0 + r, col))) = make_uint4(0, 0, 0, 0);
+  if (!producer) {
+    T *pw = s_p + warp * 2 * 16 * GP;  // hi tile; the lo tile follows
+    for (int k = 0; k < n_stages; ++k) {
+      const int s = k % NS;
+      // After a timed-out wait (here or in another warp) no stage is waited
+      // for any more; the vote keeps the warp converged for the mma/ldmatrix.
+      const bool got =
+          __all_sync(0xffffffffu, ok && !s_abort && mbar_wait(full_u32 + 8 * s, (k / NS) & 1));
+      if (!got) {
+        if (ok && lane == 0) {
+          atomicMin(&s_first_unwaited, k);
+          s_abort = 1;
         }
-        __syncwarp();
+        ok = false;
       }
-      // S^T = K Q^T with two accumulators per n-tile to halve the mma chain
-      float cacc[NT][2][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) cacc[nt][h][c] = 0.f;
-#pragma unroll
-      for (int s2 = 0; s2 < KS; ++s2) {
-        uint32_t af[4];
-        ldsm_x4(af, swz(kb, kBoxBytes, r0 + (lane & 7) + (((lane >> 3) & 1) << 3), 16 * s2 + ((lane >> 4) << 3)));
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(cacc[nt][s2 & 1], af, qf[nt][s2]);
-      }
-      const bool va = base + g < te, vb_ok = base + g + 8 < te;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        float x[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const bool valid = (c < 2) ? va : vb_ok;
-          x[c] = valid ? (cacc[nt][0][c] + cacc[nt][1][c]) * a.scale_log2 : -INFINITY;
-        }
-        float p[4];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          float mx = fmaxf(x[j], x[j + 2]);
-#pragma unroll
-          for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-          const float m_old = m_run[nt][j];
-          if (mx > m_old + kLazyRescale) {  // rescale only when the max grew a lot
-            const float alpha = (m_old == -INFINITY) ? 0.f : exp2f(m_old - mx);
-            l_run[nt][j] *= alpha;
-#pragma unroll
-            for (int i = 0; i < NM; ++i) {
-              o[nt][i][j] *= alpha;
-              o[nt][i][j + 2] *= alpha;
-            }
-            m_run[nt][j] = mx;
+      const int base = ts + k * kStageTok + warp * 16;  // this warp's first token
+      if (ok && base < te) {
+        const uint32_t kb = ring_u32 + s * Cfg::kStageBytes;
+        const uint32_t vb = kb + Cfg::kBoxes * kBoxBytes;
+        const int r0 = warp * 16;
+        if (base + 16 > te) {  // zero V rows past the split so 0 * stale data stays 0
+          uint8_t *vgen = ring + s * Cfg::kStageBytes + Cfg::kBoxes * kBoxBytes;
+          for (int i = lane; i < 16 * (D / 8); i += 32) {
+            const int r = i / (D / 8), col = (i % (D / 8)) * 8;
+            if (base + r >= te)
+              *reinterpret_cast<uint4 *>(vgen + (swz(0, kBoxBytes, r0 + r, col))) = make_uint4(0, 0, 0, 0);
           }
-          p[j] = exp2f(x[j] - m_run[nt][j]);
-          p[j + 2] = exp2f(x[j + 2] - m_run[nt][j]);
-          l_run[nt][j] += p[j] + p[j + 2];
+          __syncwarp();
         }
-        uint32_t *prow = reinterpret_cast<uint32_t *>(pw);
-        uint32_t *prow_lo = prow + 16 * GP / 2;
-        pack2_split<T>(p[0], p[1], prow[(g * GP + nt * 8 + 2 * t) / 2],
-                       prow_lo[(g * GP + nt * 8 + 2 * t) / 2]);
-        pack2_split<T>(p[2], p[3], prow[((g + 8) * GP + nt * 8 + 2 * t) / 2],
-                       prow_lo[((g + 8) * GP + nt * 8 + 2 * t) / 2]);
-      }
-      __syncwarp();
-      uint32_t pb[NT][2], pl[NT][2];
+        // S^T = K Q^T with two accumulators per n-tile to halve the mma chain
+        float cacc[NT][2][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        ldsm_x2_trans(pb[nt], pw + (lane & 15) * GP + nt * 8);
-        ldsm_x2_trans(pl[nt], pw + 16 * GP + (lane & 15) * GP + nt * 8);
-      }
-      __syncwarp();
-      // O^T += V^T P^T, V^T fragments straight from the swizzled tile
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int i = 0; i < NM; ++i) {
-        uint32_t vf[4];
-        ldsm_x4_t(vf, swz(vb, kBoxBytes, r0 + (lane & 7) + ((lane >> 4) << 3), 16 * i + (((lane >> 3) & 1) << 3)));
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) cacc[nt][h][c] = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < KS; ++s2) {
+          uint32_t af[4];
+          ldsm_x4(af, swz(kb, kBoxBytes, r0 + (lane & 7) + (((lane >> 3) & 1) << 3), 16 * s2 + ((lane >> 4) << 3)));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Mma<T>::run(cacc[nt][s2 & 1], af, qf[nt][s2]);
+        }
+        const bool va = base + g < te, vb_ok = base + g + 8 < te;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          Mma<T>::run(o[nt][i], vf, pb[nt]);
-          Mma<T>::run(o[nt][i], vf, pl[nt]);
+          float x[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const bool valid = (c < 2) ? va : vb_ok;
+            x[c] = valid ? (cacc[nt][0][c] + cacc[nt][1][c]) * a.scale_log2 : -INFINITY;
+          }
+          // Lazy rescale: the running max moves only when some score exceeds
+          // it by more than 2^8.  One vote finds out whether any head of the
+          // warp's tile does; only then are the head maxima reduced.
+          const bool grow = fmaxf(x[0], x[2]) > m_run[nt][0] + kLazyRescale ||
+                            fmaxf(x[1], x[3]) > m_run[nt][1] + kLazyRescale;
+          if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              float mx = fmaxf(x[j], x[j + 2]);
+#pragma unroll
+              for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+              const float m_old = m_run[nt][j];
+              if (mx > m_old + kLazyRescale) {
+                const float alpha = (m_old == -INFINITY) ? 0.f : exp2f(m_old - mx);
+                l_run[nt][j] *= alpha;
+#pragma unroll
+                for (int i = 0; i < NM; ++i) {
+                  o[nt][i][j] *= alpha;
+                  o[nt][i][j + 2] *= alpha;
+                }
+                m_run[nt][j] = mx;
+              }
+            }
+          }
+          float p[4];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            p[j] = exp2f(x[j] - m_run[nt][j]);
+            p[j + 2] = exp2f(x[j + 2] - m_run[nt][j]);
+            l_run[nt][j] += p[j] + p[j + 2];
+          }
+          uint32_t *prow = reinterpret_cast<uint32_t *>(pw);
+          uint32_t *prow_lo = prow + 16 * GP / 2;
+          pack2_split<T>(p[0], p[1], prow[(g * GP + nt * 8 + 2 * t) / 2],
+                         prow_lo[(g * GP + nt * 8 + 2 * t) / 2]);
+          pack2_split<T>(p[2], p[3], prow[((g + 8) * GP + nt * 8 + 2 * t) / 2],
+                         prow_lo[((g + 8) * GP + nt * 8 + 2 * t) / 2]);
+        }
+        __syncwarp();
+        uint32_t pb[NT][2], pl[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          ldsm_x2_trans(pb[nt], pw + (lane & 15) * GP + nt * 8);
+          ldsm_x2_trans(pl[nt], pw + 16 * GP + (lane & 15) * GP + nt * 8);
+        }
+        __syncwarp();
+        // O^T += V^T P^T, V^T fragments straight from the swizzled tile
+#pragma unroll
+        for (int i = 0; i < NM; ++i) {
+          uint32_t vf[4];
+          ldsm_x4_t(vf, swz(vb, kBoxBytes, r0 + (lane & 7) + ((lane >> 4) << 3), 16 * i + (((lane >> 3) & 1) << 3)));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            Mma<T>::run(o[nt][i], vf, pb[nt]);
+            Mma<T>::run(o[nt][i], vf, pl[nt]);
+          }
         }
       }
+      __syncwarp();  // every lane's reads of slot s are done
+      if (lane == 0) mbar_arrive(empty_u32 + 8 * s);
     }
-    __syncthreads();  // every warp is done with stage s
-    if (threadIdx.x == 0 && !s_abort && k + NS < n_stages) {
+  } else if (lane == 0) {
+    // Refill each slot once every consumer warp has released it; stop at the
+    // first sign of an abort (a consumer's timed-out wait is published before
+    // its release of the same stage, so it is seen here).
+    for (int k = issued; k < n_stages; ++k) {
+      const int s = k % NS;
+      if (!mbar_wait(empty_u32 + 8 * s, ((k / NS) - 1) & 1)) {
+        ok = false;
+        s_abort = 1;
+        break;
+      }
+      if (s_abort) break;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(k + NS);
+      issue(k);
       ++issued;
     }
   }
+  __syncthreads();  // every consumer is done with the ring
   if (!ok && lane == 0) flag_error(a.err, DSB_FLAG_TIMEOUT);
-  if (s_abort) {  // CTA-uniform after the loop's last barrier
-    // Let every issued copy land (bounded again) before the ring is reused
-    // for the O staging below or released with the CTA.
-    if (threadIdx.x == 0)
-      for (int k = first_unwaited; k < issued; ++k) mbar_wait(bar_u32 + 8 * (k % NS), (k / NS) & 1);
+  if (s_abort) {  // CTA-uniform after the barrier
+    // Let every issued copy that no consumer saw land (bounded again) before
+    // the ring is reused for the O staging below or released with the CTA.
+    if (producer && lane == 0)
+      for (int k = s_first_unwaited; k < issued; ++k) mbar_wait(full_u32 + 8 * (k % NS), (k / NS) & 1);
     __syncthreads();
   }
 
   // ---- combine the warps of this CTA (the ring is idle from here on)
   using Epi = TmaEpi<D, GP, kTmaWarps>;
   float *e_o = reinterpret_cast<float *>(ring) + Epi::kO;  // [warps][GP][DP], unscaled
+  if (!producer) {
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float l = l_run[nt][j];
+      for (int j = 0; j < 2; ++j) {
+        float l = l_run[nt][j];
 #pragma unroll
-      for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-      if (g == 0) {
-        s_m[warp * GP + nt * 8 + 2 * t + j] = m_run[nt][j];
-        s_l[warp * GP + nt * 8 + 2 * t + j] = l;
+        for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        if (g == 0) {
+          s_m[warp * GP + nt * 8 + 2 * t + j] = m_run[nt][j];
+          s_l[warp * GP + nt * 8 + 2 * t + j] = l;
+        }
       }
+#pragma unroll
+      for (int i = 0; i < NM; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int h = nt * 8 + 2 * t + (c & 1);
+          const int d = 16 * i + g + ((c >= 2) ? 8 : 0);
+          e_o[(warp * GP + h) * Epi::DP + d] = o[nt][i][c];
+        }
     }
-#pragma unroll
-    for (int i = 0; i < NM; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int h = nt * 8 + 2 * t + (c & 1);
-        const int d = 16 * i + g + ((c >= 2) ? 8 : 0);
-        e_o[(warp * GP + h) * Epi::DP + d] = o[nt][i][c];
-      }
   }
   __syncthreads();
   // Item `it` (head h, dims d..d+3): fold the warps with weights
@@ -1117,11 +1160,13 @@ draft_attention_umma_kernel(const __grid_constant__ CUtensorMap tmk,
       *reinterpret_cast<uint4 *>(qt + (c / 8) * 2048 + h * 128 + (((c & 7) ^ (h & 7)) << 4)) = v;
     }
   }
-  if (GPF < GP)  // P^T rows of the padding heads stay zero for the whole kernel
-    for (int i = tid; i < 4 * 2 * (GP - GPF) * 8; i += kUmmaThreads) {
-      const int c = i % 8, r = GPF + (i / 8) % (GP - GPF), tile = i / (8 * (GP - GPF));  // tile: 8 boxes
+  if constexpr (GPF < GP) {  // P^T rows of the padding heads stay zero for the whole kernel
+    constexpr int kPad = GPF < GP ? GP - GPF : 1;
+    for (int i = tid; i < 4 * 2 * kPad * 8; i += kUmmaThreads) {
+      const int c = i % 8, r = GPF + (i / 8) % kPad, tile = i / (8 * kPad);  // tile: 8 boxes
       *reinterpret_cast<uint4 *>(pt + tile * 2048 + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
     }
+  }
   constexpr int VE = 16 / sizeof(T), kNewVecs = 2 * (D / VE), kNewPerLane = (kNewVecs + 31) / 32;
   uint4 new_kv[kNewPerLane];
   if (warp == 0) {
@@ -1479,22 +1524,26 @@ int launch_tma(const AttnArgs &a, int splits, cudaStream_t st) {
   static_assert(Epi::ring_bytes() <= TmaCfg<D, NS, W>::kRingBytes,
                 "the epilogue staging must fit in the ring");
   const dim3 grid(splits, a.Hk, a.out_rows);
+  const dim3 block((W + 1) * 32);  // W consumer warps + the producer warp
   // 2..8 splits: merge through distributed shared memory inside a cluster of
-  // the (row, kv head)'s splits; otherwise (or if such a cluster cannot be
-  // scheduled) through global partials and an atomic ticket.
+  // the (row, kv head)'s splits; otherwise through global partials and an
+  // atomic ticket.  The ticket merge is also taken when the clusters would
+  // need a second wave while the plain grid fits in one (one CTA per SM).
   constexpr size_t kMaxSmem = 227 * 1024;
   const size_t smem_cl = smem + Epi::exchange_bytes(splits);
   if (splits >= 2 && splits <= 8 && smem_cl <= kMaxSmem && !legacy_merge_requested()) {
     auto kern = draft_attention_tma_kernel<T, D, NT, NS, W, true>;
     if (int e = ensure_smem((const void *)kern, smem_cl); e != DSB_OK) return e;
-    if (cluster_fits((const void *)kern, splits, W * 32, smem_cl)) {
-      launch_kernel_cluster(kern, grid, dim3(W * 32), smem_cl, st, splits, tmk, tmv, a);
+    const int64_t clusters = (int64_t)a.Hk * a.out_rows;
+    const int fit = max_active_clusters((const void *)kern, splits, block.x, smem_cl);
+    if (fit > 0 && (clusters <= fit || clusters * splits > sm_count())) {
+      launch_kernel_cluster(kern, grid, block, smem_cl, st, splits, tmk, tmv, a);
       return check_launch("draft_attention_tma_kernel (cluster merge)");
     }
   }
   auto kern = draft_attention_tma_kernel<T, D, NT, NS, W, false>;
   if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
-  launch_kernel(kern, grid, dim3(W * 32), smem, st, tmk, tmv, a);
+  launch_kernel(kern, grid, block, smem, st, tmk, tmv, a);
   return check_launch("draft_attention_tma_kernel");
 }
 
@@ -1525,7 +1574,7 @@ int launch_umma(const AttnArgs &a, int splits, cudaStream_t st) {
   if (splits >= 2 && splits <= 8 && smem_cl <= kMaxSmem && !legacy_merge_requested()) {
     auto kern = draft_attention_umma_kernel<T, NS, GPF, true>;
     if (int e = ensure_smem((const void *)kern, smem_cl); e != DSB_OK) return e;
-    if (cluster_fits((const void *)kern, splits, kUmmaThreads, smem_cl)) {
+    if (max_active_clusters((const void *)kern, splits, kUmmaThreads, smem_cl) > 0) {
       launch_kernel_cluster(kern, grid, dim3(kUmmaThreads), smem_cl, st, splits, tmk, tmv, a);
       return check_launch("draft_attention_umma_kernel (cluster merge)");
     }

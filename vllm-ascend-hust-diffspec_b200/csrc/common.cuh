@@ -69,9 +69,10 @@ void launch_kernel_cluster(void (*kernel)(Params...), dim3 grid, dim3 block, siz
   (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Whether at least one cluster of `cluster_x` CTAs with this shared memory
-// fits on the device (cached per device, kernel, cluster size and smem).
-bool cluster_fits(const void *kernel, int cluster_x, int threads, size_t smem);
+// How many clusters of `cluster_x` CTAs with this block size and shared
+// memory can be resident on the device at once (0 if none can; cached per
+// device, kernel, cluster size and smem).
+int max_active_clusters(const void *kernel, int cluster_x, int threads, size_t smem);
 
 // ------------------------------------------------------------ element types
 template <typename T> struct Elem;
@@ -196,6 +197,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 }
 __device__ __forceinline__ void mbar_init(uint32_t bar) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+// An mbarrier whose phase completes after `count` plain arrivals.
+__device__ __forceinline__ void mbar_init_count(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+// One arrival (release semantics: this thread's earlier shared-memory reads
+// and writes are ordered before the phase completes).
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
