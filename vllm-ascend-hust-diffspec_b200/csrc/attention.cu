@@ -22,6 +22,7 @@
 //  * the online softmax runs in base 2 in fp32; splits publish (m, l, O)
 //    partials and the last split of each (row, kv head) to finish merges them
 //    (an atomic ticket, no spin wait).
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 #include <type_traits>
@@ -474,23 +475,30 @@ draft_attention_kernel(const AttnArgs a) {
 
 
 // ===========================================================================
-// TMA-fed variant (the default on sm_100a): K/V stages of 16 * W tokens (W
-// warps) are copied by cp.async.bulk.tensor as 64-column boxes with 128-byte
-// swizzle into a CTA-wide ring of NS stages, completion tracked by mbarriers;
-// one thread issues all copies.  Fragments come from the swizzled tiles with
-// ldmatrix (conflict-free; V^T directly via ldmatrix.trans).  Each warp owns
-// 16 tokens of every stage.  The online softmax rescales O only when a
-// running max grows by more than 2^8, so steady-state tiles skip the rescale.
-// All mbarrier waits are bounded: a wait that runs out sets DSB_FLAG_TIMEOUT,
-// no further stage is issued, and thread 0 waits (bounded again) for the
-// copies already issued before the ring is reused or the CTA exits.
+// TMA-fed variant (the default on sm_100a): K/V stages of 8 * W tokens (W
+// consumer warps in two groups) are copied by cp.async.bulk.tensor as
+// 64-column boxes with 128-byte swizzle into a CTA-wide ring of NS stages,
+// completion tracked by mbarriers; a producer warp issues all copies.
+// Fragments come from the swizzled tiles with ldmatrix (conflict-free; V^T
+// directly via ldmatrix.trans).  The two warp groups take alternate stages and
+// each warp owns 16 tokens of its group's stages, so the two warps sharing a
+// scheduler work on different stages.  The online softmax rescales O only
+// when a running max grows by more than 2^8, so steady-state tiles skip the
+// rescale.  All mbarrier waits are bounded: a wait that runs out sets
+// DSB_FLAG_TIMEOUT, no further stage is issued, and the producer waits
+// (bounded again) for the copies already issued before the ring is reused or
+// the CTA exits.
 // ===========================================================================
 constexpr float kLazyRescale = 8.0f;  // log2 headroom before O is rescaled
 
-// W warps each own 16 tokens of a stage: stages are 16 * W tokens, copied as
-// D/64 boxes of [16 W rows x 128 bytes] for K and for V.
+// W consumer warps in kGroups groups; a warp owns 16 tokens of each of its
+// group's stages, so stages are 16 * W / kGroups tokens, copied as D/64 boxes
+// of [kStageTok rows x 128 bytes] for K and for V.
 template <int D, int NS, int W> struct TmaCfg {
-  static constexpr int kStageTok = 16 * W;
+  static constexpr int kGroups = 2;
+  static constexpr int kGroupWarps = W / kGroups;
+  static constexpr int kStageTok = 16 * kGroupWarps;
+  static_assert(W % kGroups == 0 && NS % kGroups == 0, "groups must split warps and ring evenly");
   static constexpr int kBoxBytes = 128 * kStageTok;
   static constexpr int kBoxes = D / 64;                       // boxes per K (or V) row
   static constexpr int kStageBytes = 2 * kBoxes * kBoxBytes;  // K + V
@@ -679,14 +687,6 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   constexpr int kProducer = kTmaWarps;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool producer = warp == kProducer;
-  if (producer && lane == 0) {  // descriptor fetch overlaps the wait for the previous kernel
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
-  }
-  pdl_begin();
-  // Cluster merge: arrive on the "all ranks started" phase right away; the
-  // matching wait comes just before the first remote shared-memory store.
-  if (CL) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   using Cfg = TmaCfg<D, NS, kTmaWarps>;
   constexpr int KS = D / 16, NM = D / 16, GP = NT * 8;
   constexpr int kStageTok = Cfg::kStageTok, kBoxBytes = Cfg::kBoxBytes;
@@ -706,14 +706,24 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   T *out = static_cast<T *>(a.out);
   const uint32_t ring_u32 = smem_u32(ring);
   const uint32_t full_u32 = smem_u32(bars), empty_u32 = full_u32 + 8 * NS;
-  if (producer && lane == 0) {  // independent of any global data: first
+  // Independent of any global data, so it overlaps the previous kernel: the
+  // descriptor prefetch and the mbarrier set-up, made visible to every warp.
+  if (producer && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
     for (int s = 0; s < NS; ++s) {
-      mbar_init(full_u32 + 8 * s);                    // one expect_tx arrival + the bytes
-      mbar_init_count(empty_u32 + 8 * s, kTmaWarps);  // one arrival per consumer warp
+      mbar_init(full_u32 + 8 * s);                             // one expect_tx arrival + the bytes
+      mbar_init_count(empty_u32 + 8 * s, Cfg::kGroupWarps);  // one arrival per warp of the group
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
+    s_first_unwaited = INT_MAX;
   }
+  __syncthreads();
+  pdl_begin();
+  // Cluster merge: arrive on the "all ranks started" phase right away; the
+  // matching wait comes just before the first remote shared-memory store.
+  if (CL) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   if (row >= a.rows) {
     if (split == 0) zero_heads<T, D>(out, row, a.Hq, kvh * group, group);
     return;
@@ -801,13 +811,10 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
       asm volatile("fence.proxy.async.global;" ::: "memory");
       __syncwarp();
     }
-    if (lane == 0) {
+    if (lane == 0)
       for (int k = min(n_first, k_pos); k < n_first; ++k) issue(k);
-      s_first_unwaited = n_stages;
-    }
     issued = n_first;
   }
-  __syncthreads();  // barrier initialisation, s_abort and s_first_unwaited visible to every warp
 
   float o[NT][NM][4];
   float m_run[NT][2], l_run[NT][2];
@@ -826,7 +833,8 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
   bool ok = true;
   if (!producer) {
     T *pw = s_p + warp * 2 * 16 * GP;  // hi tile; the lo tile follows
-    for (int k = 0; k < n_stages; ++k) {
+    const int wg = warp / Cfg::kGroupWarps, wr = warp % Cfg::kGroupWarps;
+    for (int k = wg; k < n_stages; k += Cfg::kGroups) {
       const int s = k % NS;
       // After a timed-out wait (here or in another warp) no stage is waited
       // for any more; the vote keeps the warp converged for the mma/ldmatrix.
@@ -839,11 +847,11 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
         }
         ok = false;
       }
-      const int base = ts + k * kStageTok + warp * 16;  // this warp's first token
+      const int base = ts + k * kStageTok + wr * 16;  // this warp's first token
       if (ok && base < te) {
         const uint32_t kb = ring_u32 + s * Cfg::kStageBytes;
         const uint32_t vb = kb + Cfg::kBoxes * kBoxBytes;
-        const int r0 = warp * 16;
+        const int r0 = wr * 16;
         if (base + 16 > te) {  // zero V rows past the split so 0 * stale data stays 0
           uint8_t *vgen = ring + s * Cfg::kStageBytes + Cfg::kBoxes * kBoxBytes;
           for (int i = lane; i < 16 * (D / 8); i += 32) {
@@ -961,7 +969,8 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
     // Let every issued copy that no consumer saw land (bounded again) before
     // the ring is reused for the O staging below or released with the CTA.
     if (producer && lane == 0)
-      for (int k = s_first_unwaited; k < issued; ++k) mbar_wait(full_u32 + 8 * (k % NS), (k / NS) & 1);
+      for (int k = min(s_first_unwaited, issued); k < issued; ++k)
+        mbar_wait(full_u32 + 8 * (k % NS), (k / NS) & 1);
     __syncthreads();
   }
 
@@ -1516,8 +1525,8 @@ int launch_tma(const AttnArgs &a, int splits, cudaStream_t st) {
   CUtensorMap tmk, tmv;
   const int64_t rows_total = (int64_t)a.num_slots * a.Hk * a.W;
   const int dt = std::is_same<T, __half>::value ? DSB_F16 : DSB_BF16;
-  if (!encode_kv_map(&tmk, a.wk, rows_total, D, dt, 16 * W) ||
-      !encode_kv_map(&tmv, a.wv, rows_total, D, dt, 16 * W))
+  if (!encode_kv_map(&tmk, a.wk, rows_total, D, dt, TmaCfg<D, NS, W>::kStageTok) ||
+      !encode_kv_map(&tmv, a.wv, rows_total, D, dt, TmaCfg<D, NS, W>::kStageTok))
     return -1;  // no tensor map: the caller uses the register-fed kernel
   const size_t smem = tma_smem_bytes<T, D, NT, NS, W>();
   using Epi = TmaEpi<D, NT * 8, W>;
@@ -1585,11 +1594,12 @@ int launch_umma(const AttnArgs &a, int splits, cudaStream_t st) {
   return check_launch("draft_attention_umma_kernel");
 }
 
-// Geometry of the TMA kernel: 8 warps and 128-token stages up to head_dim
-// 128 (a ~192 KB ring, one CTA per SM), 4 warps and 64-token stages at 256.
+// Geometry of the TMA kernel: 8 consumer warps and 64-token stages up to
+// head_dim 128 (a 192 KB ring at 128, one CTA per SM), 4 warps and 32-token
+// stages at 256 (128 KB).
 template <int D> struct TmaGeom {
   static constexpr int W = D >= 256 ? 4 : 8;
-  static constexpr int NS = D >= 256 ? 2 : (D >= 128 ? 3 : 4);
+  static constexpr int NS = D >= 256 ? 4 : (D >= 128 ? 6 : 8);
 };
 
 template <typename T, int D, int NT>
