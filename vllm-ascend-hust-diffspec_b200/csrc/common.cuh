@@ -110,6 +110,29 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
   return r;
 }
 
+// L2 policy for data read once per pass (the paged target K of the chunk
+// scores, the raw caches a rebuild gathers from): its lines are evicted
+// first, so the working cache that the draft steps re-read keeps its lines in
+// L2.  Without side effects, so the compiler may hoist it.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+#ifdef DSB_NO_L2_HINTS
+  asm("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+#else
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+#endif
+  return pol;
+}
+
+// ldg_stream with an L2 cache policy.
+__device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+
 __device__ __forceinline__ void stg_stream(void *p, const uint4 &v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)
@@ -247,6 +270,15 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           dst),
       "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// bulk_load with an L2 cache policy for the source lines.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                          uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
       : "memory");
 }
 

@@ -498,10 +498,11 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
         const uint32_t later = breaks & ~((2u << lane) - 1u);  // 2u << 31 wraps to 0: no later break
         const int end = later ? __ffs(later) - 1 : 32;
         const uint32_t bytes = (uint32_t)(end - lane) * row_bytes;
+        const uint64_t pol = l2_evict_first();
         bulk_load(smem_u32(sk + (size_t)t * row_bytes), static_cast<const T *>(a.src_k) + offs[j],
-                  bytes, bar_u32);
+                  bytes, bar_u32, pol);
         bulk_load(smem_u32(sv + (size_t)t * row_bytes), static_cast<const T *>(a.src_v) + offs[j],
-                  bytes, bar_u32);
+                  bytes, bar_u32, pol);
       }
       if (t < PT) s_kind[t] = kinds[j];
     }

@@ -70,7 +70,7 @@ template <typename T, int D>
 __device__ __forceinline__ void load_token(uint4 (&dst)[D / 32], const T *row, int t) {
   if (row != nullptr) {
 #pragma unroll
-    for (int j = 0; j < D / 32; ++j) dst[j] = ldg_stream(row + 8 * (4 * j + t));
+    for (int j = 0; j < D / 32; ++j) dst[j] = ldg_stream(row + 8 * (4 * j + t), l2_evict_first());
   } else {
 #pragma unroll
     for (int j = 0; j < D / 32; ++j) dst[j] = make_uint4(0, 0, 0, 0);
