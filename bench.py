@@ -70,8 +70,15 @@ STEPS_PER_PERIOD = INTERVAL * DEPTH
 # kind, from one ncu capture of the current kernels on a B200:
 # `ncu --set full --clock-control none -k regex:<kernel> -s 2 -c 1
 #  python bench.py --only <kind> --steps 3 --warmup 2`.
-PROFILED_TRAFFIC = {"attention": 67_276_032 + 883_968, "rebuild": 65_614_848 + 17_102,
-                    "scores": 671_360_256 + 6_041}
+PROFILED_TRAFFIC = {"attention": 67_278_592 + 482_816, "rebuild": 65_555_968 + 9_956_096,
+                    "scores": 671_409_920 + 6_066_688}
+# DRAM bytes per launch inside a running period (caches not flushed between
+# kernels), from the one-pass launch list `ncu --metrics gpu__time_duration.sum,
+# dram__bytes_read.sum,dram__bytes_write.sum --cache-control none
+# --clock-control none -s 28 -c 27 python bench.py --steps 3 --warmup 3
+# --no-cpu --no-e2e`, averaged over the period's launches of the kind: the
+# working cache stays in L2 between the rebuild and the four draft steps.
+IN_SITU_TRAFFIC = {"attention": 2_372_496, "rebuild": 89_893_248, "scores": 680_339_712}
 
 
 def _peaks() -> tuple[float, str]:
@@ -675,6 +682,7 @@ def emit_ours(args):
         roofline = dict(bound="hbm", kernel=dominant, achieved=round(achieved, 1), peak=peak,
                         peak_kind=peak_kind, unit="GB/s", frac=round(achieved / peak, 4),
                         traffic=PROFILED_TRAFFIC.get(dominant),
+                        traffic_in_situ=IN_SITU_TRAFFIC.get(dominant),
                         algorithmic_bytes_per_launch=int(per_launch[dominant]),
                         avg_launch_us=round(avg_ms * 1e3, 3),
                         timing="avg_launch_us: the kind's launches of one period back to back "
