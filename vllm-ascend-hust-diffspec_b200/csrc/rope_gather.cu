@@ -45,6 +45,7 @@ struct RopeArgs {
   int heads, head_dim, rotary_dim, neox, tokens_per_warp;
   int pt_shift;  // bulk kernel: log2 of the positions per CTA
   int vec_rope;  // NeoX with 16-byte-aligned halves and cos/sin rows: vector path
+  int cs_bulk;   // bulk kernel: the CTA's cos/sin rows are staged with its K/V rows
   int chunk_shift, block_shift;  // log2 of chunk / block_size when powers of two, else -1
   int32_t *err;
 };
@@ -61,7 +62,9 @@ __device__ __forceinline__ float cs_load(const CS *p) {
 
 // N consecutive table entries as floats (aligned vector loads; N * sizeof(CS)
 // is 8, 16 or 32 bytes).
-template <typename CS, int N>
+// SHARED: p points into shared memory (plain loads instead of the read-only
+// global path).
+template <typename CS, int N, bool SHARED = false>
 __device__ __forceinline__ void cs_load_vec(const CS *p, float (&out)[N]) {
   constexpr int bytes = N * (int)sizeof(CS);
   union {
@@ -71,9 +74,10 @@ __device__ __forceinline__ void cs_load_vec(const CS *p, float (&out)[N]) {
   } u;
   if constexpr (bytes >= 16) {
 #pragma unroll
-    for (int i = 0; i < bytes / 16; ++i) u.q[i] = __ldg(reinterpret_cast<const uint4 *>(p) + i);
+    for (int i = 0; i < bytes / 16; ++i)
+      u.q[i] = SHARED ? reinterpret_cast<const uint4 *>(p)[i] : __ldg(reinterpret_cast<const uint4 *>(p) + i);
   } else {
-    u.d = __ldg(reinterpret_cast<const uint2 *>(p));
+    u.d = SHARED ? *reinterpret_cast<const uint2 *>(p) : __ldg(reinterpret_cast<const uint2 *>(p));
   }
 #pragma unroll
   for (int i = 0; i < N; ++i) out[i] = Elem<CS>::to_f(u.e[i]);
@@ -390,11 +394,14 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
   const int heads = a.heads;
   const int row_elems = heads * DH;
   const uint32_t row_bytes = (uint32_t)row_elems * 2u;
-  // [PT][row] K, then [PT][row] V, then the mbarrier and the per-token kinds
+  // [PT][row] K, then [PT][row] V, the mbarrier, the per-token kinds and, with
+  // cs_bulk, the CTA's [PT][cs_stride] cos/sin rows (16-byte aligned)
   uint8_t *sk = bulk_smem;
   uint8_t *sv = bulk_smem + (size_t)PT * row_bytes;
   uint64_t *bar = reinterpret_cast<uint64_t *>(bulk_smem + 2 * (size_t)PT * row_bytes);
   int *s_kind = reinterpret_cast<int *>(bar + 1);
+  const CS *s_cs = reinterpret_cast<const CS *>(
+      bulk_smem + ((2 * (size_t)PT * row_bytes + 8 + 4 * (size_t)PT + 15) & ~(size_t)15));
   const int r = blockIdx.y;
   const int64_t p0 = (int64_t)blockIdx.x << a.pt_shift;
 
@@ -485,7 +492,15 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
       kinds[j] = (32 * j < PT) ? resolve(lane + 32 * j, offs[j]) : 0;
       n_loads += __popc(__ballot_sync(0xffffffffu, kinds[j] == 1));
     }
-    if (lane == 0) mbar_expect_tx(bar_u32, n_loads * 2u * row_bytes);
+    // cos/sin rows of positions p0 .. p0 + n_tok - 1: one contiguous copy
+    const uint32_t cs_bytes =
+        a.cs_bulk ? (uint32_t)(n_tok * a.cs_stride * (int64_t)sizeof(CS)) : 0u;
+    if (lane == 0) {
+      mbar_expect_tx(bar_u32, n_loads * 2u * row_bytes + cs_bytes);
+      if (cs_bytes)
+        bulk_load(smem_u32(s_cs), static_cast<const CS *>(a.cos_sin) + p0 * a.cs_stride, cs_bytes,
+                  bar_u32);
+    }
     __syncwarp();
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -553,36 +568,42 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
 
   const CS *cs = static_cast<const CS *>(a.cos_sin);
   if (a.vec_rope) {
-    // NeoX, half % 8 == 0: item (token, j) rotates vectors j and j + half/8 of
-    // every head with one cos/sin load.
+    // NeoX, half % 8 == 0: item (head, token, j) rotates vectors j and
+    // j + half/8 of one head row.  With cs_bulk the cos/sin vectors come from
+    // the staged rows; otherwise from the table in global memory.
     const int hv = half / VE;
     const int hv_shift = (hv & (hv - 1)) == 0 ? __ffs(hv) - 1 : -1;
-    const int k_items = n_tok * hv;
+    const int k_items = heads * n_tok * hv;
     for (int i = tid; i < k_items; i += kBulkThreads) {
       const int j = hv_shift >= 0 ? i & (hv - 1) : i % hv;
-      const int t = hv_shift >= 0 ? i >> hv_shift : i / hv;
+      const int th = hv_shift >= 0 ? i >> hv_shift : i / hv;  // token + n_tok * head
+      const int t = th % n_tok, h = th / n_tok;
       const int kind = s_kind[t];
       if (kind == 0) continue;
+      const int64_t o = dst_off(t, h);
+      if (kind == 2) {
+        stg_stream(dst_k + o + j * VE, zero);
+        stg_stream(dst_k + o + half + j * VE, zero);
+        continue;
+      }
       float c[VE], s[VE];
-      const CS *csr = cs + (p0 + t) * a.cs_stride;
-      cs_load_vec<CS, VE>(csr + j * VE, c);
-      cs_load_vec<CS, VE>(csr + half + j * VE, s);
+      if (a.cs_bulk) {
+        const CS *csr = s_cs + (int64_t)t * a.cs_stride;
+        cs_load_vec<CS, VE, true>(csr + j * VE, c);
+        cs_load_vec<CS, VE, true>(csr + half + j * VE, s);
+      } else {
+        const CS *csr = cs + (p0 + t) * a.cs_stride;
+        cs_load_vec<CS, VE>(csr + j * VE, c);
+        cs_load_vec<CS, VE>(csr + half + j * VE, s);
+      }
       float sneg[VE];
 #pragma unroll
       for (int e = 0; e < VE; ++e) sneg[e] = -s[e];
-      for (int h = 0; h < heads; ++h) {
-        const int64_t o = dst_off(t, h);
-        if (kind == 2) {
-          stg_stream(dst_k + o + j * VE, zero);
-          stg_stream(dst_k + o + half + j * VE, zero);
-          continue;
-        }
-        const uint8_t *hrow = sk + (size_t)t * row_bytes + (size_t)h * DH * 2;
-        const uint4 lo = *reinterpret_cast<const uint4 *>(hrow + j * VE * 2);
-        const uint4 hi = *reinterpret_cast<const uint4 *>(hrow + (half + j * VE) * 2);
-        stg_stream(dst_k + o + j * VE, rotate8<T>(lo, hi, c, sneg));
-        stg_stream(dst_k + o + half + j * VE, rotate8<T>(hi, lo, c, s));
-      }
+      const uint8_t *hrow = sk + (size_t)t * row_bytes + (size_t)h * DH * 2;
+      const uint4 lo = *reinterpret_cast<const uint4 *>(hrow + j * VE * 2);
+      const uint4 hi = *reinterpret_cast<const uint4 *>(hrow + (half + j * VE) * 2);
+      stg_stream(dst_k + o + j * VE, rotate8<T>(lo, hi, c, sneg));
+      stg_stream(dst_k + o + half + j * VE, rotate8<T>(hi, lo, c, s));
     }
   } else if (rot > 0) {
     // Any other rotary layout: one thread per (token, head, element), the
@@ -666,7 +687,14 @@ int launch_rope_bulk(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
     a.vec_rope = a.neox && a.rotary_dim > 0 && (a.rotary_dim / 2) % VE == 0 &&
                  reinterpret_cast<uintptr_t>(a.cos_sin) % 16 == 0 &&
                  (a.cs_stride * (int64_t)sizeof(CS)) % 16 == 0;
-    const size_t smem = 2 * (size_t)pt * row_bytes + 8 + 4 * (size_t)pt;
+    // Stage the cos/sin rows with the K/V rows when the table is dense (row
+    // stride = rotary_dim, so the CTA's rows are one contiguous range that
+    // ends inside the table) and they take at most 16 KB per CTA.
+    const int64_t cs_row_bytes = a.cs_stride * (int64_t)sizeof(CS);
+    a.cs_bulk = a.vec_rope && a.cs_stride == a.rotary_dim && pt * cs_row_bytes <= 16 * 1024 ? 1 : 0;
+    const size_t cs_off = (2 * (size_t)pt * row_bytes + 8 + 4 * (size_t)pt + 15) & ~(size_t)15;
+    const size_t smem = a.cs_bulk ? cs_off + (size_t)(pt * cs_row_bytes)
+                                  : 2 * (size_t)pt * row_bytes + 8 + 4 * (size_t)pt;
     auto kern = a.head_dim == 128  ? rope_bulk_kernel<T, CS, GATHER, 128>
                 : a.head_dim == 64 ? rope_bulk_kernel<T, CS, GATHER, 64>
                                    : rope_bulk_kernel<T, CS, GATHER, 256>;
