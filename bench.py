@@ -3,9 +3,10 @@
 One bench step is one retrieval period of the draft loop: the retrieval hook
 (committed-query pick, chunk scores over the target's paged K history,
 head-sharded exchange when N > 1, top-k selection) followed by
-``retrieval_interval`` = 4 draft cycles, each a device plan build, the fused
-gather + local-RoPE rebuild of the working cache and K = 4 draft attention
-steps.  That is 16 draft steps per bench step.
+``retrieval_interval`` = 4 draft cycles, each one launch that builds the
+history plan on the device and runs the fused gather + local-RoPE rebuild of
+the working cache from it, and K = 4 draft attention steps.  That is 16 draft
+steps (23 kernel launches) per bench step.
 
 Workload (config 2, per 16-request group): 16 requests at 40960 tokens,
 chunk 64, token budget 2048 (history budget 1984), 32 query / 4 kv heads,
@@ -222,18 +223,14 @@ def period_launches(w: "Workload", exchange=None, total_hq=None, gathered=None):
     else:
         seq.append(("select", select))
     for c in range(INTERVAL):
-        def plan(c=c):
-            dsb.selection.build_history_plan(
-                w.active, w.committed[c], w.sel_chunks, w.sel_count, chunk_size=CHUNK,
-                history_budget=HISTORY_BUDGET, working_budget=TOKEN_BUDGET, plan=w.plan,
+        def rebuild(c=c):  # plan + rebuild in one launch
+            dsb.compact_kv.rebuild_working_cache(
+                w.raw_key, w.raw_value, w.working_key, w.working_value, w.active, w.committed[c],
+                w.sel_chunks, w.sel_count, w.cos_sin, chunk_size=CHUNK,
+                history_budget=HISTORY_BUDGET, rotary_dim=D, is_neox_style=True, plan=w.plan,
                 history_lens=w.hist)
 
-        def rebuild():
-            dsb.compact_kv.rebuild_compact_kv_from_plan(
-                w.raw_key, w.raw_value, w.working_key, w.working_value, w.plan, w.cos_sin,
-                chunk_size=CHUNK, max_width=HISTORY_BUDGET, rotary_dim=D, is_neox_style=True)
-
-        seq += [("plan", plan), ("rebuild", rebuild)]
+        seq.append(("rebuild", rebuild))
         for j in range(DEPTH):
             def attn(j=j):
                 dsb.attention.draft_decode_attention(
@@ -703,7 +700,7 @@ def emit_ours(args):
         metric=METRIC, value=round(res["value"], 2), unit=UNIT, n_gpus=world, steps=args.steps,
         warmup=args.warmup, ms_per_step=round(period_ms, 4), higher_is_better=True,
         scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic",
-        config=dict(workload="config 2: retrieval period (1 retrieval + 4 cycles x (plan, "
+        config=dict(workload="config 2: retrieval period (1 retrieval + 4 cycles x (plan + "
                     "rebuild, 4 draft attention steps)) over 16 requests x 40960 ctx per "
                     "request group", requests=B_GROUP * world, context=CTX, chunk=CHUNK,
                     token_budget=TOKEN_BUDGET, history_budget=HISTORY_BUDGET, q_heads=HQ,
@@ -786,7 +783,7 @@ def main():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end API leg")
-    p.add_argument("--only", choices=["prepare", "scores", "select", "plan", "rebuild", "attention"],
+    p.add_argument("--only", choices=["prepare", "scores", "select", "rebuild", "attention"],
                    help="launch one kernel kind eagerly (for profiler captures)")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":

@@ -148,6 +148,30 @@ int dsb_rebuild_compact_kv_from_plan(
     int32_t max_width, int32_t rotary_dim, int32_t is_neox_style, int32_t dtype,
     int32_t *error_flag, void *stream);
 
+/* History plan and working-cache rebuild in one launch
+ * (_rebuild_working_cache_batched, diffspec/runtime.py:1737-1765, which runs
+ * _history_plan_host :1713-1735 on the host, copies the plan to the device and
+ * calls rebuild_compact_kv_from_plan).  Every row's plan is computed on the
+ * device from its slot's selection state and committed length exactly as
+ * dsb_build_history_plan does and drives the rebuild of the same launch, so
+ * the working cache is bit-identical to dsb_build_history_plan followed by
+ * dsb_rebuild_compact_kv_from_plan.  plan ([rows, plan_width], plan_width =
+ * 5 + working_budget / chunk_size), history_lens ([rows]) and working_lens
+ * ([num_slots]) receive the plan values when non-null; plan may be null only
+ * when the fused kernel takes the shape (16-bit caches, head_dim 64/128/256),
+ * otherwise it is the buffer of the two-launch path.  max_width =
+ * history_budget. */
+int dsb_rebuild_working_cache(
+    const void *raw_key, const void *raw_value, void *working_key, void *working_value,
+    const int32_t *row_slots, const int32_t *committed_lens, int32_t rows,
+    const int32_t *sel_chunks, int32_t sel_stride, const int32_t *sel_count,
+    int32_t num_slots, int32_t chunk_size, int32_t history_budget, int32_t plan_width,
+    int64_t *plan, int32_t *history_lens, int32_t *working_lens,
+    const void *cos_sin_cache, int32_t cos_sin_dtype, int64_t cos_sin_stride,
+    int64_t cos_sin_rows, int64_t max_model_len, int32_t num_heads, int32_t head_dim,
+    int32_t working_budget, int32_t rotary_dim, int32_t is_neox_style, int32_t dtype,
+    int32_t *error_flag, void *stream);
+
 /* Paged gather at selected token ids with RoPE at local positions 0..W-1
  * (gather_raw_kv_with_local_rope, diffspec/kernels.py:153-210).  Ids < 0 give
  * zero rows (which still take a local position).  Outputs are

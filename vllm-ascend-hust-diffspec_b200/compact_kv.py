@@ -2,7 +2,10 @@
 
 ``rebuild_compact_kv_from_plan`` keeps the signature, plan contract and
 ``ValueError`` conditions of diffspec/compact_kv.py:136-242; the kernel is the
-sm_100a ``rebuild_rope_kernel`` in ``libdiffspec_b200.so``.
+sm_100a ``rope_bulk_kernel`` in ``libdiffspec_b200.so``.
+``rebuild_working_cache`` is the reference's whole
+``_rebuild_working_cache_batched`` (diffspec/runtime.py:1737-1765: host plan,
+plan upload, rebuild) as one launch that computes the plan on the device.
 """
 
 from __future__ import annotations
@@ -11,7 +14,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["rebuild_compact_kv_from_plan"]
+__all__ = ["rebuild_compact_kv_from_plan", "rebuild_working_cache"]
 
 
 def _validate_compact_inputs(
@@ -125,3 +128,92 @@ def rebuild_compact_kv_from_plan(
         _lib.ptr(_lib.error_flag(device)),
         _lib.stream_ptr(device),
     )
+
+
+def rebuild_working_cache(
+    raw_key: torch.Tensor,
+    raw_value: torch.Tensor,
+    working_key: torch.Tensor,
+    working_value: torch.Tensor,
+    row_slots: torch.Tensor,
+    committed_lens: torch.Tensor,
+    sel_chunks: torch.Tensor,
+    sel_count: torch.Tensor,
+    cos_sin_cache: torch.Tensor,
+    *,
+    chunk_size: int,
+    history_budget: int,
+    rotary_dim: int,
+    is_neox_style: bool,
+    plan: torch.Tensor | None = None,
+    history_lens: torch.Tensor | None = None,
+    working_lens: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """History plan + working-cache rebuild of every row in one launch.
+
+    Row ``r`` uses slot ``row_slots[r]`` with committed length
+    ``committed_lens[r]`` (the root included; history ends before it) and the
+    slot's selection ``sel_chunks[slot, :sel_count[slot]]`` (count < 0: no
+    retrieval yet).  The plan rows, ``history_lens`` and ``working_lens`` come
+    out exactly as ``selection.build_history_plan`` computes them, and the
+    working cache exactly as ``rebuild_compact_kv_from_plan`` of that plan
+    leaves it.  Returns ``(plan, history_lens)``.
+    """
+    working_budget = working_key.shape[2]
+    rows = row_slots.shape[0]
+    if chunk_size <= 0:
+        raise ValueError("plan width must be 5 + working_budget // chunk_size")
+    width = 5 + working_budget // chunk_size
+    device = _lib.require_cuda(raw_key, row_slots, committed_lens, sel_chunks, sel_count)
+    if plan is None:
+        plan = torch.empty((rows, width), dtype=torch.int64, device=device)
+    if history_lens is None:
+        history_lens = torch.empty(rows, dtype=torch.int32, device=device)
+    _validate_compact_inputs(
+        raw_key, raw_value, working_key, working_value, plan, cos_sin_cache,
+        max_width=history_budget, rotary_dim=rotary_dim,
+    )
+    if plan.shape != (rows, width):
+        raise ValueError("plan must be contiguous int64 [rows, 5 + working_budget // chunk_size]")
+    for t in (row_slots, committed_lens, sel_chunks, sel_count, history_lens):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("slots, lengths and selection state must be contiguous int32")
+    if working_lens is not None and (working_lens.dtype != torch.int32 or not working_lens.is_contiguous()):
+        raise ValueError("working_lens must be contiguous int32")
+    if rows == 0:
+        return plan, history_lens
+    slots, max_model_len, heads, head_dim = raw_key.shape
+    _lib.call(
+        "dsb_rebuild_working_cache",
+        _lib.ptr(raw_key),
+        _lib.ptr(raw_value),
+        _lib.ptr(working_key),
+        _lib.ptr(working_value),
+        _lib.ptr(row_slots),
+        _lib.ptr(committed_lens),
+        rows,
+        _lib.ptr(sel_chunks),
+        sel_chunks.shape[1],
+        _lib.ptr(sel_count),
+        slots,
+        chunk_size,
+        history_budget,
+        width,
+        _lib.ptr(plan),
+        _lib.ptr(history_lens),
+        _lib.ptr(working_lens),
+        _lib.ptr(cos_sin_cache),
+        _lib.dtype_code(cos_sin_cache.dtype),
+        cos_sin_cache.stride(0),
+        cos_sin_cache.shape[0],
+        max_model_len,
+        heads,
+        head_dim,
+        working_budget,
+        rotary_dim,
+        int(bool(is_neox_style)),
+        _lib.dtype_code(raw_key.dtype),
+        _lib.ptr(_lib.error_flag(device)),
+        _lib.stream_ptr(device),
+    )
+    return plan, history_lens

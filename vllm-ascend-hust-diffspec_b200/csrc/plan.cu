@@ -3,13 +3,12 @@
 // write (A9).  All of them keep the reference's host Python loops on the
 // device so a draft cycle needs no device-to-host copy.
 #include "common.cuh"
+#include "plan_row.cuh"
 
 namespace dsb {
 namespace {
 
-// One warp per plan row: _history_plan_host, diffspec/runtime.py:1713-1735.
-// Lanes read the slot's selected chunks in parallel and a warp reduction
-// forms prefix_tokens, so a row costs one round of loads.
+// One warp per plan row (plan_row_warp).
 __global__ void build_plan_kernel(const int32_t *__restrict__ row_slots,
                                   const int32_t *__restrict__ committed_lens, int rows,
                                   const int32_t *__restrict__ sel_chunks, int sel_stride,
@@ -29,48 +28,13 @@ __global__ void build_plan_kernel(const int32_t *__restrict__ row_slots,
     if (lane == 0 && history_lens != nullptr) history_lens[r] = 0;
     return;
   }
-  const int64_t he = max(0, committed_lens[r] - 1);  // history ends before the root
-  const int cnt = sel_count[slot];
   const int32_t *ch = sel_chunks + (int64_t)slot * sel_stride;
-  const int n_sel = min(max(cnt, 0), sel_stride);
-  int n_chunks = n_sel;
-  if (5 + n_chunks > plan_width) {
-    if (lane == 0) flag_error(err, DSB_FLAG_CAPACITY);
-    n_chunks = plan_width - 5;
-  }
-  const int64_t tail_len = min(he, (int64_t)min(C, HB));
-  int64_t hlen, tail_start, prefix_len = 0, prefix_drop = 0;
-  if (cnt < 0) {  // no retrieval yet: the most recent history_budget tokens
-    hlen = min(he, (int64_t)HB);
-    tail_start = he - hlen;
-  } else if (cnt == 0) {
-    hlen = tail_len;
-    tail_start = he - tail_len;
-  } else {
-    tail_start = he - tail_len;
-    const int64_t prefix_end = min(tail_start, (int64_t)ch[n_sel - 1] * C);
-    int64_t part = 0;
-    for (int i = lane; i < n_sel; i += 32)
-      part += max((int64_t)0, min((int64_t)C, prefix_end - (int64_t)ch[i] * C));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    prefix_len = min(part, (int64_t)HB - tail_len);
-    prefix_drop = part - prefix_len;
-    hlen = prefix_len + tail_len;
-  }
-  for (int i = lane; i < plan_width; i += 32) {
-    int64_t v;
-    if (i == 0) v = slot;
-    else if (i == 1) v = hlen;
-    else if (i == 2) v = tail_start;
-    else if (i == 3) v = prefix_len;
-    else if (i == 4) v = prefix_drop;
-    else v = (i - 5 < n_chunks) ? ch[i - 5] : 0;
-    out[i] = v;
-  }
+  const PlanRow pr = plan_row_warp(committed_lens[r], sel_count[slot], ch, sel_stride, C, HB,
+                                   plan_width, lane, err);
+  for (int i = lane; i < plan_width; i += 32) out[i] = plan_row_value(pr, slot, ch, i);
   if (lane == 0) {
-    if (history_lens != nullptr) history_lens[r] = (int32_t)hlen;
-    if (working_lens != nullptr) working_lens[slot] = (int32_t)hlen;
+    if (history_lens != nullptr) history_lens[r] = (int32_t)pr.hlen;
+    if (working_lens != nullptr) working_lens[slot] = (int32_t)pr.hlen;
   }
 }
 

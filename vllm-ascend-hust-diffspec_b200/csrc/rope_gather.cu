@@ -17,8 +17,12 @@
 // fused multiply-add, then rounded once to the cache dtype.
 #include <algorithm>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "common.cuh"
+#include "plan_row.cuh"
 
 namespace dsb {
 namespace {
@@ -46,6 +50,13 @@ struct RopeArgs {
   int pt_shift;  // bulk kernel: log2 of the positions per CTA
   int vec_rope;  // NeoX with 16-byte-aligned halves and cos/sin rows: vector path
   int cs_bulk;   // bulk kernel: the CTA's cos/sin rows are staged with its K/V rows
+  // rebuild from the selection state: the launch computes each row's plan
+  // (plan_row_warp) instead of reading it, and CTA 0 of the row writes it out
+  int from_sel;
+  const int32_t *row_slots, *committed_lens, *sel_chunks, *sel_count;
+  int sel_stride, history_budget;
+  int64_t *plan_out;
+  int32_t *hist_out, *wlen_out;
   int chunk_shift, block_shift;  // log2 of chunk / block_size when powers of two, else -1
   int32_t *err;
 };
@@ -382,9 +393,42 @@ __global__ void __launch_bounds__(kWarpsRope * 32, 3) rope_rows_kernel(const Rop
 // item, loads its cos/sin vectors once and reuses them for every kv head.
 constexpr int kBulkThreads = 256;
 
+// Shared-memory layout of the bulk kernel: kBulkStages stages of [K rows, V
+// rows (PT each), PT int32 kinds, the cos/sin rows], then the stages'
+// mbarriers and the row's int64 chunk ids.
+constexpr int kBulkStages = 2;
+struct BulkLayout {
+  size_t v, kind, cs, stage;  // offsets inside a stage, and its size
+  size_t bars, chunks, total;
+};
+__host__ __device__ inline BulkLayout bulk_smem_layout(int pt, int64_t row_bytes, int n_chunks,
+                                                       int64_t cs_bytes) {
+  BulkLayout l;
+  l.v = (size_t)pt * (size_t)row_bytes;  // row_bytes is a multiple of 16
+  l.kind = 2 * (size_t)pt * (size_t)row_bytes;
+  l.cs = (l.kind + 4 * (size_t)pt + 15) & ~(size_t)15;
+  l.stage = (l.cs + (size_t)cs_bytes + 15) & ~(size_t)15;
+  l.bars = kBulkStages * l.stage;
+  l.chunks = l.bars + 8 * kBulkStages;
+  l.total = l.chunks + 8 * (size_t)(n_chunks > 0 ? n_chunks : 0);
+  return l;
+}
+
+// Bulk-copy rebuild / gather (the default for 16-bit caches with head_dim
+// 64/128/256).  A CTA owns one row and the position blocks b = blockIdx.x,
+// blockIdx.x + gridDim.x, ... of it (PT = 1 << pt_shift <= 64 positions
+// each), streamed through two stages: while the block in one stage is
+// rotated and written, the next block's rows are already in flight into the
+// other.  Warp 0 decodes the sources of a block (lane t: positions t and
+// t + 32) and issues 1-D bulk copies (TMA) of the K rows and V rows (all kv
+// heads), one per run of consecutive source rows (a selected chunk or the
+// rolling tail is one run), plus one copy of the block's cos/sin rows, all
+// completing on the stage's mbarrier.  The block then writes V out unchanged
+// and K rotated: for NeoX with 16-byte halves one thread per (head, token,
+// 8-element pair of vectors) item.  The row descriptor (plan row, read or
+// computed from the selection state) is decoded once per CTA.
 template <typename T, typename CS, bool GATHER, int DH>
 __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs a) {
-  pdl_begin();
   static_assert(sizeof(T) == 2 && DH > 0, "16-bit caches with a compile-time head_dim");
   constexpr int VE = 8;           // elements per 16-byte vector
   constexpr int DV = DH / VE;     // vectors per head row
@@ -394,30 +438,75 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
   const int heads = a.heads;
   const int row_elems = heads * DH;
   const uint32_t row_bytes = (uint32_t)row_elems * 2u;
-  // [PT][row] K, then [PT][row] V, the mbarrier, the per-token kinds and, with
-  // cs_bulk, the CTA's [PT][cs_stride] cos/sin rows (16-byte aligned)
-  uint8_t *sk = bulk_smem;
-  uint8_t *sv = bulk_smem + (size_t)PT * row_bytes;
-  uint64_t *bar = reinterpret_cast<uint64_t *>(bulk_smem + 2 * (size_t)PT * row_bytes);
-  int *s_kind = reinterpret_cast<int *>(bar + 1);
-  const CS *s_cs = reinterpret_cast<const CS *>(
-      bulk_smem + ((2 * (size_t)PT * row_bytes + 8 + 4 * (size_t)PT + 15) & ~(size_t)15));
+  const int64_t cs_row_bytes = a.cs_stride * (int64_t)sizeof(CS);
+  const BulkLayout lay = bulk_smem_layout(PT, row_bytes, GATHER ? 0 : a.plan_width - 5,
+                                          a.cs_bulk ? PT * cs_row_bytes : 0);
+  int64_t *s_chunks = reinterpret_cast<int64_t *>(bulk_smem + lay.chunks);
+  const uint32_t bar0 = smem_u32(bulk_smem + lay.bars);
+  __shared__ int64_t s_desc[5];
   const int r = blockIdx.y;
-  const int64_t p0 = (int64_t)blockIdx.x << a.pt_shift;
-
-  // Row descriptor (rebuild: plan row; gather: the row's index vector).
+  if (tid == 0) {  // no global data: overlaps the previous kernel
+    for (int s = 0; s < kBulkStages; ++s) mbar_init(bar0 + 8 * s);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  pdl_begin();
+  // Row descriptor (rebuild: plan row, read or computed here; gather: the
+  // row's index vector).  Warp 0 stages it and the row's chunk ids in shared
+  // memory.
   int64_t slot = 0, hlen = 0, tail_start = 0, prefix_len = 0, drop = 0;
-  const int64_t *chunks = nullptr;
-  int n_plan_chunks = 0;
+  const int64_t *chunks = s_chunks;
+  const int n_plan_chunks = GATHER ? 0 : a.plan_width - 5;
   if (!GATHER) {
-    const int64_t *pr = a.plan + (int64_t)r * a.plan_width;
-    slot = pr[0];
-    hlen = pr[1];
-    tail_start = pr[2];
-    prefix_len = pr[3];
-    drop = pr[4];
-    chunks = pr + 5;
-    n_plan_chunks = a.plan_width - 5;
+    if (tid < 32) {
+      if (a.from_sel) {
+        const int sl = (a.row_slots != nullptr) ? a.row_slots[r] : r;
+        if (sl < 0 || sl >= a.num_slots) {
+          if (blockIdx.x == 0) {
+            if (lane == 0) flag_error(a.err, DSB_FLAG_SLOT);
+            if (a.plan_out != nullptr)
+              for (int i = lane; i < a.plan_width; i += 32) a.plan_out[(int64_t)r * a.plan_width + i] = 0;
+            if (lane == 0 && a.hist_out != nullptr) a.hist_out[r] = 0;
+          }
+          if (lane == 0) {  // nothing to rebuild for this row
+            s_desc[0] = 0;
+            s_desc[1] = 0;
+            s_desc[2] = 0;
+            s_desc[3] = 0;
+            s_desc[4] = 0;
+          }
+        } else {
+          const int32_t *ch = a.sel_chunks + (int64_t)sl * a.sel_stride;
+          const PlanRow pr = plan_row_warp(a.committed_lens[r], a.sel_count[sl], ch, a.sel_stride,
+                                           a.chunk, a.history_budget, a.plan_width, lane,
+                                           blockIdx.x == 0 ? a.err : nullptr);
+          for (int i = lane; i < n_plan_chunks; i += 32) s_chunks[i] = plan_row_value(pr, sl, ch, 5 + i);
+          if (blockIdx.x == 0) {
+            if (a.plan_out != nullptr)
+              for (int i = lane; i < a.plan_width; i += 32)
+                a.plan_out[(int64_t)r * a.plan_width + i] = plan_row_value(pr, sl, ch, i);
+            if (lane == 0 && a.hist_out != nullptr) a.hist_out[r] = (int32_t)pr.hlen;
+            if (lane == 0 && a.wlen_out != nullptr) a.wlen_out[sl] = (int32_t)pr.hlen;
+          }
+          if (lane == 0) {
+            s_desc[0] = sl;
+            s_desc[1] = pr.hlen;
+            s_desc[2] = pr.tail_start;
+            s_desc[3] = pr.prefix_len;
+            s_desc[4] = pr.prefix_drop;
+          }
+        }
+      } else {
+        const int64_t *pr = a.plan + (int64_t)r * a.plan_width;
+        if (lane < 5) s_desc[lane] = pr[lane];
+        for (int i = lane; i < n_plan_chunks; i += 32) s_chunks[i] = pr[5 + i];
+      }
+    }
+    __syncthreads();
+    slot = s_desc[0];
+    hlen = s_desc[1];
+    tail_start = s_desc[2];
+    prefix_len = s_desc[3];
+    drop = s_desc[4];
     const int64_t cap = min((int64_t)a.max_width, (int64_t)a.working_budget);
     if (slot < 0 || slot >= a.num_slots || hlen < 0 || prefix_len < 0 || prefix_len > hlen ||
         drop < 0 || hlen > cap) {
@@ -429,17 +518,21 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
       drop = max((int64_t)0, drop);
     }
   }
+  if (GATHER) __syncthreads();  // the mbarrier initialisation is visible
   const int64_t width = GATHER ? a.working_tokens : hlen;
-  if (p0 >= width) return;  // CTA-uniform
-  const int n_tok = (int)min((int64_t)PT, width - p0);
-  const uint32_t bar_u32 = smem_u32(bar);
+  const int nblk = (int)((width + PT - 1) >> a.pt_shift);
+  const int n_mine = (int)blockIdx.x < nblk ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  if (n_mine == 0) return;  // CTA-uniform
 
-  if (tid < 32) {
-    if (lane == 0) {
-      mbar_init(bar_u32);
-      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncwarp();
+  // Warp 0: decode block i of this CTA and start its copies into stage i % 2.
+  auto issue = [&](int i) {
+    const int s = i % kBulkStages;
+    uint8_t *st = bulk_smem + s * lay.stage;
+    uint8_t *sk = st, *sv = st + lay.v;
+    int *s_kind = reinterpret_cast<int *>(st + lay.kind);
+    const uint32_t bar = bar0 + 8 * s;
+    const int64_t p0 = (int64_t)((int)blockIdx.x + i * (int)gridDim.x) << a.pt_shift;
+    const int n_tok = (int)min((int64_t)PT, width - p0);
     // Source row of local position p0 + t; kind: 1 = copy the row, 2 = zero
     // row (gather padding / bad block), 0 = skip.
     auto resolve = [&](int t, int64_t &off) -> int {
@@ -493,13 +586,12 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
       n_loads += __popc(__ballot_sync(0xffffffffu, kinds[j] == 1));
     }
     // cos/sin rows of positions p0 .. p0 + n_tok - 1: one contiguous copy
-    const uint32_t cs_bytes =
-        a.cs_bulk ? (uint32_t)(n_tok * a.cs_stride * (int64_t)sizeof(CS)) : 0u;
+    const uint32_t cs_bytes = a.cs_bulk ? (uint32_t)(n_tok * cs_row_bytes) : 0u;
     if (lane == 0) {
-      mbar_expect_tx(bar_u32, n_loads * 2u * row_bytes + cs_bytes);
+      mbar_expect_tx(bar, n_loads * 2u * row_bytes + cs_bytes);
       if (cs_bytes)
-        bulk_load(smem_u32(s_cs), static_cast<const CS *>(a.cos_sin) + p0 * a.cs_stride, cs_bytes,
-                  bar_u32);
+        bulk_load(smem_u32(st + lay.cs), static_cast<const CS *>(a.cos_sin) + p0 * a.cs_stride,
+                  cs_bytes, bar);
     }
     __syncwarp();
 #pragma unroll
@@ -515,132 +607,150 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
         const uint32_t bytes = (uint32_t)(end - lane) * row_bytes;
         const uint64_t pol = l2_evict_first();
         bulk_load(smem_u32(sk + (size_t)t * row_bytes), static_cast<const T *>(a.src_k) + offs[j],
-                  bytes, bar_u32, pol);
+                  bytes, bar, pol);
         bulk_load(smem_u32(sv + (size_t)t * row_bytes), static_cast<const T *>(a.src_v) + offs[j],
-                  bytes, bar_u32, pol);
+                  bytes, bar, pol);
       }
       if (t < PT) s_kind[t] = kinds[j];
     }
-  }
-  __syncthreads();
-  if (!mbar_wait(bar_u32, 0)) {
-    if (tid == 0) {
-      flag_error(a.err, DSB_FLAG_TIMEOUT);
-      mbar_wait(bar_u32, 0);  // let the copies land before the CTA releases its memory
-    }
-    return;
-  }
+  };
 
   T *dst_k = static_cast<T *>(a.dst_k);
   T *dst_v = static_cast<T *>(a.dst_v);
-  // element offset of (token t, head h, dim 0) in the destination
-  const int64_t dst_base =
-      GATHER ? ((int64_t)r * a.working_tokens + p0) * row_elems
-             : (slot * heads * (int64_t)a.working_budget + p0) * DH;
-  auto dst_off = [&](int t, int h) -> int64_t {
-    return GATHER ? dst_base + (int64_t)t * row_elems + h * DH
-                  : dst_base + ((int64_t)h * a.working_budget + t) * DH;
-  };
+  const CS *cs = static_cast<const CS *>(a.cos_sin);
   const uint4 zero = make_uint4(0, 0, 0, 0);
-
-  // V, and the K dims past the rotary part: straight copies.  Items run
-  // dim-vector fastest, then token, then head (shifts only: PT and DV are
-  // powers of two).
   const int rot = a.rotary_dim, half = rot / 2;
   const int krot_vecs = a.vec_rope ? rot / VE : 0;  // K vectors handled by the rotary pass
   const bool copy_k = a.vec_rope || rot == 0;
   constexpr int kDvShift = DV == 8 ? 3 : DV == 16 ? 4 : 5;
   static_assert((1 << kDvShift) == DV, "head_dim / 8 must be 8, 16 or 32");
-  const int n_items = heads << (a.pt_shift + kDvShift);
-  for (int i = tid; i < n_items; i += kBulkThreads) {
-    const int dv = i & (DV - 1);
-    const int t = (i >> kDvShift) & (PT - 1);
-    const int h = i >> (kDvShift + a.pt_shift);
-    if (t >= n_tok) continue;
-    const int kind = s_kind[t];
-    if (kind == 0) continue;
-    const int64_t o = dst_off(t, h) + dv * VE;
-    const size_t so = (size_t)t * row_bytes + ((size_t)h * DH + dv * VE) * 2;
-    stg_stream(dst_v + o, kind == 1 ? *reinterpret_cast<const uint4 *>(sv + so) : zero);
-    if (copy_k && dv >= krot_vecs)
-      stg_stream(dst_k + o, kind == 1 ? *reinterpret_cast<const uint4 *>(sk + so) : zero);
-  }
 
-  const CS *cs = static_cast<const CS *>(a.cos_sin);
-  if (a.vec_rope) {
-    // NeoX, half % 8 == 0: item (head, token, j) rotates vectors j and
-    // j + half/8 of one head row.  With cs_bulk the cos/sin vectors come from
-    // the staged rows; otherwise from the table in global memory.
-    const int hv = half / VE;
-    const int hv_shift = (hv & (hv - 1)) == 0 ? __ffs(hv) - 1 : -1;
-    const int k_items = heads * n_tok * hv;
-    for (int i = tid; i < k_items; i += kBulkThreads) {
-      const int j = hv_shift >= 0 ? i & (hv - 1) : i % hv;
-      const int th = hv_shift >= 0 ? i >> hv_shift : i / hv;  // token + n_tok * head
-      const int t = th % n_tok, h = th / n_tok;
-      const int kind = s_kind[t];
-      if (kind == 0) continue;
-      const int64_t o = dst_off(t, h);
-      if (kind == 2) {
-        stg_stream(dst_k + o + j * VE, zero);
-        stg_stream(dst_k + o + half + j * VE, zero);
-        continue;
+  if (tid < 32) {
+    issue(0);
+    if (n_mine > 1) issue(1);
+  }
+  __syncthreads();  // the first two blocks' kinds are visible
+  for (int i = 0; i < n_mine; ++i) {
+    const int s = i % kBulkStages;
+    const bool got = mbar_wait(bar0 + 8 * s, (i / kBulkStages) & 1);
+    if (!__syncthreads_and(got)) {  // CTA-uniform: stop, let the issued copies land, leave
+      if (tid == 0) {
+        flag_error(a.err, DSB_FLAG_TIMEOUT);
+        for (int k = i; k < min(n_mine, i + kBulkStages); ++k)
+          mbar_wait(bar0 + 8 * (k % kBulkStages), (k / kBulkStages) & 1);
       }
-      float c[VE], s[VE];
-      if (a.cs_bulk) {
-        const CS *csr = s_cs + (int64_t)t * a.cs_stride;
-        cs_load_vec<CS, VE, true>(csr + j * VE, c);
-        cs_load_vec<CS, VE, true>(csr + half + j * VE, s);
-      } else {
-        const CS *csr = cs + (p0 + t) * a.cs_stride;
-        cs_load_vec<CS, VE>(csr + j * VE, c);
-        cs_load_vec<CS, VE>(csr + half + j * VE, s);
-      }
-      float sneg[VE];
-#pragma unroll
-      for (int e = 0; e < VE; ++e) sneg[e] = -s[e];
-      const uint8_t *hrow = sk + (size_t)t * row_bytes + (size_t)h * DH * 2;
-      const uint4 lo = *reinterpret_cast<const uint4 *>(hrow + j * VE * 2);
-      const uint4 hi = *reinterpret_cast<const uint4 *>(hrow + (half + j * VE) * 2);
-      stg_stream(dst_k + o + j * VE, rotate8<T>(lo, hi, c, sneg));
-      stg_stream(dst_k + o + half + j * VE, rotate8<T>(hi, lo, c, s));
+      return;
     }
-  } else if (rot > 0) {
-    // Any other rotary layout: one thread per (token, head, element), the
-    // partner element read from the staged row.
-    const int n_el = n_tok * heads * DH;
-    for (int i = tid; i < n_el; i += kBulkThreads) {
-      const int d = i % DH, h = (i / DH) % heads, t = i / (DH * heads);
+    const uint8_t *st = bulk_smem + s * lay.stage;
+    const uint8_t *sk = st, *sv = st + lay.v;
+    const int *s_kind = reinterpret_cast<const int *>(st + lay.kind);
+    const CS *s_cs = reinterpret_cast<const CS *>(st + lay.cs);
+    const int64_t p0 = (int64_t)((int)blockIdx.x + i * (int)gridDim.x) << a.pt_shift;
+    const int n_tok = (int)min((int64_t)PT, width - p0);
+    // element offset of (token t, head h, dim 0) in the destination
+    const int64_t dst_base =
+        GATHER ? ((int64_t)r * a.working_tokens + p0) * row_elems
+               : (slot * heads * (int64_t)a.working_budget + p0) * DH;
+    auto dst_off = [&](int t, int h) -> int64_t {
+      return GATHER ? dst_base + (int64_t)t * row_elems + h * DH
+                    : dst_base + ((int64_t)h * a.working_budget + t) * DH;
+    };
+
+    // V, and the K dims past the rotary part: straight copies.  Items run
+    // dim-vector fastest, then token, then head (shifts only: PT and DV are
+    // powers of two).
+    const int n_items = heads << (a.pt_shift + kDvShift);
+    for (int it = tid; it < n_items; it += kBulkThreads) {
+      const int dv = it & (DV - 1);
+      const int t = (it >> kDvShift) & (PT - 1);
+      const int h = it >> (kDvShift + a.pt_shift);
+      if (t >= n_tok) continue;
       const int kind = s_kind[t];
       if (kind == 0) continue;
-      T out = Elem<T>::from_f(0.f);
-      if (kind == 1) {
-        const T *hx = reinterpret_cast<const T *>(sk + (size_t)t * row_bytes) + h * DH;
-        if (d >= rot) {
-          out = hx[d];
+      const int64_t o = dst_off(t, h) + dv * VE;
+      const size_t so = (size_t)t * row_bytes + ((size_t)h * DH + dv * VE) * 2;
+      stg_stream(dst_v + o, kind == 1 ? *reinterpret_cast<const uint4 *>(sv + so) : zero);
+      if (copy_k && dv >= krot_vecs)
+        stg_stream(dst_k + o, kind == 1 ? *reinterpret_cast<const uint4 *>(sk + so) : zero);
+    }
+
+    if (a.vec_rope) {
+      // NeoX, half % 8 == 0: item (head, token, j) rotates vectors j and
+      // j + half/8 of one head row.  With cs_bulk the cos/sin vectors come
+      // from the staged rows; otherwise from the table in global memory.
+      const int hv = half / VE;
+      const int hv_shift = (hv & (hv - 1)) == 0 ? __ffs(hv) - 1 : -1;
+      const int k_items = heads * n_tok * hv;
+      for (int it = tid; it < k_items; it += kBulkThreads) {
+        const int j = hv_shift >= 0 ? it & (hv - 1) : it % hv;
+        const int th = hv_shift >= 0 ? it >> hv_shift : it / hv;  // token + n_tok * head
+        const int t = th % n_tok, h = th / n_tok;
+        const int kind = s_kind[t];
+        if (kind == 0) continue;
+        const int64_t o = dst_off(t, h);
+        if (kind == 2) {
+          stg_stream(dst_k + o + j * VE, zero);
+          stg_stream(dst_k + o + half + j * VE, zero);
+          continue;
+        }
+        float c[VE], sn[VE];
+        if (a.cs_bulk) {
+          const CS *csr = s_cs + (int64_t)t * a.cs_stride;
+          cs_load_vec<CS, VE, true>(csr + j * VE, c);
+          cs_load_vec<CS, VE, true>(csr + half + j * VE, sn);
         } else {
           const CS *csr = cs + (p0 + t) * a.cs_stride;
-          int ii;
-          float x1, x2;
-          bool first;
-          if (a.neox) {
-            first = d < half;
-            ii = first ? d : d - half;
-            x1 = Elem<T>::to_f(hx[ii]);
-            x2 = Elem<T>::to_f(hx[ii + half]);
-          } else {
-            first = (d & 1) == 0;
-            ii = d >> 1;
-            x1 = Elem<T>::to_f(hx[2 * ii]);
-            x2 = Elem<T>::to_f(hx[2 * ii + 1]);
-          }
-          const float cc = cs_load(csr + ii), sn = cs_load(csr + half + ii);
-          out = Elem<T>::from_f(first ? __fmul_rn(x1, cc) - __fmul_rn(x2, sn)
-                                      : __fmul_rn(x2, cc) + __fmul_rn(x1, sn));
+          cs_load_vec<CS, VE>(csr + j * VE, c);
+          cs_load_vec<CS, VE>(csr + half + j * VE, sn);
         }
+        float sneg[VE];
+#pragma unroll
+        for (int e = 0; e < VE; ++e) sneg[e] = -sn[e];
+        const uint8_t *hrow = sk + (size_t)t * row_bytes + (size_t)h * DH * 2;
+        const uint4 lo = *reinterpret_cast<const uint4 *>(hrow + j * VE * 2);
+        const uint4 hi = *reinterpret_cast<const uint4 *>(hrow + (half + j * VE) * 2);
+        stg_stream(dst_k + o + j * VE, rotate8<T>(lo, hi, c, sneg));
+        stg_stream(dst_k + o + half + j * VE, rotate8<T>(hi, lo, c, sn));
       }
-      dst_k[dst_off(t, h) + d] = out;
+    } else if (rot > 0) {
+      // Any other rotary layout: one thread per (token, head, element), the
+      // partner element read from the staged row.
+      const int n_el = n_tok * heads * DH;
+      for (int it = tid; it < n_el; it += kBulkThreads) {
+        const int d = it % DH, h = (it / DH) % heads, t = it / (DH * heads);
+        const int kind = s_kind[t];
+        if (kind == 0) continue;
+        T out = Elem<T>::from_f(0.f);
+        if (kind == 1) {
+          const T *hx = reinterpret_cast<const T *>(sk + (size_t)t * row_bytes) + h * DH;
+          if (d >= rot) {
+            out = hx[d];
+          } else {
+            const CS *csr = cs + (p0 + t) * a.cs_stride;
+            int ii;
+            float x1, x2;
+            bool first;
+            if (a.neox) {
+              first = d < half;
+              ii = first ? d : d - half;
+              x1 = Elem<T>::to_f(hx[ii]);
+              x2 = Elem<T>::to_f(hx[ii + half]);
+            } else {
+              first = (d & 1) == 0;
+              ii = d >> 1;
+              x1 = Elem<T>::to_f(hx[2 * ii]);
+              x2 = Elem<T>::to_f(hx[2 * ii + 1]);
+            }
+            const float cc = cs_load(csr + ii), snv = cs_load(csr + half + ii);
+            out = Elem<T>::from_f(first ? __fmul_rn(x1, cc) - __fmul_rn(x2, snv)
+                                        : __fmul_rn(x2, cc) + __fmul_rn(x1, snv));
+          }
+        }
+        dst_k[dst_off(t, h) + d] = out;
+      }
     }
+    __syncthreads();  // every thread is done with stage s (and sees the next kinds)
+    if (tid < 32 && i + kBulkStages < n_mine) issue(i + kBulkStages);
   }
 }
 
@@ -668,6 +778,26 @@ bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0;
 
 // The bulk kernel when its preconditions hold: 16-bit caches, head_dim 64,
 // 128 or 256, 16-byte aligned bases and at least one K+V row pair per stage.
+// Resident CTAs of `kernel` on this device (occupancy x SMs), cached per
+// device, kernel, block size and shared memory.
+int resident_ctas(const void *kernel, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void *, int, size_t>, int> known;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return sm_count();
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(dev, kernel, threads, smem);
+  auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+      per_sm <= 0) {
+    (void)cudaGetLastError();
+    per_sm = 1;
+  }
+  return known[key] = per_sm * sm_count();
+}
+
 template <typename T, typename CS, bool GATHER>
 int launch_rope_bulk(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
   if constexpr (sizeof(T) != 2) {
@@ -692,26 +822,36 @@ int launch_rope_bulk(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
     // ends inside the table) and they take at most 16 KB per CTA.
     const int64_t cs_row_bytes = a.cs_stride * (int64_t)sizeof(CS);
     a.cs_bulk = a.vec_rope && a.cs_stride == a.rotary_dim && pt * cs_row_bytes <= 16 * 1024 ? 1 : 0;
-    const size_t cs_off = (2 * (size_t)pt * row_bytes + 8 + 4 * (size_t)pt + 15) & ~(size_t)15;
-    const size_t smem = a.cs_bulk ? cs_off + (size_t)(pt * cs_row_bytes)
-                                  : 2 * (size_t)pt * row_bytes + 8 + 4 * (size_t)pt;
+    const size_t smem = bulk_smem_layout(pt, row_bytes, GATHER ? 0 : a.plan_width - 5,
+                                         a.cs_bulk ? pt * cs_row_bytes : 0)
+                            .total;
     auto kern = a.head_dim == 128  ? rope_bulk_kernel<T, CS, GATHER, 128>
                 : a.head_dim == 64 ? rope_bulk_kernel<T, CS, GATHER, 64>
                                    : rope_bulk_kernel<T, CS, GATHER, 256>;
     if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
-    const int64_t gx = (width + pt - 1) / pt;
+    // One wave of resident CTAs, each streaming an equal share of its row's
+    // position blocks.
+    const int64_t nblk = (width + pt - 1) / pt;
+    const int64_t fill = std::max<int64_t>(
+        1, ((int64_t)resident_ctas((const void *)kern, kBulkThreads, smem) + rows - 1) / rows);
+    int64_t gx = std::min<int64_t>(nblk, fill);
+    const int64_t per = (nblk + gx - 1) / gx;
+    gx = (nblk + per - 1) / per;
     if (gx > 0x7fffffff || rows > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
     launch_kernel(kern, dim3((unsigned)gx, rows), dim3(kBulkThreads), smem, st, a);
     return check_launch(GATHER ? "gather_rope_bulk_kernel" : "rebuild_rope_bulk_kernel");
   }
 }
 
+// -1: no kernel of this build takes the launch (only for a rebuild from the
+// selection state, which the caller then runs as plan + rebuild).
 template <typename T, typename CS, bool GATHER>
 int launch_rope(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
   if (!legacy_rope_requested()) {
     const int e = launch_rope_bulk<T, CS, GATHER>(a, rows, width, st);
     if (e >= 0) return e;
   }
+  if (a.from_sel) return -1;
   const int row_bytes = a.heads * a.head_dim * (int)sizeof(T);
   int U = row_bytes <= 1024 ? 2 : 1;
   const size_t smem = (size_t)kWarpsRope * 2 * U * 2 * row_bytes;  // double-buffered K+V rows
@@ -819,6 +959,80 @@ extern "C" int dsb_rebuild_compact_kv_from_plan(
   a.err = error_flag;
   return dispatch_rope<false>(a, dtype, rotary_dim > 0 ? cos_sin_dtype : DSB_F32, plan_rows,
                               max_width, as_stream(stream));
+}
+
+extern "C" int dsb_rebuild_working_cache(
+    const void *raw_key, const void *raw_value, void *working_key, void *working_value,
+    const int32_t *row_slots, const int32_t *committed_lens, int32_t rows,
+    const int32_t *sel_chunks, int32_t sel_stride, const int32_t *sel_count, int32_t num_slots,
+    int32_t chunk_size, int32_t history_budget, int32_t plan_width, int64_t *plan,
+    int32_t *history_lens, int32_t *working_lens, const void *cos_sin_cache,
+    int32_t cos_sin_dtype, int64_t cos_sin_stride, int64_t cos_sin_rows, int64_t max_model_len,
+    int32_t num_heads, int32_t head_dim, int32_t working_budget, int32_t rotary_dim,
+    int32_t is_neox_style, int32_t dtype, int32_t *error_flag, void *stream) {
+  int c = common_checks(num_heads, head_dim, rotary_dim, dtype);
+  if (c != DSB_OK) return c;
+  if (rows < 0) return fail(DSB_ERR_INVALID, "negative rows");
+  if (rows == 0) return DSB_OK;
+  if (max_model_len <= 0 || num_slots <= 0)
+    return fail(DSB_ERR_INVALID, "raw sequence, head and head dimensions must be positive");
+  if (chunk_size <= 0 || history_budget <= 0 || sel_stride <= 0)
+    return fail(DSB_ERR_INVALID, "bad chunk size, budget, plan width or selection stride");
+  if (rows > num_slots || history_budget > working_budget)
+    return fail(DSB_ERR_INVALID, "KV plan exceeds the working cache batch or token capacity");
+  if (plan_width != 5 + working_budget / chunk_size)
+    return fail(DSB_ERR_INVALID, "plan width must be 5 + working_budget // chunk_size");
+  if (rotary_dim > 0 && (cos_sin_rows < history_budget || cos_sin_stride < rotary_dim))
+    return fail(DSB_ERR_INVALID, "cos/sin cache must contain all local positions and rotary dimensions");
+  if (!raw_key || !raw_value || !working_key || !working_value || !committed_lens ||
+      !sel_chunks || !sel_count || (rotary_dim > 0 && !cos_sin_cache))
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  RopeArgs a{};
+  a.src_k = raw_key;
+  a.src_v = raw_value;
+  a.dst_k = working_key;
+  a.dst_v = working_value;
+  a.plan_width = plan_width;
+  a.num_slots = num_slots;
+  a.max_model_len = max_model_len;
+  a.working_budget = working_budget;
+  a.chunk = chunk_size;
+  a.max_width = history_budget;
+  a.cos_sin = cos_sin_cache;
+  a.cs_stride = cos_sin_stride;
+  a.cs_rows = cos_sin_rows;
+  a.heads = num_heads;
+  a.head_dim = head_dim;
+  a.rotary_dim = rotary_dim;
+  a.neox = is_neox_style ? 1 : 0;
+  a.err = error_flag;
+  a.from_sel = 1;
+  a.row_slots = row_slots;
+  a.committed_lens = committed_lens;
+  a.sel_chunks = sel_chunks;
+  a.sel_count = sel_count;
+  a.sel_stride = sel_stride;
+  a.history_budget = history_budget;
+  a.plan_out = plan;
+  a.hist_out = history_lens;
+  a.wlen_out = working_lens;
+  const int e = dispatch_rope<false>(a, dtype, rotary_dim > 0 ? cos_sin_dtype : DSB_F32, rows,
+                                     history_budget, as_stream(stream));
+  if (e != -1) return e;
+  // No fused kernel for this shape (or the row kernel was requested): plan,
+  // then rebuild from it.
+  if (plan == nullptr)
+    return fail(DSB_ERR_UNSUPPORTED, "this cache layout needs a plan buffer (two-launch path)");
+  c = dsb_build_history_plan(row_slots, committed_lens, rows, sel_chunks, sel_stride, sel_count,
+                             num_slots, chunk_size, history_budget, plan_width, plan,
+                             history_lens, working_lens, error_flag, stream);
+  if (c != DSB_OK) return c;
+  return dsb_rebuild_compact_kv_from_plan(raw_key, raw_value, working_key, working_value, plan,
+                                          rows, plan_width, cos_sin_cache, cos_sin_dtype,
+                                          cos_sin_stride, cos_sin_rows, num_slots, max_model_len,
+                                          num_heads, head_dim, working_budget, chunk_size,
+                                          history_budget, rotary_dim, is_neox_style, dtype,
+                                          error_flag, stream);
 }
 
 extern "C" int dsb_gather_raw_kv_with_local_rope(

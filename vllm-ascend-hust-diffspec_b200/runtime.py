@@ -10,8 +10,8 @@ Mirrors the hot-path subset of ``DiffSpecDraftCache``
   reference's ``counts.to("cpu")`` sync (:1248) and per-request Python loop
   (:1298-1308) are gone: rows with nothing committed are masked in-kernel.
 * ``prepare_compact_prefill`` / ``rebuild`` — ``_history_plan_host`` +
-  ``rebuild_compact_kv_from_plan`` (:1683-1765) with the plan built on the
-  device (no D2H of selections, no host plan upload).
+  ``rebuild_compact_kv_from_plan`` (:1683-1765) as one launch that computes
+  the plan on the device (no D2H of selections, no host plan upload).
 * ``forward_attention`` — the draft attention (:2024-2134) over the working
   cache through a slot vector (no copy for reordered slots).
 * ``write_raw`` / ``populate_prefill`` — canonical pre-RoPE KV (:1336-1347,
@@ -32,12 +32,11 @@ import torch
 
 from . import _lib
 from .attention import AttentionWorkspace, draft_decode_attention
-from .compact_kv import rebuild_compact_kv_from_plan
+from .compact_kv import rebuild_working_cache
 from .kernels import paged_chunk_head_scores
 from .parallel import gather_head_scores
 from .selection import (
     DiffSpecSelection,
-    build_history_plan,
     select_context_chunks,
     select_rows,
 )
@@ -488,17 +487,12 @@ class DiffSpecDraftCache:
             (committed,) = self._staging.upload(list(committed_seq_lens)[:rows])
         plan = self._plan[:rows]
         hl = self._history_lens[:rows]
-        build_history_plan(
-            self._active_slots_dev, committed, self.sel_chunks, self.sel_count,
+        rebuild_working_cache(
+            self.raw_key, self.raw_value, self.working_key, self.working_value,
+            self._active_slots_dev, committed, self.sel_chunks, self.sel_count, self._cos_sin(),
             chunk_size=self.settings.chunk_size, history_budget=self.history_budget,
-            working_budget=self.settings.token_budget, plan=plan, history_lens=hl,
-            working_lens=self.working_lens,
-        )
-        rebuild_compact_kv_from_plan(
-            self.raw_key, self.raw_value, self.working_key, self.working_value, plan,
-            self._cos_sin(), chunk_size=self.settings.chunk_size,
-            max_width=self.history_budget, rotary_dim=self.rotary_dim,
-            is_neox_style=self.is_neox_style,
+            rotary_dim=self.rotary_dim, is_neox_style=self.is_neox_style, plan=plan,
+            history_lens=hl, working_lens=self.working_lens,
         )
         self._pending_rows = rows
         self._draft_step = 0
