@@ -396,7 +396,10 @@ constexpr int kBulkThreads = 256;
 // Shared-memory layout of the bulk kernel: kBulkStages stages of [K rows, V
 // rows (PT each), PT int32 kinds, the cos/sin rows], then the stages'
 // mbarriers and the row's int64 chunk ids.
-constexpr int kBulkStages = 2;
+#ifndef DSB_BULK_STAGES
+#define DSB_BULK_STAGES 2
+#endif
+constexpr int kBulkStages = DSB_BULK_STAGES;
 struct BulkLayout {
   size_t v, kind, cs, stage;  // offsets inside a stage, and its size
   size_t bars, chunks, total;
@@ -625,11 +628,9 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
   constexpr int kDvShift = DV == 8 ? 3 : DV == 16 ? 4 : 5;
   static_assert((1 << kDvShift) == DV, "head_dim / 8 must be 8, 16 or 32");
 
-  if (tid < 32) {
-    issue(0);
-    if (n_mine > 1) issue(1);
-  }
-  __syncthreads();  // the first two blocks' kinds are visible
+  if (tid < 32)
+    for (int k = 0; k < min(n_mine, kBulkStages); ++k) issue(k);
+  __syncthreads();  // the first blocks' kinds are visible
   for (int i = 0; i < n_mine; ++i) {
     const int s = i % kBulkStages;
     const bool got = mbar_wait(bar0 + 8 * s, (i / kBulkStages) & 1);
