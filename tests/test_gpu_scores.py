@@ -162,4 +162,3 @@ def test_out_of_range_pages_and_query_rows_are_flagged_not_read(dsb, cuda):
     torch.cuda.synchronize()
     assert dsb._lib.read_and_clear_error_flag(cuda) & 2
     assert not out[1].any()
-

@@ -51,11 +51,29 @@ int ensure_smem(const void *kernel, size_t bytes) {
   return DSB_OK;
 }
 
+int resident_ctas(const void *kernel, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void *, int, size_t>, int> known;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return sm_count();
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(dev, kernel, threads, smem);
+  auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+      per_sm <= 0) {
+    (void)cudaGetLastError();
+    per_sm = 1;
+  }
+  return known[key] = per_sm * sm_count();
+}
+
 int max_active_clusters(const void *kernel, int cluster_x, int threads, size_t smem) {
   static std::mutex mu;
   static std::map<std::tuple<int, const void *, int, size_t>, int> known;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   std::lock_guard<std::mutex> lock(mu);
   const auto key = std::make_tuple(dev, kernel, cluster_x, smem);
   auto it = known.find(key);

@@ -70,12 +70,6 @@ __device__ __forceinline__ void cp_async16_zfill(void *smem_dst, const void *gme
     *reinterpret_cast<uint4 *>(smem_dst) = make_uint4(0, 0, 0, 0);
   }
 }
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 template <typename T, int D, int NT>
 constexpr size_t attn_smem_bytes() {

@@ -69,6 +69,10 @@ void launch_kernel_cluster(void (*kernel)(Params...), dim3 grid, dim3 block, siz
   (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Resident CTAs of `kernel` with this block size and dynamic shared memory on
+// the current device (occupancy x SMs, at least one per SM), cached.
+int resident_ctas(const void *kernel, int threads, size_t smem);
+
 // How many clusters of `cluster_x` CTAs with this block size and shared
 // memory can be resident on the device at once (0 if none can; cached per
 // device, kernel, cluster size and smem).
@@ -108,6 +112,14 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
   return r;
+}
+
+// cp.async groups: close the current group; wait until at most N are pending.
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // L2 policy for data read once per pass (the paged target K of the chunk

@@ -17,9 +17,6 @@
 // fused multiply-add, then rounded once to the cache dtype.
 #include <algorithm>
 #include <cstdlib>
-#include <map>
-#include <mutex>
-#include <tuple>
 
 #include "common.cuh"
 #include "plan_row.cuh"
@@ -779,26 +776,6 @@ bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0;
 
 // The bulk kernel when its preconditions hold: 16-bit caches, head_dim 64,
 // 128 or 256, 16-byte aligned bases and at least one K+V row pair per stage.
-// Resident CTAs of `kernel` on this device (occupancy x SMs), cached per
-// device, kernel, block size and shared memory.
-int resident_ctas(const void *kernel, int threads, size_t smem) {
-  static std::mutex mu;
-  static std::map<std::tuple<int, const void *, int, size_t>, int> known;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return sm_count();
-  std::lock_guard<std::mutex> lock(mu);
-  const auto key = std::make_tuple(dev, kernel, threads, smem);
-  auto it = known.find(key);
-  if (it != known.end()) return it->second;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
-      per_sm <= 0) {
-    (void)cudaGetLastError();
-    per_sm = 1;
-  }
-  return known[key] = per_sm * sm_count();
-}
-
 template <typename T, typename CS, bool GATHER>
 int launch_rope_bulk(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
   if constexpr (sizeof(T) != 2) {

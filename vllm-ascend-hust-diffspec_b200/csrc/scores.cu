@@ -18,13 +18,17 @@
 // order, so the per-(row, kv head, chunk) mass is deterministic and
 // independent of how kv heads are sharded across GPUs.
 //
-// Measured alternative, not kept: a persistent TMA-fed variant (a producer
+// Measured alternatives, not kept: a per-warp cp.async ring in shared memory
+// (3 tiles per warp, twice the bytes in flight, block table staged in shared
+// memory) gave the same bits and ran 1 us slower (121.4 vs 120.3 us), and a
+// persistent TMA-fed variant (a producer
 // warp bulk-copying 16 KB pages into a 3 x 64 KB shared-memory ring, eight
 // consumer warps scoring from it) ran at 148 us against this kernel's 133 us
 // on the config-2 retrieval (671 MB): with ~128 KB in flight per SM the bulk
 // copies saw 2-4 us of latency under full load, while 16 register-fed warps
 // per SM keep more, smaller requests in flight.
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 
@@ -34,7 +38,7 @@ namespace dsb {
 namespace {
 
 constexpr int kWarps = 8;
-constexpr int kChunksPerCta = 8;
+constexpr int kMaxChunksPerCta = 16;  // chunks of one row per CTA: 2 .. 16, chosen per launch
 
 template <int D> struct KTile {
   uint4 lo[D / 32];  // token g of the 16-token tile
@@ -190,7 +194,7 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
                         const T *__restrict__ key_cache, const int32_t *__restrict__ block_table,
                         int64_t bt_stride, int64_t bt_cols, const int32_t *__restrict__ seq_lens,
                         int Hq, int Hk, int block_size, int64_t num_blocks, int chunk,
-                        int max_chunks, float scale_log2, float *__restrict__ out,
+                        int max_chunks, int cpc, float scale_log2, float *__restrict__ out,
                         float *__restrict__ out_sum, int32_t *err) {
   pdl_begin();
   constexpr int KS = D / 16;  // mma k-steps over head_dim
@@ -203,8 +207,8 @@ chunk_scores_mma_kernel(const T *__restrict__ query, const float *__restrict__ l
   if (!qrow_ok && threadIdx.x == 0 && blockIdx.x == 0 && seq_lens[b] > 0)
     flag_error(err, DSB_FLAG_POSITION);
   const int L = qrow_ok ? seq_lens[b] : 0;
-  const int c_begin = blockIdx.x * kChunksPerCta;
-  const int n_ch = min(kChunksPerCta, max_chunks - c_begin);
+  const int c_begin = blockIdx.x * cpc;
+  const int n_ch = min(cpc, max_chunks - c_begin);
   if (n_ch <= 0) return;
   const int total = Hk * n_ch;  // items, kv-head major
   const int per_warp = (total + kWarps - 1) / kWarps;
@@ -499,13 +503,37 @@ int validate(const ScoreArgs &a, bool stats) {
   return DSB_OK;
 }
 
+// Chunks per CTA: the per-launch time is about (waves of CTAs) x (items of
+// the busiest warp), so the count minimising that product (the largest such
+// count, for fewer CTAs) is taken; the tail wave and uneven warps cost as
+// much as they weigh.
+int pick_chunks_per_cta(int64_t max_chunks, int64_t rows, int hk, int64_t resident) {
+  int best = 2;
+  int64_t best_cost = INT64_MAX;
+  for (int cpc = 2; cpc <= kMaxChunksPerCta; ++cpc) {
+    const int64_t ctas = (max_chunks + cpc - 1) / cpc * rows;
+    const int64_t waves = (ctas + resident - 1) / resident;
+    const int64_t per_warp = ((int64_t)hk * cpc + kWarps - 1) / kWarps;
+    const int64_t cost = waves * per_warp;
+    if (cost <= best_cost) {
+      best_cost = cost;
+      best = cpc;
+    }
+  }
+  return best;
+}
+
 template <typename T, int D, int NT, bool STATS>
-void launch_mma(const ScoreArgs &a) {
-  dim3 grid((a.max_chunks + kChunksPerCta - 1) / kChunksPerCta, a.B);
-  launch_kernel(chunk_scores_mma_kernel<T, D, NT, STATS>, dim3(grid), dim3(kWarps * 32), 0, a.st,
+int launch_mma(const ScoreArgs &a) {
+  auto kern = chunk_scores_mma_kernel<T, D, NT, STATS>;
+  const int cpc = pick_chunks_per_cta(a.max_chunks, a.B, a.Hk,
+                                      resident_ctas((const void *)kern, kWarps * 32, 0));
+  const dim3 grid((unsigned)((a.max_chunks + cpc - 1) / cpc), a.B);
+  launch_kernel(kern, grid, dim3(kWarps * 32), 0, a.st,
       static_cast<const T *>(a.query), a.lse, a.qidx, a.qrows, static_cast<const T *>(a.kc), a.bt,
-      a.bt_stride, a.bt_cols, a.seq, a.Hq, a.Hk, a.bs, a.nblocks, a.C, a.max_chunks,
+      a.bt_stride, a.bt_cols, a.seq, a.Hq, a.Hk, a.bs, a.nblocks, a.C, a.max_chunks, cpc,
       a.scale * kLog2e, a.out, a.out_sum, a.err);
+  return check_launch("chunk_scores_mma_kernel");
 }
 
 template <typename T, bool STATS>
@@ -517,10 +545,7 @@ int dispatch_typed(const ScoreArgs &a) {
     if (mma_ok) {
       const int nt = group <= 8 ? 1 : 2;
 #define DSB_SC(DD, NN)                                                     \
-  if (a.D == DD && nt == NN) {                                             \
-    launch_mma<T, DD, NN, STATS>(a);                                       \
-    return check_launch("chunk_scores_mma_kernel");                        \
-  }
+  if (a.D == DD && nt == NN) return launch_mma<T, DD, NN, STATS>(a);
       DSB_SC(64, 1) DSB_SC(64, 2) DSB_SC(128, 1) DSB_SC(128, 2) DSB_SC(256, 1) DSB_SC(256, 2)
 #undef DSB_SC
     }
@@ -541,7 +566,7 @@ template <bool STATS>
 int run_scores(const ScoreArgs &a) {
   int v = validate(a, STATS);
   if (v != DSB_OK || a.B == 0 || a.max_chunks == 0) return v;
-  if (a.max_chunks > 65535 * kChunksPerCta || a.B > 65535)
+  if (a.max_chunks > 65535 * 2 || a.B > 65535)
     return fail(DSB_ERR_UNSUPPORTED, "grid too large");
   switch (a.dtype) {
     case DSB_BF16: return dispatch_typed<__nv_bfloat16, STATS>(a);
