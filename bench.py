@@ -76,10 +76,10 @@ PROFILED_TRAFFIC = {"attention": 67_278_592 + 482_816, "rebuild": 65_555_968 + 9
 # DRAM bytes per launch inside a running period (caches not flushed between
 # kernels), from the one-pass launch list `ncu --metrics gpu__time_duration.sum,
 # dram__bytes_read.sum,dram__bytes_write.sum --cache-control none
-# --clock-control none -s 28 -c 27 python bench.py --steps 3 --warmup 3
+# --clock-control none -s 24 -c 23 python bench.py --steps 3 --warmup 3
 # --no-cpu --no-e2e`, averaged over the period's launches of the kind: the
 # working cache stays in L2 between the rebuild and the four draft steps.
-IN_SITU_TRAFFIC = {"attention": 2_372_496, "rebuild": 89_893_248, "scores": 680_339_712}
+IN_SITU_TRAFFIC = {"attention": 2_153_520, "rebuild": 88_181_440, "scores": 680_546_560}
 
 
 def _peaks() -> tuple[float, str]:
