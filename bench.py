@@ -589,35 +589,40 @@ def run_e2e(res, args):
         process_group=res["group"])
     cache.raw_key, cache.raw_value = w.raw_key, w.raw_value  # share the canonical cache
     cache.max_model_len = w.raw_key.shape[1]
-    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
-    h_query, h_lse, h_counts = pin(w.query), pin(w.lse), pin(w.counts)
-    h_dq, h_dk, h_dv = pin(w.dq), pin(w.dk), pin(w.dv)
+    # Each cycle's verify-pass inputs (query, LSE, accepted counts) and each
+    # draft step's q/k/v travel as one pinned host buffer and one copy; the
+    # device tensors are views of the copied bytes.
+    def packed(tensors):
+        flat = [t.reshape(-1).view(torch.uint8) for t in tensors]
+        host = torch.cat([f.cpu() for f in flat]).pin_memory()
+        dev = torch.empty_like(host, device=device)
+        views, o = [], 0
+        for t, f in zip(tensors, flat):
+            views.append(dev[o:o + f.numel()].view(t.dtype).view(t.shape))
+            o += f.numel()
+        return host, dev, views
+
+    h_cycle, d_cycle, (d_query, d_lse, d_counts) = packed([w.query, w.lse, w.counts])
+    h_step, d_step, (d_dq, d_dk, d_dv) = packed([w.dq, w.dk, w.dv])
     h_out = [torch.empty_like(w.out, device="cpu").pin_memory() for _ in range(DEPTH)]
-    d_query, d_lse, d_counts = (torch.empty_like(x) for x in (w.query, w.lse, w.counts))
-    d_dq, d_dk, d_dv = (torch.empty_like(x) for x in (w.dq, w.dk, w.dv))
     out = torch.empty_like(w.out)
     ids = [f"req{i}" for i in range(rows)]
     meta = SimpleNamespace(actual_seq_lengths_q=[5 * (i + 1) for i in range(rows)],
                            seq_lens_list=[CTX] * rows, block_tables=w.block_table, num_prefills=0)
     committed = [[CTX - REJECTED + ACCEPT_PER_CYCLE * c] * rows for c in range(INTERVAL)]
-    h2d = (h_query.numel() * 2 + h_lse.numel() * 4 + h_counts.numel() * 8) * INTERVAL + \
-        (h_dq.numel() + h_dk.numel() + h_dv.numel()) * 2 * INTERVAL * DEPTH
+    h2d = h_cycle.numel() * INTERVAL + h_step.numel() * INTERVAL * DEPTH
     d2h = out.numel() * 2 * INTERVAL * DEPTH
 
     def period():
         for c in range(INTERVAL):
-            d_query.copy_(h_query, non_blocking=True)
-            d_lse.copy_(h_lse, non_blocking=True)
-            d_counts.copy_(h_counts, non_blocking=True)
+            d_cycle.copy_(h_cycle, non_blocking=True)
             cache.begin_target_forward(ids)
             cache.capture_target_attention(d_query, d_lse, w.key_cache, meta, D ** -0.5)
             cache.accept_target_queries(d_counts, is_prefill=False)
             cache.begin_cycle(ids)
             cache.rebuild(committed[c])
             for j in range(DEPTH):
-                d_dq.copy_(h_dq, non_blocking=True)
-                d_dk.copy_(h_dk, non_blocking=True)
-                d_dv.copy_(h_dv, non_blocking=True)
+                d_step.copy_(h_step, non_blocking=True)
                 cache.forward_attention(d_dq, d_dk, d_dv, D ** -0.5, out)
                 h_out[j].copy_(out, non_blocking=True)
             cache.end_cycle()

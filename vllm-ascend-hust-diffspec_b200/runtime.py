@@ -259,6 +259,7 @@ class DiffSpecDraftCache:
         self._cycle_open = False
         self._draft_step = 0
         self._pending_rows = 0
+        self._attn_fast = None  # per-cycle prepared arguments of the draft attention call
         self._target: dict[str, Any] | None = None
         self.target_is_prefill = True
 
@@ -295,10 +296,12 @@ class DiffSpecDraftCache:
         self.set_active_requests(request_ids)
         self._cycle_open = True
         self._draft_step = 0
+        self._attn_fast = None
 
     def end_cycle(self) -> None:
         self._cycle_open = False
         self._pending_rows = 0
+        self._attn_fast = None
 
     # ------------------------------------------------------------ retrieval
     def begin_target_forward(self, request_ids: list[str]) -> None:
@@ -496,6 +499,7 @@ class DiffSpecDraftCache:
         )
         self._pending_rows = rows
         self._draft_step = 0
+        self._attn_fast = None
         return hl
 
     def prepare_compact_prefill(self, metadata: Any, num_tokens: int, *,
@@ -520,13 +524,49 @@ class DiffSpecDraftCache:
             raise RuntimeError("DiffSpec attention called without prepared state")
         if self._draft_step + 1 > self.settings.token_budget - self.history_budget:
             raise RuntimeError("DiffSpec working cache exhausted")
-        draft_decode_attention(
-            query, key, value, self.working_key, self.working_value,
-            self._active_slots_dev, self._history_lens[:rows], scale, output,
-            rows=rows, position_offset=self._draft_step, workspace=self._attn_workspace,
-        )
+        fast = self._attn_fast
+        sig = (query.shape, key.shape, value.shape, output.shape, query.dtype, key.dtype,
+               value.dtype, output.dtype, query.device, key.device, value.device, output.device,
+               float(scale))
+        if (fast is not None and fast[0] == sig and query.is_contiguous() and key.is_contiguous()
+                and value.is_contiguous() and output.is_contiguous()):
+            # The later steps of a cycle repeat the first step's validated call
+            # with new q/k/v/output addresses and the next position offset.
+            fn, head, tail = fast[1], fast[2], fast[3]
+            _lib.check(
+                fn(query.data_ptr(), key.data_ptr(), value.data_ptr(), *head, self._draft_step,
+                   *tail[0], output.data_ptr(), *tail[1], _lib.stream_ptr(self.device)),
+                "dsb_draft_decode_attention",
+            )
+        else:
+            draft_decode_attention(
+                query, key, value, self.working_key, self.working_value,
+                self._active_slots_dev, self._history_lens[:rows], scale, output,
+                rows=rows, position_offset=self._draft_step, workspace=self._attn_workspace,
+            )
+            self._attn_fast = self._prepare_attention_fast(sig, query, output, rows, scale)
         self._draft_step += 1
         return output
+
+    def _prepare_attention_fast(self, sig, query, output, rows, scale):
+        """Arguments of the C call that stay fixed for the rest of the cycle
+        (working caches, slots, history lengths, split scratch), captured after
+        draft_decode_attention validated and ran the cycle's first step."""
+        if not (query.is_contiguous() and output.is_contiguous()):
+            return None
+        lib = _lib.load()
+        ws = self._attn_workspace
+        splits = lib.dsb_draft_attention_default_splits(
+            rows, self.num_kv_heads, self.working_key.shape[2], _lib.sm_count(self.device))
+        hist = self._history_lens[:rows]
+        head = (self.working_key.data_ptr(), self.working_value.data_ptr(),
+                self._active_slots_dev.data_ptr(), hist.data_ptr())
+        tail = ((rows, output.shape[0], self.working_key.shape[0], query.shape[1],
+                 self.num_kv_heads, self.head_dim, self.working_key.shape[2], float(scale),
+                 _lib.dtype_code(query.dtype)),
+                (ws.scratch.data_ptr(), ws.scratch.numel(), ws.counters.data_ptr(), splits,
+                 _lib.error_flag(self.device).data_ptr()))
+        return (sig, lib.dsb_draft_decode_attention, head, tail)
 
     def _cos_sin(self) -> torch.Tensor:
         cs = self.cos_sin_cache
