@@ -260,6 +260,8 @@ class DiffSpecDraftCache:
         self._draft_step = 0
         self._pending_rows = 0
         self._attn_fast = None  # per-cycle prepared arguments of the draft attention call
+        self._rebuild_fast = None  # prepared arguments of the plan + rebuild call
+        self._active_ids: list[str] | None = None
         self._target: dict[str, Any] | None = None
         self.target_is_prefill = True
 
@@ -267,6 +269,8 @@ class DiffSpecDraftCache:
     def set_active_requests(self, request_ids: list[str]) -> None:
         """Keep canonical rows stable across batch reorder and cancellation
         (diffspec/runtime.py:755-778)."""
+        if self._active_ids is not None and request_ids == self._active_ids:
+            return  # same batch in the same order: slots unchanged
         active = set(request_ids)
         released = []
         for request_id in list(self._request_slots):
@@ -284,6 +288,7 @@ class DiffSpecDraftCache:
                     self._request_slots[request_id] = next(free)
                 except StopIteration as error:
                     raise RuntimeError("DiffSpec canonical request slots are exhausted") from error
+        self._active_ids = list(request_ids)
         slots = [self._request_slots[r] for r in request_ids]
         if slots != self._active_slots or self._active_slots_dev is None:
             self._active_slots = slots
@@ -490,13 +495,36 @@ class DiffSpecDraftCache:
             (committed,) = self._staging.upload(list(committed_seq_lens)[:rows])
         plan = self._plan[:rows]
         hl = self._history_lens[:rows]
-        rebuild_working_cache(
-            self.raw_key, self.raw_value, self.working_key, self.working_value,
-            self._active_slots_dev, committed, self.sel_chunks, self.sel_count, self._cos_sin(),
-            chunk_size=self.settings.chunk_size, history_budget=self.history_budget,
-            rotary_dim=self.rotary_dim, is_neox_style=self.is_neox_style, plan=plan,
-            history_lens=hl, working_lens=self.working_lens,
-        )
+        cs = self._cos_sin()
+        fast = self._rebuild_fast
+        sig = (rows, self._active_slots_dev.data_ptr(), self.raw_key.data_ptr(),
+               self.raw_value.data_ptr(), cs.data_ptr(), cs.dtype, cs.shape, cs.stride(0))
+        if (fast is not None and fast[0] == sig and committed.dtype == torch.int32
+                and committed.is_contiguous() and committed.device == self.device):
+            # Same batch, caches and table as a validated call: only the
+            # committed lengths change.
+            _lib.check(fast[1](*fast[2], committed.data_ptr(), *fast[3], _lib.stream_ptr(self.device)),
+                       "dsb_rebuild_working_cache")
+        else:
+            rebuild_working_cache(
+                self.raw_key, self.raw_value, self.working_key, self.working_value,
+                self._active_slots_dev, committed, self.sel_chunks, self.sel_count, cs,
+                chunk_size=self.settings.chunk_size, history_budget=self.history_budget,
+                rotary_dim=self.rotary_dim, is_neox_style=self.is_neox_style, plan=plan,
+                history_lens=hl, working_lens=self.working_lens,
+            )
+            lib = _lib.load()
+            head = (self.raw_key.data_ptr(), self.raw_value.data_ptr(), self.working_key.data_ptr(),
+                    self.working_value.data_ptr(), self._active_slots_dev.data_ptr())
+            tail = (rows, self.sel_chunks.data_ptr(), self.sel_chunks.shape[1],
+                    self.sel_count.data_ptr(), self.raw_key.shape[0], self.settings.chunk_size,
+                    self.history_budget, plan.shape[1], plan.data_ptr(), hl.data_ptr(),
+                    self.working_lens.data_ptr(), cs.data_ptr(), _lib.dtype_code(cs.dtype),
+                    cs.stride(0), cs.shape[0], self.raw_key.shape[1], self.num_kv_heads,
+                    self.head_dim, self.working_key.shape[2], self.rotary_dim,
+                    int(bool(self.is_neox_style)), _lib.dtype_code(self.raw_key.dtype),
+                    _lib.error_flag(self.device).data_ptr())
+            self._rebuild_fast = (sig, lib.dsb_rebuild_working_cache, head, tail)
         self._pending_rows = rows
         self._draft_step = 0
         self._attn_fast = None
