@@ -237,6 +237,26 @@ int64_t dsb_draft_attention_scratch_floats(int32_t rows, int32_t num_query_heads
                                            int32_t num_kv_heads, int32_t head_dim,
                                            int32_t num_splits);
 
+/* Draft-layer KV projection with the canonical raw-KV write in its epilogue:
+ * the producer side of the draft-context path, replacing the projection ->
+ * temporary -> _write_raw copy of diffspec/runtime.py:1602-1618 (fed by the
+ * Eagle3 sink op, diffspec/vllm_patch.py:132-178).  out[t, f] =
+ * sum_k hidden[t, k] * weight[f, k] (fp32 accumulation on the tensor cores,
+ * rounded once to the cache dtype) for f < 2 * num_kv_heads * head_dim; the
+ * first half of each output row is K, the second V.  The same values go to
+ * raw_key / raw_value [num_slots, max_model_len, num_kv_heads, head_dim] at
+ * [slots[t], positions[t]] (slots[t] < 0: padding, no cache row; bad slots or
+ * positions set DSB_FLAG_SLOT / DSB_FLAG_POSITION).  hidden [tokens,
+ * hidden_size] and weight [2 * num_kv_heads * head_dim, hidden_size] are
+ * contiguous and 16-byte aligned; hidden_size is a multiple of 64 up to 4096
+ * and num_kv_heads * head_dim a multiple of 128.  out (nullable) is
+ * [tokens, 2 * num_kv_heads * head_dim]. */
+int dsb_kv_projection_write_raw(
+    const void *hidden, int32_t tokens, int32_t hidden_size, const void *weight,
+    int32_t num_kv_heads, int32_t head_dim, const int32_t *slots, const int64_t *positions,
+    void *raw_key, void *raw_value, int32_t num_slots, int64_t max_model_len, int32_t dtype,
+    void *out, int32_t *error_flag, void *stream);
+
 /* Committed-query pick of the retrieval hook
  * (_accept_target_queries, diffspec/runtime.py:1211-1276): for each of `rows`
  * real requests with query span [query_ends[r-1], query_ends[r]) and count

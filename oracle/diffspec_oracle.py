@@ -418,3 +418,16 @@ def write_raw(raw_key, raw_value, slots, positions, key, value):
             continue
         raw_key[int(slot), int(pos)] = key[i]
         raw_value[int(slot), int(pos)] = value[i]
+
+
+def kv_projection_write_raw(hidden, weight, slots, positions, raw_key, raw_value, dtype="bf16"):
+    """The draft layer's K/V projection (vLLM linear: ``hidden @ weight.T``,
+    weight rows K then V) followed by _write_raw (diffspec/runtime.py:1602-1618),
+    in place on the raw caches.  Returns the projected rows rounded to `dtype`
+    (fp32 products and sums, one rounding)."""
+    kv = round_to(hidden.astype(np.float32) @ weight.astype(np.float32).T, dtype)
+    hk, d = raw_key.shape[2], raw_key.shape[3]
+    half = hk * d
+    write_raw(raw_key, raw_value, slots, positions, kv[:, :half].reshape(-1, hk, d),
+              kv[:, half:].reshape(-1, hk, d))
+    return kv

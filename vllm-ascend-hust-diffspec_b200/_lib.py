@@ -86,6 +86,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _P, _P, _P, _P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _I32,
          _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P],
     ),
+    "dsb_kv_projection_write_raw": (
+        ctypes.c_int,
+        [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _P, _I32, _I64, _I32, _P, _P, _P],
+    ),
     "dsb_gather_raw_kv_with_local_rope": (
         ctypes.c_int,
         [_P, _P, _I64, _I32, _I32, _I32, _P, _I64, _I64, _P, _I32, _I32, _P, _I32, _I64, _I64,

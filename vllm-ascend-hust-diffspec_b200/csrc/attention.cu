@@ -34,6 +34,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "tma_umma.cuh"
 
 namespace dsb {
 namespace {
@@ -506,14 +507,6 @@ constexpr size_t tma_smem_bytes() {
          sizeof(float) * 2 * W * NT * 8 + sizeof(T) * W * 2 * 16 * NT * 8;
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -529,34 +522,6 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
 __device__ __forceinline__ uint32_t swz(uint32_t base, int box_bytes, int row, int col) {
   const int box = col >> 6, chunk = (col & 63) >> 3;
   return base + box * box_bytes + row * 128 + (((chunk ^ (row & 7)) << 4) | ((col & 7) << 1));
-}
-
-// Thread-block-cluster primitives for the split merge: the CTAs of one
-// (row, kv head) form a cluster along x; rank r writes its partial into the
-// shared memory of rank 0 (distributed shared memory), ordered by the
-// cluster barrier.
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void st_cluster(uint32_t addr, const float4 &v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x),
-               "f"(v.y), "f"(v.z), "f"(v.w)
-               : "memory");
-}
-__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-// Every thread of every CTA in the cluster arrives (release) and waits
-// (acquire).  Only called on paths that all CTAs of a cluster take.
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // Shared-memory layout of the TMA kernel's epilogue: the per-warp O rows,
@@ -1042,65 +1007,6 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
 constexpr int kUmmaThreads = 128;
 constexpr int kUmmaN = 16;  // query heads per kv head, padded (tcgen05 N)
 
-// UMMA shared-memory descriptor for a 128-byte-swizzled operand.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) /* version */ |
-         (2ull << 61) /* SWIZZLE_128B */;
-}
-// Instruction descriptor: kind::f16, fp32 accumulate, M = 128, N = 16.
-template <typename T>
-__device__ __forceinline__ uint32_t umma_idesc(bool a_mn_major) {
-  constexpr uint32_t fmt = std::is_same<T, __half>::value ? 0u : 1u;  // F16 = 0, BF16 = 1
-  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((a_mn_major ? 1u : 0u) << 15) |
-         ((uint32_t)(kUmmaN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                     bool accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate ? 1u : 0u)
-      : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                 "=r"(r[6]), "=r"(r[7])
-               : "r"(addr));
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-                 "=r"(r[14]), "=r"(r[15])
-               : "r"(addr + 8));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_st16(uint32_t addr, const float (&v)[16]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(addr),
-               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
-               : "memory");
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(addr + 8),
-               "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-               "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
-               "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
-               : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
 template <int NS> struct UmmaCfg {
   static constexpr int D = 128, kStageTok = 128, kBoxes = 2;
   static constexpr int kBoxBytes = 128 * kStageTok;               // [128 rows][64 cols] x 2 B
@@ -1468,38 +1374,6 @@ draft_attention_umma_kernel(const __grid_constant__ CUtensorMap tmk,
   finish_split<T, D, GPF, CL>(a, fold, out, row, kvh, split, active, group,
                               reinterpret_cast<float *>(smem + Cfg::kXOffset),
                               e_l + 4 * GP, &s_last);
-}
-
-// ---- host: tensor maps and the kernel choice shared by both entry points
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// 2-D map over a working cache viewed as [slots * kv_heads * W rows, D]:
-// 64-column x box_rows boxes with the 128-byte swizzle.
-bool encode_kv_map(CUtensorMap *map, const void *base, int64_t rows, int head_dim, int dtype,
-                   int box_rows) {
-  auto fn = tensor_map_encoder();
-  if (fn == nullptr || reinterpret_cast<uintptr_t>(base) % 16 || rows <= 0 || rows > 0x7fffffff)
-    return false;
-  cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, dtype == DSB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        2, const_cast<void *>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
 }
 
 bool legacy_attention_requested() {

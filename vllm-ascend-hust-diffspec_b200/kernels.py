@@ -18,6 +18,7 @@ __all__ = [
     "stats_to_head_scores",
     "finalize_chunk_scores",
     "gather_raw_kv_with_local_rope",
+    "kv_projection_write_raw",
 ]
 
 
@@ -372,3 +373,55 @@ def gather_raw_kv_with_local_rope(
         _lib.stream_ptr(device),
     )
     return out_key, out_value
+
+
+def kv_projection_write_raw(
+    hidden: torch.Tensor,
+    weight: torch.Tensor,
+    slots: torch.Tensor,
+    positions: torch.Tensor,
+    raw_key: torch.Tensor,
+    raw_value: torch.Tensor,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Draft-layer K/V projection that also stores its rows in the raw cache.
+
+    ``out = hidden @ weight.T`` (``hidden [T, hidden_size]``, ``weight
+    [2 * Hk * D, hidden_size]``: K rows then V rows; fp32 accumulation, one
+    rounding), returned as ``[T, 2 * Hk * D]``; row ``t``'s K and V halves
+    are also written, pre-RoPE, to ``raw_key/raw_value [S, max_model_len, Hk,
+    D]`` at ``[slots[t], positions[t]]`` (``slots[t] < 0``: padding).  This
+    is the projection + ``_write_raw`` pair of diffspec/runtime.py:1602-1618
+    in one launch.
+    """
+    if hidden.ndim != 2 or weight.ndim != 2 or weight.shape[1] != hidden.shape[1]:
+        raise ValueError("hidden must be [T, hidden] and weight [2 * Hk * D, hidden]")
+    if raw_key.ndim != 4 or raw_key.shape != raw_value.shape:
+        raise ValueError("raw key/value must have matching 4-D shapes")
+    num_slots, max_model_len, hk, d = raw_key.shape
+    if weight.shape[0] != 2 * hk * d:
+        raise ValueError("weight rows must be 2 * kv_heads * head_dim")
+    if not (hidden.dtype == weight.dtype == raw_key.dtype == raw_value.dtype):
+        raise ValueError("hidden, weight and raw caches must share a dtype")
+    tokens = hidden.shape[0]
+    if slots.shape[0] < tokens or positions.shape[0] < tokens:
+        raise ValueError("slots/positions must cover every token")
+    device = _lib.require_cuda(hidden, weight, slots, positions, raw_key, raw_value)
+    if out is None:
+        out = torch.empty((tokens, weight.shape[0]), dtype=hidden.dtype, device=device)
+    elif out.shape != (tokens, weight.shape[0]) or out.dtype != hidden.dtype or not out.is_contiguous():
+        raise ValueError("out must be contiguous [T, 2 * Hk * D] in the hidden dtype")
+    hidden = hidden.contiguous()
+    weight = weight.contiguous()
+    slots = slots.to(torch.int32).contiguous()
+    positions = positions.to(torch.int64).contiguous()
+    if not (raw_key.is_contiguous() and raw_value.is_contiguous()):
+        raise ValueError("raw caches must be contiguous")
+    _lib.call(
+        "dsb_kv_projection_write_raw",
+        _lib.ptr(hidden), tokens, hidden.shape[1], _lib.ptr(weight), hk, d, _lib.ptr(slots),
+        _lib.ptr(positions), _lib.ptr(raw_key), _lib.ptr(raw_value), num_slots, max_model_len,
+        _lib.dtype_code(hidden.dtype), _lib.ptr(out), _lib.ptr(_lib.error_flag(device)),
+        _lib.stream_ptr(device),
+    )
+    return out
