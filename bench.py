@@ -779,6 +779,73 @@ def run_only(args):
         raise SystemExit(1)
 
 
+def run_kv_projection(args):
+    """Time the draft-layer K/V projection + raw-cache write (config 5 decode
+    step: 16 tokens, Eagle3 qkv input 4096, 4 kv heads x 128) against the
+    library-call path it replaces (cuBLAS matmul, then the raw-cache scatter).
+    The launches cycle through 24 weight copies (201 MB, more than L2), so
+    every launch streams its weight from HBM."""
+    import torch
+
+    dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(99)
+    tokens, hidden, hk = 16, 4096, HK
+    bf = torch.bfloat16
+    weights = [(torch.randn((2 * hk * D, hidden), generator=g, device=device) / 64).to(bf)
+               for _ in range(24)]
+    h = torch.randn((tokens, hidden), generator=g, device=device).to(bf)
+    rk = torch.zeros((B_GROUP, 4096, hk, D), dtype=bf, device=device)
+    rv = torch.zeros_like(rk)
+    slots = torch.arange(tokens, dtype=torch.int32, device=device)
+    pos = torch.full((tokens,), 1000, dtype=torch.int64, device=device)
+    out = torch.empty((tokens, 2 * hk * D), dtype=bf, device=device)
+
+    def ours(i):
+        dsb.kernels.kv_projection_write_raw(h, weights[i % 24], slots, pos, rk, rv, out=out)
+
+    def reference(i):
+        kv = h @ weights[i % 24].t()
+        rk[slots.long(), pos] = kv[:, : hk * D].view(tokens, hk, D)
+        rv[slots.long(), pos] = kv[:, hk * D:].view(tokens, hk, D)
+
+    def time_graph(fn):
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            for i in range(24):
+                fn(i)
+        torch.cuda.current_stream(device).wait_stream(s)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(24):
+                fn(i)
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) * 1e3 / (args.steps * 24)
+
+    ours_us = time_graph(ours)
+    assert dsb._lib.read_and_clear_error_flag(device) == 0
+    ref_us = time_graph(reference)
+    nbytes = 2 * hk * D * hidden * 2 + tokens * hidden * 2 + 2 * tokens * 2 * hk * D * 2
+    peak, peak_kind = _peaks()
+    gbs = nbytes / (ours_us * 1e-6) / 1e9
+    print(json.dumps(dict(mode="kv_projection", tokens=tokens, hidden=hidden, kv_heads=hk,
+                          head_dim=D, dtype="bf16", bytes_per_launch=nbytes,
+                          us_per_launch=round(ours_us, 3), achieved_gbs=round(gbs, 1),
+                          frac_of_hbm_peak=round(gbs / peak, 4), peak_kind=peak_kind,
+                          cublas_matmul_plus_scatter_us=round(ref_us, 3))))
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -790,10 +857,14 @@ def main():
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end API leg")
     p.add_argument("--only", choices=["prepare", "scores", "select", "rebuild", "attention"],
                    help="launch one kernel kind eagerly (for profiler captures)")
+    p.add_argument("--kv-projection", action="store_true",
+                   help="time the K/V projection + raw-cache write (config 5 decode step)")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.only:
+    if args.kv_projection:
+        run_kv_projection(args)
+    elif args.only:
         run_only(args)
     elif args.impl == "reference":
         emit_reference(args)
