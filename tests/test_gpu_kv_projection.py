@@ -12,6 +12,15 @@ from oracle import diffspec_oracle as O
 pytestmark = pytest.mark.gpu
 
 _T = {"bf16": torch.bfloat16, "f16": torch.float16}
+
+
+@pytest.fixture(autouse=True, params=["ranks16", "ranks8"])
+def cluster_size(request, monkeypatch):
+    """Every case with the default 16-CTA split-K clusters and with the 8-CTA
+    ones (DSB_KV_PROJECTION_RANKS8=1)."""
+    if request.param == "ranks8":
+        monkeypatch.setenv("DSB_KV_PROJECTION_RANKS8", "1")
+    return request.param
 _FRAC = {"bf16": 7, "f16": 10}  # fraction bits of the stored type
 
 

@@ -16,14 +16,19 @@
 // 128-byte swizzle, brought in by TMA; fp32 accumulators in tensor memory
 // (tcgen05.mma issued by one thread, tcgen05.commit to an mbarrier).  A decode
 // step is weight-streaming bound (16 tokens against a [2 Hk D, K] weight), so
-// K is split over a cluster of 8 CTAs: each loads all of its k-blocks at once
-// (up to 8 x 18 KB in flight) and reduces into its own accumulator; the
-// partials meet in distributed shared memory, each rank summing 2 of the 16
-// tokens over the ranks in rank order (deterministic), and writes them.
+// K is split over a cluster of 16 CTAs (8 where 16 cannot be scheduled): each
+// loads all of its k-blocks at once and reduces into its own accumulator; the
+// partials meet in distributed shared memory, each rank summing 16 / ranks
+// of the tile's tokens over the ranks in rank order (deterministic), and
+// writes them.
 // Every wait is bounded; a wait that runs out sets DSB_FLAG_TIMEOUT, and the
 // CTA still frees its tensor memory and takes part in the cluster barriers.
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "tma_umma.cuh"
@@ -32,14 +37,21 @@ namespace dsb {
 namespace {
 
 constexpr int kPjThreads = 128;           // 4 warps: one TMEM lane per thread
-constexpr int kPjRanks = 8;               // split-K: one cluster of 8 CTAs per tile
-constexpr int kPjMaxKb = 8;               // 64-wide k-blocks per rank (K <= 4096)
 constexpr int kPjTok = 16;                // tokens per tile (the MMA's N)
+constexpr int kPjMaxK = 4096;             // hidden size limit: 64 k-blocks over the ranks
 constexpr int kPjABytes = 128 * 64 * 2;   // weight box [128 rows][64 cols]
 constexpr int kPjBBytes = kPjTok * 64 * 2;  // hidden box [16 rows][64 cols]
-constexpr int kPjBarOff = kPjMaxKb * (kPjABytes + kPjBBytes);
-constexpr int kPjXchOff = kPjBarOff + 128;  // [ranks][128 features][2 tokens] fp32
-constexpr size_t kPjSmem = 1024 + kPjXchOff + sizeof(float) * kPjRanks * 128 * 2;
+
+// Split-K over a cluster of RANKS CTAs (16 where the device schedules such
+// clusters, else 8): every rank holds all of its k-blocks at once and, after
+// the exchange, sums 16 / RANKS of the tile's tokens.
+template <int RANKS> struct PjCfg {
+  static constexpr int kMaxKb = kPjMaxK / 64 / RANKS;  // k-blocks per rank
+  static constexpr int kTpr = kPjTok / RANKS;          // tokens each rank sums
+  static constexpr int kBarOff = kMaxKb * (kPjABytes + kPjBBytes);
+  static constexpr int kXchOff = kBarOff + 8 * (kMaxKb + 1) + 16;  // [ranks][128][kTpr] fp32
+  static constexpr size_t kSmem = 1024 + kXchOff + sizeof(float) * RANKS * 128 * kTpr;
+};
 
 struct PjArgs {
   const int32_t *slots;
@@ -50,18 +62,26 @@ struct PjArgs {
   int32_t *err;
 };
 
-template <typename T>
+// DSB_KV_PROJECTION_RANKS8=1 keeps the 8-CTA clusters (both are tested).
+bool pj_ranks8_requested() {
+  const char *v = std::getenv("DSB_KV_PROJECTION_RANKS8");
+  return v != nullptr && v[0] == '1';
+}
+
+template <typename T, int RANKS>
 __global__ void __launch_bounds__(kPjThreads)
 kv_projection_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap th,
                      const PjArgs a) {
+  using Cfg = PjCfg<RANKS>;
+  constexpr int kPjMaxKb = Cfg::kMaxKb, kPjRanks = RANKS, kTpr = Cfg::kTpr;
   extern __shared__ uint8_t pj_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(pj_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t s_a = smem_u32(smem), s_b = s_a + kPjMaxKb * kPjABytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kPjBarOff);  // full[kPjMaxKb], done
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff);  // full[kPjMaxKb], done
   const uint32_t full0 = smem_u32(bars), done = full0 + 8 * kPjMaxKb;
   uint32_t *s_tmem = reinterpret_cast<uint32_t *>(bars + kPjMaxKb + 1);
-  float *xch = reinterpret_cast<float *>(smem + kPjXchOff);
+  float *xch = reinterpret_cast<float *>(smem + Cfg::kXchOff);
   __shared__ int s_abort;
   const int tid = threadIdx.x, warp = tid >> 5;
 
@@ -136,14 +156,15 @@ kv_projection_kernel(const __grid_constant__ CUtensorMap tw, const __grid_consta
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" ::"r"(tmem) : "memory");
 
-  // Rank q sums tokens 2q and 2q + 1 over the ranks: send them there.
+  // Rank q sums tokens q * kTpr .. q * kTpr + kTpr - 1 over the ranks: send
+  // them there.
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");  // every rank is running
   const uint32_t x0 = smem_u32(xch);
 #pragma unroll
   for (int q = 0; q < kPjRanks; ++q) {
-    const uint32_t remote = cluster_map(x0, (uint32_t)q) + 4u * (uint32_t)((rank * 128 + tid) * 2);
-    st_cluster(remote, acc[2 * q]);
-    st_cluster(remote + 4u, acc[2 * q + 1]);
+    const uint32_t remote = cluster_map(x0, (uint32_t)q) + 4u * (uint32_t)((rank * 128 + tid) * kTpr);
+#pragma unroll
+    for (int j = 0; j < kTpr; ++j) st_cluster(remote + 4u * j, acc[q * kTpr + j]);
   }
   cluster_sync_all();  // every partial delivered
 
@@ -151,12 +172,12 @@ kv_projection_kernel(const __grid_constant__ CUtensorMap tw, const __grid_consta
   T *raw_k = static_cast<T *>(a.raw_k), *raw_v = static_cast<T *>(a.raw_v);
   const int g = f0 + tid;  // output feature
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int t = t0 + 2 * rank + j;
+  for (int j = 0; j < kTpr; ++j) {
+    const int t = t0 + kTpr * rank + j;
     if (t >= a.T) continue;
     float v = 0.f;
 #pragma unroll
-    for (int r = 0; r < kPjRanks; ++r) v += xch[(r * 128 + tid) * 2 + j];
+    for (int r = 0; r < kPjRanks; ++r) v += xch[(r * 128 + tid) * kTpr + j];
     const T y = Elem<T>::from_f(v);
     if (out != nullptr) out[(int64_t)t * a.N + g] = y;
     const int slot = a.slots[t];
@@ -172,6 +193,39 @@ kv_projection_kernel(const __grid_constant__ CUtensorMap tw, const __grid_consta
   }
 }
 
+// 16-CTA clusters are beyond the portable size: allowed per kernel once, and
+// used only if the device can schedule one.
+bool allow_cluster16(const void *kernel) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void *>, bool> known;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(dev, kernel);
+  auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  const bool ok =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  if (!ok) (void)cudaGetLastError();
+  known[key] = ok;
+  return ok;
+}
+
+template <typename T, int RANKS>
+int launch_ranks(const CUtensorMap &tw, const CUtensorMap &th, const PjArgs &a, cudaStream_t st,
+                 bool &launched) {
+  launched = false;
+  auto kern = kv_projection_kernel<T, RANKS>;
+  constexpr size_t smem = PjCfg<RANKS>::kSmem;
+  if (RANKS > 8 && !allow_cluster16((const void *)kern)) return DSB_OK;
+  if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
+  if (max_active_clusters((const void *)kern, RANKS, kPjThreads, smem) <= 0) return DSB_OK;
+  const dim3 grid(RANKS, a.N / 128, (a.T + kPjTok - 1) / kPjTok);
+  launch_kernel_cluster(kern, grid, dim3(kPjThreads), smem, st, RANKS, tw, th, a);
+  launched = true;
+  return check_launch("kv_projection_kernel");
+}
+
 template <typename T>
 int launch_kv_projection(const void *hidden, const void *weight, const PjArgs &a, int dtype,
                          cudaStream_t st) {
@@ -179,13 +233,12 @@ int launch_kv_projection(const void *hidden, const void *weight, const PjArgs &a
   if (!encode_kv_map(&tw, weight, a.N, a.K, dtype, 128) ||
       !encode_kv_map(&th, hidden, a.T, a.K, dtype, kPjTok))
     return fail(DSB_ERR_UNSUPPORTED, "no tensor map for the weight or hidden rows");
-  auto kern = kv_projection_kernel<T>;
-  if (int e = ensure_smem((const void *)kern, kPjSmem); e != DSB_OK) return e;
-  if (max_active_clusters((const void *)kern, kPjRanks, kPjThreads, kPjSmem) <= 0)
-    return fail(DSB_ERR_UNSUPPORTED, "a cluster of 8 projection CTAs does not fit on this device");
-  const dim3 grid(kPjRanks, a.N / 128, (a.T + kPjTok - 1) / kPjTok);
-  launch_kernel_cluster(kern, grid, dim3(kPjThreads), kPjSmem, st, kPjRanks, tw, th, a);
-  return check_launch("kv_projection_kernel");
+  bool launched = false;
+  if (!pj_ranks8_requested()) {
+    if (int e = launch_ranks<T, 16>(tw, th, a, st, launched); e != DSB_OK || launched) return e;
+  }
+  if (int e = launch_ranks<T, 8>(tw, th, a, st, launched); e != DSB_OK || launched) return e;
+  return fail(DSB_ERR_UNSUPPORTED, "a cluster of 8 projection CTAs does not fit on this device");
 }
 
 }  // namespace
@@ -209,7 +262,7 @@ extern "C" int dsb_kv_projection_write_raw(const void *hidden, int32_t tokens, i
   const int64_t kv_feats = (int64_t)num_kv_heads * head_dim;
   if (kv_feats % 128)
     return fail(DSB_ERR_UNSUPPORTED, "num_kv_heads * head_dim must be a multiple of 128");
-  if (hidden_size <= 0 || hidden_size % 64 || hidden_size > 64 * kPjMaxKb * kPjRanks)
+  if (hidden_size <= 0 || hidden_size % 64 || hidden_size > kPjMaxK)
     return fail(DSB_ERR_UNSUPPORTED, "hidden_size must be a multiple of 64 and at most 4096");
   if ((tokens + kPjTok - 1) / kPjTok > 65535 || 2 * kv_feats / 128 > 65535)
     return fail(DSB_ERR_UNSUPPORTED, "grid too large");
