@@ -90,3 +90,26 @@ def test_bad_cache_cells_are_flagged_and_skipped(dsb, cuda):
     assert flag & 1 and flag & 2  # slot and position bits
     assert torch.equal(rk[0, 3].reshape(-1), out[0, :d]) and torch.equal(rk[2, 9].reshape(-1), out[3, :d])
     assert int((rk != 0).sum()) == 2 * d and int((rv != 0).sum()) == 2 * d
+
+
+def test_runtime_projection_writes_the_draft_cache(dsb, cuda):
+    """DiffSpecDraftCache.project_and_write_raw fills its own raw caches with
+    the rows the kernel returns."""
+    settings = dsb.runtime.DiffSpecSettings(16, 256, 4, 4, 4, 0.7, False)
+    cache = dsb.runtime.DiffSpecDraftCache(settings, max_num_reqs=4, max_model_len=64, num_kv_heads=2,
+                                           head_dim=64, target_num_layers=2, dtype=torch.bfloat16,
+                                           device=cuda,
+                                           cos_sin_cache=torch.zeros((256, 64), device=cuda).bfloat16())
+    cache.raw_key.zero_()
+    cache.raw_value.zero_()
+    g = torch.Generator(device="cpu").manual_seed(3)
+    h = torch.randn((3, 512), generator=g).bfloat16().to(cuda)
+    w = torch.randn((256, 512), generator=g).bfloat16().to(cuda)
+    slots = torch.tensor([2, 0, 3], dtype=torch.int32, device=cuda)
+    pos = torch.tensor([5, 63, 0], dtype=torch.int64, device=cuda)
+    out = cache.project_and_write_raw(slots, pos, h, w)
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+    for t in range(3):
+        s, p = int(slots[t]), int(pos[t])
+        assert torch.equal(cache.raw_key[s, p].reshape(-1), out[t, :128])
+        assert torch.equal(cache.raw_value[s, p].reshape(-1), out[t, 128:])

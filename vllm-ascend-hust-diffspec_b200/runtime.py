@@ -15,7 +15,8 @@ Mirrors the hot-path subset of ``DiffSpecDraftCache``
 * ``forward_attention`` — the draft attention (:2024-2134) over the working
   cache through a slot vector (no copy for reordered slots).
 * ``write_raw`` / ``populate_prefill`` — canonical pre-RoPE KV (:1336-1347,
-  :1602-1618).
+  :1602-1618); ``project_and_write_raw`` — the draft layer's K/V projection
+  with that write in its epilogue.
 
 Host-visible counters that depend on device data (retrievals run, rows with
 nothing committed) live on the device and are read only by
@@ -33,7 +34,7 @@ import torch
 from . import _lib
 from .attention import AttentionWorkspace, draft_decode_attention
 from .compact_kv import rebuild_working_cache
-from .kernels import paged_chunk_head_scores
+from .kernels import kv_projection_write_raw, paged_chunk_head_scores
 from .parallel import gather_head_scores
 from .selection import (
     DiffSpecSelection,
@@ -471,6 +472,15 @@ class DiffSpecDraftCache:
             self.max_model_len, self.num_kv_heads, self.head_dim, _lib.dtype_code(self.dtype),
             _lib.ptr(_lib.error_flag(self.device)), _lib.stream_ptr(self.device),
         )
+
+    def project_and_write_raw(self, slots: torch.Tensor, positions: torch.Tensor,
+                              hidden: torch.Tensor, weight: torch.Tensor,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+        """The draft layer's K/V projection (``hidden @ weight.T``, weight rows K
+        then V) with the raw-cache write of write_raw in the same launch; returns
+        the projected ``[tokens, 2 * Hk * D]`` rows (pre-RoPE)."""
+        return kv_projection_write_raw(hidden, weight, slots, positions, self.raw_key,
+                                       self.raw_value, out)
 
     def populate_prefill(self, request_rows: list[int], absolute_positions: torch.Tensor,
                          key: torch.Tensor, value: torch.Tensor) -> None:
