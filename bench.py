@@ -109,7 +109,9 @@ def algorithmic_bytes(retrieval_lens, history_lens_per_cycle, hk_local, group_re
 class Workload:
     """Device buffers for one rank: `rows` requests x `hk` local kv heads."""
 
-    def __init__(self, torch, dsb, device, rows, hk_local, hq_local, seed):
+    def __init__(self, torch, dsb, device, rows, hk_local, hq_local, seed, ctx=None):
+        CTX = ctx or globals()["CTX"]  # noqa: N806 - the context length of this workload
+        self.ctx = CTX
         self.torch, self.dsb, self.device = torch, dsb, device
         self.rows, self.hk, self.hq = rows, hk_local, hq_local
         g = torch.Generator(device=device)
@@ -167,7 +169,7 @@ class Workload:
         for r in range(self.rows):
             q_root = self.query[5 * r + (5 - REJECTED) - 1].float()       # committed query
             target = q_root.view(self.hk, group, D).mean(1)                 # [hk, D]
-            chunks = torch.randperm(CTX // CHUNK - 1, generator=g, device=self.device)[:PLANTED]
+            chunks = torch.randperm(self.ctx // CHUNK - 1, generator=g, device=self.device)[:PLANTED]
             tok = (chunks[:, None] * CHUNK + torch.arange(CHUNK, device=self.device)).reshape(-1)
             pages = self.block_table[r].long()[tok // PAGE]
             noise = 0.1 * torch.randn((tok.numel(), self.hk, D), generator=g, device=self.device)
@@ -178,10 +180,10 @@ class Workload:
         torch = self.torch
         lse_rows = torch.empty((self.rows, self.hq), dtype=torch.float32, device=self.device)
         qi = torch.arange(self.rows, device=self.device) * 5 + (5 - REJECTED) - 1
-        seq = torch.full((self.rows,), CTX - REJECTED, dtype=torch.int32, device=self.device)
+        seq = torch.full((self.rows,), self.ctx - REJECTED, dtype=torch.int32, device=self.device)
         cmax, csum = self.dsb.kernels.paged_chunk_stats(
             self.query[qi].contiguous(), self.key_cache, self.block_table, seq,
-            chunk_size=CHUNK, max_seq_len=CTX, scale=D ** -0.5)
+            chunk_size=CHUNK, max_seq_len=self.ctx, scale=D ** -0.5)
         self.dsb.kernels.stats_to_head_scores(cmax, csum, seq, self.hk, chunk_size=CHUNK,
                                               lse_out=lse_rows)
         lse = torch.zeros((5 * self.rows, self.hq), dtype=torch.float32, device=self.device)
@@ -209,7 +211,7 @@ def period_launches(w: "Workload", exchange=None, total_hq=None, gathered=None):
     def scores():
         dsb.kernels.paged_chunk_head_scores(
             w.query, w.key_cache, w.lse, w.block_table, w.r_len, chunk_size=CHUNK,
-            max_seq_len=CTX, scale=D ** -0.5, query_index=w.q_index, out=w.parts)
+            max_seq_len=w.ctx, scale=D ** -0.5, query_index=w.q_index, out=w.parts)
 
     def select(parts_fn=lambda: w.parts):
         dsb.selection.select_rows(parts_fn(), w.r_len, chunk_size=CHUNK, token_budget=HISTORY_BUDGET,
@@ -779,6 +781,78 @@ def run_only(args):
         raise SystemExit(1)
 
 
+def run_draft_step(args):
+    """a random-init Eagle3-style draft layer (hidden 2048,
+    qkv input 4096, 32 / 4 heads of 128, SwiGLU 6144, RMSNorm, bf16) drafting
+    for 16 requests at 65536 context: one period = retrieval (committed-query
+    pick, chunk scores over the paged target K, selection) + 4 cycles x (plan +
+    rebuild, 4 draft steps through the layer: query GEMM, K/V projection with
+    the raw-cache write, RoPE, draft attention, output GEMM, SwiGLU MLP).  The
+    LM head is excluded (its vocabulary is unspecified).  Captured as one CUDA
+    graph; prints draft tokens/s."""
+    import torch
+
+    dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    ctx = 65536
+    w = Workload(torch, dsb, device, B_GROUP, HK, HQ, seed=555, ctx=ctx)
+    layer = dsb.draft_layer.Eagle3DraftLayer(device, seed=5)
+    g = torch.Generator(device=device).manual_seed(17)
+    bf = torch.bfloat16
+    x_in = torch.randn((B_GROUP, 4096), generator=g, device=device).to(bf)
+    residual = torch.randn((B_GROUP, 2048), generator=g, device=device).to(bf)
+    launches = period_launches(w)
+    retrieval = [(k, fn) for k, fn in launches if k in ("prepare", "scores", "select")]
+    rebuilds = [fn for k, fn in launches if k == "rebuild"]
+    abs_pos = [[(w.committed[c] + j).to(torch.int64) for j in range(DEPTH)] for c in range(INTERVAL)]
+    local = [torch.empty_like(w.hist) for _ in range(DEPTH)]
+    outs = [torch.empty_like(residual) for _ in range(DEPTH)]
+
+    def step(c, j):
+        torch.add(w.hist, j, out=local[j])
+        outs[j].copy_(layer.step(x_in, residual, slots=w.active, abs_positions=abs_pos[c][j],
+                                 local_positions=local[j], raw_key=w.raw_key,
+                                 raw_value=w.raw_value, working_key=w.working_key,
+                                 working_value=w.working_value, cos_sin=w.cos_sin))
+
+    seq = list(retrieval)
+    for c in range(INTERVAL):
+        seq.append(("rebuild", rebuilds[c]))
+        for j in range(DEPTH):
+            seq.append(("layer", lambda c=c, j=j: step(c, j)))
+    graph = Graph(torch, seq, device)
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b) / args.steps
+    assert dsb._lib.read_and_clear_error_flag(device) == 0
+    steps_only = Graph(torch, [("layer", lambda j=j: step(0, j)) for j in range(DEPTH)], device)
+    for _ in range(3):
+        steps_only.replay()
+    torch.cuda.synchronize(device)
+    a.record()
+    for _ in range(args.steps):
+        steps_only.replay()
+    b.record()
+    torch.cuda.synchronize(device)
+    step_us = a.elapsed_time(b) * 1e3 / (args.steps * DEPTH)
+    tokens = B_GROUP * INTERVAL * DEPTH
+    print(json.dumps(dict(
+        mode="draft_step", metric="draft tokens/s (config 5, one draft layer, LM head excluded)",
+        value=round(tokens / (ms / 1e3), 1), unit="draft tokens/s", ms_per_period=round(ms, 4),
+        draft_tokens_per_period=tokens, layer_step_us=round(step_us, 2),
+        layer_weight_bytes=layer.weight_bytes(), requests=B_GROUP, context=ctx,
+        token_budget=TOKEN_BUDGET, chunk=CHUNK, retrieval_interval=INTERVAL, draft_depth=DEPTH,
+        dtype="bf16", data="synthetic (random weights and KV)")))
+
+
 def run_kv_projection(args):
     """Time the draft-layer K/V projection + raw-cache write (config 5 decode
     step: 16 tokens, Eagle3 qkv input 4096, 4 kv heads x 128) against the
@@ -859,11 +933,15 @@ def main():
                    help="launch one kernel kind eagerly (for profiler captures)")
     p.add_argument("--kv-projection", action="store_true",
                    help="time the K/V projection + raw-cache write (config 5 decode step)")
+    p.add_argument("--draft-step", action="store_true",
+                   help="config 5: draft tokens/s of a draft layer over the DiffSpec cache")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.kv_projection:
         run_kv_projection(args)
+    elif args.draft_step:
+        run_draft_step(args)
     elif args.only:
         run_only(args)
     elif args.impl == "reference":

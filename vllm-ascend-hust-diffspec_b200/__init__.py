@@ -13,6 +13,7 @@ operator surface:
 * ``attention``   — ``draft_decode_attention``
 * ``runtime``     — ``DiffSpecDraftCache`` retrieval hook / rebuild / attention
 * ``parallel``    — head-sharded score exchange over NCCL
+* ``draft_layer`` — one Eagle3-style draft decoder layer built on the above
 
 All compute runs in ``libdiffspec_b200.so`` (C ABI: include/diffspec_b200.h).
 The directory name is not a Python identifier; importing it under any name
@@ -21,7 +22,7 @@ also registers it (and its submodules) as ``diffspec_b200``.
 
 import sys as _sys
 
-from . import _lib, attention, compact_kv, kernels, parallel, runtime, selection  # noqa: F401
+from . import _lib, attention, compact_kv, draft_layer, kernels, parallel, runtime, selection  # noqa: F401
 from .attention import AttentionWorkspace, draft_decode_attention  # noqa: F401
 from .compact_kv import rebuild_compact_kv_from_plan  # noqa: F401
 from .kernels import (  # noqa: F401
@@ -37,7 +38,7 @@ from .runtime import (  # noqa: F401
 from .selection import DiffSpecSelection, build_history_plan, select_context_chunks, select_rows  # noqa: F401
 
 _sys.modules.setdefault("diffspec_b200", _sys.modules[__name__])
-for _name in ("_lib", "attention", "compact_kv", "kernels", "parallel", "runtime", "selection"):
+for _name in ("_lib", "attention", "compact_kv", "draft_layer", "kernels", "parallel", "runtime", "selection"):
     _sys.modules.setdefault(f"diffspec_b200.{_name}", _sys.modules[f"{__name__}.{_name}"])
 
 
