@@ -786,8 +786,9 @@ def run_draft_step(args):
     qkv input 4096, 32 / 4 heads of 128, SwiGLU 6144, RMSNorm, bf16) drafting
     for 16 requests at 65536 context: one period = retrieval (committed-query
     pick, chunk scores over the paged target K, selection) + 4 cycles x (plan +
-    rebuild, 4 draft steps through the layer: query GEMM, K/V projection with
-    the raw-cache write, RoPE, draft attention, output GEMM, SwiGLU MLP).  The
+    rebuild, 4 draft steps through the layer: RMSNorm, query GEMM, K/V
+    projection with the raw-cache write, RoPE, draft attention, output GEMM,
+    RMSNorm, SwiGLU MLP).  The
     LM head is excluded (its vocabulary is unspecified).  Captured as one CUDA
     graph; prints draft tokens/s."""
     import torch
@@ -811,10 +812,10 @@ def run_draft_step(args):
 
     def step(c, j):
         torch.add(w.hist, j, out=local[j])
-        outs[j].copy_(layer.step(x_in, residual, slots=w.active, abs_positions=abs_pos[c][j],
-                                 local_positions=local[j], raw_key=w.raw_key,
-                                 raw_value=w.raw_value, working_key=w.working_key,
-                                 working_value=w.working_value, cos_sin=w.cos_sin))
+        layer.step(x_in, residual, slots=w.active, abs_positions=abs_pos[c][j],
+                   local_positions=local[j], raw_key=w.raw_key, raw_value=w.raw_value,
+                   working_key=w.working_key, working_value=w.working_value, cos_sin=w.cos_sin,
+                   out=outs[j])
 
     seq = list(retrieval)
     for c in range(INTERVAL):

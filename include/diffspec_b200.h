@@ -257,6 +257,47 @@ int dsb_kv_projection_write_raw(
     void *raw_key, void *raw_value, int32_t num_slots, int64_t max_model_len, int32_t dtype,
     void *out, int32_t *error_flag, void *stream);
 
+/* Elementwise stages of one draft decoder layer (the vLLM Eagle3 Llama layer
+ * of the diffspec draft model, qkv input built at diffspec/vllm_patch.py:
+ * 189-225; RoPE at the working cache's local positions, diffspec/runtime.py:
+ * 1767-1794).  The reference runs each as eager tensor ops; these are one
+ * launch apiece.
+ *
+ * dsb_rms_norm: out[r] = round(x[r] * rsqrt(mean(x[r]^2) + eps) * weight),
+ * fp32 math, for rows r < rows of cols elements (row strides in elements,
+ * multiples of 8; cols a multiple of 8; 16-byte aligned; out must not
+ * overlap x). */
+int dsb_rms_norm(const void *x, int64_t x_row_stride, const void *weight, void *out,
+                 int64_t out_row_stride, int32_t rows, int32_t cols, float eps, int32_t dtype,
+                 void *stream);
+
+/* dsb_rope_qk: NeoX rotation at positions[t] of a [cos | sin] table with
+ * rotary_rows rows (products rounded before the add, as in the working-cache
+ * rebuild) of one step's query heads, in place ([tokens, num_query_heads,
+ * head_dim] with row stride query_row_stride), and of its key heads, read
+ * from key (row stride key_row_stride, e.g. the packed rows of
+ * dsb_kv_projection_write_raw) and written to key_out as contiguous [tokens,
+ * num_kv_heads, head_dim] (key_out == key: in place, contiguous rows only).
+ * With value non-NULL the value heads (row stride value_row_stride) are
+ * copied unchanged to value_out in the same layout.  A position outside
+ * [0, rotary_rows) leaves its rows unrotated and sets DSB_FLAG_POSITION.
+ * Strides are in elements. */
+int dsb_rope_qk(void *query, int64_t query_row_stride, int32_t num_query_heads,
+                const void *key, int64_t key_row_stride, void *key_out,
+                const void *value, int64_t value_row_stride, void *value_out,
+                int32_t num_kv_heads, int32_t head_dim, const int32_t *positions,
+                int32_t tokens, const void *cos_sin, int64_t cos_sin_row_stride,
+                int32_t rotary_rows, int32_t cos_sin_dtype, int32_t dtype,
+                int32_t *error_flag, void *stream);
+
+/* dsb_silu_mul: out[r, i] = round(silu(gate_up[r, i]) * gate_up[r, intermediate
+ * + i]) for i < intermediate (fp32 math, one rounding; SwiGLU with the gate
+ * and up projections in one GEMM output).  intermediate and row strides are
+ * multiples of 8 and rows 16-byte aligned. */
+int dsb_silu_mul(const void *gate_up, int64_t gate_up_row_stride, void *out,
+                 int64_t out_row_stride, int32_t rows, int32_t intermediate, int32_t dtype,
+                 void *stream);
+
 /* Committed-query pick of the retrieval hook
  * (_accept_target_queries, diffspec/runtime.py:1211-1276): for each of `rows`
  * real requests with query span [query_ends[r-1], query_ends[r]) and count

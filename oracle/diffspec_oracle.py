@@ -431,3 +431,44 @@ def kv_projection_write_raw(hidden, weight, slots, positions, raw_key, raw_value
     write_raw(raw_key, raw_value, slots, positions, kv[:, :half].reshape(-1, hk, d),
               kv[:, half:].reshape(-1, hk, d))
     return kv
+
+
+# ------------------------------------------------------- draft layer elementwise stages
+# The draft model is vLLM's Eagle3 Llama layer (a dependency of the reference,
+# vllm>=0.28.1rc1.dev319,<0.28.2 in pyproject.toml, not vendored); these
+# restate the published algorithms of its RMSNorm and SiLU-and-mul at the
+# storage dtype, and its RoPE at the working cache's local positions
+# (diffspec/runtime.py:1767-1794) with rope_rotate above.
+def rms_norm(x, weight, eps, dtype="bf16"):
+    """round(x * 1/sqrt(mean(x^2) + eps) * weight) per row (fp64 sum of
+    squares, fp32 scaling: products rounded in fp32)."""
+    x = np.asarray(x, dtype=np.float32)
+    ms = (x.astype(np.float64) ** 2).mean(-1, keepdims=True)
+    inv = (1.0 / np.sqrt(ms + eps)).astype(np.float32)
+    return round_to((x * inv) * np.asarray(weight, dtype=np.float32), dtype)
+
+
+def silu_mul(gate_up, dtype="bf16"):
+    """SwiGLU of [rows, 2 * inter] rows holding gate then up:
+    round(gate / (1 + e^-gate) * up)."""
+    gu = np.asarray(gate_up, dtype=np.float64)
+    inter = gu.shape[-1] // 2
+    g, u = gu[..., :inter], gu[..., inter:]
+    return round_to((g / (1.0 + np.exp(-g)) * u).astype(np.float32), dtype)
+
+
+def rope_qk(query, kv, positions, cos_sin, num_kv_heads, dtype="bf16"):
+    """One draft step's RoPE: query [T, Hq * D] and the K half of kv [T, 2 * Hk
+    * D] rotated (NeoX) at positions[t]; returns (query, key [T, Hk, D], value
+    [T, Hk, D]) rounded to `dtype`."""
+    t_n = query.shape[0]
+    feats = kv.shape[1] // 2
+    d = feats // num_kv_heads
+    q = np.asarray(query, dtype=np.float32).reshape(t_n, -1, d).copy()
+    k = np.asarray(kv[:, :feats], dtype=np.float32).reshape(t_n, num_kv_heads, d).copy()
+    v = np.asarray(kv[:, feats:], dtype=np.float32).reshape(t_n, num_kv_heads, d).copy()
+    for t in range(t_n):
+        row = np.asarray(cos_sin[int(positions[t])], dtype=np.float32)
+        q[t] = round_to(rope_rotate(q[t], row, d, True), dtype)
+        k[t] = round_to(rope_rotate(k[t], row, d, True), dtype)
+    return q.reshape(t_n, -1), k, v

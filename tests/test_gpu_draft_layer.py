@@ -1,13 +1,16 @@
 """One Eagle3-style draft layer step (library kernels + cuBLAS GEMMs) against a
 torch fp32 restatement of the same layer that rounds to bf16 at the same
-points (so only accumulation order differs)."""
+points (so only accumulation order differs), and the layer's elementwise
+kernels (RMSNorm, RoPE of q/k, SwiGLU) against the oracle."""
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
 from conftest import close_bf16
+from oracle import diffspec_oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -42,7 +45,7 @@ def _ref_step(layer, x_in, residual, slots, abs_pos, local_pos, wk0, wv0, cos_si
         for h_ in range(hq):
             sc = (K[h_ // g] @ q[i, h_]) * d ** -0.5
             attn[i, h_] = torch.softmax(sc, 0) @ V[h_ // g]
-    x = r(residual.float() + r(attn).view(n, hq * d) @ layer.w_o.float().t())
+    x = r(residual.float() + r(attn).view(n, hq * d) @ layer.w_o.float().t())  # addmm: one rounding
     gu = r(norm(x, layer.post_norm) @ layer.w_gate_up.float().t())
     act = r(torch.nn.functional.silu(gu[:, : layer.inter]) * gu[:, layer.inter:])
     return r(x + act @ layer.w_down.float().t()), kv
@@ -84,3 +87,61 @@ def test_draft_layer_step_matches_fp32_reference(dsb, cuda):
             s, p = int(slots[i]), int(abs_pos[i])
             close_bf16(raw_k[s, p].reshape(-1).float().cpu().numpy(), kv[i, :128].cpu().numpy())
             close_bf16(raw_v[s, p].reshape(-1).float().cpu().numpy(), kv[i, 128:].cpu().numpy())
+
+
+_T = {"bf16": torch.bfloat16, "f16": torch.float16}
+_FRAC = {"bf16": 7, "f16": 10}
+
+
+def _within_one_ulp(got, ref, dtype):
+    mag = np.maximum(np.abs(ref), 2.0 ** -14)
+    return np.abs(got - ref) <= np.exp2(np.floor(np.log2(mag)) - _FRAC[dtype])
+
+
+@pytest.mark.parametrize("dtype,rows,cols,pad", [("bf16", 16, 4096, 0), ("f16", 37, 2048, 64),
+                                                 ("bf16", 1, 8, 8)])
+def test_rms_norm_matches_oracle(dsb, cuda, dtype, rows, cols, pad):
+    rng = np.random.default_rng(rows + cols)
+    x = O.round_to(rng.standard_normal((rows, cols + pad), dtype=np.float32) * 3, dtype)
+    w = O.round_to(rng.uniform(0.5, 1.5, cols).astype(np.float32), dtype)
+    xt = torch.from_numpy(x).to(cuda).to(_T[dtype])[:, :cols]  # row stride cols + pad
+    got = dsb.draft_layer.rms_norm(xt, torch.from_numpy(w).to(cuda).to(_T[dtype]), 1e-6)
+    ref = O.rms_norm(x[:, :cols], w, 1e-6, dtype)
+    g = got.float().cpu().numpy()
+    assert _within_one_ulp(g, ref, dtype).all()  # fp32 sum order differs from the oracle's
+    assert (g == ref).mean() > 0.99
+
+
+@pytest.mark.parametrize("dtype,cs_dtype", [("bf16", torch.bfloat16), ("f16", torch.float32)])
+def test_rope_qk_matches_oracle(dsb, cuda, dtype, cs_dtype):
+    rng = np.random.default_rng(5)
+    t_n, hq, hk, d, rows = 9, 8, 2, 128, 300
+    q = O.round_to(rng.standard_normal((t_n, hq * d), dtype=np.float32), dtype)
+    kv = O.round_to(rng.standard_normal((t_n, 2 * hk * d), dtype=np.float32), dtype)
+    ang = np.arange(rows)[:, None] * (1e4 ** (-np.arange(d // 2) / (d // 2)))[None]
+    cs = O.round_to(np.concatenate((np.cos(ang), np.sin(ang)), -1).astype(np.float32),
+                    "bf16" if cs_dtype == torch.bfloat16 else "f32")
+    pos = rng.integers(0, rows, t_n).astype(np.int32)
+    pos[3] = rows  # outside the table: rows left unrotated, flagged
+    dev = lambda a, tdt: torch.from_numpy(np.ascontiguousarray(a)).to(cuda).to(tdt)  # noqa: E731
+    qt, kvt = dev(q, _T[dtype]), dev(kv, _T[dtype])
+    k, v = dsb.draft_layer.rope_qk(qt, kvt, dev(pos, torch.int32), dev(cs, cs_dtype), hk)
+    flag = dsb._lib.read_and_clear_error_flag(cuda)
+    assert flag == 2  # DSB_FLAG_POSITION
+    ok = np.arange(t_n) != 3
+    rq, rk, rv = O.rope_qk(q[ok], kv[ok], pos[ok], cs, hk, dtype)
+    np.testing.assert_array_equal(qt.float().cpu().numpy()[ok], rq)
+    np.testing.assert_array_equal(k.float().cpu().numpy()[ok], rk)
+    np.testing.assert_array_equal(v.float().cpu().numpy(), kv[:, hk * d:].reshape(t_n, hk, d))
+    np.testing.assert_array_equal(qt.float().cpu().numpy()[3], q[3])
+    np.testing.assert_array_equal(k.float().cpu().numpy()[3], kv[3, : hk * d].reshape(hk, d))
+
+
+@pytest.mark.parametrize("dtype,rows,inter", [("bf16", 16, 6144), ("f16", 5, 520)])
+def test_silu_mul_matches_oracle(dsb, cuda, dtype, rows, inter):
+    rng = np.random.default_rng(rows)
+    gu = O.round_to(rng.standard_normal((rows, 2 * inter), dtype=np.float32) * 4, dtype)
+    got = dsb.draft_layer.silu_mul(torch.from_numpy(gu).to(cuda).to(_T[dtype])).float().cpu().numpy()
+    ref = O.silu_mul(gu, dtype)
+    assert _within_one_ulp(got, ref, dtype).all()  # fp32 exp / divide against fp64
+    assert (got == ref).mean() > 0.99

@@ -1,0 +1,58 @@
+"""The oracle's draft-layer elementwise stages (RMSNorm, SwiGLU, RoPE of one
+step) against torch fp32 statements of the same formulas, and the host-side
+validation of the library wrappers (no GPU)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import diffspec_oracle as O
+
+
+def test_rms_norm_and_silu_mul_agree_with_torch():
+    rng = np.random.default_rng(0)
+    x = O.round_to(rng.standard_normal((6, 256), dtype=np.float32), "bf16")
+    w = O.round_to(rng.uniform(0.5, 1.5, 256).astype(np.float32), "bf16")
+    xt = torch.from_numpy(x)
+    ref = (xt * torch.rsqrt(xt.pow(2).mean(-1, keepdim=True) + 1e-6) * torch.from_numpy(w)).bfloat16()
+    got = O.rms_norm(x, w, 1e-6)
+    assert (got == ref.float().numpy()).mean() > 0.99
+    assert np.abs(got - ref.float().numpy()).max() <= 2.0 ** -6 * np.abs(got).max()
+    gu = O.round_to(rng.standard_normal((6, 64), dtype=np.float32) * 4, "bf16")
+    gt = torch.from_numpy(gu)
+    ref = (torch.nn.functional.silu(gt[:, :32]) * gt[:, 32:]).bfloat16().float().numpy()
+    got = O.silu_mul(gu)
+    assert (got == ref).mean() > 0.99
+
+
+def test_rope_qk_rotates_queries_and_keys_and_passes_values():
+    rng = np.random.default_rng(1)
+    t_n, hq, hk, d = 3, 4, 2, 8
+    q = O.round_to(rng.standard_normal((t_n, hq * d), dtype=np.float32), "bf16")
+    kv = O.round_to(rng.standard_normal((t_n, 2 * hk * d), dtype=np.float32), "bf16")
+    ang = np.arange(10)[:, None] * (1e4 ** (-np.arange(d // 2) / (d // 2)))[None]
+    cs = np.concatenate((np.cos(ang), np.sin(ang)), -1).astype(np.float32)
+    pos = np.array([0, 4, 9])
+    rq, rk, rv = O.rope_qk(q, kv, pos, cs, hk)
+    np.testing.assert_array_equal(rq[0], q[0])  # position 0: identity
+    np.testing.assert_array_equal(rv, kv[:, hk * d:].reshape(t_n, hk, d))
+    # rotation keeps the norm of each (i, i + half) pair
+    kk = kv[:, : hk * d].reshape(t_n, hk, d)
+    np.testing.assert_allclose(rk[..., :4] ** 2 + rk[..., 4:] ** 2, kk[..., :4] ** 2 + kk[..., 4:] ** 2,
+                               rtol=3e-2, atol=1e-3)
+
+
+def test_layer_op_wrappers_reject_host_tensors(dsb):
+    x = torch.zeros((2, 16), dtype=torch.bfloat16)
+    with pytest.raises((ValueError, RuntimeError)):
+        dsb.draft_layer.rms_norm(x, torch.ones(16, dtype=torch.bfloat16), 1e-6)
+    with pytest.raises(ValueError):
+        dsb.draft_layer.rms_norm(x, torch.ones(8, dtype=torch.bfloat16), 1e-6)
+    with pytest.raises((ValueError, RuntimeError)):
+        dsb.draft_layer.silu_mul(torch.zeros((2, 32), dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        dsb.draft_layer.rope_qk(torch.zeros((2, 16), dtype=torch.bfloat16),
+                                torch.zeros((2, 16), dtype=torch.bfloat16),
+                                torch.zeros(2, dtype=torch.int64), torch.zeros((4, 8)), 1)

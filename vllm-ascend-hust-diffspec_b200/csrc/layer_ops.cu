@@ -1,0 +1,279 @@
+// Elementwise ops of one draft decoder layer: RMSNorm, NeoX RoPE of the
+// step's queries and keys, and the SwiGLU activation.
+//
+// Reference: the draft model of diffspec is a vLLM Eagle3 Llama layer (its
+// qkv input is the embedding concatenated with the target hidden state,
+// diffspec/vllm_patch.py:189-225) whose RoPE positions are the working
+// cache's local positions (diffspec/runtime.py:1767-1794).  Between the
+// GEMMs a decode step of that layer runs three elementwise stages; each is a
+// handful of small tensor ops in eager PyTorch (one launch per op, ~2-3 us
+// each for a 16-row step), here one launch apiece:
+//   * rms_norm:   out = round(x * rsqrt(mean(x^2) + eps) * w), fp32 math;
+//   * rope_qk:    queries of the step rotated in place and keys rotated
+//                 out of the K/V projection's packed rows into the
+//                 contiguous rows the draft attention reads, values copied
+//                 beside them (NeoX halves, products rounded before the add,
+//                 as in the working-cache rebuild);
+//   * silu_mul:   out = round(silu(gate) * up) over a [rows, 2 * inter] GEMM
+//                 output holding gate then up.
+// All three are latency bound at decode sizes (tens of KB per launch): one
+// CTA per row (norm), one warp per (token, head) (RoPE), a grid-stride loop
+// of 16-byte vectors (activation), with programmatic dependent launch so a
+// launch overlaps the previous kernel's tail.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace dsb {
+namespace {
+
+constexpr int kNormThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ void load8(const T *p, float (&v)[8]) {
+  const uint4 w = *reinterpret_cast<const uint4 *>(p);
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack2<T>(u[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T *p, const float (&v)[8]) {
+  uint4 w;
+  w.x = pack2<T>(v[0], v[1]);
+  w.y = pack2<T>(v[2], v[3]);
+  w.z = pack2<T>(v[4], v[5]);
+  w.w = pack2<T>(v[6], v[7]);
+  *reinterpret_cast<uint4 *>(p) = w;
+}
+
+// One CTA per row; cols is a multiple of 8 and rows are 16-byte aligned.
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
+    rms_norm_kernel(const T *__restrict__ x, int64_t x_stride, const T *__restrict__ w,
+                    T *__restrict__ out, int64_t out_stride, int cols, float eps) {
+  __shared__ float part[kNormThreads / 32];
+  pdl_begin();
+  const T *row = x + blockIdx.x * x_stride;
+  const int vecs = cols / 8;
+  float ss = 0.f;
+  for (int v = threadIdx.x; v < vecs; v += kNormThreads) {
+    float f[8];
+    load8(row + 8 * v, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) total += part[i];
+  const float inv = rsqrtf(total / static_cast<float>(cols) + eps);
+  T *orow = out + blockIdx.x * out_stride;
+  for (int v = threadIdx.x; v < vecs; v += kNormThreads) {
+    float f[8], g[8];
+    load8(row + 8 * v, f);
+    load8(w + 8 * v, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = __fmul_rn(__fmul_rn(f[i], inv), g[i]);
+    store8(orow + 8 * v, f);
+  }
+}
+
+struct RopeArgs {
+  void *q;
+  const void *k, *v;
+  void *k_out, *v_out;
+  int64_t q_stride, k_stride, v_stride;  // elements between tokens
+  const void *cos_sin;
+  int64_t cs_stride;
+  const int32_t *positions;
+  int tokens, hq, hk, hv, head_dim, half, rotary_rows;
+  int32_t *error_flag;
+};
+
+// One warp per (token, head) over hq query heads (rotated in place), hk key
+// heads (rotated from k into k_out) and hv value heads (copied from v into
+// v_out): element i of a head pairs with element i + half.  A position
+// outside the table leaves the token's rows unrotated (keys still copied)
+// and sets DSB_FLAG_POSITION.
+template <typename T, typename CS>
+__global__ void __launch_bounds__(256) rope_qk_kernel(RopeArgs a) {
+  pdl_begin();
+  const int warp = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = a.hq + a.hk + a.hv;
+  if (warp >= a.tokens * heads) return;
+  const int t = warp / heads, h = warp % heads;
+  const int64_t hd = a.head_dim;
+  if (h >= a.hq + a.hk) {  // value head: plain copy into the contiguous layout
+    const T *src = static_cast<const T *>(a.v) + t * a.v_stride + (h - a.hq - a.hk) * hd;
+    T *dst = static_cast<T *>(a.v_out) + (static_cast<int64_t>(t) * a.hv + h - a.hq - a.hk) * hd;
+    for (int i = lane; i < a.head_dim; i += 32) dst[i] = src[i];
+    return;
+  }
+  const T *src = h < a.hq ? static_cast<const T *>(a.q) + t * a.q_stride + h * hd
+                          : static_cast<const T *>(a.k) + t * a.k_stride + (h - a.hq) * hd;
+  T *dst = h < a.hq ? static_cast<T *>(a.q) + t * a.q_stride + h * hd
+                    : static_cast<T *>(a.k_out) + (static_cast<int64_t>(t) * a.hk + h - a.hq) * hd;
+  const int pos = a.positions[t];
+  if (pos < 0 || pos >= a.rotary_rows) {
+    if (lane == 0 && h == 0) flag_error(a.error_flag, DSB_FLAG_POSITION);
+    if (src != dst)
+      for (int i = lane; i < a.head_dim; i += 32) dst[i] = src[i];
+    return;
+  }
+  const CS *cs = static_cast<const CS *>(a.cos_sin) + pos * a.cs_stride;
+  for (int i = lane; i < a.half; i += 32) {
+    const float x1 = Elem<T>::to_f(src[i]), x2 = Elem<T>::to_f(src[i + a.half]);
+    const float c = Elem<CS>::to_f(cs[i]), s = Elem<CS>::to_f(cs[i + a.half]);
+    dst[i] = Elem<T>::from_f(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+    dst[i + a.half] = Elem<T>::from_f(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
+  }
+}
+
+// silu(g) = g / (1 + e^-g) in fp32, times up, one rounding; inter % 8 == 0.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    silu_mul_kernel(const T *__restrict__ gate_up, int64_t gu_stride, T *__restrict__ out,
+                    int64_t out_stride, int rows, int inter) {
+  pdl_begin();
+  const int vpr = inter / 8;
+  const int64_t total = static_cast<int64_t>(rows) * vpr;
+  for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = v / vpr;
+    const int c = static_cast<int>(v % vpr) * 8;
+    float g[8], u[8];
+    load8(gate_up + r * gu_stride + c, g);
+    load8(gate_up + r * gu_stride + inter + c, u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) g[i] = __fmul_rn(__fdiv_rn(g[i], 1.f + expf(-g[i])), u[i]);
+    store8(out + r * out_stride + c, g);
+  }
+}
+
+bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+}  // namespace
+}  // namespace dsb
+
+using namespace dsb;
+
+extern "C" int dsb_rms_norm(const void *x, int64_t x_row_stride, const void *weight, void *out,
+                            int64_t out_row_stride, int32_t rows, int32_t cols, float eps,
+                            int32_t dtype, void *stream) {
+  if (rows < 0 || cols <= 0) return fail(DSB_ERR_INVALID, "rows must be >= 0 and cols > 0");
+  if (rows == 0) return DSB_OK;
+  if (dtype != DSB_BF16 && dtype != DSB_F16)
+    return fail(DSB_ERR_INVALID, "rms_norm rows and weight must be BF16 or FP16");
+  if (!x || !weight || !out) return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (!(eps >= 0.f)) return fail(DSB_ERR_INVALID, "eps must be >= 0");
+  if (cols % 8 || x_row_stride % 8 || out_row_stride % 8 || x_row_stride < cols ||
+      out_row_stride < cols || !aligned16(x) || !aligned16(weight) || !aligned16(out))
+    return fail(DSB_ERR_UNSUPPORTED,
+                "rms_norm needs cols and row strides that are multiples of 8 (>= cols) and "
+                "16-byte aligned rows");
+  const cudaStream_t st = as_stream(stream);
+  if (dtype == DSB_BF16)
+    launch_kernel(rms_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), 0, st,
+                  static_cast<const __nv_bfloat16 *>(x), x_row_stride,
+                  static_cast<const __nv_bfloat16 *>(weight), static_cast<__nv_bfloat16 *>(out),
+                  out_row_stride, (int)cols, eps);
+  else
+    launch_kernel(rms_norm_kernel<__half>, dim3(rows), dim3(kNormThreads), 0, st,
+                  static_cast<const __half *>(x), x_row_stride, static_cast<const __half *>(weight),
+                  static_cast<__half *>(out), out_row_stride, (int)cols, eps);
+  return check_launch("rms_norm_kernel");
+}
+
+extern "C" int dsb_rope_qk(void *query, int64_t query_row_stride, int32_t num_query_heads,
+                           const void *key, int64_t key_row_stride, void *key_out,
+                           const void *value, int64_t value_row_stride, void *value_out,
+                           int32_t num_kv_heads, int32_t head_dim, const int32_t *positions,
+                           int32_t tokens, const void *cos_sin, int64_t cos_sin_row_stride,
+                           int32_t rotary_rows, int32_t cos_sin_dtype, int32_t dtype,
+                           int32_t *error_flag, void *stream) {
+  if (tokens < 0) return fail(DSB_ERR_INVALID, "negative token count");
+  if (tokens == 0) return DSB_OK;
+  if (dtype != DSB_BF16 && dtype != DSB_F16)
+    return fail(DSB_ERR_INVALID, "queries and keys must be BF16 or FP16");
+  if (cos_sin_dtype != DSB_BF16 && cos_sin_dtype != DSB_F16 && cos_sin_dtype != DSB_F32)
+    return fail(DSB_ERR_INVALID, "cos_sin must be BF16, FP16 or FP32");
+  if (num_query_heads < 0 || num_kv_heads < 0 || num_query_heads + num_kv_heads <= 0)
+    return fail(DSB_ERR_INVALID, "head counts must be >= 0 with at least one head");
+  if (head_dim <= 0 || head_dim % 2 || rotary_rows <= 0 || cos_sin_row_stride < head_dim)
+    return fail(DSB_ERR_INVALID,
+                "head_dim must be even and positive; cos_sin rows hold [cos | sin] of head_dim");
+  if (!positions || !cos_sin) return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (num_query_heads && (!query || query_row_stride < (int64_t)num_query_heads * head_dim))
+    return fail(DSB_ERR_INVALID, "null query or query row stride shorter than its heads");
+  const int64_t kv_row = (int64_t)num_kv_heads * head_dim;
+  if (num_kv_heads && (!key || !key_out || key_row_stride < kv_row))
+    return fail(DSB_ERR_INVALID, "null key / key_out or key row stride shorter than its heads");
+  if (value && (!value_out || !num_kv_heads || value_row_stride < kv_row))
+    return fail(DSB_ERR_INVALID, "value needs value_out and a row stride covering its heads");
+  if (key_out && key_out != key && key_row_stride < kv_row)
+    return fail(DSB_ERR_INVALID, "key row stride shorter than its heads");
+  // key_out is contiguous [tokens, num_kv_heads, head_dim]: in place needs
+  // the key rows to be that layout too.
+  if (num_kv_heads && key_out == key && key_row_stride != kv_row)
+    return fail(DSB_ERR_INVALID, "in-place keys must be contiguous");
+  const int hv = value ? num_kv_heads : 0;
+  const int64_t warps = (int64_t)tokens * (num_query_heads + num_kv_heads + hv);
+  if ((warps + 7) / 8 > INT32_MAX) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
+  RopeArgs a{query, key, value, key_out, value_out, query_row_stride, key_row_stride,
+             value_row_stride, cos_sin, cos_sin_row_stride, positions, tokens, num_query_heads,
+             num_kv_heads, hv, head_dim, head_dim / 2, rotary_rows, error_flag};
+  const cudaStream_t st = as_stream(stream);
+  const dim3 grid(static_cast<unsigned>((warps + 7) / 8)), block(256);
+  auto go = [&](auto tag_t) {
+    using T = decltype(tag_t);
+    if (cos_sin_dtype == DSB_BF16)
+      launch_kernel(rope_qk_kernel<T, __nv_bfloat16>, grid, block, 0, st, a);
+    else if (cos_sin_dtype == DSB_F16)
+      launch_kernel(rope_qk_kernel<T, __half>, grid, block, 0, st, a);
+    else
+      launch_kernel(rope_qk_kernel<T, float>, grid, block, 0, st, a);
+  };
+  if (dtype == DSB_BF16)
+    go(__nv_bfloat16());
+  else
+    go(__half());
+  return check_launch("rope_qk_kernel");
+}
+
+extern "C" int dsb_silu_mul(const void *gate_up, int64_t gate_up_row_stride, void *out,
+                            int64_t out_row_stride, int32_t rows, int32_t intermediate,
+                            int32_t dtype, void *stream) {
+  if (rows < 0 || intermediate <= 0)
+    return fail(DSB_ERR_INVALID, "rows must be >= 0 and intermediate > 0");
+  if (rows == 0) return DSB_OK;
+  if (dtype != DSB_BF16 && dtype != DSB_F16)
+    return fail(DSB_ERR_INVALID, "silu_mul rows must be BF16 or FP16");
+  if (!gate_up || !out) return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (intermediate % 8 || gate_up_row_stride % 8 || out_row_stride % 8 ||
+      gate_up_row_stride < 2 * (int64_t)intermediate || out_row_stride < intermediate ||
+      !aligned16(gate_up) || !aligned16(out))
+    return fail(DSB_ERR_UNSUPPORTED,
+                "silu_mul needs intermediate and row strides that are multiples of 8 and "
+                "16-byte aligned rows");
+  const int64_t vecs = (int64_t)rows * (intermediate / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, 4L * sm_count()));
+  const cudaStream_t st = as_stream(stream);
+  if (dtype == DSB_BF16)
+    launch_kernel(silu_mul_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st,
+                  static_cast<const __nv_bfloat16 *>(gate_up), gate_up_row_stride,
+                  static_cast<__nv_bfloat16 *>(out), out_row_stride, (int)rows, (int)intermediate);
+  else
+    launch_kernel(silu_mul_kernel<__half>, dim3(blocks), dim3(256), 0, st,
+                  static_cast<const __half *>(gate_up), gate_up_row_stride,
+                  static_cast<__half *>(out), out_row_stride, (int)rows, (int)intermediate);
+  return check_launch("silu_mul_kernel");
+}

@@ -8,10 +8,10 @@ applied at the working cache's local positions (runtime.py:1767-1794), and
 the attention runs over the compact working cache (runtime.py:2024-2134),
 followed by the output projection and a SwiGLU MLP with RMSNorm.
 
-Here the K/V projection, the raw-cache write and the draft attention are this
-library's kernels (``kv_projection_write_raw``, ``draft_decode_attention``);
-the query / output projections and the MLP are plain GEMMs (cuBLAS through
-torch) and the norms, RoPE and activation are torch elementwise ops.  The
+Here the K/V projection with the raw-cache write, the draft attention and the
+elementwise stages (RMSNorm, RoPE of q/k, SwiGLU: one launch each) are this
+library's kernels; the query / output projections and the MLP are plain
+GEMMs (cuBLAS through torch, residual adds in their epilogue).  The
 weights are random (no checkpoint is involved); the layer exists to turn the
 kernels into draft tokens per second and to show how the
 pieces compose.  The LM head is not included: its vocabulary is unspecified.
@@ -21,26 +21,88 @@ from __future__ import annotations
 
 import torch
 
+from . import _lib
 from .attention import AttentionWorkspace, draft_decode_attention
 from .kernels import kv_projection_write_raw
 
-__all__ = ["Eagle3DraftLayer", "rope_neox"]
+__all__ = ["Eagle3DraftLayer", "rms_norm", "rope_qk", "silu_mul"]
 
 
-def rope_neox(x: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
-    """NeoX rotation of ``x [n, heads, D]`` at ``positions [n]`` with a
-    ``[cos | sin]`` table (fp32 math, one rounding)."""
-    half = x.shape[-1] // 2
-    cs = cos_sin.index_select(0, positions.long()).float()
-    cos, sin = cs[:, None, :half], cs[:, None, half:]
-    xf = x.float()
-    x1, x2 = xf[..., :half], xf[..., half:]
-    return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), -1).to(x.dtype)
+def _rows(t: torch.Tensor, what: str) -> int:
+    """Row stride (elements) of a 2-D tensor with unit column stride."""
+    if t.ndim != 2 or t.stride(1) != 1:
+        raise ValueError(f"{what} must be 2-D with contiguous rows")
+    return t.stride(0)
 
 
-def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()).to(x.dtype)
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """``round(x * rsqrt(mean(x^2) + eps) * weight)`` per row of ``x [rows,
+    cols]`` (fp32 math), one launch (``dsb_rms_norm``)."""
+    if weight.shape != (x.shape[-1],) or weight.dtype != x.dtype:
+        raise ValueError("weight must be [cols] in the rows' dtype")
+    device = _lib.require_cuda(x, weight, out)
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=device)
+    elif out.shape != x.shape or out.dtype != x.dtype:
+        raise ValueError("out must match x")
+    _lib.call("dsb_rms_norm", _lib.ptr(x), _rows(x, "x"), _lib.ptr(weight.contiguous()),
+              _lib.ptr(out), _rows(out, "out"), x.shape[0], x.shape[1], float(eps),
+              _lib.dtype_code(x.dtype), _lib.stream_ptr(device))
+    return out
+
+
+def rope_qk(query: torch.Tensor, kv: torch.Tensor, positions: torch.Tensor,
+            cos_sin: torch.Tensor, num_kv_heads: int,
+            key_out: torch.Tensor | None = None, value_out: torch.Tensor | None = None):
+    """NeoX RoPE of one step at ``positions [T]`` (int32) of a ``[rows, cos |
+    sin]`` table: ``query [T, Hq * D]`` is rotated in place; the K half of
+    the packed K/V projection rows ``kv [T, 2 * Hk * D]`` is rotated into
+    ``key_out [T, Hk, D]`` and its V half copied into ``value_out``, the
+    contiguous rows the draft attention reads.  One launch
+    (``dsb_rope_qk``); returns ``(key_out, value_out)``."""
+    tokens = query.shape[0]
+    feats = kv.shape[1] // 2
+    d = feats // num_kv_heads
+    if kv.shape[0] != tokens or kv.shape[1] != 2 * num_kv_heads * d or query.shape[1] % d:
+        raise ValueError("query must be [T, Hq * D] and kv [T, 2 * Hk * D]")
+    if not (query.dtype == kv.dtype) or cos_sin.ndim != 2 or cos_sin.stride(1) != 1:
+        raise ValueError("query and kv share a dtype; cos_sin is a [rows, D] table")
+    if positions.dtype != torch.int32 or positions.numel() < tokens:
+        raise ValueError("positions must be int32 with one entry per token")
+    device = _lib.require_cuda(query, kv, positions, cos_sin, key_out, value_out)
+    shape = (tokens, num_kv_heads, d)
+    for name, t in (("key_out", key_out), ("value_out", value_out)):
+        if t is not None and (t.shape != shape or t.dtype != kv.dtype or not t.is_contiguous()):
+            raise ValueError(f"{name} must be contiguous [T, Hk, D] in the kv dtype")
+    if key_out is None:
+        key_out = torch.empty(shape, dtype=kv.dtype, device=device)
+    if value_out is None:
+        value_out = torch.empty(shape, dtype=kv.dtype, device=device)
+    kv_stride = _rows(kv, "kv")
+    _lib.call("dsb_rope_qk", _lib.ptr(query), _rows(query, "query"), query.shape[1] // d,
+              _lib.ptr(kv), kv_stride, _lib.ptr(key_out), kv.data_ptr() + feats * kv.element_size(),
+              kv_stride, _lib.ptr(value_out), num_kv_heads, d, _lib.ptr(positions), tokens,
+              _lib.ptr(cos_sin), cos_sin.stride(0), cos_sin.shape[0],
+              _lib.dtype_code(cos_sin.dtype), _lib.dtype_code(kv.dtype),
+              _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device))
+    return key_out, value_out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU ``round(silu(gate) * up)`` of ``gate_up [rows, 2 * inter]``
+    (gate columns first, fp32 math), one launch (``dsb_silu_mul``)."""
+    rows, two_inter = gate_up.shape
+    inter = two_inter // 2
+    device = _lib.require_cuda(gate_up, out)
+    if out is None:
+        out = torch.empty((rows, inter), dtype=gate_up.dtype, device=device)
+    elif out.shape != (rows, inter) or out.dtype != gate_up.dtype:
+        raise ValueError("out must be [rows, inter] in the input dtype")
+    _lib.call("dsb_silu_mul", _lib.ptr(gate_up), _rows(gate_up, "gate_up"), _lib.ptr(out),
+              _rows(out, "out"), rows, inter, _lib.dtype_code(gate_up.dtype),
+              _lib.stream_ptr(device))
+    return out
 
 
 class Eagle3DraftLayer:
@@ -78,15 +140,13 @@ class Eagle3DraftLayer:
         ``[n, hidden]``."""
         n = x_in.shape[0]
         h = rms_norm(x_in, self.in_norm, self.eps)
-        q = (h @ self.w_q.t()).view(n, self.hq, self.d)
+        q = h @ self.w_q.t()
         kv = kv_projection_write_raw(h, self.w_kv, slots, abs_positions, raw_key, raw_value)
-        k = kv[:, : self.hk * self.d].view(n, self.hk, self.d)
-        v = kv[:, self.hk * self.d:].view(n, self.hk, self.d)
-        q = rope_neox(q, cos_sin, local_positions)
-        k = rope_neox(k, cos_sin, local_positions)
-        attn = draft_decode_attention(q, k, v, working_key, working_value, slots, local_positions,
-                                      self.d ** -0.5, workspace=self.workspace)
-        x = residual + attn.view(n, self.hq * self.d) @ self.w_o.t()
-        gu = rms_norm(x, self.post_norm, self.eps) @ self.w_gate_up.t()
-        act = torch.nn.functional.silu(gu[:, : self.inter].float()) * gu[:, self.inter:].float()
-        return x + act.to(x.dtype) @ self.w_down.t()
+        k, v = rope_qk(q, kv, local_positions, cos_sin, self.hk)
+        attn = draft_decode_attention(q.view(n, self.hq, self.d), k, v, working_key, working_value,
+                                      slots, local_positions, self.d ** -0.5,
+                                      workspace=self.workspace)
+        # residual adds in the GEMM epilogue (cuBLAS beta = 1: one rounding)
+        x = torch.addmm(residual, attn.view(n, self.hq * self.d), self.w_o.t())
+        act = silu_mul(rms_norm(x, self.post_norm, self.eps) @ self.w_gate_up.t())
+        return torch.addmm(x, act, self.w_down.t(), out=out)
