@@ -248,7 +248,7 @@ int64_t dsb_draft_attention_scratch_floats(int32_t rows, int32_t num_query_heads
  * [slots[t], positions[t]] (slots[t] < 0: padding, no cache row; bad slots or
  * positions set DSB_FLAG_SLOT / DSB_FLAG_POSITION).  hidden [tokens,
  * hidden_size] and weight [2 * num_kv_heads * head_dim, hidden_size] are
- * contiguous and 16-byte aligned; hidden_size is a multiple of 64 up to 4096
+ * contiguous and 16-byte aligned; hidden_size is a multiple of 64 up to 65536
  * and num_kv_heads * head_dim a multiple of 128.  out (nullable) is
  * [tokens, 2 * num_kv_heads * head_dim]. */
 int dsb_kv_projection_write_raw(
@@ -256,6 +256,48 @@ int dsb_kv_projection_write_raw(
     int32_t num_kv_heads, int32_t head_dim, const int32_t *slots, const int64_t *positions,
     void *raw_key, void *raw_value, int32_t num_slots, int64_t max_model_len, int32_t dtype,
     void *out, int32_t *error_flag, void *stream);
+
+/* Epilogues and flags of the draft-layer linear entry points. */
+#define DSB_LINEAR_PLAIN 0    /* out = x . W^T                                 */
+#define DSB_LINEAR_RESIDUAL 1 /* out = x . W^T + residual (one rounding)       */
+#define DSB_LINEAR_SWIGLU 2   /* out = silu(gate) * up of a gate/up-interleaved W */
+/* Request the weight before the previous kernel in the stream has finished
+ * (programmatic dependent launch): the weight must not be written by that
+ * kernel.  Activations, residuals and outputs are touched only after it. */
+#define DSB_LINEAR_PREFETCH_WEIGHT 1
+
+/* The draft layer's query + K/V projection in one launch (vLLM
+ * QKVParallelLinear of the Eagle3 layer, qkv input built at
+ * diffspec/vllm_patch.py:189-225; K/V handed pre-RoPE to the canonical cache
+ * by the sink op, vllm_patch.py:132-178 -> _write_raw, runtime.py:1602-1618).
+ * weight is [q_features + 2 * num_kv_heads * head_dim, hidden_size]: query
+ * rows, then K rows, then V rows.  q_out [tokens, q_features] receives the
+ * query features; kv_out (nullable) [tokens, 2 * num_kv_heads * head_dim]
+ * and the raw caches (as dsb_kv_projection_write_raw) the K/V features.
+ * q_features is a multiple of 128 (0: K/V only). */
+int dsb_qkv_projection_write_raw(
+    const void *hidden, int32_t tokens, int32_t hidden_size, const void *weight,
+    int32_t q_features, int32_t num_kv_heads, int32_t head_dim, const int32_t *slots,
+    const int64_t *positions, void *raw_key, void *raw_value, int32_t num_slots,
+    int64_t max_model_len, int32_t dtype, void *q_out, void *kv_out, int32_t flags,
+    int32_t *error_flag, void *stream);
+
+/* A linear layer of a draft decode step (the Eagle3 layer's o_proj,
+ * gate_up_proj + SiluAndMul, down_proj): out[t, f] = sum_k x[t, k] *
+ * weight[f, k] with fp32 accumulation, x [tokens, in_features] and weight
+ * [weight_rows, in_features] contiguous and 16-byte aligned, in_features a
+ * multiple of 64 (up to 65536), weight_rows a multiple of 128.
+ * DSB_LINEAR_RESIDUAL adds residual[t, f] before the one rounding.
+ * DSB_LINEAR_SWIGLU takes weight rows in 128-row tiles whose first 64 rows
+ * are gate rows and last 64 the up rows of the same 64 output features
+ * (tile i: gate rows 64 i .. 64 i + 63, then the matching up rows); the gate
+ * and up values are rounded to the storage type and out[t, f] =
+ * round(silu(gate) * up) for f < weight_rows / 2.  Row strides are in
+ * elements. */
+int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_features, const void *weight,
+                     int32_t weight_rows, int32_t epilogue, const void *residual,
+                     int64_t residual_row_stride, void *out, int64_t out_row_stride,
+                     int32_t dtype, int32_t flags, int32_t *error_flag, void *stream);
 
 /* Elementwise stages of one draft decoder layer (the vLLM Eagle3 Llama layer
  * of the diffspec draft model, qkv input built at diffspec/vllm_patch.py:

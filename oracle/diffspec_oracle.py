@@ -439,6 +439,15 @@ def kv_projection_write_raw(hidden, weight, slots, positions, raw_key, raw_value
 # restate the published algorithms of its RMSNorm and SiLU-and-mul at the
 # storage dtype, and its RoPE at the working cache's local positions
 # (diffspec/runtime.py:1767-1794) with rope_rotate above.
+def linear(x, weight, residual=None, dtype="bf16"):
+    """A draft-layer linear (vLLM linear layers: ``x @ weight.T``), fp32
+    products and sums, plus ``residual`` before the one rounding when given."""
+    y = np.asarray(x, dtype=np.float32) @ np.asarray(weight, dtype=np.float32).T
+    if residual is not None:
+        y = y + np.asarray(residual, dtype=np.float32)
+    return round_to(y, dtype)
+
+
 def rms_norm(x, weight, eps, dtype="bf16"):
     """round(x * 1/sqrt(mean(x^2) + eps) * weight) per row (fp64 sum of
     squares, fp32 scaling: products rounded in fp32)."""

@@ -1,5 +1,7 @@
 """Draft-layer K/V projection with the raw-cache write in its epilogue
-(dsb_kv_projection_write_raw) against the oracle's projection + _write_raw."""
+(dsb_kv_projection_write_raw, dsb_qkv_projection_write_raw) and the
+draft-layer linear with its plain / residual / SwiGLU epilogues
+(dsb_draft_linear) against the oracle."""
 
 from __future__ import annotations
 
@@ -14,22 +16,26 @@ pytestmark = pytest.mark.gpu
 _T = {"bf16": torch.bfloat16, "f16": torch.float16}
 
 
-@pytest.fixture(autouse=True, params=["ranks16", "ranks8"])
+@pytest.fixture(autouse=True, params=["auto", "ranks16", "ranks8", "ranks1"])
 def cluster_size(request, monkeypatch):
-    """Every case with the default 16-CTA split-K clusters and with the 8-CTA
-    ones (DSB_KV_PROJECTION_RANKS8=1)."""
+    """Every case with the split-K cluster size chosen per launch and with it
+    forced to 16, 8 (DSB_KV_PROJECTION_RANKS8=1) and 1 (DSB_LINEAR_RANKS)."""
     if request.param == "ranks8":
         monkeypatch.setenv("DSB_KV_PROJECTION_RANKS8", "1")
+    elif request.param != "auto":
+        monkeypatch.setenv("DSB_LINEAR_RANKS", request.param[5:])
     return request.param
 _FRAC = {"bf16": 7, "f16": 10}  # fraction bits of the stored type
 
 
-def within_one_ulp(got, ref_f32, dtype):
+def within_one_ulp(got, ref_f32, dtype, k=0):
     """|got - ref| <= one unit in the last place of the stored type at |ref|
-    (the fp32 sums differ only in order from the oracle's)."""
+    (the fp32 sums differ only in order from the oracle's), or, for outputs
+    near zero whose ulp is below the fp32 summation error of k unit-scale
+    products, <= sqrt(k) * 2^-20 (about 16x that error's typical size)."""
     mag = np.maximum(np.abs(ref_f32), 2.0 ** -14)
     ulp = np.exp2(np.floor(np.log2(mag)) - _FRAC[dtype])
-    return np.abs(got - ref_f32) <= ulp
+    return np.abs(got - ref_f32) <= np.maximum(ulp, np.sqrt(k) * 2.0 ** -20)
 
 
 @pytest.mark.parametrize("dtype,tokens,hidden,hk,d", [
@@ -37,6 +43,7 @@ def within_one_ulp(got, ref_f32, dtype):
     ("bf16", 37, 512, 2, 64),     # three token tiles, ragged last one
     ("f16", 5, 1024, 1, 128),     # fewer tokens than a tile, ranks with one k-block each
     ("bf16", 20, 256, 4, 128),    # fewer k-blocks than cluster ranks
+    ("bf16", 16, 6144, 4, 128),   # more k-blocks per rank than ring slots
 ])
 def test_projection_and_raw_write_match_oracle(dsb, cuda, dtype, tokens, hidden, hk, d):
     rng = np.random.default_rng(tokens * 31 + hidden)
@@ -62,7 +69,7 @@ def test_projection_and_raw_write_match_oracle(dsb, cuda, dtype, tokens, hidden,
     ref = O.kv_projection_write_raw(h, w, slots, positions, ok_, ov_, dtype)
     ref_f32 = h.astype(np.float64) @ w.astype(np.float64).T
     got = out.float().cpu().numpy()
-    assert within_one_ulp(got, ref_f32, dtype).all()
+    assert within_one_ulp(got, ref_f32, dtype, hidden).all()
     assert (got == ref).mean() > 0.99  # nearly all round the same way as the oracle
     # the cache rows hold exactly the returned rows; every other row is untouched
     half = hk * d
@@ -113,3 +120,89 @@ def test_runtime_projection_writes_the_draft_cache(dsb, cuda):
         s, p = int(slots[t]), int(pos[t])
         assert torch.equal(cache.raw_key[s, p].reshape(-1), out[t, :128])
         assert torch.equal(cache.raw_value[s, p].reshape(-1), out[t, 128:])
+
+
+def _cells(rng, tokens, slots_n, max_len):
+    slots = (np.arange(tokens) % slots_n).astype(np.int32)
+    positions = (np.arange(tokens) // slots_n * 7 + 2).astype(np.int64) % max_len
+    return slots, positions
+
+
+@pytest.mark.parametrize("prefetch", [False, True])
+@pytest.mark.parametrize("tokens,hidden,qf,hk,d", [(16, 4096, 4096, 4, 128), (21, 1024, 256, 1, 128)])
+def test_qkv_projection_routes_query_and_kv(dsb, cuda, prefetch, tokens, hidden, qf, hk, d):
+    rng = np.random.default_rng(hidden + qf)
+    slots_n, max_len = 8, 64
+    h = O.round_to(rng.standard_normal((tokens, hidden), dtype=np.float32), "bf16")
+    w = O.round_to(rng.standard_normal((qf + 2 * hk * d, hidden), dtype=np.float32) / np.sqrt(hidden),
+                   "bf16")
+    slots, positions = _cells(rng, tokens, slots_n, max_len)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    rk = torch.zeros((slots_n, max_len, hk, d), dtype=torch.bfloat16, device=cuda)
+    rv = torch.zeros_like(rk)
+    q, kv = dsb.kernels.qkv_projection_write_raw(dev(h).bfloat16(), dev(w).bfloat16(), qf,
+                                                 dev(slots), dev(positions), rk, rv,
+                                                 prefetch_weight=prefetch)
+    torch.cuda.synchronize()
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+    ref = h.astype(np.float64) @ w.astype(np.float64).T
+    got = torch.cat((q, kv), 1).float().cpu().numpy()
+    assert within_one_ulp(got, ref, "bf16", hidden).all()
+    assert (got == O.linear(h, w)).mean() > 0.99
+    half = hk * d
+    for t in range(tokens):
+        np.testing.assert_array_equal(rk[slots[t], positions[t]].reshape(-1).float().cpu().numpy(),
+                                      got[t, qf: qf + half])
+        np.testing.assert_array_equal(rv[slots[t], positions[t]].reshape(-1).float().cpu().numpy(),
+                                      got[t, qf + half:])
+
+
+@pytest.mark.parametrize("epilogue", ["plain", "residual", "swiglu"])
+@pytest.mark.parametrize("dtype,tokens,k,rows", [
+    ("bf16", 16, 4096, 2048),    # config-5 o_proj shape
+    ("bf16", 16, 2048, 1024),    # gate_up-like (inter 512)
+    ("f16", 37, 6144, 256),      # down_proj K: ring refills; ragged token tiles
+    ("bf16", 3, 64, 128),        # one k-block: most ranks have none
+])
+def test_draft_linear_epilogues_match_oracle(dsb, cuda, epilogue, dtype, tokens, k, rows):
+    rng = np.random.default_rng(tokens * 7 + k + rows)
+    x = O.round_to(rng.standard_normal((tokens, k), dtype=np.float32), dtype)
+    w = O.round_to(rng.standard_normal((rows, k), dtype=np.float32) / np.sqrt(k), dtype)
+    tdt = _T[dtype]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda).to(tdt)  # noqa: E731
+    dl = dsb.draft_layer
+    if epilogue == "swiglu":
+        got = dl.draft_linear(dev(x), dl.interleave_gate_up(dev(w)), "swiglu").float().cpu().numpy()
+        torch.cuda.synchronize()
+        gu = O.linear(x, w, dtype=dtype)
+        ref = O.silu_mul(gu, dtype)
+        # gate and up are rounded sums, each of which may round one ulp away
+        # from the oracle's (summation order; more near zero): bound = what
+        # that moves silu(gate) * up by, plus two ulp of the output
+        def ulp(a):
+            return np.exp2(np.floor(np.log2(np.maximum(np.abs(a), 2.0 ** -14))) - _FRAC[dtype])
+        inter = rows // 2
+        g, u = gu[:, :inter].astype(np.float64), gu[:, inter:].astype(np.float64)
+        sig = 1.0 / (1.0 + np.exp(-g))
+        floor = np.sqrt(k) * 2.0 ** -20  # fp32 summation error near zero (within_one_ulp)
+        err_g, err_u = np.maximum(ulp(g), floor), np.maximum(ulp(u), floor)
+        bound = (np.abs(sig * (1 + g * (1 - sig))) * err_g * np.abs(u) + np.abs(g * sig) * err_u
+                 + 2 * ulp(ref))
+        assert (np.abs(got - ref) <= bound).all()
+        # two rounded inputs per output: 0.955 equal seen with one unsplit fp16
+        # accumulator over K = 6144, > 0.99 with split ones
+        assert (got == ref).mean() > 0.94
+    else:
+        res = O.round_to(rng.standard_normal((tokens, rows), dtype=np.float32), dtype)
+        got = dl.draft_linear(dev(x), dev(w), epilogue,
+                              residual=dev(res) if epilogue == "residual" else None)
+        got = got.float().cpu().numpy()
+        ref64 = x.astype(np.float64) @ w.astype(np.float64).T
+        if epilogue == "residual":
+            ref64 = ref64 + res
+        assert within_one_ulp(got, ref64, dtype, k).all()
+        # one unsplit accumulator over K = 6144 (forced 1-CTA clusters) rounds
+        # fp16 outputs away from the oracle's sequential fp32 sum slightly more often
+        same = (got == O.linear(x, w, res if epilogue == "residual" else None, dtype)).mean()
+        assert same > 0.97
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0

@@ -90,6 +90,15 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _P, _I32, _I64, _I32, _P, _P, _P],
     ),
+    "dsb_qkv_projection_write_raw": (
+        ctypes.c_int,
+        [_P, _I32, _I32, _P, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _I64, _I32, _P, _P, _I32,
+         _P, _P],
+    ),
+    "dsb_draft_linear": (
+        ctypes.c_int,
+        [_P, _I32, _I32, _P, _I32, _I32, _P, _I64, _P, _I64, _I32, _I32, _P, _P],
+    ),
     "dsb_rms_norm": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _I32, _I32, _F32, _I32, _P]),
     "dsb_rope_qk": (
         ctypes.c_int,

@@ -8,10 +8,11 @@ applied at the working cache's local positions (runtime.py:1767-1794), and
 the attention runs over the compact working cache (runtime.py:2024-2134),
 followed by the output projection and a SwiGLU MLP with RMSNorm.
 
-Here the K/V projection with the raw-cache write, the draft attention and the
-elementwise stages (RMSNorm, RoPE of q/k, SwiGLU: one launch each) are this
-library's kernels; the query / output projections and the MLP are plain
-GEMMs (cuBLAS through torch, residual adds in their epilogue).  The
+Every stage is this library's kernels: RMSNorm, the query + K/V projection
+with the raw-cache write (one tcgen05 launch), RoPE of q/k, the draft
+attention, and the output / gate-up / down projections on the same
+weight-streaming tcgen05 linear kernel with the residual adds and SwiGLU in
+its epilogue.  The
 weights are random (no checkpoint is involved); the layer exists to turn the
 kernels into draft tokens per second and to show how the
 pieces compose.  The LM head is not included: its vocabulary is unspecified.
@@ -23,9 +24,10 @@ import torch
 
 from . import _lib
 from .attention import AttentionWorkspace, draft_decode_attention
-from .kernels import kv_projection_write_raw
+from .kernels import qkv_projection_write_raw
 
-__all__ = ["Eagle3DraftLayer", "rms_norm", "rope_qk", "silu_mul"]
+__all__ = ["Eagle3DraftLayer", "draft_linear", "interleave_gate_up", "rms_norm", "rope_qk",
+           "silu_mul"]
 
 
 def _rows(t: torch.Tensor, what: str) -> int:
@@ -33,6 +35,55 @@ def _rows(t: torch.Tensor, what: str) -> int:
     if t.ndim != 2 or t.stride(1) != 1:
         raise ValueError(f"{what} must be 2-D with contiguous rows")
     return t.stride(0)
+
+
+_EPILOGUES = {"plain": 0, "residual": 1, "swiglu": 2}
+
+
+def interleave_gate_up(weight: torch.Tensor) -> torch.Tensor:
+    """A ``[2 * inter, K]`` gate_up weight (gate rows, then up rows) in the
+    tile order ``draft_linear(..., "swiglu")`` reads: 128-row tiles whose
+    first 64 rows are gate rows ``64 i .. 64 i + 63`` and last 64 the
+    matching up rows.  A one-time permutation at load time."""
+    inter = weight.shape[0] // 2
+    if weight.shape[0] != 2 * inter or inter % 64:
+        raise ValueError("gate_up weight rows must be 2 * inter with inter a multiple of 64")
+    gate, up = weight[:inter].view(inter // 64, 64, -1), weight[inter:].view(inter // 64, 64, -1)
+    return torch.stack((gate, up), 1).reshape(2 * inter, -1).contiguous()
+
+
+def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
+                 residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 prefetch_weight: bool = True) -> torch.Tensor:
+    """``x [T, K] @ weight.T`` on the tensor cores (``dsb_draft_linear``),
+    with ``epilogue`` "plain", "residual" (``+ residual`` before the one
+    rounding) or "swiglu" (``weight`` from :func:`interleave_gate_up`; out
+    ``[T, rows / 2] = silu(gate) * up``).  ``prefetch_weight`` starts the
+    weight stream before the previous kernel has finished (the weight must
+    not be written by that kernel)."""
+    if epilogue not in _EPILOGUES:
+        raise ValueError(f"epilogue must be one of {sorted(_EPILOGUES)}")
+    if x.ndim != 2 or weight.ndim != 2 or weight.shape[1] != x.shape[1] or x.dtype != weight.dtype:
+        raise ValueError("x must be [T, K] and weight [rows, K] in one dtype")
+    if not (x.is_contiguous() and weight.is_contiguous()):
+        raise ValueError("x and weight must be contiguous")
+    cols = weight.shape[0] // 2 if epilogue == "swiglu" else weight.shape[0]
+    device = _lib.require_cuda(x, weight, residual, out)
+    if epilogue == "residual":
+        if residual is None or residual.shape != (x.shape[0], cols) or residual.dtype != x.dtype:
+            raise ValueError("residual must be [T, rows] in the input dtype")
+        res_stride = _rows(residual, "residual")
+    else:
+        res_stride = 0
+    if out is None:
+        out = torch.empty((x.shape[0], cols), dtype=x.dtype, device=device)
+    elif out.shape != (x.shape[0], cols) or out.dtype != x.dtype:
+        raise ValueError("out has the wrong shape or dtype")
+    _lib.call("dsb_draft_linear", _lib.ptr(x), x.shape[0], x.shape[1], _lib.ptr(weight),
+              weight.shape[0], _EPILOGUES[epilogue], _lib.ptr(residual), res_stride, _lib.ptr(out),
+              _rows(out, "out"), _lib.dtype_code(x.dtype), 1 if prefetch_weight else 0,
+              _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device))
+    return out
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
@@ -118,11 +169,16 @@ class Eagle3DraftLayer:
 
         self.hq, self.hk, self.d, self.eps = num_heads, num_kv_heads, head_dim, eps
         self.inter = intermediate
-        self.w_q = w(num_heads * head_dim, qkv_in)
-        self.w_kv = w(2 * num_kv_heads * head_dim, qkv_in)  # K rows, then V rows
+        # one [q | K | V] weight for the fused projection; w_q / w_kv are views
+        self.w_qkv = w((num_heads + 2 * num_kv_heads) * head_dim, qkv_in)
+        self.w_q = self.w_qkv[: num_heads * head_dim]
+        self.w_kv = self.w_qkv[num_heads * head_dim:]  # K rows, then V rows
         self.w_o = w(hidden, num_heads * head_dim)
         self.w_gate_up = w(2 * intermediate, hidden)
         self.w_down = w(hidden, intermediate)
+        # the gate/up weight in the tile order of the SwiGLU epilogue (a
+        # one-time permutation; w_gate_up keeps the [gate | up] order)
+        self.w_gate_up_tiles = interleave_gate_up(self.w_gate_up)
         self.in_norm = torch.ones(qkv_in, dtype=dtype, device=device)
         self.post_norm = torch.ones(hidden, dtype=dtype, device=device)
         self.workspace = AttentionWorkspace(device)
@@ -140,13 +196,12 @@ class Eagle3DraftLayer:
         ``[n, hidden]``."""
         n = x_in.shape[0]
         h = rms_norm(x_in, self.in_norm, self.eps)
-        q = h @ self.w_q.t()
-        kv = kv_projection_write_raw(h, self.w_kv, slots, abs_positions, raw_key, raw_value)
+        q, kv = qkv_projection_write_raw(h, self.w_qkv, self.hq * self.d, slots, abs_positions,
+                                         raw_key, raw_value, prefetch_weight=True)
         k, v = rope_qk(q, kv, local_positions, cos_sin, self.hk)
         attn = draft_decode_attention(q.view(n, self.hq, self.d), k, v, working_key, working_value,
                                       slots, local_positions, self.d ** -0.5,
                                       workspace=self.workspace)
-        # residual adds in the GEMM epilogue (cuBLAS beta = 1: one rounding)
-        x = torch.addmm(residual, attn.view(n, self.hq * self.d), self.w_o.t())
-        act = silu_mul(rms_norm(x, self.post_norm, self.eps) @ self.w_gate_up.t())
-        return torch.addmm(x, act, self.w_down.t(), out=out)
+        x = draft_linear(attn.view(n, self.hq * self.d), self.w_o, "residual", residual)
+        act = draft_linear(rms_norm(x, self.post_norm, self.eps), self.w_gate_up_tiles, "swiglu")
+        return draft_linear(act, self.w_down, "residual", x, out=out)

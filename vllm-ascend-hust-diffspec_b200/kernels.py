@@ -19,6 +19,7 @@ __all__ = [
     "finalize_chunk_scores",
     "gather_raw_kv_with_local_rope",
     "kv_projection_write_raw",
+    "qkv_projection_write_raw",
 ]
 
 
@@ -425,3 +426,62 @@ def kv_projection_write_raw(
         _lib.stream_ptr(device),
     )
     return out
+
+
+def qkv_projection_write_raw(
+    hidden: torch.Tensor,
+    weight: torch.Tensor,
+    q_features: int,
+    slots: torch.Tensor,
+    positions: torch.Tensor,
+    raw_key: torch.Tensor,
+    raw_value: torch.Tensor,
+    q_out: torch.Tensor | None = None,
+    kv_out: torch.Tensor | None = None,
+    prefetch_weight: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """The draft layer's query + K/V projection in one launch.
+
+    ``weight [q_features + 2 * Hk * D, hidden_size]`` holds the query rows,
+    then the K rows, then the V rows (a QKVParallelLinear weight).  Returns
+    ``(q [T, q_features], kv [T, 2 * Hk * D])``; the K/V rows are also
+    written, pre-RoPE, to the raw caches at ``[slots[t], positions[t]]`` as
+    in :func:`kv_projection_write_raw`.  ``prefetch_weight`` lets the weight
+    stream start before the previous kernel in the stream has finished (the
+    weight must not be written by that kernel).
+    """
+    if hidden.ndim != 2 or weight.ndim != 2 or weight.shape[1] != hidden.shape[1]:
+        raise ValueError("hidden must be [T, hidden] and weight [q + 2 * Hk * D, hidden]")
+    if raw_key.ndim != 4 or raw_key.shape != raw_value.shape:
+        raise ValueError("raw key/value must have matching 4-D shapes")
+    num_slots, max_model_len, hk, d = raw_key.shape
+    if q_features < 0 or weight.shape[0] != q_features + 2 * hk * d:
+        raise ValueError("weight rows must be q_features + 2 * kv_heads * head_dim")
+    if not (hidden.dtype == weight.dtype == raw_key.dtype == raw_value.dtype):
+        raise ValueError("hidden, weight and raw caches must share a dtype")
+    tokens = hidden.shape[0]
+    if slots.shape[0] < tokens or positions.shape[0] < tokens:
+        raise ValueError("slots/positions must cover every token")
+    device = _lib.require_cuda(hidden, weight, slots, positions, raw_key, raw_value, q_out, kv_out)
+    for name, t, cols in (("q_out", q_out, q_features), ("kv_out", kv_out, 2 * hk * d)):
+        if t is not None and (t.shape != (tokens, cols) or t.dtype != hidden.dtype
+                              or not t.is_contiguous()):
+            raise ValueError(f"{name} must be contiguous [T, {cols}] in the hidden dtype")
+    if q_out is None:
+        q_out = torch.empty((tokens, q_features), dtype=hidden.dtype, device=device)
+    if kv_out is None:
+        kv_out = torch.empty((tokens, 2 * hk * d), dtype=hidden.dtype, device=device)
+    if not (hidden.is_contiguous() and weight.is_contiguous()):
+        raise ValueError("hidden and weight must be contiguous")
+    if slots.dtype != torch.int32 or positions.dtype != torch.int64:
+        raise ValueError("slots must be int32 and positions int64")
+    if not (raw_key.is_contiguous() and raw_value.is_contiguous()):
+        raise ValueError("raw caches must be contiguous")
+    _lib.call(
+        "dsb_qkv_projection_write_raw",
+        _lib.ptr(hidden), tokens, hidden.shape[1], _lib.ptr(weight), q_features, hk, d,
+        _lib.ptr(slots), _lib.ptr(positions), _lib.ptr(raw_key), _lib.ptr(raw_value), num_slots,
+        max_model_len, _lib.dtype_code(hidden.dtype), _lib.ptr(q_out), _lib.ptr(kv_out),
+        1 if prefetch_weight else 0, _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device),
+    )
+    return q_out, kv_out
