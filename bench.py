@@ -921,6 +921,89 @@ def run_kv_projection(args):
                           cublas_matmul_plus_scatter_us=round(ref_us, 3))))
 
 
+def run_draft_linear(args):
+    """Time the config-5 draft layer's four linears at a 16-token decode step
+    on the tcgen05 weight-streaming kernel (qkv with the raw-cache write,
+    o_proj + residual, gate_up + SwiGLU, down_proj + residual) against cuBLAS
+    for the same products (torch.mm; the K/V raw write, the residual add and
+    SwiGLU not included on that side).  Each shape cycles enough weight copies
+    (>= 300 MB, more than L2) that every launch streams its weight from HBM."""
+    import torch
+
+    dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(7)
+    bf = torch.bfloat16
+    tokens = 16
+    dl = dsb.draft_layer
+    rk = torch.zeros((B_GROUP, 4096, HK, D), dtype=bf, device=device)
+    rv = torch.zeros_like(rk)
+    slots = torch.arange(tokens, dtype=torch.int32, device=device)
+    pos = torch.full((tokens,), 1000, dtype=torch.int64, device=device)
+    shapes = {"qkv": (HQ * D + 2 * HK * D, 4096), "o_proj": (2048, HQ * D),
+              "gate_up": (2 * 6144, 2048), "down_proj": (2048, 6144)}
+    peak, peak_kind = _peaks()
+    result = {}
+    for name, (rows, k) in shapes.items():
+        copies = int(300e6 // (rows * k * 2)) + 1
+        ws = [(torch.randn((rows, k), generator=g, device=device) / k ** 0.5).to(bf)
+              for _ in range(copies)]
+        x = torch.randn((tokens, k), generator=g, device=device).to(bf)
+        res = torch.randn((tokens, rows), generator=g, device=device).to(bf)
+        out = torch.empty((tokens, rows), dtype=bf, device=device)
+        half = torch.empty((tokens, rows // 2), dtype=bf, device=device)
+        q_out = torch.empty((tokens, HQ * D), dtype=bf, device=device)
+        kv_out = torch.empty((tokens, 2 * HK * D), dtype=bf, device=device)
+
+        def ours(w, name=name, x=x, res=res, out=out, half=half, q_out=q_out, kv_out=kv_out):
+            if name == "qkv":
+                dsb.kernels.qkv_projection_write_raw(x, w, HQ * D, slots, pos, rk, rv, q_out=q_out,
+                                                     kv_out=kv_out, prefetch_weight=True)
+            elif name == "gate_up":  # the weight's tile order does not change the time
+                dl.draft_linear(x, w, "swiglu", out=half)
+            else:
+                dl.draft_linear(x, w, "residual", residual=res, out=out)
+
+        def cublas(w, x=x, out=out):
+            torch.mm(x, w.t(), out=out)
+
+        def time_graph(fn):
+            s = torch.cuda.Stream(device)
+            s.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(s):
+                for w in ws:
+                    fn(w)
+            torch.cuda.current_stream(device).wait_stream(s)
+            torch.cuda.synchronize(device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for w in ws:
+                    fn(w)
+            for _ in range(max(3, args.warmup)):
+                graph.replay()
+            torch.cuda.synchronize(device)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(args.steps):
+                graph.replay()
+            b.record()
+            torch.cuda.synchronize(device)
+            return a.elapsed_time(b) * 1e3 / (args.steps * len(ws))
+
+        us = time_graph(ours)
+        assert dsb._lib.read_and_clear_error_flag(device) == 0
+        ref = time_graph(cublas)
+        wbytes = rows * k * 2
+        result[name] = dict(weight_rows=rows, k=k, us=round(us, 2), weight_gbs=round(wbytes / us / 1e3, 1),
+                            frac_of_hbm_peak=round(wbytes / us / 1e3 / peak, 3),
+                            cublas_mm_us=round(ref, 2))
+        del ws
+        torch.cuda.empty_cache()
+    print(json.dumps(dict(mode="draft_linear", tokens=tokens, dtype="bf16", peak_gbs=peak,
+                          peak_kind=peak_kind, shapes=result)))
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -936,6 +1019,8 @@ def main():
                    help="time the K/V projection + raw-cache write (config 5 decode step)")
     p.add_argument("--draft-step", action="store_true",
                    help="config 5: draft tokens/s of a draft layer over the DiffSpec cache")
+    p.add_argument("--draft-linear", action="store_true",
+                   help="time the config-5 draft layer's four linears against cuBLAS")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -943,6 +1028,8 @@ def main():
         run_kv_projection(args)
     elif args.draft_step:
         run_draft_step(args)
+    elif args.draft_linear:
+        run_draft_linear(args)
     elif args.only:
         run_only(args)
     elif args.impl == "reference":
