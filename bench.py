@@ -807,15 +807,13 @@ def run_draft_step(args):
     retrieval = [(k, fn) for k, fn in launches if k in ("prepare", "scores", "select")]
     rebuilds = [fn for k, fn in launches if k == "rebuild"]
     abs_pos = [[(w.committed[c] + j).to(torch.int64) for j in range(DEPTH)] for c in range(INTERVAL)]
-    local = [torch.empty_like(w.hist) for _ in range(DEPTH)]
     outs = [torch.empty_like(residual) for _ in range(DEPTH)]
 
-    def step(c, j):
-        torch.add(w.hist, j, out=local[j])
+    def step(c, j):  # step j writes at the plan's history length + j
         layer.step(x_in, residual, slots=w.active, abs_positions=abs_pos[c][j],
-                   local_positions=local[j], raw_key=w.raw_key, raw_value=w.raw_value,
-                   working_key=w.working_key, working_value=w.working_value, cos_sin=w.cos_sin,
-                   out=outs[j])
+                   local_positions=w.hist, position_offset=j, raw_key=w.raw_key,
+                   raw_value=w.raw_value, working_key=w.working_key,
+                   working_value=w.working_value, cos_sin=w.cos_sin, out=outs[j])
 
     seq = list(retrieval)
     for c in range(INTERVAL):

@@ -321,14 +321,16 @@ int dsb_rms_norm(const void *x, int64_t x_row_stride, const void *weight, void *
  * dsb_kv_projection_write_raw) and written to key_out as contiguous [tokens,
  * num_kv_heads, head_dim] (key_out == key: in place, contiguous rows only).
  * With value non-NULL the value heads (row stride value_row_stride) are
- * copied unchanged to value_out in the same layout.  A position outside
- * [0, rotary_rows) leaves its rows unrotated and sets DSB_FLAG_POSITION.
- * Strides are in elements. */
+ * copied unchanged to value_out in the same layout.  Token t is rotated at
+ * positions[t] + position_offset (the K draft steps of one cycle share the
+ * plan's history lengths, step j passing j, as in
+ * dsb_draft_decode_attention); a position outside [0, rotary_rows) leaves
+ * its rows unrotated and sets DSB_FLAG_POSITION.  Strides are in elements. */
 int dsb_rope_qk(void *query, int64_t query_row_stride, int32_t num_query_heads,
                 const void *key, int64_t key_row_stride, void *key_out,
                 const void *value, int64_t value_row_stride, void *value_out,
                 int32_t num_kv_heads, int32_t head_dim, const int32_t *positions,
-                int32_t tokens, const void *cos_sin, int64_t cos_sin_row_stride,
+                int32_t position_offset, int32_t tokens, const void *cos_sin, int64_t cos_sin_row_stride,
                 int32_t rotary_rows, int32_t cos_sin_dtype, int32_t dtype,
                 int32_t *error_flag, void *stream);
 

@@ -71,12 +71,13 @@ def test_draft_layer_step_matches_fp32_reference(dsb, cuda):
     inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float64) / 128))
     fr = torch.arange(budget, dtype=torch.float64)[:, None] * inv[None]
     cos_sin = dev(torch.cat((fr.cos(), fr.sin()), -1)).to(bf)
-    for _ in range(2):  # the second step re-uses the layer's attention workspace
-        wk.copy_(wk0)
+    for offset in (0, 2):  # the second step re-uses the layer's attention workspace and
+        wk.copy_(wk0)       # reaches the same positions through position_offset
         wv.copy_(wv0)
         out = layer.step(x_in, residual, slots=slots, abs_positions=abs_pos,
-                         local_positions=local_pos, raw_key=raw_k, raw_value=raw_v,
-                         working_key=wk, working_value=wv, cos_sin=cos_sin)
+                         local_positions=local_pos - offset, position_offset=offset,
+                         raw_key=raw_k, raw_value=raw_v, working_key=wk, working_value=wv,
+                         cos_sin=cos_sin)
         torch.cuda.synchronize()
         assert dsb._lib.read_and_clear_error_flag(cuda) == 0
         ref, kv = _ref_step(layer, x_in, residual, slots, abs_pos, local_pos, wk0, wv0, cos_sin)
@@ -112,8 +113,10 @@ def test_rms_norm_matches_oracle(dsb, cuda, dtype, rows, cols, pad):
     assert (g == ref).mean() > 0.99
 
 
-@pytest.mark.parametrize("dtype,cs_dtype", [("bf16", torch.bfloat16), ("f16", torch.float32)])
-def test_rope_qk_matches_oracle(dsb, cuda, dtype, cs_dtype):
+@pytest.mark.parametrize("dtype,cs_dtype,offset", [("bf16", torch.bfloat16, 0),
+                                                   ("f16", torch.float32, 0),
+                                                   ("bf16", torch.bfloat16, 5)])
+def test_rope_qk_matches_oracle(dsb, cuda, dtype, cs_dtype, offset):
     rng = np.random.default_rng(5)
     t_n, hq, hk, d, rows = 9, 8, 2, 128, 300
     q = O.round_to(rng.standard_normal((t_n, hq * d), dtype=np.float32), dtype)
@@ -121,15 +124,16 @@ def test_rope_qk_matches_oracle(dsb, cuda, dtype, cs_dtype):
     ang = np.arange(rows)[:, None] * (1e4 ** (-np.arange(d // 2) / (d // 2)))[None]
     cs = O.round_to(np.concatenate((np.cos(ang), np.sin(ang)), -1).astype(np.float32),
                     "bf16" if cs_dtype == torch.bfloat16 else "f32")
-    pos = rng.integers(0, rows, t_n).astype(np.int32)
-    pos[3] = rows  # outside the table: rows left unrotated, flagged
+    pos = rng.integers(0, rows - offset, t_n).astype(np.int32)
+    pos[3] = rows - offset  # + offset: outside the table, rows left unrotated, flagged
     dev = lambda a, tdt: torch.from_numpy(np.ascontiguousarray(a)).to(cuda).to(tdt)  # noqa: E731
     qt, kvt = dev(q, _T[dtype]), dev(kv, _T[dtype])
-    k, v = dsb.draft_layer.rope_qk(qt, kvt, dev(pos, torch.int32), dev(cs, cs_dtype), hk)
+    k, v = dsb.draft_layer.rope_qk(qt, kvt, dev(pos, torch.int32), dev(cs, cs_dtype), hk,
+                                   position_offset=offset)
     flag = dsb._lib.read_and_clear_error_flag(cuda)
     assert flag == 2  # DSB_FLAG_POSITION
     ok = np.arange(t_n) != 3
-    rq, rk, rv = O.rope_qk(q[ok], kv[ok], pos[ok], cs, hk, dtype)
+    rq, rk, rv = O.rope_qk(q[ok], kv[ok], pos[ok] + offset, cs, hk, dtype)
     np.testing.assert_array_equal(qt.float().cpu().numpy()[ok], rq)
     np.testing.assert_array_equal(k.float().cpu().numpy()[ok], rk)
     np.testing.assert_array_equal(v.float().cpu().numpy(), kv[:, hk * d:].reshape(t_n, hk, d))

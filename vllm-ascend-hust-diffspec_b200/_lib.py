@@ -102,8 +102,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dsb_rms_norm": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _I32, _I32, _F32, _I32, _P]),
     "dsb_rope_qk": (
         ctypes.c_int,
-        [_P, _I64, _I32, _P, _I64, _P, _P, _I64, _P, _I32, _I32, _P, _I32, _P, _I64, _I32, _I32,
-         _I32, _P, _P],
+        [_P, _I64, _I32, _P, _I64, _P, _P, _I64, _P, _I32, _I32, _P, _I32, _I32, _P, _I64, _I32,
+         _I32, _I32, _P, _P],
     ),
     "dsb_silu_mul": (ctypes.c_int, [_P, _I64, _P, _I64, _I32, _I32, _I32, _P]),
     "dsb_gather_raw_kv_with_local_rope": (

@@ -120,6 +120,9 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   const int kb0 = rank * per;
   const int nkb = max(0, min(per, nkb_all - kb0));
   const int first = min(nkb, S);
+  // weights are streamed once per step: evicted first, so the working cache
+  // the draft attention re-reads keeps its L2 lines
+  const uint64_t wpol = l2_evict_first();
 
   // No activations yet: descriptor prefetch, barriers, tensor memory and
   // (when allowed) the first weight tiles overlap the previous kernel.
@@ -134,7 +137,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     if (a.prefetch)
       for (int kb = 0; kb < first; ++kb) {
         mbar_expect_tx(full0 + 8 * kb, kLnABytes + kLnBBytes);
-        tma_load_2d(s_a + kb * kLnABytes, &tw, (kb0 + kb) * 64, f0, full0 + 8 * kb);
+        tma_load_2d_hint(s_a + kb * kLnABytes, &tw, (kb0 + kb) * 64, f0, full0 + 8 * kb, wpol);
       }
   }
   if (warp == 0) {
@@ -163,7 +166,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
       }
       if (!(a.prefetch && kb < first)) {
         mbar_expect_tx(full0 + 8 * s, kLnABytes + kLnBBytes);
-        tma_load_2d(s_a + s * kLnABytes, &tw, (kb0 + kb) * 64, f0, full0 + 8 * s);
+        tma_load_2d_hint(s_a + s * kLnABytes, &tw, (kb0 + kb) * 64, f0, full0 + 8 * s, wpol);
       }
       tma_load_2d(s_b + s * kLnBBytes, &tx, (kb0 + kb) * 64, t0, full0 + 8 * s);
     }

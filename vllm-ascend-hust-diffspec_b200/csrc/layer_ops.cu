@@ -94,6 +94,7 @@ struct RopeArgs {
   const void *cos_sin;
   int64_t cs_stride;
   const int32_t *positions;
+  int pos_offset;
   int tokens, hq, hk, hv, head_dim, half, rotary_rows;
   int32_t *error_flag;
 };
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(256) rope_qk_kernel(RopeArgs a) {
                           : static_cast<const T *>(a.k) + t * a.k_stride + (h - a.hq) * hd;
   T *dst = h < a.hq ? static_cast<T *>(a.q) + t * a.q_stride + h * hd
                     : static_cast<T *>(a.k_out) + (static_cast<int64_t>(t) * a.hk + h - a.hq) * hd;
-  const int pos = a.positions[t];
+  const int pos = a.positions[t] + a.pos_offset;
   if (pos < 0 || pos >= a.rotary_rows) {
     if (lane == 0 && h == 0) flag_error(a.error_flag, DSB_FLAG_POSITION);
     if (src != dst)
@@ -197,7 +198,8 @@ extern "C" int dsb_rope_qk(void *query, int64_t query_row_stride, int32_t num_qu
                            const void *key, int64_t key_row_stride, void *key_out,
                            const void *value, int64_t value_row_stride, void *value_out,
                            int32_t num_kv_heads, int32_t head_dim, const int32_t *positions,
-                           int32_t tokens, const void *cos_sin, int64_t cos_sin_row_stride,
+                           int32_t position_offset, int32_t tokens, const void *cos_sin,
+                           int64_t cos_sin_row_stride,
                            int32_t rotary_rows, int32_t cos_sin_dtype, int32_t dtype,
                            int32_t *error_flag, void *stream) {
   if (tokens < 0) return fail(DSB_ERR_INVALID, "negative token count");
@@ -229,7 +231,8 @@ extern "C" int dsb_rope_qk(void *query, int64_t query_row_stride, int32_t num_qu
   const int64_t warps = (int64_t)tokens * (num_query_heads + num_kv_heads + hv);
   if ((warps + 7) / 8 > INT32_MAX) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
   RopeArgs a{query, key, value, key_out, value_out, query_row_stride, key_row_stride,
-             value_row_stride, cos_sin, cos_sin_row_stride, positions, tokens, num_query_heads,
+             value_row_stride, cos_sin, cos_sin_row_stride, positions, position_offset, tokens,
+             num_query_heads,
              num_kv_heads, hv, head_dim, head_dim / 2, rotary_rows, error_flag};
   const cudaStream_t st = as_stream(stream);
   const dim3 grid(static_cast<unsigned>((warps + 7) / 8)), block(256);

@@ -105,9 +105,10 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
 
 def rope_qk(query: torch.Tensor, kv: torch.Tensor, positions: torch.Tensor,
             cos_sin: torch.Tensor, num_kv_heads: int,
-            key_out: torch.Tensor | None = None, value_out: torch.Tensor | None = None):
-    """NeoX RoPE of one step at ``positions [T]`` (int32) of a ``[rows, cos |
-    sin]`` table: ``query [T, Hq * D]`` is rotated in place; the K half of
+            key_out: torch.Tensor | None = None, value_out: torch.Tensor | None = None,
+            position_offset: int = 0):
+    """NeoX RoPE of one step at ``positions [T] + position_offset`` (int32) of
+    a ``[rows, cos | sin]`` table: ``query [T, Hq * D]`` is rotated in place; the K half of
     the packed K/V projection rows ``kv [T, 2 * Hk * D]`` is rotated into
     ``key_out [T, Hk, D]`` and its V half copied into ``value_out``, the
     contiguous rows the draft attention reads.  One launch
@@ -133,7 +134,8 @@ def rope_qk(query: torch.Tensor, kv: torch.Tensor, positions: torch.Tensor,
     kv_stride = _rows(kv, "kv")
     _lib.call("dsb_rope_qk", _lib.ptr(query), _rows(query, "query"), query.shape[1] // d,
               _lib.ptr(kv), kv_stride, _lib.ptr(key_out), kv.data_ptr() + feats * kv.element_size(),
-              kv_stride, _lib.ptr(value_out), num_kv_heads, d, _lib.ptr(positions), tokens,
+              kv_stride, _lib.ptr(value_out), num_kv_heads, d, _lib.ptr(positions),
+              int(position_offset), tokens,
               _lib.ptr(cos_sin), cos_sin.stride(0), cos_sin.shape[0],
               _lib.dtype_code(cos_sin.dtype), _lib.dtype_code(kv.dtype),
               _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device))
@@ -188,20 +190,21 @@ class Eagle3DraftLayer:
                    for t in (self.w_q, self.w_kv, self.w_o, self.w_gate_up, self.w_down))
 
     def step(self, x_in, residual, *, slots, abs_positions, local_positions, raw_key, raw_value,
-             working_key, working_value, cos_sin, out=None):
+             working_key, working_value, cos_sin, out=None, position_offset=0):
         """One draft step for ``n`` rows: ``x_in [n, qkv_in]`` (embedding +
         hidden), ``residual [n, hidden]``.  Writes this step's pre-RoPE K/V to
         the raw caches at ``[slots, abs_positions]`` and its RoPE'd K/V into
-        the working caches at ``local_positions``; returns the layer output
-        ``[n, hidden]``."""
+        the working caches at ``local_positions + position_offset`` (step j
+        of a cycle passes the plan's history lengths and j); returns the
+        layer output ``[n, hidden]``."""
         n = x_in.shape[0]
         h = rms_norm(x_in, self.in_norm, self.eps)
         q, kv = qkv_projection_write_raw(h, self.w_qkv, self.hq * self.d, slots, abs_positions,
                                          raw_key, raw_value, prefetch_weight=True)
-        k, v = rope_qk(q, kv, local_positions, cos_sin, self.hk)
+        k, v = rope_qk(q, kv, local_positions, cos_sin, self.hk, position_offset=position_offset)
         attn = draft_decode_attention(q.view(n, self.hq, self.d), k, v, working_key, working_value,
                                       slots, local_positions, self.d ** -0.5,
-                                      workspace=self.workspace)
+                                      position_offset=position_offset, workspace=self.workspace)
         x = draft_linear(attn.view(n, self.hq * self.d), self.w_o, "residual", residual)
         act = draft_linear(rms_norm(x, self.post_norm, self.eps), self.w_gate_up_tiles, "swiglu")
         return draft_linear(act, self.w_down, "residual", x, out=out)
