@@ -55,3 +55,43 @@ def test_split_and_scratch_helpers(dsb):
     assert 1 <= splits <= 64
     assert lib.dsb_draft_attention_scratch_floats(16, 32, 4, 128, splits) == 16 * 4 * splits * 8 * 130
     assert lib.dsb_draft_attention_scratch_floats(2, 32, 2, 128, 3) == 2 * 2 * 3 * 16 * 130
+
+
+def test_draft_layer_entry_points_reject_bad_arguments(dsb):
+    """The draft-layer entry points validate on the host: no device pointer
+    is dereferenced (fake non-null addresses) and nothing is launched."""
+    lib = dsb._lib.load()
+    P, L = dsb._lib, lib
+    fake = ctypes.c_void_p(256)
+    # linear: unknown epilogue, K not a multiple of 64, rows not a multiple of 128,
+    # output stride shorter than a row, residual missing
+    assert L.dsb_draft_linear(fake, 16, 128, fake, 128, 7, None, 0, fake, 128, 0, 0, None, None) \
+        == P.DSB_ERR_INVALID
+    assert b"epilogue" in L.dsb_last_error()
+    assert L.dsb_draft_linear(fake, 16, 100, fake, 128, 0, None, 0, fake, 128, 0, 0, None, None) \
+        == P.DSB_ERR_UNSUPPORTED
+    assert L.dsb_draft_linear(fake, 16, 128, fake, 96, 0, None, 0, fake, 96, 0, 0, None, None) \
+        == P.DSB_ERR_UNSUPPORTED
+    assert L.dsb_draft_linear(fake, 16, 128, fake, 256, 2, None, 0, fake, 100, 0, 0, None, None) \
+        == P.DSB_ERR_INVALID  # SwiGLU output has 128 columns
+    assert L.dsb_draft_linear(fake, 16, 128, fake, 128, 1, None, 0, fake, 128, 0, 0, None, None) \
+        == P.DSB_ERR_INVALID
+    assert b"residual" in L.dsb_last_error()
+    assert L.dsb_draft_linear(fake, 16, 128, fake, 128, 0, None, 0, fake, 128, 5, 0, None, None) \
+        == P.DSB_ERR_INVALID  # fp32 is not a tensor-core operand type here
+    assert L.dsb_draft_linear(fake, 0, 128, fake, 128, 0, None, 0, fake, 128, 0, 0, None, None) \
+        == P.DSB_OK  # no tokens: nothing to do
+    # qkv projection: q features not a multiple of 128, missing q output
+    args = [fake, 16, 256, fake, 100, 1, 128, fake, fake, fake, fake, 4, 64, 0, fake, fake, 0, None,
+            None]
+    assert L.dsb_qkv_projection_write_raw(*args) == P.DSB_ERR_UNSUPPORTED
+    args[4], args[14] = 128, None
+    assert L.dsb_qkv_projection_write_raw(*args) == P.DSB_ERR_INVALID
+    # elementwise stages
+    assert L.dsb_rms_norm(fake, 12, fake, fake, 12, 2, 12, 1e-6, 0, None) == P.DSB_ERR_UNSUPPORTED
+    assert L.dsb_rms_norm(fake, 16, fake, fake, 16, 2, 16, -1.0, 0, None) == P.DSB_ERR_INVALID
+    assert L.dsb_silu_mul(fake, 8, fake, 8, 2, 8, 0, None) == P.DSB_ERR_UNSUPPORTED  # row < 2 * inter
+    assert L.dsb_rope_qk(fake, 256, 2, fake, 200, fake, None, 0, None, 2, 128, fake, 0, 3, fake, 128,
+                         64, 0, 0, None, None) == P.DSB_ERR_INVALID  # key row < 2 heads * 128
+    assert L.dsb_rope_qk(fake, 256, 2, fake, 256, fake, None, 0, None, 2, 127, fake, 0, 3, fake, 128,
+                         64, 0, 0, None, None) == P.DSB_ERR_INVALID  # odd head_dim
