@@ -292,7 +292,7 @@ int dsb_qkv_projection_write_raw(
  * are gate rows and last 64 the up rows of the same 64 output features
  * (tile i: gate rows 64 i .. 64 i + 63, then the matching up rows); the gate
  * and up values are rounded to the storage type and out[t, f] =
- * round(silu(gate) * up) for f < weight_rows / 2.  Row strides are in
+ * round(round(silu(gate)) * up) for f < weight_rows / 2 (vLLM SiluAndMul).  Row strides are in
  * elements. */
 int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_features, const void *weight,
                      int32_t weight_rows, int32_t epilogue, const void *residual,
@@ -305,8 +305,9 @@ int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_features, const v
  * 1767-1794).  The reference runs each as eager tensor ops; these are one
  * launch apiece.
  *
- * dsb_rms_norm: out[r] = round(x[r] * rsqrt(mean(x[r]^2) + eps) * weight),
- * fp32 math, for rows r < rows of cols elements (row strides in elements,
+ * dsb_rms_norm: out[r] = round(round(x[r] * rsqrt(mean(x[r]^2) + eps)) *
+ * weight), fp32 math rounded where vLLM's rms_norm rounds, for rows r < rows
+ * of cols elements (row strides in elements,
  * multiples of 8; cols a multiple of 8; 16-byte aligned; out must not
  * overlap x). */
 int dsb_rms_norm(const void *x, int64_t x_row_stride, const void *weight, void *out,
@@ -334,9 +335,9 @@ int dsb_rope_qk(void *query, int64_t query_row_stride, int32_t num_query_heads,
                 int32_t rotary_rows, int32_t cos_sin_dtype, int32_t dtype,
                 int32_t *error_flag, void *stream);
 
-/* dsb_silu_mul: out[r, i] = round(silu(gate_up[r, i]) * gate_up[r, intermediate
- * + i]) for i < intermediate (fp32 math, one rounding; SwiGLU with the gate
- * and up projections in one GEMM output).  intermediate and row strides are
+/* dsb_silu_mul: out[r, i] = round(round(silu(gate_up[r, i])) * gate_up[r,
+ * intermediate + i]) for i < intermediate (fp32 math rounded where vLLM's
+ * SiluAndMul rounds; the gate and up projections in one GEMM output).  intermediate and row strides are
  * multiples of 8 and rows 16-byte aligned. */
 int dsb_silu_mul(const void *gate_up, int64_t gate_up_row_stride, void *out,
                  int64_t out_row_stride, int32_t rows, int32_t intermediate, int32_t dtype,

@@ -436,9 +436,10 @@ def kv_projection_write_raw(hidden, weight, slots, positions, raw_key, raw_value
 # ------------------------------------------------------- draft layer elementwise stages
 # The draft model is vLLM's Eagle3 Llama layer (a dependency of the reference,
 # vllm>=0.28.1rc1.dev319,<0.28.2 in pyproject.toml, not vendored); these
-# restate the published algorithms of its RMSNorm and SiLU-and-mul at the
-# storage dtype, and its RoPE at the working cache's local positions
-# (diffspec/runtime.py:1767-1794) with rope_rotate above.
+# restate its RMSNorm and SiLU-and-mul at the storage dtype with vLLM's
+# rounding points, pinned by tests/golden/make_layer_golden.py against the
+# vLLM installed in this image, and its RoPE at the working cache's local
+# positions (diffspec/runtime.py:1767-1794) with rope_rotate above.
 def linear(x, weight, residual=None, dtype="bf16"):
     """A draft-layer linear (vLLM linear layers: ``x @ weight.T``), fp32
     products and sums, plus ``residual`` before the one rounding when given."""
@@ -449,21 +450,25 @@ def linear(x, weight, residual=None, dtype="bf16"):
 
 
 def rms_norm(x, weight, eps, dtype="bf16"):
-    """round(x * 1/sqrt(mean(x^2) + eps) * weight) per row (fp64 sum of
-    squares, fp32 scaling: products rounded in fp32)."""
+    """vLLM rms_norm (vllm/ir/ops/layernorm.py in the vLLM of this image):
+    round(round(x * 1/sqrt(mean(x^2) + eps)) * weight) per row, the
+    normalised value rounded to the weight dtype before the weight product
+    (fp64 sum of squares here, fp32 products)."""
     x = np.asarray(x, dtype=np.float32)
     ms = (x.astype(np.float64) ** 2).mean(-1, keepdims=True)
     inv = (1.0 / np.sqrt(ms + eps)).astype(np.float32)
-    return round_to((x * inv) * np.asarray(weight, dtype=np.float32), dtype)
+    return round_to(round_to(x * inv, dtype) * np.asarray(weight, dtype=np.float32), dtype)
 
 
 def silu_mul(gate_up, dtype="bf16"):
-    """SwiGLU of [rows, 2 * inter] rows holding gate then up:
-    round(gate / (1 + e^-gate) * up)."""
+    """vLLM SiluAndMul of [rows, 2 * inter] rows holding gate then up:
+    round(round(gate / (1 + e^-gate)) * up), silu rounded to the storage
+    dtype before the product."""
     gu = np.asarray(gate_up, dtype=np.float64)
     inter = gu.shape[-1] // 2
     g, u = gu[..., :inter], gu[..., inter:]
-    return round_to((g / (1.0 + np.exp(-g)) * u).astype(np.float32), dtype)
+    silu = round_to((g / (1.0 + np.exp(-g))).astype(np.float32), dtype)
+    return round_to(silu * u.astype(np.float32), dtype)
 
 
 def rope_qk(query, kv, positions, cos_sin, num_kv_heads, dtype="bf16"):

@@ -21,8 +21,8 @@ def _ref_step(layer, x_in, residual, slots, abs_pos, local_pos, wk0, wv0, cos_si
     bf = torch.bfloat16
     r = lambda t: t.to(bf).float()  # noqa: E731
 
-    def norm(x, w):
-        return r(x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + layer.eps) * w.float())
+    def norm(x, w):  # vLLM rms_norm: the normalised value rounded before the weight
+        return r(r(x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + layer.eps)) * w.float())
 
     def rope(x, pos):
         half = x.shape[-1] // 2
@@ -47,7 +47,7 @@ def _ref_step(layer, x_in, residual, slots, abs_pos, local_pos, wk0, wv0, cos_si
             attn[i, h_] = torch.softmax(sc, 0) @ V[h_ // g]
     x = r(residual.float() + r(attn).view(n, hq * d) @ layer.w_o.float().t())  # addmm: one rounding
     gu = r(norm(x, layer.post_norm) @ layer.w_gate_up.float().t())
-    act = r(torch.nn.functional.silu(gu[:, : layer.inter]) * gu[:, layer.inter:])
+    act = r(r(torch.nn.functional.silu(gu[:, : layer.inter])) * gu[:, layer.inter:])  # SiluAndMul
     return r(x + act @ layer.w_down.float().t()), kv
 
 

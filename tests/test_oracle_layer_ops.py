@@ -16,13 +16,14 @@ def test_rms_norm_and_silu_mul_agree_with_torch():
     x = O.round_to(rng.standard_normal((6, 256), dtype=np.float32), "bf16")
     w = O.round_to(rng.uniform(0.5, 1.5, 256).astype(np.float32), "bf16")
     xt = torch.from_numpy(x)
-    ref = (xt * torch.rsqrt(xt.pow(2).mean(-1, keepdim=True) + 1e-6) * torch.from_numpy(w)).bfloat16()
+    ref = ((xt * torch.rsqrt(xt.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16().float()
+           * torch.from_numpy(w)).bfloat16()
     got = O.rms_norm(x, w, 1e-6)
     assert (got == ref.float().numpy()).mean() > 0.99
     assert np.abs(got - ref.float().numpy()).max() <= 2.0 ** -6 * np.abs(got).max()
     gu = O.round_to(rng.standard_normal((6, 64), dtype=np.float32) * 4, "bf16")
     gt = torch.from_numpy(gu)
-    ref = (torch.nn.functional.silu(gt[:, :32]) * gt[:, 32:]).bfloat16().float().numpy()
+    ref = (torch.nn.functional.silu(gt[:, :32]).bfloat16().float() * gt[:, 32:]).bfloat16().float().numpy()
     got = O.silu_mul(gu)
     assert (got == ref).mean() > 0.99
 
@@ -56,3 +57,28 @@ def test_layer_op_wrappers_reject_host_tensors(dsb):
         dsb.draft_layer.rope_qk(torch.zeros((2, 16), dtype=torch.bfloat16),
                                 torch.zeros((2, 16), dtype=torch.bfloat16),
                                 torch.zeros(2, dtype=torch.int64), torch.zeros((4, 8)), 1)
+
+
+_FRAC = {"bf16": 7, "f16": 10}
+
+
+def _ulp(a, dtype):
+    return np.exp2(np.floor(np.log2(np.maximum(np.abs(a), 2.0 ** -14))) - _FRAC[dtype])
+
+
+@pytest.mark.parametrize("case", ["rms_bf16", "rms_f16", "silu_bf16", "silu_f16"])
+def test_oracle_matches_vllm_golden_vectors(case):
+    """tests/golden/layer_ops.npz holds vLLM's own rms_norm / SiluAndMul
+    outputs (tests/golden/make_layer_golden.py)."""
+    from conftest import ROOT
+    g = np.load(ROOT / "tests" / "golden" / "layer_ops.npz")
+    dtype = case.split("_")[1]
+    x, y = g[f"{case}_x"], g[f"{case}_y"]
+    if case.startswith("rms"):
+        got = O.rms_norm(x, g[f"{case}_w"], float(g["eps"]), dtype)
+    else:
+        got = O.silu_mul(x, dtype)
+    # same rounding points; only the fp32 reduction / exp of vLLM's torch ops
+    # can put a value on the other side of a rounding boundary
+    assert (np.abs(got - y) <= _ulp(y, dtype)).all()
+    assert (got == y).mean() > 0.99

@@ -241,7 +241,8 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   if (a.mode == kSwiglu) {
     // Tile rows 0..63 are gate rows and 64..127 the up rows of output
     // features f0 / 2 .. f0 / 2 + 63: both rounded to the storage type, as a
-    // gate_up GEMM output is, then silu(gate) * up rounded once.
+    // gate_up GEMM output is, then round(round(silu(gate)) * up) as vLLM's
+    // SiluAndMul computes it.
 #pragma unroll
     for (int j = 0; j < kTpr; ++j) sw[tid * kTpr + j] = Elem<T>::to_f(Elem<T>::from_f(v[j]));
     __syncthreads();
@@ -252,7 +253,8 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
         const int t = t0 + kTpr * rank + j;
         if (t >= a.T) continue;
         const float g = sw[tid * kTpr + j], u = sw[(tid + 64) * kTpr + j];
-        out[(int64_t)t * a.ldo + f0 / 2 + tid] = Elem<T>::from_f(__fmul_rn(silu_f(g), u));
+        const float sg = Elem<T>::to_f(Elem<T>::from_f(silu_f(g)));  // SiluAndMul rounds silu
+        out[(int64_t)t * a.ldo + f0 / 2 + tid] = Elem<T>::from_f(__fmul_rn(sg, u));
       }
     }
     return;

@@ -8,14 +8,17 @@
 // GEMMs a decode step of that layer runs three elementwise stages; each is a
 // handful of small tensor ops in eager PyTorch (one launch per op, ~2-3 us
 // each for a 16-row step), here one launch apiece:
-//   * rms_norm:   out = round(x * rsqrt(mean(x^2) + eps) * w), fp32 math;
+//   * rms_norm:   out = round(round(x * rsqrt(mean(x^2) + eps)) * w), fp32
+//                 math, rounded where vLLM's rms_norm rounds (the normalised
+//                 value to the weight dtype, then the product);
 //   * rope_qk:    queries of the step rotated in place and keys rotated
 //                 out of the K/V projection's packed rows into the
 //                 contiguous rows the draft attention reads, values copied
 //                 beside them (NeoX halves, products rounded before the add,
 //                 as in the working-cache rebuild);
-//   * silu_mul:   out = round(silu(gate) * up) over a [rows, 2 * inter] GEMM
-//                 output holding gate then up.
+//   * silu_mul:   out = round(round(silu(gate)) * up) over a [rows, 2 * inter]
+//                 GEMM output holding gate then up (vLLM SiluAndMul's rounding
+//                 points).
 // All three are latency bound at decode sizes (tens of KB per launch): one
 // CTA per row (norm), one warp per (token, head) (RoPE), a grid-stride loop
 // of 16-byte vectors (activation), with programmatic dependent launch so a
@@ -81,7 +84,8 @@ __global__ void __launch_bounds__(kNormThreads)
     load8(row + 8 * v, f);
     load8(w + 8 * v, g);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = __fmul_rn(__fmul_rn(f[i], inv), g[i]);
+    for (int i = 0; i < 8; ++i)  // normalised value rounded to T, then times the weight
+      f[i] = __fmul_rn(Elem<T>::to_f(Elem<T>::from_f(__fmul_rn(f[i], inv))), g[i]);
     store8(orow + 8 * v, f);
   }
 }
@@ -139,7 +143,7 @@ __global__ void __launch_bounds__(256) rope_qk_kernel(RopeArgs a) {
   }
 }
 
-// silu(g) = g / (1 + e^-g) in fp32, times up, one rounding; inter % 8 == 0.
+// silu(g) = g / (1 + e^-g) in fp32, rounded, times up, rounded; inter % 8 == 0.
 template <typename T>
 __global__ void __launch_bounds__(256)
     silu_mul_kernel(const T *__restrict__ gate_up, int64_t gu_stride, T *__restrict__ out,
@@ -155,7 +159,8 @@ __global__ void __launch_bounds__(256)
     load8(gate_up + r * gu_stride + c, g);
     load8(gate_up + r * gu_stride + inter + c, u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) g[i] = __fmul_rn(__fdiv_rn(g[i], 1.f + expf(-g[i])), u[i]);
+    for (int i = 0; i < 8; ++i)  // silu(gate) rounded to T, then times up
+      g[i] = __fmul_rn(Elem<T>::to_f(Elem<T>::from_f(__fdiv_rn(g[i], 1.f + expf(-g[i])))), u[i]);
     store8(out + r * out_stride + c, g);
   }
 }
