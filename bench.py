@@ -1002,6 +1002,54 @@ def run_draft_linear(args):
                           peak_kind=peak_kind, shapes=result)))
 
 
+def run_target_attention(args):
+    """Time the target paged decode attention with the LSE export at config 2's
+    shape (16 decode rows x 40960 tokens, 32 / 4 heads of 128, 16-token pages
+    in a shuffled block table: 1.34 GB of K/V per launch, more than L2) and
+    report its K/V streaming rate against the measured HBM copy peak."""
+    import torch
+
+    dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(21)
+    rows, ctx, bs = B_GROUP, CTX, 16
+    cols = ctx // bs
+    nblocks = rows * cols
+    bf = torch.bfloat16
+    kc = torch.randn((nblocks, bs, HK, D), generator=g, device=device).to(bf)
+    vc = torch.randn((nblocks, bs, HK, D), generator=g, device=device).to(bf)
+    table = torch.randperm(nblocks, generator=g, device=device).to(torch.int32).view(rows, cols)
+    q = torch.randn((rows, HQ, D), generator=g, device=device).to(bf)
+    lens = torch.full((rows,), ctx, dtype=torch.int32, device=device)
+    out = torch.empty_like(q)
+    lse = torch.empty((rows, HQ), dtype=torch.float32, device=device)
+
+    def launch():
+        dsb.kernels.paged_decode_attention_lse(q, kc, vc, table, lens, scale=D ** -0.5,
+                                               max_seq_len=ctx, out=out, lse=lse)
+
+    for _ in range(max(3, args.warmup)):
+        launch()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        launch()
+    b.record()
+    torch.cuda.synchronize(device)
+    assert dsb._lib.read_and_clear_error_flag(device) == 0
+    us = a.elapsed_time(b) * 1e3 / args.steps
+    nbytes = 2 * rows * ctx * HK * D * 2 + 2 * rows * HQ * D * 2 + rows * HQ * 4
+    peak, peak_kind = _peaks()
+    gbs = nbytes / us / 1e3
+    print(json.dumps(dict(mode="target_attention", rows=rows, context=ctx, q_heads=HQ, kv_heads=HK,
+                          head_dim=D, dtype="bf16", bytes_per_launch=nbytes,
+                          us_per_launch=round(us, 2), achieved_gbs=round(gbs, 1),
+                          frac_of_hbm_peak=round(gbs / peak, 3), peak_kind=peak_kind,
+                          l2="K/V 1.34 GB per launch, larger than L2")))
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -1019,6 +1067,8 @@ def main():
                    help="config 5: draft tokens/s of a draft layer over the DiffSpec cache")
     p.add_argument("--draft-linear", action="store_true",
                    help="time the config-5 draft layer's four linears against cuBLAS")
+    p.add_argument("--target-attention", action="store_true",
+                   help="time the target paged decode attention with the LSE export")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -1028,6 +1078,8 @@ def main():
         run_draft_step(args)
     elif args.draft_linear:
         run_draft_linear(args)
+    elif args.target_attention:
+        run_target_attention(args)
     elif args.only:
         run_only(args)
     elif args.impl == "reference":

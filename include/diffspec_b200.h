@@ -257,6 +257,33 @@ int dsb_kv_projection_write_raw(
     void *raw_key, void *raw_value, int32_t num_slots, int64_t max_model_len, int32_t dtype,
     void *out, int32_t *error_flag, void *stream);
 
+/* Target-model paged decode attention with the softmax LSE exported (the
+ * FIA call with softmax_lse_flag of diffspec/ascend_patch.py:191-240 whose
+ * LSE capture_target_attention keeps, diffspec/runtime.py:841-894).  For
+ * query row r (block-table row table_rows[r], or r when table_rows is NULL;
+ * the first seq_lens[r] tokens of that row visible) and query head h of kv
+ * group h / (num_query_heads / num_kv_heads):
+ *   out[r, h] = softmax(scale * q[r, h] . K^T) V      (rounded to dtype)
+ *   lse[r, h] = log(sum_t exp(scale * q[r, h] . k_t))  (fp32, natural log;
+ *               -inf and a zero output for an empty row)
+ * query / out [query_rows, num_query_heads, 128]; caches [num_blocks,
+ * block_size, num_kv_heads, 128]; block_table [block_table_rows,
+ * block_table_cols] with row stride block_table_stride.  max_seq_len bounds
+ * seq_lens and sets the split count (ceil(max_seq_len / tokens_per_split);
+ * tokens_per_split <= 0 picks 512); scratch holds
+ * dsb_paged_decode_scratch_floats floats.  Bad table rows set DSB_FLAG_SLOT,
+ * bad page entries DSB_FLAG_BLOCK (the token is skipped). */
+int64_t dsb_paged_decode_scratch_floats(int32_t query_rows, int32_t num_query_heads,
+                                        int32_t max_seq_len, int32_t tokens_per_split);
+int dsb_paged_decode_attention_lse(
+    const void *query, int32_t query_rows, int32_t num_query_heads, int32_t num_kv_heads,
+    int32_t head_dim, const void *key_cache, const void *value_cache, int64_t num_blocks,
+    int32_t block_size, const int32_t *block_table, int64_t block_table_stride,
+    int64_t block_table_rows, int64_t block_table_cols, const int32_t *seq_lens,
+    const int32_t *table_rows, int32_t max_seq_len, float scale, int32_t dtype,
+    int32_t tokens_per_split, void *out, float *lse, float *scratch, int64_t scratch_floats,
+    int32_t *error_flag, void *stream);
+
 /* Epilogues and flags of the draft-layer linear entry points. */
 #define DSB_LINEAR_PLAIN 0    /* out = x . W^T                                 */
 #define DSB_LINEAR_RESIDUAL 1 /* out = x . W^T + residual (one rounding)       */

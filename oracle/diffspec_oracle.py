@@ -433,6 +433,38 @@ def kv_projection_write_raw(hidden, weight, slots, positions, raw_key, raw_value
     return kv
 
 
+# ------------------------------------------------------- target attention + LSE
+def paged_decode_attention_lse(query, key_cache, value_cache, block_table, seq_lens, scale,
+                               table_rows=None, dtype="bf16"):
+    """The target verifier's attention with its softmax LSE (the FIA call with
+    softmax_lse_flag, diffspec/ascend_patch.py:191-240, whose LSE
+    capture_target_attention keeps, diffspec/runtime.py:841-894), in fp64:
+    out [rows, Hq, D] rounded to `dtype`, lse [rows, Hq] (natural log of the
+    softmax denominator of scale * q . k; -inf for an empty row)."""
+    q = np.asarray(query, dtype=np.float64)
+    rows, hq, d = q.shape
+    _, bs, hk, _ = key_cache.shape
+    group = hq // hk
+    out = np.zeros((rows, hq, d), dtype=np.float32)
+    lse = np.full((rows, hq), -np.inf, dtype=np.float32)
+    for r in range(rows):
+        length = int(seq_lens[r])
+        if length <= 0:
+            continue
+        trow = r if table_rows is None else int(table_rows[r])
+        toks = np.arange(length)
+        blocks = np.asarray(block_table[trow], dtype=np.int64)[toks // bs]
+        k = np.asarray(key_cache, dtype=np.float64)[blocks, toks % bs]   # [L, Hk, D]
+        v = np.asarray(value_cache, dtype=np.float64)[blocks, toks % bs]
+        for h in range(hq):
+            s = (k[:, h // group] @ q[r, h]) * scale
+            m = s.max()
+            p = np.exp(s - m)
+            out[r, h] = (p @ v[:, h // group]) / p.sum()
+            lse[r, h] = m + np.log(p.sum())
+    return round_to(out, dtype), lse
+
+
 # ------------------------------------------------------- draft layer elementwise stages
 # The draft model is vLLM's Eagle3 Llama layer (a dependency of the reference,
 # vllm>=0.28.1rc1.dev319,<0.28.2 in pyproject.toml, not vendored); these

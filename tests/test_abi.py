@@ -95,3 +95,27 @@ def test_draft_layer_entry_points_reject_bad_arguments(dsb):
                          64, 0, 0, None, None) == P.DSB_ERR_INVALID  # key row < 2 heads * 128
     assert L.dsb_rope_qk(fake, 256, 2, fake, 256, fake, None, 0, None, 2, 127, fake, 0, 3, fake, 128,
                          64, 0, 0, None, None) == P.DSB_ERR_INVALID  # odd head_dim
+
+
+def test_target_attention_rejects_bad_arguments(dsb):
+    lib = dsb._lib.load()
+    P = dsb._lib
+    fake = ctypes.c_void_p(256)
+    ok = [fake, 4, 32, 4, 128, fake, fake, 100, 16, fake, 8, 4, 8, fake, None, 128, 0.088, 0, 512,
+          fake, fake, fake, 10 ** 6, None, None]
+
+    def call(**over):
+        a = list(ok)
+        for i, v in over.items():
+            a[int(i[1:])] = v
+        return lib.dsb_paged_decode_attention_lse(*a)
+
+    assert call(a4=64) == P.DSB_ERR_UNSUPPORTED          # head_dim 64
+    assert call(a2=30) == P.DSB_ERR_INVALID              # 30 query heads over 4 kv heads
+    assert call(a16=0.0) == P.DSB_ERR_INVALID            # scale
+    assert call(a22=10) == P.DSB_ERR_INVALID             # scratch too small
+    assert b"scratch" in lib.dsb_last_error()
+    assert call(a10=4) == P.DSB_ERR_INVALID              # table stride shorter than its columns
+    assert call(a17=2) == P.DSB_ERR_INVALID              # fp32 caches
+    assert call(a1=0) == P.DSB_OK                        # no rows
+    assert lib.dsb_paged_decode_scratch_floats(4, 32, 1000, 512) == 4 * 32 * 2 * 130

@@ -90,6 +90,12 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _P, _I32, _I64, _I32, _P, _P, _P],
     ),
+    "dsb_paged_decode_scratch_floats": (_I64, [_I32, _I32, _I32, _I32]),
+    "dsb_paged_decode_attention_lse": (
+        ctypes.c_int,
+        [_P, _I32, _I32, _I32, _I32, _P, _P, _I64, _I32, _P, _I64, _I64, _I64, _P, _P, _I32, _F32,
+         _I32, _I32, _P, _P, _P, _I64, _P, _P],
+    ),
     "dsb_qkv_projection_write_raw": (
         ctypes.c_int,
         [_P, _I32, _I32, _P, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _I64, _I32, _P, _P, _I32,

@@ -20,6 +20,7 @@ __all__ = [
     "gather_raw_kv_with_local_rope",
     "kv_projection_write_raw",
     "qkv_projection_write_raw",
+    "paged_decode_attention_lse",
 ]
 
 
@@ -485,3 +486,72 @@ def qkv_projection_write_raw(
         1 if prefetch_weight else 0, _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device),
     )
     return q_out, kv_out
+
+
+def paged_decode_attention_lse(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    *,
+    scale: float,
+    max_seq_len: int,
+    table_rows: torch.Tensor | None = None,
+    tokens_per_split: int = 512,
+    out: torch.Tensor | None = None,
+    lse: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Target paged decode attention that also returns the softmax LSE.
+
+    The B200 stand-in for the target's FIA call with ``softmax_lse_flag``
+    (diffspec/ascend_patch.py:191-240) whose LSE ``capture_target_attention``
+    stores (diffspec/runtime.py:841-894): ``query [rows, Hq, 128]`` against
+    the paged ``key_cache`` / ``value_cache [blocks, block_size, Hk, 128]``,
+    row ``r`` seeing the first ``seq_lens[r]`` tokens of block-table row
+    ``table_rows[r]`` (default ``r``).  Returns ``(out [rows, Hq, 128],
+    lse [rows, Hq] fp32)``, ``lse`` the natural log of the softmax
+    denominator of ``scale * q . k`` — the ``softmax_lse`` that
+    :func:`paged_chunk_attention_scores` takes.
+    """
+    if query.ndim != 3 or key_cache.ndim != 4 or key_cache.shape != value_cache.shape:
+        raise ValueError("query must be [rows, Hq, D] and the caches matching [blocks, bs, Hk, D]")
+    rows, hq, d = query.shape
+    num_blocks, block_size, hk, kd = key_cache.shape
+    if d != kd or hq % hk:
+        raise ValueError("head dims must match and Hq must be a multiple of Hk")
+    if not (query.dtype == key_cache.dtype == value_cache.dtype):
+        raise ValueError("query and caches must share a dtype")
+    if block_table.ndim != 2 or seq_lens.numel() < rows:
+        raise ValueError("block_table must be 2-D and seq_lens cover every row")
+    device = _lib.require_cuda(query, key_cache, value_cache, block_table, seq_lens, table_rows)
+    if out is None:
+        out = torch.empty_like(query)
+    if lse is None:
+        lse = torch.empty((rows, hq), dtype=torch.float32, device=device)
+    if out.shape != query.shape or out.dtype != query.dtype or not out.is_contiguous():
+        raise ValueError("out must be contiguous and shaped like query")
+    if lse.shape != (rows, hq) or lse.dtype != torch.float32 or not lse.is_contiguous():
+        raise ValueError("lse must be contiguous fp32 [rows, Hq]")
+    if rows == 0:
+        return out, lse
+    query = query.contiguous()
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous")
+    table = _prep_index(block_table)
+    if table.stride(1) != 1:
+        table = table.contiguous()
+    seq = _prep_index(seq_lens).contiguous()
+    trows = None if table_rows is None else _prep_index(table_rows).contiguous()
+    floats = _lib.load().dsb_paged_decode_scratch_floats(rows, hq, int(max_seq_len), tokens_per_split)
+    scratch = torch.empty(max(floats, 1), dtype=torch.float32, device=device)
+    _lib.call(
+        "dsb_paged_decode_attention_lse",
+        _lib.ptr(query), rows, hq, hk, d, _lib.ptr(key_cache), _lib.ptr(value_cache), num_blocks,
+        block_size, _lib.ptr(table), table.stride(0), table.shape[0], table.shape[1],
+        _lib.ptr(seq), _lib.ptr(trows), int(max_seq_len), float(scale),
+        _lib.dtype_code(query.dtype), int(tokens_per_split), _lib.ptr(out), _lib.ptr(lse),
+        _lib.ptr(scratch), scratch.numel(), _lib.ptr(_lib.error_flag(device)),
+        _lib.stream_ptr(device),
+    )
+    return out, lse
