@@ -14,9 +14,9 @@
 // per token and kv head).  Split-KV: CTA (split, kv head, row) streams
 // tokens_per_split tokens of one kv head for all G = Hq / Hk query heads of
 // the group (the K/V rows are read once per group, not once per query
-// head); a warp takes every fourth token, lane l holding elements
-// 4l..4l+3 of the K and V rows (256-byte coalesced rows), two tokens in
-// flight per warp; online softmax in base 2 per query head.  The warps'
+// head); each warp takes every fourth 16-token tile and runs it through the
+// tensor cores (S = Q K^T and O += P V with mma.sync, base-2 online softmax
+// on the accumulators, P split into hi + lo 16-bit terms).  The warps'
 // states merge in shared memory and each CTA writes one (max, sum, acc[D])
 // partial per query head; a second launch merges the splits in order
 // (deterministic) and writes out and lse.  No waits on other CTAs.
@@ -45,23 +45,41 @@ struct TaArgs {
   int32_t *err;
 };
 
-template <typename T>
-__device__ __forceinline__ void load4(const T *p, float (&f)[4]) {
-  const uint2 w = *reinterpret_cast<const uint2 *>(p);
-  const float2 a = unpack2<T>(w.x), b = unpack2<T>(w.y);
-  f[0] = a.x;
-  f[1] = a.y;
-  f[2] = b.x;
-  f[3] = b.y;
+__device__ __forceinline__ uint32_t ta_word(const uint4 &v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
 
+constexpr int kTaTile = 16;                // tokens per warp tile
+constexpr int kTaVStride = kTaD * 2 + 16;  // bytes per staged V row (padded: ldmatrix without conflicts)
+constexpr int kTaVBytes = kTaTile * kTaVStride;
+
+template <int G> struct TaSmem {
+  static constexpr int kMerge = kTaWarps * G * kTaD * 4 + kTaWarps * 16 * 2 * 4;
+  static constexpr int kStage = kTaWarps * kTaVBytes;
+  static constexpr int kBytes = kMerge > kStage ? kMerge : kStage;
+};
+
+// Split-KV partial of one (split, kv head, row) on the tensor cores
+// (mma.sync m16n8k16, fp32 accumulate).  Per 16-token tile a warp computes
+//   S[16 heads x 16 tokens] = Q . K^T   (A = the group's query heads, rows
+//                                         >= G zero; B = the K rows, loaded
+//                                         straight into fragments with the
+//                                         head dim permuted the same way in
+//                                         A and B)
+// then the base-2 online softmax on S's accumulators, and
+//   O[16 heads x 128] += P . V          (A = P from S's accumulators, split
+//                                         into hi + lo 16-bit terms; B = V
+//                                         rows staged in padded shared memory
+//                                         and read with ldmatrix.trans).
 template <typename T, int G>
 __global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const TaArgs a) {
-  __shared__ float s_m[kTaWarps][G], s_l[kTaWarps][G];
-  __shared__ float s_acc[kTaWarps][G][kTaD];
+  static_assert(G <= 16, "at most 16 query heads per kv head");
+  // V staging during the loop, the warps' states for the merge after it
+  __shared__ __align__(16) uint8_t s_raw[TaSmem<G>::kBytes];
   pdl_begin();
   const int split = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
   int L = a.seq[r];
   const int trow = a.trows != nullptr ? a.trows[r] : r;
   if (trow < 0 || trow >= a.bt_rows) {
@@ -73,105 +91,174 @@ __global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const
   if (L < 0) L = 0;
   const int s0 = split * a.tps, s1 = min(L, s0 + a.tps);
 
-  float q[G][4], m[G], l[G], acc[G][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    load4(static_cast<const T *>(a.q) + ((int64_t)r * a.hq + h * G + g) * kTaD + 4 * lane, q[g]);
+  // Q A-fragments: rows g and g + 8 are query heads h * G + g (+ 8) when < G.
+  uint4 qlo[4], qhi[4];
+  {
+    const T *qb = static_cast<const T *>(a.q) + ((int64_t)r * a.hq + h * G) * kTaD;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      q[g][j] *= a.scale_log2;
-      acc[g][j] = 0.f;
+      qlo[j] = g < G ? *reinterpret_cast<const uint4 *>(qb + g * kTaD + 8 * (4 * j + t))
+                     : make_uint4(0, 0, 0, 0);
+      qhi[j] = g + 8 < G ? *reinterpret_cast<const uint4 *>(qb + (g + 8) * kTaD + 8 * (4 * j + t))
+                         : make_uint4(0, 0, 0, 0);
     }
-    m[g] = -INFINITY;
-    l[g] = 0.f;
   }
+  float o[16][4];
+#pragma unroll
+  for (int dn = 0; dn < 16; ++dn)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[dn][j] = 0.f;
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;  // rows g, g + 8
+
   const T *kc = static_cast<const T *>(a.k), *vc = static_cast<const T *>(a.v);
   const int32_t *row_bt = a.bt + (int64_t)trow * a.bt_stride;
-
-  // One token: its K/V row offset, or -1 when the page entry is bad.
-  auto row_of = [&](int t) -> int64_t {
-    const int blk = row_bt[t / a.bs];
-    if (blk < 0 || blk >= a.nblocks) return -1;
-    return (((int64_t)blk * a.bs + t % a.bs) * a.hk + h) * kTaD + 4 * lane;
-  };
-  auto consume = [&](const float (&kf)[4], const float (&vf)[4]) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float s = q[g][0] * kf[0];
-      s = fmaf(q[g][1], kf[1], s);
-      s = fmaf(q[g][2], kf[2], s);
-      s = fmaf(q[g][3], kf[3], s);
-#pragma unroll
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      const float mn = fmaxf(m[g], s);
-      const float c = exp2f(m[g] - mn), p = exp2f(s - mn);
-      l[g] = fmaf(l[g], c, p);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(acc[g][j], c, p * vf[j]);
-      m[g] = mn;
-    }
-  };
-
+  uint8_t *vs = s_raw + warp * kTaVBytes;
   bool bad = false;
-  int t = s0 + warp;
-  for (; t + kTaWarps < s1; t += 2 * kTaWarps) {  // two tokens in flight
-    const int64_t o0 = row_of(t), o1 = row_of(t + kTaWarps);
-    float k0[4] = {0.f, 0.f, 0.f, 0.f}, v0[4] = {0.f, 0.f, 0.f, 0.f};
-    float k1[4] = {0.f, 0.f, 0.f, 0.f}, v1[4] = {0.f, 0.f, 0.f, 0.f};
-    if (o0 >= 0) {
-      load4(kc + o0, k0);
-      load4(vc + o0, v0);
-    }
-    if (o1 >= 0) {
-      load4(kc + o1, k1);
-      load4(vc + o1, v1);
-    }
-    if (o0 >= 0) consume(k0, v0); else bad = true;
-    if (o1 >= 0) consume(k1, v1); else bad = true;
-  }
-  if (t < s1) {
-    const int64_t o0 = row_of(t);
-    if (o0 >= 0) {
-      float k0[4], v0[4];
-      load4(kc + o0, k0);
-      load4(vc + o0, v0);
-      consume(k0, v0);
-    } else {
-      bad = true;
-    }
-  }
-  if (bad && lane == 0) flag_error(a.err, DSB_FLAG_BLOCK);
+  // element offset of token `tok`'s row for this kv head, or -1
+  auto row_of = [&](int tok) -> int64_t {
+    const int blk = row_bt[tok / a.bs];
+    if (blk < 0 || blk >= a.nblocks) return -1;
+    return (((int64_t)blk * a.bs + tok % a.bs) * a.hk + h) * kTaD;
+  };
 
-  // Merge the four warps' states, then write this split's partial.
+  for (int T0 = s0 + warp * kTaTile; T0 < s1; T0 += kTaWarps * kTaTile) {
+    // ---- loads: K rows of tokens T0 + g and T0 + 8 + g; V chunks to stage
+    uint4 k0[4], k1[4], vv[8];
+    {
+      const int ta = T0 + g, tb = T0 + 8 + g;
+      const int64_t oa = ta < s1 ? row_of(ta) : -2, ob = tb < s1 ? row_of(tb) : -2;
+      bad |= (oa == -1) || (ob == -1);
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (lane == 0) {
-      s_m[warp][g] = m[g];
-      s_l[warp][g] = l[g];
+      for (int j = 0; j < 4; ++j) {
+        k0[j] = oa >= 0 ? *reinterpret_cast<const uint4 *>(kc + oa + 8 * (4 * j + t))
+                        : make_uint4(0, 0, 0, 0);
+        k1[j] = ob >= 0 ? *reinterpret_cast<const uint4 *>(kc + ob + 8 * (4 * j + t))
+                        : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {  // chunk c = lane + 32 i: row c / 16, 16-byte column c % 16
+        const int c = lane + 32 * i, row = c >> 4, col = c & 15;
+        const int tok = T0 + row;
+        const int64_t ov = tok < s1 ? row_of(tok) : -2;
+        vv[i] = ov >= 0 ? *reinterpret_cast<const uint4 *>(vc + ov + 8 * col) : make_uint4(0, 0, 0, 0);
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) s_acc[warp][g][4 * lane + j] = acc[g][j];
+    for (int i = 0; i < 8; ++i) {
+      const int c = lane + 32 * i;
+      *reinterpret_cast<uint4 *>(vs + (c >> 4) * kTaVStride + (c & 15) * 16) = vv[i];
+    }
+
+    // ---- S = Q K^T: two n-tiles of 8 tokens, 8 k-steps of 16 head-dim values
+    float sc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const int w0 = 2 * s, w1 = 2 * s + 1;
+        const uint32_t af[4] = {ta_word(qlo[w0 / 4], w0 % 4), ta_word(qhi[w0 / 4], w0 % 4),
+                                ta_word(qlo[w1 / 4], w1 % 4), ta_word(qhi[w1 / 4], w1 % 4)};
+        const uint4 *kk = nt == 0 ? k0 : k1;
+        const uint32_t bf[2] = {ta_word(kk[w0 / 4], w0 % 4), ta_word(kk[w1 / 4], w1 % 4)};
+        Mma<T>::run((s & 1) ? co : ce, af, bf);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int tok = T0 + 8 * nt + 2 * t + (j & 1);
+        sc[nt][j] = tok < s1 ? (ce[j] + co[j]) * a.scale_log2 : -INFINITY;
+      }
+    }
+    // ---- online softmax (rows g: j = 0, 1; rows g + 8: j = 2, 3)
+    float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+    float mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
+    }
+    // finite: token T0 is visible to every row of the tile
+    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+    const float c_lo = exp2f(m_lo - mn_lo), c_hi = exp2f(m_hi - mn_hi);
+    m_lo = mn_lo;
+    m_hi = mn_hi;
+    float p[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      p[nt][0] = exp2f(sc[nt][0] - mn_lo);
+      p[nt][1] = exp2f(sc[nt][1] - mn_lo);
+      p[nt][2] = exp2f(sc[nt][2] - mn_hi);
+      p[nt][3] = exp2f(sc[nt][3] - mn_hi);
+    }
+    l_lo = l_lo * c_lo + (p[0][0] + p[0][1] + p[1][0] + p[1][1]);  // this lane's share
+    l_hi = l_hi * c_hi + (p[0][2] + p[0][3] + p[1][2] + p[1][3]);
+#pragma unroll
+    for (int dn = 0; dn < 16; ++dn) {
+      o[dn][0] *= c_lo;
+      o[dn][1] *= c_lo;
+      o[dn][2] *= c_hi;
+      o[dn][3] *= c_hi;
+    }
+    uint32_t ph[4], pl[4];
+    pack2_split<T>(p[0][0], p[0][1], ph[0], pl[0]);
+    pack2_split<T>(p[0][2], p[0][3], ph[1], pl[1]);
+    pack2_split<T>(p[1][0], p[1][1], ph[2], pl[2]);
+    pack2_split<T>(p[1][2], p[1][3], ph[3], pl[3]);
+    __syncwarp();
+    // ---- O += P V over 16 n-tiles of 8 head-dim values
+#pragma unroll
+    for (int dn = 0; dn < 16; ++dn) {
+      uint32_t bv[2];
+      ldsm_x2_trans(bv, vs + (lane & 15) * kTaVStride + dn * 16);
+      Mma<T>::run(o[dn], ph, bv);
+      Mma<T>::run(o[dn], pl, bv);
+    }
+    __syncwarp();  // the next tile overwrites the staged V
+  }
+  if (bad) flag_error(a.err, DSB_FLAG_BLOCK);
+
+  // Warp state -> shared memory (rows < G), then merge the four warps.
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
+  }
+  __syncthreads();  // V staging no longer needed
+  float *s_acc = reinterpret_cast<float *>(s_raw);  // [warps][G][D]
+  float *s_ml = s_acc + kTaWarps * G * kTaD;        // [warps][16][2]: max, sum
+#pragma unroll
+  for (int dn = 0; dn < 16; ++dn)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int row = g + ((j & 2) ? 8 : 0), d = 8 * dn + 2 * t + (j & 1);
+      if (row < G) s_acc[(warp * G + row) * kTaD + d] = o[dn][j];
+    }
+  if (t == 0) {
+    s_ml[(warp * 16 + g) * 2] = m_lo;
+    s_ml[(warp * 16 + g) * 2 + 1] = l_lo;
+    s_ml[(warp * 16 + g + 8) * 2] = m_hi;
+    s_ml[(warp * 16 + g + 8) * 2 + 1] = l_hi;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < G * kTaD; i += kTaWarps * 32) {
-    const int g = i / kTaD, d = i % kTaD;
+    const int hh = i / kTaD, d = i % kTaD;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kTaWarps; ++w) M = fmaxf(M, s_m[w][g]);
+    for (int w = 0; w < kTaWarps; ++w) M = fmaxf(M, s_ml[(w * 16 + hh) * 2]);
     float sum = 0.f, ac = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kTaWarps; ++w) {
-        const float f = exp2f(s_m[w][g] - M);
-        sum = fmaf(s_l[w][g], f, sum);
-        ac = fmaf(s_acc[w][g][d], f, ac);
+        const float f = exp2f(s_ml[(w * 16 + hh) * 2] - M);
+        sum = fmaf(s_ml[(w * 16 + hh) * 2 + 1], f, sum);
+        ac = fmaf(s_acc[(w * G + hh) * kTaD + d], f, ac);
       }
     }
-    float *p = a.part + (((int64_t)r * a.hq + h * G + g) * a.splits + split) * (kTaD + 2);
-    p[d] = ac;
+    float *pp = a.part + (((int64_t)r * a.hq + h * G + hh) * a.splits + split) * (kTaD + 2);
+    pp[d] = ac;
     if (d == 0) {
-      p[kTaD] = M;
-      p[kTaD + 1] = sum;
+      pp[kTaD] = M;
+      pp[kTaD + 1] = sum;
     }
   }
 }
@@ -264,9 +351,9 @@ extern "C" int dsb_paged_decode_attention_lse(
   if (scratch_floats < dsb_paged_decode_scratch_floats(query_rows, num_query_heads, max_seq_len,
                                                        tokens_per_split))
     return fail(DSB_ERR_INVALID, "scratch smaller than dsb_paged_decode_scratch_floats");
-  if (reinterpret_cast<uintptr_t>(query) % 8 || reinterpret_cast<uintptr_t>(key_cache) % 8 ||
-      reinterpret_cast<uintptr_t>(value_cache) % 8)
-    return fail(DSB_ERR_UNSUPPORTED, "query and caches must be 8-byte aligned");
+  if (reinterpret_cast<uintptr_t>(query) % 16 || reinterpret_cast<uintptr_t>(key_cache) % 16 ||
+      reinterpret_cast<uintptr_t>(value_cache) % 16)
+    return fail(DSB_ERR_UNSUPPORTED, "query and caches must be 16-byte aligned");
   TaArgs a{};
   a.q = query;
   a.k = key_cache;
