@@ -4,6 +4,8 @@ driving the chunk-retrieval scores the way the captured FIA LSE does."""
 
 from __future__ import annotations
 
+from types import SimpleNamespace
+
 import numpy as np
 import pytest
 import torch
@@ -93,3 +95,34 @@ def test_exported_lse_drives_retrieval_scores(dsb, cuda):
     torch.cuda.synchronize()
     assert dsb._lib.read_and_clear_error_flag(cuda) == 0
     np.testing.assert_allclose(with_lse.cpu().numpy(), own.cpu().numpy(), rtol=1e-3, atol=1e-7)
+
+
+def test_runtime_runs_target_attention_and_captures_its_lse(dsb, cuda):
+    """DiffSpecDraftCache.run_target_attention: causal verify spans of three
+    rows per request, the output against the oracle, the captured LSE used by
+    the next retrieval."""
+    rng = np.random.default_rng(17)
+    seq_lens = [300, 150]
+    q, kc, vc, bt, _ = _case(rng, "bf16", 6, 8, 1, 16, seq_lens)
+    bt = bt[:2]
+    settings = dsb.runtime.DiffSpecSettings(16, 128, 1, 4, 3, 0.7, False)
+    cache = dsb.runtime.DiffSpecDraftCache(
+        settings, max_num_reqs=2, max_model_len=512, num_kv_heads=1, head_dim=128,
+        target_num_layers=2, dtype=torch.bfloat16, device=cuda,
+        cos_sin_cache=torch.zeros((128, 128), device=cuda).bfloat16())
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    meta = SimpleNamespace(actual_seq_lengths_q=[3, 6], seq_lens_list=seq_lens,
+                           block_tables=dev(bt), num_prefills=0)
+    cache.begin_target_forward(["a", "b"])
+    qt = dev(q).bfloat16()
+    out = cache.run_target_attention(qt, dev(kc).bfloat16(), dev(vc).bfloat16(), meta, 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+    visible = np.array([298, 299, 300, 148, 149, 150])
+    ref_out, ref_lse = O.paged_decode_attention_lse(q, kc, vc, bt, visible, 128 ** -0.5,
+                                                    table_rows=np.array([0, 0, 0, 1, 1, 1]))
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref_out, rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(cache._target["lse"].cpu().numpy(), ref_lse, atol=1e-4)
+    cache.accept_target_queries(torch.tensor([2, 3], device=cuda), is_prefill=False)
+    assert cache.retrieval_status()["retrieval_count"] == 1
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0

@@ -34,7 +34,7 @@ import torch
 from . import _lib
 from .attention import AttentionWorkspace, draft_decode_attention
 from .compact_kv import rebuild_working_cache
-from .kernels import kv_projection_write_raw, paged_chunk_head_scores
+from .kernels import kv_projection_write_raw, paged_chunk_head_scores, paged_decode_attention_lse
 from .parallel import gather_head_scores
 from .selection import (
     DiffSpecSelection,
@@ -349,6 +349,49 @@ class DiffSpecDraftCache:
             seq_lens=seq_lens, scale=scale,
         )
         self.target_is_prefill = is_prefill
+
+    def run_target_attention(
+        self,
+        query: torch.Tensor,
+        key_cache: torch.Tensor,
+        value_cache: torch.Tensor,
+        metadata: Any,
+        scale: float,
+    ) -> torch.Tensor:
+        """The target verifier's attention with its softmax LSE, captured for
+        retrieval: the B200 counterpart of the FIA call with softmax_lse_flag
+        whose LSE capture_target_attention keeps (diffspec/ascend_patch.py:
+        191-240, runtime.py:841-878).
+
+        ``query [n, Hq, D]`` holds each request's span of query rows in order
+        (``metadata.actual_seq_lengths_q``: cumulative ends); the j-th of a
+        span of s rows sees the first ``seq_lens_list[i] - (s - 1 - j)``
+        tokens of block-table row i (causal, for verify spans and prompts
+        alike).  Runs ``paged_decode_attention_lse`` once, stores the query,
+        LSE, cache and table through :meth:`capture_target_attention`, and
+        returns the attention output ``[n, Hq, D]``.
+        """
+        query_ends = [int(e) for e in metadata.actual_seq_lengths_q]
+        seq_lens = [int(x) for x in metadata.seq_lens_list]
+        if len(query_ends) > len(seq_lens) or (query_ends and query_ends[-1] != query.shape[0]):
+            raise ValueError("query rows must match actual_seq_lengths_q, one span per request")
+        visible, table_rows, start = [], [], 0
+        for i, end in enumerate(query_ends):
+            span = end - start
+            if span < 0:
+                raise ValueError("actual_seq_lengths_q must be non-decreasing")
+            for j in range(span):
+                visible.append(max(0, seq_lens[i] - (span - 1 - j)))
+                table_rows.append(i)
+            start = end
+        lens = torch.tensor(visible, dtype=torch.int32).to(self.device)
+        rows = torch.tensor(table_rows, dtype=torch.int32).to(self.device)
+        out, lse = paged_decode_attention_lse(
+            query, key_cache, value_cache, metadata.block_tables, lens, scale=scale,
+            max_seq_len=max(seq_lens, default=0), table_rows=rows,
+        )
+        self.capture_target_attention(query, lse, key_cache, metadata, scale)
+        return out
 
     def accept_target_queries(self, valid_sampled_token_count: torch.Tensor, *, is_prefill: bool) -> None:
         """Retrieve context with the last committed target query per request
