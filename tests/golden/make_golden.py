@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory by running the REFERENCE.
 
-Runs vllm-ascend-hust-diffspec 0.3.0 from a source checkout (default
-/root/reference, override with DIFFSPEC_REFERENCE) on seeded inputs:
+Runs vllm-ascend-hust-diffspec 0.3.0 from a source checkout (its directory
+given by the DIFFSPEC_REFERENCE environment variable) on seeded inputs:
 
 * its PyTorch CPU path (chunk_attention_scores, select_context_chunks,
   DiffSpecDraftCache._history_indices / _history_plan_host /
@@ -15,7 +15,7 @@ ref_stubs/vllm_ascend/ops/triton/rope.py for the one with math in it).  The
 outputs are written as compressed .npz files; bf16 tensors are stored as
 uint16 bit patterns (keys ending in "_bf16").
 
-Usage: python tests/golden/make_golden.py
+Usage: DIFFSPEC_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 """
 
 from __future__ import annotations
@@ -28,7 +28,9 @@ from types import SimpleNamespace
 
 os.environ["TRITON_INTERPRET"] = "1"
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("DIFFSPEC_REFERENCE", "/root/reference"))
+if "DIFFSPEC_REFERENCE" not in os.environ:
+    raise SystemExit("set DIFFSPEC_REFERENCE to the reference source checkout")
+REF = Path(os.environ["DIFFSPEC_REFERENCE"])
 sys.path.insert(0, str(HERE / "ref_stubs"))
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(HERE.parents[1]))  # repository root: oracle/, tests/golden/recipes.py
