@@ -82,3 +82,15 @@ def test_oracle_matches_vllm_golden_vectors(case):
     # can put a value on the other side of a rounding boundary
     assert (np.abs(got - y) <= _ulp(y, dtype)).all()
     assert (got == y).mean() > 0.99
+
+
+def test_causal_row_lengths_of_target_spans(dsb):
+    """Each query row of a target pass sees its request's prefix up to itself."""
+    f = dsb.runtime.causal_row_lengths
+    assert f([3, 6], [300, 150]) == ([298, 299, 300, 148, 149, 150], [0, 0, 0, 1, 1, 1])
+    assert f([1, 2], [7, 5]) == ([7, 5], [0, 1])          # plain decode: one row each
+    assert f([2, 2, 4], [1, 9, 3]) == ([0, 1, 2, 3], [0, 0, 2, 2])  # empty span; short prefix
+    with pytest.raises(ValueError):
+        f([3, 2], [5, 5])
+    with pytest.raises(ValueError):
+        f([1, 2, 3], [5, 5])

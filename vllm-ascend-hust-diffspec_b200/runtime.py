@@ -179,6 +179,25 @@ class _Staging:
         return self.dev[:n]
 
 
+def causal_row_lengths(query_ends: list[int], seq_lens: list[int]) -> tuple[list[int], list[int]]:
+    """Visible token count and block-table row of every query row of a
+    target pass: request i owns rows ``[query_ends[i-1], query_ends[i])`` (a
+    verify span or a prompt) and its j-th of s rows sees the first
+    ``seq_lens[i] - (s - 1 - j)`` tokens (causal; at least 0)."""
+    if len(query_ends) > len(seq_lens):
+        raise ValueError("one seq_lens entry per request span")
+    visible, table_rows, start = [], [], 0
+    for i, end in enumerate(query_ends):
+        span = end - start
+        if span < 0:
+            raise ValueError("actual_seq_lengths_q must be non-decreasing")
+        for j in range(span):
+            visible.append(max(0, seq_lens[i] - (span - 1 - j)))
+            table_rows.append(i)
+        start = end
+    return visible, table_rows
+
+
 class DiffSpecDraftCache:
     """Canonical raw KV and compact attention state for one-layer Eagle3 drafts."""
 
@@ -373,17 +392,9 @@ class DiffSpecDraftCache:
         """
         query_ends = [int(e) for e in metadata.actual_seq_lengths_q]
         seq_lens = [int(x) for x in metadata.seq_lens_list]
-        if len(query_ends) > len(seq_lens) or (query_ends and query_ends[-1] != query.shape[0]):
-            raise ValueError("query rows must match actual_seq_lengths_q, one span per request")
-        visible, table_rows, start = [], [], 0
-        for i, end in enumerate(query_ends):
-            span = end - start
-            if span < 0:
-                raise ValueError("actual_seq_lengths_q must be non-decreasing")
-            for j in range(span):
-                visible.append(max(0, seq_lens[i] - (span - 1 - j)))
-                table_rows.append(i)
-            start = end
+        if query_ends and query_ends[-1] != query.shape[0]:
+            raise ValueError("query rows must match actual_seq_lengths_q")
+        visible, table_rows = causal_row_lengths(query_ends, seq_lens)
         lens = torch.tensor(visible, dtype=torch.int32).to(self.device)
         rows = torch.tensor(table_rows, dtype=torch.int32).to(self.device)
         out, lse = paged_decode_attention_lse(
