@@ -47,6 +47,7 @@ __all__ = [
     "DiffSpecSelection",
     "DiffSpecRuntimeMetrics",
     "DiffSpecDraftCache",
+    "causal_row_lengths",
     "chunk_attention_scores",
     "select_context_chunks",
 ]
