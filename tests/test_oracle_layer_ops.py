@@ -94,3 +94,29 @@ def test_causal_row_lengths_of_target_spans(dsb):
         f([3, 2], [5, 5])
     with pytest.raises(ValueError):
         f([1, 2, 3], [5, 5])
+
+
+def test_oracle_target_lse_reproduces_the_scores_own_lse():
+    """oracle.paged_decode_attention_lse's LSE, given to the chunk scores,
+    gives the scores whose LSE they compute themselves (the softmax_lse=None
+    branch, pinned to the reference's fixtures), and its output is the
+    softmax-weighted V."""
+    rng = np.random.default_rng(8)
+    rows, hq, hk, bs, d = 3, 8, 2, 16, 128
+    lens = np.array([100, 37, 64])
+    table = rng.permutation(3 * 7).reshape(3, 7).astype(np.int32)
+    kc = O.round_to(rng.standard_normal((21, bs, hk, d), dtype=np.float32), "bf16")
+    vc = O.round_to(rng.standard_normal((21, bs, hk, d), dtype=np.float32), "bf16")
+    q = O.round_to(rng.standard_normal((rows, hq, d), dtype=np.float32), "bf16")
+    out, lse = O.paged_decode_attention_lse(q, kc, vc, table, lens, d ** -0.5, dtype="f32")
+    with_lse = O.paged_chunk_attention_scores(q, kc, lse, table, lens, 16, 112, d ** -0.5)
+    own = O.paged_chunk_attention_scores(q, kc, None, table, lens, 16, 112, d ** -0.5)
+    np.testing.assert_allclose(with_lse, own, rtol=1e-5, atol=1e-9)
+    # row 1, head 3 by hand
+    toks = np.arange(37)
+    k = kc[table[1][toks // bs], toks % bs, 3 // 4].astype(np.float64)
+    v = vc[table[1][toks // bs], toks % bs, 3 // 4].astype(np.float64)
+    s = k @ q[1, 3].astype(np.float64) * d ** -0.5
+    p = np.exp(s - s.max())
+    np.testing.assert_allclose(out[1, 3], p @ v / p.sum(), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(lse[1, 3], s.max() + np.log(p.sum()), rtol=1e-6)
