@@ -58,7 +58,8 @@ def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
     """``x [T, K] @ weight.T`` on the tensor cores (``dsb_draft_linear``),
     with ``epilogue`` "plain", "residual" (``+ residual`` before the one
     rounding) or "swiglu" (``weight`` from :func:`interleave_gate_up`; out
-    ``[T, rows / 2] = silu(gate) * up``).  ``prefetch_weight`` starts the
+    ``[T, rows / 2] = round(round(silu(gate)) * up)`` with gate and up
+    rounded first, as vLLM's gate_up output and SiluAndMul round them).  ``prefetch_weight`` starts the
     weight stream before the previous kernel has finished (the weight must
     not be written by that kernel)."""
     if epilogue not in _EPILOGUES:
@@ -88,8 +89,9 @@ def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
              out: torch.Tensor | None = None) -> torch.Tensor:
-    """``round(x * rsqrt(mean(x^2) + eps) * weight)`` per row of ``x [rows,
-    cols]`` (fp32 math), one launch (``dsb_rms_norm``)."""
+    """``round(round(x * rsqrt(mean(x^2) + eps)) * weight)`` per row of ``x
+    [rows, cols]`` (fp32 math, rounded where vLLM's rms_norm rounds), one
+    launch (``dsb_rms_norm``)."""
     if weight.shape != (x.shape[-1],) or weight.dtype != x.dtype:
         raise ValueError("weight must be [cols] in the rows' dtype")
     device = _lib.require_cuda(x, weight, out)
@@ -143,8 +145,9 @@ def rope_qk(query: torch.Tensor, kv: torch.Tensor, positions: torch.Tensor,
 
 
 def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """SwiGLU ``round(silu(gate) * up)`` of ``gate_up [rows, 2 * inter]``
-    (gate columns first, fp32 math), one launch (``dsb_silu_mul``)."""
+    """SwiGLU ``round(round(silu(gate)) * up)`` of ``gate_up [rows, 2 *
+    inter]`` (gate columns first, fp32 math rounded where vLLM's SiluAndMul
+    rounds), one launch (``dsb_silu_mul``)."""
     rows, two_inter = gate_up.shape
     inter = two_inter // 2
     device = _lib.require_cuda(gate_up, out)
