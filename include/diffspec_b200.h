@@ -272,7 +272,9 @@ int dsb_kv_projection_write_raw(
  * seq_lens and sets the split count (ceil(max_seq_len / tokens_per_split);
  * tokens_per_split <= 0 picks 512); scratch holds
  * dsb_paged_decode_scratch_floats floats.  Bad table rows set DSB_FLAG_SLOT,
- * bad page entries DSB_FLAG_BLOCK (the token is skipped). */
+ * bad page entries DSB_FLAG_BLOCK (the token is skipped), a seq_lens entry
+ * above the split count's reach (max_seq_len too small) DSB_FLAG_POSITION
+ * (the row is cut there). */
 int64_t dsb_paged_decode_scratch_floats(int32_t query_rows, int32_t num_query_heads,
                                         int32_t max_seq_len, int32_t tokens_per_split);
 int dsb_paged_decode_attention_lse(

@@ -126,3 +126,20 @@ def test_runtime_runs_target_attention_and_captures_its_lse(dsb, cuda):
     cache.accept_target_queries(torch.tensor([2, 3], device=cuda), is_prefill=False)
     assert cache.retrieval_status()["retrieval_count"] == 1
     assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+
+
+def test_rows_beyond_max_seq_len_are_flagged_and_cut(dsb, cuda):
+    """A max_seq_len below a row's length cannot cover it with splits: the
+    row is cut at the splits' reach (64 tokens here) and DSB_FLAG_POSITION
+    is raised instead of silently dropping the tail."""
+    rng = np.random.default_rng(23)
+    q, kc, vc, bt, _ = _case(rng, "bf16", 1, 8, 2, 16, [100])
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    out, lse = dsb.kernels.paged_decode_attention_lse(
+        dev(q).bfloat16(), dev(kc).bfloat16(), dev(vc).bfloat16(), dev(bt),
+        dev(np.array([100], np.int32)), scale=128 ** -0.5, max_seq_len=50, tokens_per_split=16)
+    torch.cuda.synchronize()
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 2  # DSB_FLAG_POSITION
+    ref_out, ref_lse = O.paged_decode_attention_lse(q, kc, vc, bt, np.array([64]), 128 ** -0.5)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref_out, rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=1e-4)

@@ -89,6 +89,10 @@ __global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const
   const int64_t cap = a.bt_cols * a.bs;  // tokens the table row can address
   if ((int64_t)L > cap) L = (int)cap;
   if (L < 0) L = 0;
+  if ((int64_t)L > (int64_t)a.splits * a.tps) {  // seq_lens[r] above max_seq_len
+    if (threadIdx.x == 0 && split == 0 && h == 0) flag_error(a.err, DSB_FLAG_POSITION);
+    L = a.splits * a.tps;
+  }
   const int s0 = split * a.tps, s1 = min(L, s0 + a.tps);
 
   // Q A-fragments: rows g and g + 8 are query heads h * G + g (+ 8) when < G.
