@@ -120,3 +120,19 @@ def test_oracle_target_lse_reproduces_the_scores_own_lse():
     p = np.exp(s - s.max())
     np.testing.assert_allclose(out[1, 3], p @ v / p.sum(), rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(lse[1, 3], s.max() + np.log(p.sum()), rtol=1e-6)
+
+
+def test_target_attention_wrapper_rejects_bad_arguments(dsb):
+    f = dsb.kernels.paged_decode_attention_lse
+    q = torch.zeros((2, 8, 128), dtype=torch.bfloat16)
+    kc = torch.zeros((4, 16, 2, 128), dtype=torch.bfloat16)
+    bt = torch.zeros((2, 2), dtype=torch.int32)
+    lens = torch.ones(2, dtype=torch.int32)
+    with pytest.raises(ValueError, match="table_rows"):
+        f(q, kc, kc, bt, lens, scale=0.1, max_seq_len=32, table_rows=torch.zeros(1, dtype=torch.int32))
+    with pytest.raises(ValueError, match="tokens_per_split"):
+        f(q, kc, kc, bt, lens, scale=0.1, max_seq_len=32, tokens_per_split=0)
+    with pytest.raises(ValueError):
+        f(q, kc[..., :64], kc[..., :64], bt, lens, scale=0.1, max_seq_len=32)  # head dims differ
+    with pytest.raises(ValueError):
+        f(q, kc, kc, bt, lens[:1], scale=0.1, max_seq_len=32)  # seq_lens short
