@@ -51,7 +51,7 @@ struct RopeArgs {
   // (plan_row_warp) instead of reading it, and CTA 0 of the row writes it out
   int from_sel;
   const int32_t *row_slots, *committed_lens, *sel_chunks, *sel_count;
-  int sel_stride, history_budget;
+  int sel_stride, history_budget, window;
   int64_t *plan_out;
   int32_t *hist_out, *wlen_out;
   int chunk_shift, block_shift;  // log2 of chunk / block_size when powers of two, else -1
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kBulkThreads) rope_bulk_kernel(const RopeArgs 
         } else {
           const int32_t *ch = a.sel_chunks + (int64_t)sl * a.sel_stride;
           const PlanRow pr = plan_row_warp(a.committed_lens[r], a.sel_count[sl], ch, a.sel_stride,
-                                           a.chunk, a.history_budget, a.plan_width, lane,
+                                           a.chunk, a.history_budget, a.window, a.plan_width, lane,
                                            blockIdx.x == 0 ? a.err : nullptr);
           for (int i = lane; i < n_plan_chunks; i += 32) s_chunks[i] = plan_row_value(pr, sl, ch, 5 + i);
           if (blockIdx.x == 0) {
@@ -771,8 +771,37 @@ bool legacy_rope_requested() {
 #ifndef DSB_BULK_STAGE_BYTES
 #define DSB_BULK_STAGE_BYTES (32 * 1024)  // K + V rows staged per bulk-kernel CTA
 #endif
+#ifndef DSB_BULK_PT_MAX
+#define DSB_BULK_PT_MAX 64  // positions per stage at most (two per lane of the issuing warp)
+#endif
+#ifndef DSB_BULK_CS_MAX_BYTES
+#define DSB_BULK_CS_MAX_BYTES (16 * 1024)  // cos/sin rows staged per stage at most
+#endif
 
 bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// CTAs per row for `rows` rows of `nblk` position blocks when `resident`
+// CTAs fit on the device at once: a CTA streams per = ceil(nblk / gx) blocks
+// through its stages, so it takes about per + 1 block times (the first
+// block's copies are not hidden), and a launch takes that many times its
+// number of waves.  The smallest such cost wins (fewer CTAs on a tie), so a
+// grid never spills a few CTAs into a second wave.
+int64_t bulk_ctas_per_row(int64_t rows, int64_t nblk, int64_t resident) {
+  resident = std::max<int64_t>(1, resident);
+  int64_t best_gx = 1, best_cost = INT64_MAX, best_ctas = INT64_MAX;
+  for (int64_t want = 1; want <= nblk; ++want) {
+    const int64_t gx = (nblk + want - 1) / want;
+    const int64_t per = (nblk + gx - 1) / gx;  // blocks of the busiest CTA
+    const int64_t ctas = rows * gx;
+    const int64_t cost = ((ctas + resident - 1) / resident) * (per + 1);
+    if (cost < best_cost || (cost == best_cost && ctas < best_ctas)) {
+      best_cost = cost;
+      best_ctas = ctas;
+      best_gx = gx;
+    }
+  }
+  return best_gx;
+}
 
 // The bulk kernel when its preconditions hold: 16-bit caches, head_dim 64,
 // 128 or 256, 16-byte aligned bases and at least one K+V row pair per stage.
@@ -785,36 +814,55 @@ int launch_rope_bulk(RopeArgs a, int rows, int64_t width, cudaStream_t st) {
     if (!aligned16(a.src_k) || !aligned16(a.src_v) || !aligned16(a.dst_k) || !aligned16(a.dst_v))
       return -1;
     const int64_t row_bytes = (int64_t)a.heads * a.head_dim * 2;
-    int pt = 64;  // two positions per lane of the issuing warp at most
+    int pt = DSB_BULK_PT_MAX;  // two positions per lane of the issuing warp at most
     while (pt > 1 && 2 * pt * row_bytes > DSB_BULK_STAGE_BYTES) pt >>= 1;
     if (2 * pt * row_bytes > DSB_BULK_STAGE_BYTES) return -1;
-    a.pt_shift = log2_exact(pt);
     a.chunk_shift = log2_exact(a.chunk);
     a.block_shift = log2_exact(a.block_size);
     constexpr int VE = 8;
     a.vec_rope = a.neox && a.rotary_dim > 0 && (a.rotary_dim / 2) % VE == 0 &&
                  reinterpret_cast<uintptr_t>(a.cos_sin) % 16 == 0 &&
                  (a.cs_stride * (int64_t)sizeof(CS)) % 16 == 0;
+    auto kern = a.head_dim == 128  ? rope_bulk_kernel<T, CS, GATHER, 128>
+                : a.head_dim == 64 ? rope_bulk_kernel<T, CS, GATHER, 64>
+                                   : rope_bulk_kernel<T, CS, GATHER, 256>;
     // Stage the cos/sin rows with the K/V rows when the table is dense (row
     // stride = rotary_dim, so the CTA's rows are one contiguous range that
     // ends inside the table) and they take at most 16 KB per CTA.
     const int64_t cs_row_bytes = a.cs_stride * (int64_t)sizeof(CS);
-    a.cs_bulk = a.vec_rope && a.cs_stride == a.rotary_dim && pt * cs_row_bytes <= 16 * 1024 ? 1 : 0;
-    const size_t smem = bulk_smem_layout(pt, row_bytes, GATHER ? 0 : a.plan_width - 5,
-                                         a.cs_bulk ? pt * cs_row_bytes : 0)
-                            .total;
-    auto kern = a.head_dim == 128  ? rope_bulk_kernel<T, CS, GATHER, 128>
-                : a.head_dim == 64 ? rope_bulk_kernel<T, CS, GATHER, 64>
-                                   : rope_bulk_kernel<T, CS, GATHER, 256>;
+    auto stage_smem = [&](int p, int &cs_bulk) {
+      cs_bulk = a.vec_rope && a.cs_stride == a.rotary_dim && p * cs_row_bytes <= DSB_BULK_CS_MAX_BYTES;
+      return bulk_smem_layout(p, row_bytes, GATHER ? 0 : a.plan_width - 5, cs_bulk ? p * cs_row_bytes : 0)
+          .total;
+    };
+    // The largest block (up to 32 KB of K + V rows) at which kBulkMinCtas
+    // CTAs stay resident per SM.  Measured at config 2's lengths (µs per
+    // launch; rows x kv heads of 128): 16 x 4 takes 16 positions (22.7),
+    // 32 x 2 16 (22.8; 32 positions leave 2 CTAs per SM: 24.5), 64 x 1 32
+    // (23.1; 64 positions with their cos/sin rows leave 2 per SM: 28.2).
+    constexpr int kBulkMinCtas = 3;
+    const int sms = std::max(1, sm_count());
+    int cs_bulk = 0;
+    size_t smem = stage_smem(pt, cs_bulk);
+    for (int p = pt; p >= 1; p >>= 1) {
+      int csb = 0;
+      const size_t sm_p = stage_smem(p, csb);
+      if (int e = ensure_smem((const void *)kern, sm_p); e != DSB_OK) return e;
+      if (resident_ctas((const void *)kern, kBulkThreads, sm_p) >= kBulkMinCtas * sms) {
+        pt = p;
+        smem = sm_p;
+        cs_bulk = csb;
+        break;
+      }
+    }
+    a.pt_shift = log2_exact(pt);
+    a.cs_bulk = cs_bulk;
     if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
-    // One wave of resident CTAs, each streaming an equal share of its row's
-    // position blocks.
+    // Each CTA streams an equal share of its row's position blocks; the
+    // share is picked against the resident CTA count (bulk_ctas_per_row).
     const int64_t nblk = (width + pt - 1) / pt;
-    const int64_t fill = std::max<int64_t>(
-        1, ((int64_t)resident_ctas((const void *)kern, kBulkThreads, smem) + rows - 1) / rows);
-    int64_t gx = std::min<int64_t>(nblk, fill);
-    const int64_t per = (nblk + gx - 1) / gx;
-    gx = (nblk + per - 1) / per;
+    const int64_t gx =
+        bulk_ctas_per_row(rows, nblk, resident_ctas((const void *)kern, kBulkThreads, smem));
     if (gx > 0x7fffffff || rows > 65535) return fail(DSB_ERR_UNSUPPORTED, "grid too large");
     launch_kernel(kern, dim3((unsigned)gx, rows), dim3(kBulkThreads), smem, st, a);
     return check_launch(GATHER ? "gather_rope_bulk_kernel" : "rebuild_rope_bulk_kernel");
@@ -943,8 +991,8 @@ extern "C" int dsb_rebuild_working_cache(
     const void *raw_key, const void *raw_value, void *working_key, void *working_value,
     const int32_t *row_slots, const int32_t *committed_lens, int32_t rows,
     const int32_t *sel_chunks, int32_t sel_stride, const int32_t *sel_count, int32_t num_slots,
-    int32_t chunk_size, int32_t history_budget, int32_t plan_width, int64_t *plan,
-    int32_t *history_lens, int32_t *working_lens, const void *cos_sin_cache,
+    int32_t chunk_size, int32_t history_budget, int32_t recent_window, int32_t plan_width,
+    int64_t *plan, int32_t *history_lens, int32_t *working_lens, const void *cos_sin_cache,
     int32_t cos_sin_dtype, int64_t cos_sin_stride, int64_t cos_sin_rows, int64_t max_model_len,
     int32_t num_heads, int32_t head_dim, int32_t working_budget, int32_t rotary_dim,
     int32_t is_neox_style, int32_t dtype, int32_t *error_flag, void *stream) {
@@ -956,6 +1004,10 @@ extern "C" int dsb_rebuild_working_cache(
     return fail(DSB_ERR_INVALID, "raw sequence, head and head dimensions must be positive");
   if (chunk_size <= 0 || history_budget <= 0 || sel_stride <= 0)
     return fail(DSB_ERR_INVALID, "bad chunk size, budget, plan width or selection stride");
+  if (recent_window == 0) recent_window = chunk_size;
+  if (recent_window < chunk_size || recent_window % chunk_size || recent_window > history_budget)
+    return fail(DSB_ERR_INVALID,
+                "recent_window must be a chunk-size multiple in [chunk_size, history_budget]");
   if (rows > num_slots || history_budget > working_budget)
     return fail(DSB_ERR_INVALID, "KV plan exceeds the working cache batch or token capacity");
   if (plan_width != 5 + working_budget / chunk_size)
@@ -991,6 +1043,7 @@ extern "C" int dsb_rebuild_working_cache(
   a.sel_count = sel_count;
   a.sel_stride = sel_stride;
   a.history_budget = history_budget;
+  a.window = recent_window;
   a.plan_out = plan;
   a.hist_out = history_lens;
   a.wlen_out = working_lens;
@@ -1002,8 +1055,8 @@ extern "C" int dsb_rebuild_working_cache(
   if (plan == nullptr)
     return fail(DSB_ERR_UNSUPPORTED, "this cache layout needs a plan buffer (two-launch path)");
   c = dsb_build_history_plan(row_slots, committed_lens, rows, sel_chunks, sel_stride, sel_count,
-                             num_slots, chunk_size, history_budget, plan_width, plan,
-                             history_lens, working_lens, error_flag, stream);
+                             num_slots, chunk_size, history_budget, recent_window, plan_width,
+                             plan, history_lens, working_lens, error_flag, stream);
   if (c != DSB_OK) return c;
   return dsb_rebuild_compact_kv_from_plan(raw_key, raw_value, working_key, working_value, plan,
                                           rows, plan_width, cos_sin_cache, cos_sin_dtype,
