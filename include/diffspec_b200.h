@@ -106,30 +106,42 @@ int dsb_finalize_chunk_scores(
 /* Device top-k chunk selection, one CTA per row (select_context_chunks,
  * diffspec/runtime.py:348-414, via set_chunk_scores :1554-1567).
  * Row scores are sum_p parts[row, p, c], divided by n_valid * normalize_heads
- * when normalize_heads > 0.  With n = ceil(L / C) chunks and
- * S = history_budget / C: n <= S keeps every chunk, otherwise the S - 1
- * highest-scoring chunks among 0..n-2 (ties go to the lower chunk index) plus
- * chunk n-1, in ascending order.  Rows whose row_slots entry is < 0 are left
- * alone; the others overwrite sel_chunks[slot, :count] / sel_count[slot].
- * The optional outputs mirror DiffSpecSelection (-1 padded). */
+ * when normalize_heads > 0.  Part p = q * parts_per_group + i of a row lies at
+ * parts + row * row_stride + q * group_stride + i * part_stride
+ * (parts_per_group <= 0: one group, the [rows, parts, N] layout; world groups
+ * of Hk / world parts: the [world, rows, Hk / world, N] result of an
+ * all-gather of per-rank parts, read without a copy).  With n = ceil(L / C)
+ * chunks, S = history_budget / C and WC = recent_window / C (recent_window 0
+ * means C, the reference): n <= S keeps every chunk, otherwise the S - WC
+ * highest-scoring chunks among 0..n-1-WC (ties go to the lower chunk index)
+ * plus chunk n-1, in ascending order.  WC > 1 is the rolling-recent-window
+ * mode, which has no reference counterpart: the newest WC chunks belong to
+ * the plan's rolling tail and are not ranked.  recent_window must be a
+ * chunk-size multiple in [C, history_budget].  Rows whose row_slots entry is
+ * < 0 are left alone; the others overwrite sel_chunks[slot, :count] /
+ * sel_count[slot].  The optional outputs mirror DiffSpecSelection (-1
+ * padded). */
 int dsb_select_context_chunks(
     const float *parts, int64_t row_stride, int64_t part_stride, int32_t num_parts,
-    int32_t normalize_heads, const int32_t *seq_lens, const int32_t *row_slots,
-    int32_t rows, int32_t max_chunks, int32_t chunk_size, int32_t history_budget,
-    int32_t *sel_chunks, int32_t sel_stride, int32_t *sel_count, int32_t num_slots,
-    int64_t *out_chunk_indices, int64_t *out_token_indices, float *out_chunk_scores,
-    int32_t *error_flag, void *stream);
+    int32_t parts_per_group, int64_t group_stride, int32_t normalize_heads,
+    const int32_t *seq_lens, const int32_t *row_slots, int32_t rows, int32_t max_chunks,
+    int32_t chunk_size, int32_t history_budget, int32_t recent_window, int32_t *sel_chunks,
+    int32_t sel_stride, int32_t *sel_count, int32_t num_slots, int64_t *out_chunk_indices,
+    int64_t *out_token_indices, float *out_chunk_scores, int32_t *error_flag, void *stream);
 
 /* Compact history plan rows (_history_plan_host, diffspec/runtime.py:1713-1735,
  * equal to _history_indices :1650-1681 once expanded).  history_end =
  * max(0, committed_lens[row] - 1); sel_count[slot] < 0 means "no retrieval
- * yet".  plan is [rows, plan_width] int64 with plan_width = 5 + W / C.
- * history_lens (nullable, [rows]) and working_lens (nullable, [num_slots])
- * receive history_len. */
+ * yet".  The rolling tail is the last min(recent_window, history_budget)
+ * history tokens (recent_window 0 means chunk_size, the reference; a longer
+ * window, a chunk-size multiple up to history_budget, is the window mode of
+ * dsb_select_context_chunks).  plan is [rows, plan_width] int64 with
+ * plan_width = 5 + W / C.  history_lens (nullable, [rows]) and working_lens
+ * (nullable, [num_slots]) receive history_len. */
 int dsb_build_history_plan(
     const int32_t *row_slots, const int32_t *committed_lens, int32_t rows,
     const int32_t *sel_chunks, int32_t sel_stride, const int32_t *sel_count,
-    int32_t num_slots, int32_t chunk_size, int32_t history_budget,
+    int32_t num_slots, int32_t chunk_size, int32_t history_budget, int32_t recent_window,
     int32_t plan_width, int64_t *plan, int32_t *history_lens, int32_t *working_lens,
     int32_t *error_flag, void *stream);
 
@@ -160,13 +172,13 @@ int dsb_rebuild_compact_kv_from_plan(
  * ([num_slots]) receive the plan values when non-null; plan may be null only
  * when the fused kernel takes the shape (16-bit caches, head_dim 64/128/256),
  * otherwise it is the buffer of the two-launch path.  max_width =
- * history_budget. */
+ * history_budget; recent_window as in dsb_build_history_plan. */
 int dsb_rebuild_working_cache(
     const void *raw_key, const void *raw_value, void *working_key, void *working_value,
     const int32_t *row_slots, const int32_t *committed_lens, int32_t rows,
     const int32_t *sel_chunks, int32_t sel_stride, const int32_t *sel_count,
-    int32_t num_slots, int32_t chunk_size, int32_t history_budget, int32_t plan_width,
-    int64_t *plan, int32_t *history_lens, int32_t *working_lens,
+    int32_t num_slots, int32_t chunk_size, int32_t history_budget, int32_t recent_window,
+    int32_t plan_width, int64_t *plan, int32_t *history_lens, int32_t *working_lens,
     const void *cos_sin_cache, int32_t cos_sin_dtype, int64_t cos_sin_stride,
     int64_t cos_sin_rows, int64_t max_model_len, int32_t num_heads, int32_t head_dim,
     int32_t working_budget, int32_t rotary_dim, int32_t is_neox_style, int32_t dtype,
@@ -393,6 +405,28 @@ int dsb_write_raw_kv(
     const int32_t *slots, const int64_t *positions, int32_t tokens,
     int32_t num_slots, int64_t max_model_len, int32_t num_heads, int32_t head_dim,
     int32_t dtype, int32_t *error_flag, void *stream);
+
+/* The draft step's KV sink (capture_raw_kv, diffspec/runtime.py:1797-1877,
+ * with _write_raw :1602-1618 and the position buffer of
+ * graph_safe_rope_positions :1767-1794): rows i < tokens are the active
+ * requests, whose key/value rows (row stride kv_row_stride elements, e.g.
+ * the packed K/V of a projection) go to raw_key / raw_value at [slots[i],
+ * positions[i]] (slots[i] < 0: no cache row) and whose local RoPE position
+ * local_positions[i] = history_lens[i] + position_offset is returned
+ * (DSB_FLAG_CAPACITY when it reaches working_budget), and working_lens
+ * (nullable, [num_slots]) of its slot becomes that position + 1, the length
+ * once the step's token is stored (as forward_attention leaves it,
+ * runtime.py:2057-2058); rows tokens <= i < padded_tokens are graph padding:
+ * no cache row, local position 0.  positions and local_positions are int64
+ * when positions_are_int64, else int32; local_positions may be NULL (write
+ * only). */
+int dsb_capture_raw_kv(
+    const void *key, const void *value, int64_t kv_row_stride, void *raw_key, void *raw_value,
+    const int32_t *slots, const void *positions, int32_t positions_are_int64, int32_t tokens,
+    int32_t padded_tokens, int32_t num_slots, int64_t max_model_len, int32_t num_heads,
+    int32_t head_dim, int32_t dtype, const int32_t *history_lens, int32_t position_offset,
+    int32_t working_budget, void *local_positions, int32_t *working_lens, int32_t *error_flag,
+    void *stream);
 
 #ifdef __cplusplus
 }

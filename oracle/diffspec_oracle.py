@@ -42,6 +42,8 @@ __all__ = [
     "draft_decode_attention",
     "prepare_retrieval_rows",
     "write_raw",
+    "request_rows",
+    "capture_raw_kv",
     "selection_margin",
 ]
 
@@ -171,9 +173,24 @@ def paged_chunk_attention_scores(query, key_cache, softmax_lse, block_table, seq
 
 
 # ------------------------------------------------------- A4: selection
-def select_context_chunks(chunk_scores, seq_len, chunk_size, token_budget):
+def _window_chunks(recent_window, chunk_size, token_budget):
+    """Chunks of the rolling recent window; 1 (the reference) when it is None."""
+    if recent_window is None:
+        return 1
+    if recent_window < chunk_size or recent_window % chunk_size or recent_window > token_budget:
+        raise ValueError("recent_window must be a chunk-size multiple in [chunk_size, budget]")
+    return recent_window // chunk_size
+
+
+def select_context_chunks(chunk_scores, seq_len, chunk_size, token_budget, recent_window=None):
     """diffspec/runtime.py:348-414 with ties ranked by ascending chunk index.
 
+    ``recent_window`` (tokens, a multiple of the chunk size; None = one chunk,
+    the reference) is the window mode, which has no reference counterpart:
+    with wc = recent_window / C the newest wc chunks are left out of the
+    ranking (the rolling recent window of the plan holds them) and the top
+    S - wc of chunks 0..n-1-wc are kept, plus the newest chunk, ascending.
+    wc = 1 is exactly the reference's top S - 1 of chunks 0..n-2.
     Returns (chunk_indices, token_indices, chunk_scores) as numpy arrays.
     """
     chunk_scores = np.asarray(chunk_scores)
@@ -190,14 +207,15 @@ def select_context_chunks(chunk_scores, seq_len, chunk_size, token_budget):
         e = np.zeros(0, dtype=np.int64)
         return e, e, chunk_scores
     max_chunks = token_budget // chunk_size
+    wc = _window_chunks(recent_window, chunk_size, token_budget)
     if n <= max_chunks:
         chosen = np.arange(n, dtype=np.int64)
     else:
-        # top (max_chunks - 1) of chunks 0..n-2 plus the newest (:371-390)
-        cand = np.arange(n - 1)
-        s = chunk_scores[: n - 1]
+        # top (max_chunks - wc) of chunks 0..n-1-wc plus the newest (:371-390)
+        cand = np.arange(n - wc)
+        s = chunk_scores[: n - wc]
         order = np.lexsort((cand, -s.astype(np.float64)))  # score desc, index asc
-        ranked = np.sort(cand[order[: max_chunks - 1]])
+        ranked = np.sort(cand[order[: max_chunks - wc]])
         chosen = np.concatenate([ranked, [n - 1]]).astype(np.int64)
     offsets = np.arange(chunk_size, dtype=np.int64)
     if seq_len % chunk_size:
@@ -209,19 +227,20 @@ def select_context_chunks(chunk_scores, seq_len, chunk_size, token_budget):
     return chosen, tokens, chunk_scores[chosen]
 
 
-def selection_margin(chunk_scores, seq_len, chunk_size, token_budget):
+def selection_margin(chunk_scores, seq_len, chunk_size, token_budget, recent_window=None):
     """Relative score gap at the top-k boundary (inf when nothing is ranked).
 
     Used to certify that a fp32 GPU score vector must select exactly what the
     fp64 oracle selects: the selection cannot change unless the rounding
-    error exceeds this gap.
+    error exceeds this gap.  ``recent_window`` as in select_context_chunks.
     """
     s = np.asarray(chunk_scores, dtype=np.float64)
     n = (seq_len + chunk_size - 1) // chunk_size
-    k = token_budget // chunk_size - 1
-    if n <= k + 1 or k <= 0:
+    wc = _window_chunks(recent_window, chunk_size, token_budget)
+    k = token_budget // chunk_size - wc
+    if n <= token_budget // chunk_size or k <= 0:
         return math.inf
-    cand = np.sort(s[: n - 1])[::-1]
+    cand = np.sort(s[: n - wc])[::-1]
     gap = cand[k - 1] - cand[k]
     return gap / max(abs(cand[k - 1]), 1e-30)
 
@@ -232,14 +251,17 @@ def history_budget(token_budget, max_tree_depth, chunk_size):
     return (token_budget - max_tree_depth - 1) // chunk_size * chunk_size
 
 
-def history_indices(selected_tokens, history_end, chunk_size, hbudget):
+def history_indices(selected_tokens, history_end, chunk_size, hbudget, recent_window=None):
     """diffspec/runtime.py:1650-1681 (_history_indices).
 
     ``selected_tokens`` is None (no retrieval yet) or the selection's token ids.
+    ``recent_window`` (window mode, no reference counterpart; None = one
+    chunk, the reference) is the length of the rolling tail.
     """
+    window = chunk_size if recent_window is None else recent_window
     if selected_tokens is not None:
         selected = np.asarray(selected_tokens, dtype=np.int64)
-        tail_start = max(0, history_end - min(chunk_size, hbudget))
+        tail_start = max(0, history_end - min(window, hbudget))
         prefix = selected[(selected >= 0) & (selected < tail_start)]
         if selected.size:
             newest_start = (selected[-1] // chunk_size) * chunk_size
@@ -254,16 +276,18 @@ def history_indices(selected_tokens, history_end, chunk_size, hbudget):
     return np.arange(start, history_end, dtype=np.int64)
 
 
-def history_plan(slot, selected_chunks, history_end, chunk_size, hbudget):
+def history_plan(slot, selected_chunks, history_end, chunk_size, hbudget, recent_window=None):
     """diffspec/runtime.py:1713-1735 (_history_plan_host) -> plan row (list).
 
     ``selected_chunks`` is None (no retrieval yet), [] (empty selection) or
-    the ascending chunk ids of the slot's selection.
+    the ascending chunk ids of the slot's selection.  ``recent_window`` as in
+    :func:`history_indices` (the rolling tail's length; None = one chunk).
     """
+    window = chunk_size if recent_window is None else recent_window
     if selected_chunks is None:
         length = min(history_end, hbudget)
         return [slot, length, history_end - length, 0, 0]
-    tail_length = min(history_end, chunk_size, hbudget)
+    tail_length = min(history_end, window, hbudget)
     tail_start = history_end - tail_length
     chunks = [int(c) for c in selected_chunks]
     if not chunks:
@@ -418,6 +442,31 @@ def write_raw(raw_key, raw_value, slots, positions, key, value):
             continue
         raw_key[int(slot), int(pos)] = key[i]
         raw_value[int(slot), int(pos)] = value[i]
+
+
+def request_rows(query_ends, num_tokens):
+    """Batch row of each token of a pass (diffspec/runtime.py:1580-1595)."""
+    starts = [0, *[int(e) for e in query_ends]]
+    rows, r = [], 0
+    for t in range(num_tokens):
+        while r + 1 < len(starts) - 1 and t >= starts[r + 1]:
+            r += 1
+        rows.append(r)
+    return rows
+
+
+def capture_raw_kv(raw_key, raw_value, slots, positions, key, value, history_lens, draft_step):
+    """diffspec/runtime.py:1797-1877 inside a draft cycle (linear proposals):
+    the first len(slots) rows are the requests (later rows are graph
+    padding), written to the raw caches at their absolute positions; returns
+    the step's local RoPE positions, history_len + draft_step for the
+    requests (the root step at the history length, then one further per
+    step, as the working lengths advance) and 0 for padding rows."""
+    rows = len(slots)
+    write_raw(raw_key, raw_value, slots, positions[:rows], key[:rows], value[:rows])
+    local = np.zeros(len(positions), dtype=np.int64)
+    local[:rows] = np.asarray(history_lens[:rows], dtype=np.int64) + draft_step
+    return local
 
 
 def kv_projection_write_raw(hidden, weight, slots, positions, raw_key, raw_value, dtype="bf16"):

@@ -22,7 +22,7 @@ def test_header_symbols_are_exported_and_bound(dsb):
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(dsb._lib.exported_symbols())
-    assert lib.dsb_abi_version() == 1
+    assert lib.dsb_abi_version() == 2
 
 
 def test_library_is_the_in_tree_build(dsb):
@@ -33,10 +33,24 @@ def test_library_is_the_in_tree_build(dsb):
 def test_invalid_arguments_fail_before_any_launch(dsb):
     lib = dsb._lib.load()
     # budget not a multiple of the chunk size
-    st = lib.dsb_select_context_chunks(ctypes.c_void_p(8), 0, 0, 1, 0, ctypes.c_void_p(8), None, 1, 10, 16, 50,
-                                       None, 0, None, 0, None, None, None, None, None)
-    assert st == dsb._lib.DSB_ERR_INVALID
+    def select(budget=64, window=0, per_group=0, parts=1):
+        return lib.dsb_select_context_chunks(ctypes.c_void_p(8), 0, 0, parts, per_group, 0, 0,
+                                             ctypes.c_void_p(8), None, 1, 10, 16, budget, window,
+                                             None, 0, None, 0, None, None, None, None, None)
+
+    assert select(budget=50) == dsb._lib.DSB_ERR_INVALID
     assert b"chunk-size multiple" in lib.dsb_last_error()
+    # rolling recent window: a chunk multiple within [chunk, budget]
+    for window in (8, 24, 80):
+        assert select(window=window) == dsb._lib.DSB_ERR_INVALID
+        assert b"recent_window" in lib.dsb_last_error()
+    # grouped parts must tile the part count
+    assert select(parts=4, per_group=3) == dsb._lib.DSB_ERR_INVALID
+    assert b"parts_per_group" in lib.dsb_last_error()
+    fake = ctypes.c_void_p(256)
+    assert lib.dsb_build_history_plan(fake, fake, 1, fake, 4, fake, 4, 16, 64, 24, 9, fake, None,
+                                      None, None, None) == dsb._lib.DSB_ERR_INVALID
+    assert b"recent_window" in lib.dsb_last_error()
     # plan width must be 5 + W / C
     st = lib.dsb_rebuild_compact_kv_from_plan(None, None, None, None, None, 1, 7, None, 0, 0, 0, 1,
                                               8, 1, 64, 64, 8, 8, 64, 1, 0, None, None)

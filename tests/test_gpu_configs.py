@@ -86,6 +86,11 @@ def test_config4_retrieval_identical_at_any_head_shard_count(dsb, cuda):
         sel = dsb.selection.select_rows(gathered, seq, chunk_size=c, token_budget=hb,
                                         normalize_heads=hq, with_outputs=True)[0]
         assert torch.equal(sel, sel_full)
+        # the all-gather's rank-major layout, read in place by the selection
+        stacked = torch.stack(parts, dim=0)
+        sel = dsb.selection.select_rows(stacked, seq, chunk_size=c, token_budget=hb,
+                                        normalize_heads=hq, with_outputs=True)[0]
+        assert torch.equal(sel, sel_full)
     sel_host = sel_full.cpu().numpy()
     for r in range(b):
         assert set(planted[r]) <= set(sel_host[r].tolist())

@@ -44,8 +44,12 @@ def _worker(rank, world, port, queue):
         local = O.paged_chunk_head_scores(q[:, qh], kc[:, :, heads], lse[:, qh], table, seq, c,
                                           length, d ** -0.5, acc=np.float32)
         gathered = dsb.parallel.gather_head_scores(torch.from_numpy(np.ascontiguousarray(local)))
-        queue.put((rank, bool(np.array_equal(gathered.numpy(), full)),
-                   dsb.parallel.shard_heads(hk, world, rank)))
+        # rank-major [world, rows, Hk_local, N], the layout the selection reads
+        ok = tuple(gathered.shape) == (world, rows, per, full.shape[-1])
+        ok = ok and all(np.array_equal(gathered[w].numpy(), full[:, w * per:(w + 1) * per])
+                        for w in range(world))
+        ok = ok and np.array_equal(dsb.parallel.head_major(gathered).numpy(), full)
+        queue.put((rank, bool(ok), dsb.parallel.shard_heads(hk, world, rank)))
     finally:
         dist.destroy_process_group()
 

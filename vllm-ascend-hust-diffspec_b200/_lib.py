@@ -69,12 +69,12 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "dsb_select_context_chunks": (
         ctypes.c_int,
-        [_P, _I64, _I64, _I32, _I32, _P, _P, _I32, _I32, _I32, _I32, _P, _I32, _P, _I32, _P,
-         _P, _P, _P, _P],
+        [_P, _I64, _I64, _I32, _I32, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _I32,
+         _P, _I32, _P, _P, _P, _P, _P],
     ),
     "dsb_build_history_plan": (
         ctypes.c_int,
-        [_P, _P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P],
+        [_P, _P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P],
     ),
     "dsb_rebuild_compact_kv_from_plan": (
         ctypes.c_int,
@@ -83,8 +83,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "dsb_rebuild_working_cache": (
         ctypes.c_int,
-        [_P, _P, _P, _P, _P, _P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _I32,
-         _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P],
+        [_P, _P, _P, _P, _P, _P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P,
+         _I32, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P],
     ),
     "dsb_kv_projection_write_raw": (
         ctypes.c_int,
@@ -136,6 +136,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dsb_write_raw_kv": (
         ctypes.c_int,
         [_P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I32, _I32, _I32, _P, _P],
+    ),
+    "dsb_capture_raw_kv": (
+        ctypes.c_int,
+        [_P, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I32, _I32, _I32, _P, _I32,
+         _I32, _P, _P, _P, _P],
     ),
 }
 

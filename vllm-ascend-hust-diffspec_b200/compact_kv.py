@@ -148,6 +148,7 @@ def rebuild_working_cache(
     plan: torch.Tensor | None = None,
     history_lens: torch.Tensor | None = None,
     working_lens: torch.Tensor | None = None,
+    recent_window: int | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """History plan + working-cache rebuild of every row in one launch.
 
@@ -157,7 +158,9 @@ def rebuild_working_cache(
     retrieval yet).  The plan rows, ``history_lens`` and ``working_lens`` come
     out exactly as ``selection.build_history_plan`` computes them, and the
     working cache exactly as ``rebuild_compact_kv_from_plan`` of that plan
-    leaves it.  Returns ``(plan, history_lens)``.
+    leaves it.  ``recent_window`` is the rolling tail's length
+    (``selection.build_history_plan``; one chunk when None).  Returns
+    ``(plan, history_lens)``.
     """
     working_budget = working_key.shape[2]
     rows = row_slots.shape[0]
@@ -198,6 +201,7 @@ def rebuild_working_cache(
         slots,
         chunk_size,
         history_budget,
+        0 if recent_window is None else int(recent_window),
         width,
         _lib.ptr(plan),
         _lib.ptr(history_lens),

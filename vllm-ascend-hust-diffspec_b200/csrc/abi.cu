@@ -102,4 +102,4 @@ int max_active_clusters(const void *kernel, int cluster_x, int threads, size_t s
 
 extern "C" const char *dsb_last_error(void) { return dsb::g_last_error.c_str(); }
 
-extern "C" int dsb_abi_version(void) { return 1; }
+extern "C" int dsb_abi_version(void) { return 2; }

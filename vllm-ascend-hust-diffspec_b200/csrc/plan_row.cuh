@@ -2,7 +2,9 @@
 // plan + rebuild launch: _history_plan_host, diffspec/runtime.py:1713-1735.
 //
 // History ends just before the root (history_end = committed_len - 1).  The
-// rolling tail is the last min(chunk, history_budget) history tokens; the
+// rolling tail is the last min(window, history_budget) history tokens (window
+// = one chunk in the reference; a longer rolling recent window is the window
+// mode, which has no reference counterpart); the
 // selected chunks (ascending, the newest last) contribute their tokens that
 // lie before both the tail and the newest selected chunk's start, keeping the
 // last history_budget - tail of them (prefix_drop counts the dropped oldest
@@ -24,8 +26,8 @@ struct PlanRow {
 // it with the same arguments and get the same result.  `ch` is the slot's
 // row of selected chunk ids, `cnt` its count.
 __device__ __forceinline__ PlanRow plan_row_warp(int committed_len, int cnt, const int32_t *ch,
-                                                 int sel_stride, int C, int HB, int plan_width,
-                                                 int lane, int32_t *err) {
+                                                 int sel_stride, int C, int HB, int window,
+                                                 int plan_width, int lane, int32_t *err) {
   PlanRow pr;
   const int64_t he = max(0, committed_len - 1);  // history ends before the root
   const int n_sel = min(max(cnt, 0), sel_stride);
@@ -34,7 +36,7 @@ __device__ __forceinline__ PlanRow plan_row_warp(int committed_len, int cnt, con
     if (lane == 0) flag_error(err, DSB_FLAG_CAPACITY);
     pr.n_chunks = plan_width - 5;
   }
-  const int64_t tail_len = min(he, (int64_t)min(C, HB));
+  const int64_t tail_len = min(he, (int64_t)min(window, HB));
   pr.prefix_len = 0;
   pr.prefix_drop = 0;
   if (cnt < 0) {  // no retrieval yet: the most recent history_budget tokens

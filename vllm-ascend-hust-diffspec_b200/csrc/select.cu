@@ -1,7 +1,9 @@
 // Device chunk selection (DiffSpec row A4): exact top-k by radix select.
 //
 // Reference: select_context_chunks, diffspec/runtime.py:348-414, applied per
-// request by set_chunk_scores :1554-1567 and the loop at :1298-1308.  The
+// request by set_chunk_scores :1554-1567 and the loop at :1298-1308.  A
+// rolling recent window of WC chunks (window mode, no reference counterpart;
+// WC = 1 is the reference) leaves the newest WC chunks out of the ranking.  The
 // reference runs torch.topk + sort per request on the host's behalf; here one
 // CTA per row finds the (S-1)-th largest score with a 4-pass 8-bit radix
 // select on order-preserving 32-bit keys, then emits the winners in ascending
@@ -27,11 +29,22 @@ __device__ __forceinline__ float key_value(uint32_t k) {
   return __uint_as_float(u);
 }
 
-__device__ __forceinline__ float chunk_score(const float *__restrict__ row, int64_t part_stride,
-                                             int num_parts, int normalize_heads, int L, int C,
-                                             int c) {
+// Where the score parts of a row lie: part p = q * per_group + i sits at
+// row + q * group_stride + i * part_stride (one group: the [rows, parts, N]
+// layout; world groups: the [world, rows, parts / world, N] layout of an
+// all-gather of per-rank parts).
+struct PartsLayout {
+  int64_t part_stride, group_stride;
+  int num_parts, per_group;
+};
+
+__device__ __forceinline__ float chunk_score(const float *__restrict__ row, const PartsLayout &pl,
+                                             int normalize_heads, int L, int C, int c) {
   float s = 0.f;
-  for (int p = 0; p < num_parts; ++p) s += row[(int64_t)p * part_stride + c];
+  for (int p = 0; p < pl.num_parts; ++p) {
+    const int q = p / pl.per_group, i = p - q * pl.per_group;
+    s += row[(int64_t)q * pl.group_stride + (int64_t)i * pl.part_stride + c];
+  }
   if (normalize_heads > 0) {
     const int nv = max(0, min(C, L - c * C));
     s = (nv > 0) ? s / (float)nv / (float)normalize_heads : 0.f;
@@ -69,9 +82,9 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *warp_tot, int &e
 }
 
 __global__ void __launch_bounds__(kThreads)
-select_chunks_kernel(const float *__restrict__ parts, int64_t row_stride, int64_t part_stride,
-                     int num_parts, int normalize_heads, const int32_t *__restrict__ seq_lens,
-                     const int32_t *__restrict__ row_slots, int max_chunks, int C, int S,
+select_chunks_kernel(const float *__restrict__ parts, int64_t row_stride, const PartsLayout pl,
+                     int normalize_heads, const int32_t *__restrict__ seq_lens,
+                     const int32_t *__restrict__ row_slots, int max_chunks, int C, int S, int WC,
                      int32_t *__restrict__ sel_chunks, int sel_stride,
                      int32_t *__restrict__ sel_count, int num_slots,
                      int64_t *__restrict__ out_ci, int64_t *__restrict__ out_ti,
@@ -98,10 +111,12 @@ select_chunks_kernel(const float *__restrict__ parts, int64_t row_stride, int64_
     for (int i = threadIdx.x; i < n; i += kThreads) chosen[i] = i;
     count = n;
   } else {
-    const int m = n - 1;  // rank chunks 0..n-2; chunk n-1 is always kept
-    const int k = S - 1;
+    // Rank chunks 0..n-1-WC (the newest WC chunks are the rolling window's;
+    // WC = 1 is the reference) for S - WC places; chunk n-1 is always kept.
+    const int m = n - WC;
+    const int k = S - WC;
     for (int i = threadIdx.x; i < m; i += kThreads)
-      keys[i] = order_key(chunk_score(srow, part_stride, num_parts, normalize_heads, L, C, i));
+      keys[i] = order_key(chunk_score(srow, pl, normalize_heads, L, C, i));
     __syncthreads();
     uint32_t prefix = 0, pmask = 0;
     int k_rem = k;
@@ -177,7 +192,7 @@ select_chunks_kernel(const float *__restrict__ parts, int64_t row_stride, int64_
       }
     }
     if (threadIdx.x == 0) chosen[k] = n - 1;
-    count = S;
+    count = k + 1;
   }
   __syncthreads();
 
@@ -196,8 +211,7 @@ select_chunks_kernel(const float *__restrict__ parts, int64_t row_stride, int64_
   if (out_cs != nullptr)
     for (int i = threadIdx.x; i < S; i += kThreads)
       out_cs[(int64_t)row * S + i] =
-          (i < count) ? chunk_score(srow, part_stride, num_parts, normalize_heads, L, C, chosen[i])
-                      : 0.f;
+          (i < count) ? chunk_score(srow, pl, normalize_heads, L, C, chosen[i]) : 0.f;
   if (out_ti != nullptr) {
     for (int j = threadIdx.x; j < S * C; j += kThreads) {
       const int i = j / C, o = j % C;
@@ -220,8 +234,9 @@ using namespace dsb;
 
 extern "C" int dsb_select_context_chunks(
     const float *parts, int64_t row_stride, int64_t part_stride, int32_t num_parts,
-    int32_t normalize_heads, const int32_t *seq_lens, const int32_t *row_slots, int32_t rows,
-    int32_t max_chunks, int32_t chunk_size, int32_t history_budget, int32_t *sel_chunks,
+    int32_t parts_per_group, int64_t group_stride, int32_t normalize_heads,
+    const int32_t *seq_lens, const int32_t *row_slots, int32_t rows, int32_t max_chunks,
+    int32_t chunk_size, int32_t history_budget, int32_t recent_window, int32_t *sel_chunks,
     int32_t sel_stride, int32_t *sel_count, int32_t num_slots, int64_t *out_chunk_indices,
     int64_t *out_token_indices, float *out_chunk_scores, int32_t *error_flag, void *stream) {
   if (rows < 0 || max_chunks < 0 || num_parts < 0) return fail(DSB_ERR_INVALID, "negative sizes");
@@ -229,6 +244,13 @@ extern "C" int dsb_select_context_chunks(
   if (!seq_lens || (max_chunks > 0 && !parts)) return fail(DSB_ERR_INVALID, "null pointer argument");
   if (chunk_size <= 0 || history_budget < chunk_size || history_budget % chunk_size)
     return fail(DSB_ERR_INVALID, "token_budget must be a positive chunk-size multiple");
+  if (parts_per_group <= 0) parts_per_group = num_parts > 0 ? num_parts : 1;
+  if (num_parts % parts_per_group)
+    return fail(DSB_ERR_INVALID, "num_parts must be a multiple of parts_per_group");
+  if (recent_window == 0) recent_window = chunk_size;
+  if (recent_window < chunk_size || recent_window % chunk_size || recent_window > history_budget)
+    return fail(DSB_ERR_INVALID,
+                "recent_window must be a chunk-size multiple in [chunk_size, token_budget]");
   const int S = history_budget / chunk_size;
   if ((sel_chunks != nullptr) != (sel_count != nullptr))
     return fail(DSB_ERR_INVALID, "sel_chunks and sel_count go together");
@@ -237,9 +259,10 @@ extern "C" int dsb_select_context_chunks(
   const size_t smem = sizeof(uint32_t) * ((size_t)max_chunks + (size_t)S);
   if (smem > 220 * 1024) return fail(DSB_ERR_UNSUPPORTED, "too many chunks for one CTA");
   if (int st_ = ensure_smem((const void *)select_chunks_kernel, smem); st_ != DSB_OK) return st_;
+  const PartsLayout pl{part_stride, group_stride, num_parts, parts_per_group};
   launch_kernel(select_chunks_kernel, dim3(rows), dim3(kThreads), smem, as_stream(stream),
-      parts, row_stride, part_stride, num_parts, normalize_heads, seq_lens, row_slots,
-      max_chunks, chunk_size, S, sel_chunks, sel_stride, sel_count, num_slots,
+      parts, row_stride, pl, normalize_heads, seq_lens, row_slots, max_chunks, chunk_size, S,
+      recent_window / chunk_size, sel_chunks, sel_stride, sel_count, num_slots,
       out_chunk_indices, out_token_indices, out_chunk_scores, error_flag);
   return check_launch("select_chunks_kernel");
 }

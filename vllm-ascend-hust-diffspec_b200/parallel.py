@@ -6,9 +6,10 @@ summation order of an all-reduce depends on the number of ranks, so the
 selected chunks could change with the GPU count.  Here every rank computes
 the unnormalised mass of each of its kv heads (deterministic, see the score
 kernel), the per-kv-head vectors are all-gathered over NCCL, and every rank
-sums them in global kv-head order inside the selection kernel.  The result is
-bit-identical for any number of ranks that holds the kv heads in contiguous,
-rank-ordered shards.
+sums them in global kv-head order inside the selection kernel, which reads
+the all-gather's rank-major layout directly.  The result is bit-identical for
+any number of ranks that holds the kv heads in contiguous, rank-ordered
+shards.
 """
 
 from __future__ import annotations
@@ -16,7 +17,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-__all__ = ["gather_head_scores", "shard_heads"]
+__all__ = ["gather_head_scores", "head_major", "shard_heads"]
 
 
 def shard_heads(num_kv_heads: int, world_size: int, rank: int) -> tuple[int, int]:
@@ -32,21 +33,32 @@ def gather_head_scores(
     group: dist.ProcessGroup | None = None,
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """All-gather ``[rows, Hk_local, N]`` mass into ``[rows, Hk_local * world, N]``.
+    """All-gather ``[rows, Hk_local, N]`` mass into ``[world, rows, Hk_local, N]``.
 
-    The result is ordered by (rank, local kv head), i.e. by global kv head
-    when shards are contiguous and rank-ordered.
+    Rank w's slice is its local mass, so global kv head ``w * Hk_local + i``
+    is ``result[w, :, i]`` when shards are contiguous and rank-ordered.  The
+    selection reads this layout in place (``selection.select_rows`` with a
+    4-D ``parts``), so the exchange is the collective alone, with no
+    reordering copy.  ``out`` (optional) is the ``[world, rows, Hk_local, N]``
+    buffer to gather into; with one rank the result is ``local[None]``.
     """
     world = dist.get_world_size(group)
-    if world == 1:
-        return local
     rows, hk_local, n = local.shape
-    stacked = torch.empty((world, rows, hk_local, n), dtype=local.dtype, device=local.device)
-    if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(stacked, local.contiguous(), group=group)
-    else:  # gloo (CPU tests) has no all_gather_into_tensor
-        dist.all_gather(list(stacked.unbind(0)), local.contiguous(), group=group)
+    if world == 1:
+        return local.unsqueeze(0)
     if out is None:
-        out = torch.empty((rows, world * hk_local, n), dtype=local.dtype, device=local.device)
-    out.view(rows, world, hk_local, n).copy_(stacked.permute(1, 0, 2, 3))
+        out = torch.empty((world, rows, hk_local, n), dtype=local.dtype, device=local.device)
+    if out.shape != (world, rows, hk_local, n) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [world, rows, Hk_local, N] buffer")
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    else:  # gloo (CPU tests) has no all_gather_into_tensor
+        dist.all_gather(list(out.unbind(0)), local.contiguous(), group=group)
     return out
+
+
+def head_major(gathered: torch.Tensor) -> torch.Tensor:
+    """``[world, rows, Hk_local, N]`` -> ``[rows, Hk, N]`` in global kv-head
+    order (a copy; the selection does not need it)."""
+    world, rows, hk_local, n = gathered.shape
+    return gathered.permute(1, 0, 2, 3).reshape(rows, world * hk_local, n)

@@ -15,8 +15,10 @@ Mirrors the hot-path subset of ``DiffSpecDraftCache``
 * ``forward_attention`` — the draft attention (:2024-2134) over the working
   cache through a slot vector (no copy for reordered slots).
 * ``write_raw`` / ``populate_prefill`` — canonical pre-RoPE KV (:1336-1347,
-  :1602-1618); ``project_and_write_raw`` — the draft layer's K/V projection
-  with that write in its epilogue.
+  :1602-1618); ``capture_raw_kv`` / ``graph_safe_rope_positions`` — the draft
+  step's KV sink returning local RoPE positions in a persistent buffer
+  (:1767-1877), one launch; ``project_and_write_raw`` — the draft layer's K/V
+  projection with the raw write in its epilogue.
 
 Host-visible counters that depend on device data (retrievals run, rows with
 nothing committed) live on the device and are read only by
@@ -127,30 +129,32 @@ class _Staging:
     Uploads go through a ring of preallocated pinned host buffers; each slot
     records an event after its asynchronous copy and is reused only once that
     event has completed, so no host synchronisation happens in steady state
-    and no pinned memory is allocated per call.
+    and no pinned memory is allocated per call.  Slot i owns its own region of
+    the device buffer, so an upload never overwrites the values of the
+    SLOTS - 1 uploads before it, which kernels queued earlier may still read.
     """
 
     SLOTS = 8
 
     def __init__(self, device: torch.device, capacity: int):
         self.device = device
-        self.dev = torch.empty(capacity, dtype=torch.int32, device=device)
-        self._alloc_host(capacity)
+        self._alloc(max(1, capacity // self.SLOTS))
 
-    def _alloc_host(self, capacity: int) -> None:
-        self.host = [torch.empty(capacity, dtype=torch.int32).pin_memory() for _ in range(self.SLOTS)]
+    def _alloc(self, per: int) -> None:
+        self.per = per  # int32 values per slot
+        self.dev = torch.empty(self.SLOTS * per, dtype=torch.int32, device=self.device)
+        self.host = [torch.empty(per, dtype=torch.int32).pin_memory() for _ in range(self.SLOTS)]
         self.events: list[torch.cuda.Event | None] = [None] * self.SLOTS
         self.next = 0
 
     def upload(self, *lists: list[int]) -> list[torch.Tensor]:
         flat = [v for x in lists for v in x]
         n = len(flat)
-        if n > self.dev.numel():
-            for ev in self.events:
-                if ev is not None:
-                    ev.synchronize()
-            self.dev = torch.empty(2 * n, dtype=torch.int32, device=self.device)
-            self._alloc_host(2 * n)
+        if n > self.per:
+            # every queued copy and the kernels before it must be done with
+            # the old buffers before they are dropped
+            torch.cuda.current_stream(self.device).synchronize()
+            self._alloc(2 * n)
         slot = self.next
         self.next = (slot + 1) % self.SLOTS
         ev = self.events[slot]
@@ -159,9 +163,7 @@ class _Staging:
         host = self.host[slot]
         if n:
             host[:n] = torch.tensor(flat, dtype=torch.int32)
-        # each upload gets its own device region of the staging buffer too:
-        # earlier kernels may still read the previous region
-        dev = self._dev_region(slot, n)
+        dev = self.dev[slot * self.per: slot * self.per + n]
         dev.copy_(host[:n], non_blocking=True)
         if ev is None:
             ev = torch.cuda.Event()
@@ -172,12 +174,6 @@ class _Staging:
             views.append(dev[off:off + len(x)])
             off += len(x)
         return views
-
-    def _dev_region(self, slot: int, n: int) -> torch.Tensor:
-        per = self.dev.numel() // self.SLOTS
-        if n <= per:
-            return self.dev[slot * per: slot * per + n]
-        return self.dev[:n]
 
 
 def causal_row_lengths(query_ends: list[int], seq_lens: list[int]) -> tuple[list[int], list[int]]:
@@ -219,6 +215,7 @@ class DiffSpecDraftCache:
         is_neox_style: bool = True,
         target_tensor_parallel_size: int = 1,
         process_group: Any = None,
+        recent_window: int | None = None,
     ) -> None:
         if target_tensor_parallel_size < 1:
             raise ValueError("Target tensor parallel size must be positive")
@@ -240,6 +237,15 @@ class DiffSpecDraftCache:
         )
         if self.history_budget <= 0:
             raise ValueError("DiffSpec token budget is too small for tree tokens")
+        # Rolling recent window (tokens): one chunk is the reference; a longer
+        # window (a chunk multiple up to the history budget) is the window
+        # mode of selection.select_context_chunks / build_history_plan.
+        window = settings.chunk_size if recent_window is None else int(recent_window)
+        if (window < settings.chunk_size or window % settings.chunk_size
+                or window > self.history_budget):
+            raise ValueError("recent_window must be a chunk-size multiple in "
+                             "[chunk_size, history_budget]")
+        self.recent_window = window
         if rotary_embedding is not None:
             cos_sin_cache = rotary_embedding.cos_sin_cache
             rotary_dim = rotary_embedding.rotary_dim
@@ -283,6 +289,8 @@ class DiffSpecDraftCache:
         self._attn_fast = None  # per-cycle prepared arguments of the draft attention call
         self._rebuild_fast = None  # prepared arguments of the plan + rebuild call
         self._active_ids: list[str] | None = None
+        self._position_buffers: dict[torch.dtype, torch.Tensor] = {}
+        self._positions_written: dict[torch.dtype, int] = {}
         self._target: dict[str, Any] | None = None
         self.target_is_prefill = True
 
@@ -479,14 +487,15 @@ class DiffSpecDraftCache:
         select_rows(
             parts, r_len, chunk_size=self.settings.chunk_size, token_budget=self.history_budget,
             normalize_heads=total_heads, row_slots=r_slot, sel_chunks=self.sel_chunks,
-            sel_count=self.sel_count,
+            sel_count=self.sel_count, recent_window=self.recent_window,
         )
         self.metrics.retrieval_launches += 1
         self.metrics.retrieval_seconds += time.perf_counter() - started
 
     def set_chunk_scores(self, slot: int, chunk_scores: torch.Tensor, seq_len: int) -> DiffSpecSelection:
         """Select from a score vector and store it for ``slot`` (runtime.py:1554-1567)."""
-        selection = select_context_chunks(chunk_scores, seq_len, self.settings.chunk_size, self.history_budget)
+        selection = select_context_chunks(chunk_scores, seq_len, self.settings.chunk_size,
+                                          self.history_budget, recent_window=self.recent_window)
         n = selection.chunk_indices.numel()
         if n:
             self.sel_chunks[slot, :n].copy_(selection.chunk_indices.to(torch.int32))
@@ -537,11 +546,121 @@ class DiffSpecDraftCache:
         return kv_projection_write_raw(hidden, weight, slots, positions, self.raw_key,
                                        self.raw_value, out)
 
-    def populate_prefill(self, request_rows: list[int], absolute_positions: torch.Tensor,
-                         key: torch.Tensor, value: torch.Tensor) -> None:
-        """Write projected pre-RoPE KV of batch rows ``request_rows`` (runtime.py:1336-1347)."""
-        slots = torch.tensor([self._active_slots[r] for r in request_rows], dtype=torch.int32)
-        self.write_raw(slots.to(self.device, non_blocking=True), absolute_positions, key, value)
+    @staticmethod
+    def _request_indices(metadata: Any, num_tokens: int) -> list[int]:
+        """Batch row of each token of a pass (runtime.py:1580-1595): request i
+        owns tokens ``[ends[i-1], ends[i])`` of ``actual_seq_lengths_q`` (or of
+        ``query_start_loc``); tokens past the last end stay with the last row."""
+        query_ends = getattr(metadata, "actual_seq_lengths_q", None)
+        if query_ends:
+            starts = [0, *[int(e) for e in query_ends]]
+        else:
+            starts = [int(x) for x in metadata.query_start_loc.to("cpu").tolist()]
+        rows, r = [], 0
+        for t in range(num_tokens):
+            while r + 1 < len(starts) - 1 and t >= starts[r + 1]:
+                r += 1
+            rows.append(r)
+        return rows
+
+    def _canonical_slots(self, batch_rows: list[int]) -> list[int]:
+        if not self._active_slots:
+            raise RuntimeError("DiffSpec request slots have not been initialized")
+        return [self._active_slots[r] for r in batch_rows]
+
+    def populate_prefill(self, absolute_positions: torch.Tensor, key: torch.Tensor,
+                         value: torch.Tensor, metadata: Any) -> None:
+        """Canonical raw KV of a cache-only draft projection (runtime.py:1336-1347):
+        token t of the pass belongs to the batch row ``metadata`` gives it and
+        is written at ``[slot, absolute_positions[t]]``."""
+        slots = self._canonical_slots(self._request_indices(metadata, key.shape[0]))
+        (slots_d,) = self._staging.upload(slots)
+        self.write_raw(slots_d, absolute_positions, key, value)
+
+    def capture_raw_kv(self, layer_index: int, absolute_positions: torch.Tensor,
+                       key: torch.Tensor, value: torch.Tensor,
+                       metadata: Any = None) -> torch.Tensor | None:
+        """The draft layer's KV sink (runtime.py:1797-1877, linear proposals).
+
+        Inside a draft cycle the first ``len(active requests)`` rows are the
+        requests (later rows are graph padding and write nothing): their
+        pre-RoPE K/V go to the raw cache at their absolute positions, and the
+        method returns the step's local RoPE positions — history length +
+        draft step for those rows, 0 for padding rows — in a persistent
+        cache-owned buffer shaped like ``absolute_positions`` (see
+        :meth:`graph_safe_rope_positions`).  One launch does both.  The
+        step's :meth:`forward_attention` then stores its K/V at the same
+        positions.  If the cycle has no rebuilt history yet, ``metadata``'s
+        ``seq_lens_list`` drives the rebuild first (the reference's step-0
+        path).  Outside a cycle (prefill) the rows map to requests through
+        ``metadata`` as in :meth:`populate_prefill` and nothing is returned.
+        """
+        if layer_index != 0:
+            raise ValueError("DiffSpec draft cache only supports one layer")
+        if not self._cycle_open:
+            if metadata is None:
+                return None
+            self.populate_prefill(absolute_positions.reshape(-1), key, value, metadata)
+            return None
+        rows = len(self._active_slots)
+        flat = absolute_positions.reshape(-1)
+        if key.shape[0] < rows or flat.numel() < rows:
+            raise RuntimeError("DiffSpec draft tensors omit active request rows")
+        if self._pending_rows == 0:
+            seq_lens = list(getattr(metadata, "seq_lens_list", ()) or ())
+            if not seq_lens:
+                return None
+            self.rebuild(seq_lens)
+        if self._draft_step + 1 > self.settings.token_budget - self.history_budget:
+            raise RuntimeError("DiffSpec working cache exhausted")
+        if flat.dtype not in (torch.int32, torch.int64):
+            raise ValueError("absolute positions must be int32 or int64")
+        out = self._position_buffer(flat.dtype, flat.numel())
+        k = key.reshape(key.shape[0], -1)
+        v = value.reshape(value.shape[0], -1)
+        if k.stride(1) != 1 or v.stride(1) != 1 or k.stride(0) != v.stride(0):
+            k, v = k.contiguous(), v.contiguous()
+        _lib.call(
+            "dsb_capture_raw_kv",
+            _lib.ptr(k), _lib.ptr(v), k.stride(0), _lib.ptr(self.raw_key), _lib.ptr(self.raw_value),
+            _lib.ptr(self._active_slots_dev), _lib.ptr(flat.contiguous()),
+            int(flat.dtype == torch.int64), rows, flat.numel(), self.max_num_reqs,
+            self.max_model_len, self.num_kv_heads, self.head_dim, _lib.dtype_code(self.dtype),
+            _lib.ptr(self._history_lens), self._draft_step, self.settings.token_budget,
+            _lib.ptr(out), _lib.ptr(self.working_lens), _lib.ptr(_lib.error_flag(self.device)),
+            _lib.stream_ptr(self.device),
+        )
+        return out.view_as(absolute_positions)
+
+    def _position_buffer(self, dtype: torch.dtype, count: int) -> torch.Tensor:
+        """``count`` entries of the persistent position buffer of ``dtype``
+        (runtime.py:1767-1794): one allocation of max_num_reqs *
+        max_model_len entries per dtype, so the address a captured graph
+        holds stays valid; entries past ``count`` that the previous call
+        wrote are cleared, the rest of the tail is zero from allocation."""
+        buf = self._position_buffers.get(dtype)
+        if buf is None:
+            buf = torch.zeros(self.max_num_reqs * self.max_model_len, dtype=dtype, device=self.device)
+            self._position_buffers[dtype] = buf
+        if count > buf.numel():
+            raise RuntimeError("DiffSpec RoPE input exceeds its persistent buffer")
+        prev = self._positions_written.get(dtype, 0)
+        if count < prev:
+            buf[count:prev].zero_()
+        self._positions_written[dtype] = count
+        return buf[:count]
+
+    def graph_safe_rope_positions(self, absolute_positions: torch.Tensor,
+                                  local_positions: torch.Tensor | None) -> torch.Tensor:
+        """A cache-owned, stable RoPE position input (runtime.py:1767-1794):
+        ``local_positions`` when given (e.g. what :meth:`capture_raw_kv`
+        returned, which already lives in the buffer), else the absolute
+        positions, copied into the persistent buffer of their dtype."""
+        src = absolute_positions if local_positions is None else local_positions
+        out = self._position_buffer(absolute_positions.dtype, absolute_positions.numel())
+        if src.data_ptr() != out.data_ptr():
+            out.copy_(src.reshape(-1))
+        return out.view_as(absolute_positions)
 
     def rebuild(self, committed_seq_lens: list[int] | torch.Tensor) -> torch.Tensor:
         """Plan + fused gather/RoPE rebuild of every active row's working cache.
@@ -562,8 +681,15 @@ class DiffSpecDraftCache:
         hl = self._history_lens[:rows]
         cs = self._cos_sin()
         fast = self._rebuild_fast
+        # Every buffer the prepared call below holds a pointer to: rebinding
+        # any of them (the caches, the selection state, the slot vector or
+        # the cos/sin table) sends the next call through validation again.
         sig = (rows, self._active_slots_dev.data_ptr(), self.raw_key.data_ptr(),
-               self.raw_value.data_ptr(), cs.data_ptr(), cs.dtype, cs.shape, cs.stride(0))
+               self.raw_value.data_ptr(), self.working_key.data_ptr(),
+               self.working_value.data_ptr(), self.sel_chunks.data_ptr(),
+               self.sel_count.data_ptr(), self.working_lens.data_ptr(), plan.data_ptr(),
+               hl.data_ptr(), self.raw_key.shape, self.working_key.shape,
+               self.sel_chunks.shape, cs.data_ptr(), cs.dtype, cs.shape, cs.stride(0))
         if (fast is not None and fast[0] == sig and committed.dtype == torch.int32
                 and committed.is_contiguous() and committed.device == self.device):
             # Same batch, caches and table as a validated call: only the
@@ -576,14 +702,15 @@ class DiffSpecDraftCache:
                 self._active_slots_dev, committed, self.sel_chunks, self.sel_count, cs,
                 chunk_size=self.settings.chunk_size, history_budget=self.history_budget,
                 rotary_dim=self.rotary_dim, is_neox_style=self.is_neox_style, plan=plan,
-                history_lens=hl, working_lens=self.working_lens,
+                history_lens=hl, working_lens=self.working_lens, recent_window=self.recent_window,
             )
             lib = _lib.load()
             head = (self.raw_key.data_ptr(), self.raw_value.data_ptr(), self.working_key.data_ptr(),
                     self.working_value.data_ptr(), self._active_slots_dev.data_ptr())
             tail = (rows, self.sel_chunks.data_ptr(), self.sel_chunks.shape[1],
                     self.sel_count.data_ptr(), self.raw_key.shape[0], self.settings.chunk_size,
-                    self.history_budget, plan.shape[1], plan.data_ptr(), hl.data_ptr(),
+                    self.history_budget, self.recent_window, plan.shape[1], plan.data_ptr(),
+                    hl.data_ptr(),
                     self.working_lens.data_ptr(), cs.data_ptr(), _lib.dtype_code(cs.dtype),
                     cs.stride(0), cs.shape[0], self.raw_key.shape[1], self.num_kv_heads,
                     self.head_dim, self.working_key.shape[2], self.rotary_dim,
@@ -620,7 +747,8 @@ class DiffSpecDraftCache:
         fast = self._attn_fast
         sig = (query.shape, key.shape, value.shape, output.shape, query.dtype, key.dtype,
                value.dtype, output.dtype, query.device, key.device, value.device, output.device,
-               float(scale))
+               float(scale), self.working_key.data_ptr(), self.working_value.data_ptr(),
+               self._active_slots_dev.data_ptr(), self._history_lens.data_ptr())
         if (fast is not None and fast[0] == sig and query.is_contiguous() and key.is_contiguous()
                 and value.is_contiguous() and output.is_contiguous()):
             # The later steps of a cycle repeat the first step's validated call
