@@ -9,7 +9,9 @@ the working cache from it, and K = 4 draft attention steps.  That is 16 draft
 steps (23 kernel launches) per bench step.
 
 Workload (config 2, per 16-request group): 16 requests at 40960 tokens,
-chunk 64, token budget 2048 (history budget 1984), 32 query / 4 kv heads,
+chunk 64, token budget 2048 (history budget 1984), rolling recent window 256
+(27 ranked chunks + the newest; the plan's tail is the last 256 history
+tokens), 32 query / 4 kv heads,
 head_dim 128, bf16, RoPE theta 1e6, 8 planted high-score chunks per request,
 paged target K with 16-token pages in a shuffled block table.  Data are
 synthetic (seeded Gaussian); every buffer is larger than L2 except the
@@ -21,9 +23,11 @@ ranks and request groups over N / hg, so each GPU always holds 16 requests x
 request group all-gather their per-kv-head chunk mass over NCCL before the
 selection, which is bit-identical at any N.
 
-``--impl reference`` times the reference algorithm's CPU restatement (the
-oracle port; the reference itself is a vLLM/Ascend plugin that cannot run
-here) on the host cores over a bounded sample of the same workload.
+``--impl reference`` times the reference's own PyTorch CPU path (the
+package installed in baseline/_ref: chunk_attention_scores,
+select_context_chunks, the _rebuild_working_cache and forward_attention CPU
+loops) on the host cores over a bounded sample of the same workload; the
+oracle port stands in only when that package does not import.
 """
 
 from __future__ import annotations
@@ -60,6 +64,7 @@ THETA = 1.0e6
 PLANTED = 8
 PAGE = 16             # paged target K block size
 HISTORY_BUDGET = (TOKEN_BUDGET - DEPTH - 1) // CHUNK * CHUNK  # 1984
+RECENT_WINDOW = 256   # rolling recent window of config 2 (window mode: 4 chunks)
 REJECTED = 3          # rejected draft suffix at the retrieval pass
 ACCEPT_PER_CYCLE = 2  # committed tokens added per cycle inside a period
 METRIC = "DiffSpec draft steps/sec (B=16, 40k ctx, budget 2048) and % of HBM peak"
@@ -191,12 +196,14 @@ class Workload:
         return lse
 
 
-def period_launches(w: "Workload", exchange=None, total_hq=None, gathered=None):
+def period_launches(w: "Workload", exchange=None, total_hq=None, gathered=None,
+                    window=RECENT_WINDOW):
     """The kernels of one retrieval period as (kind, callable) in stream order.
 
-    `exchange` (multi-GPU) gathers the local [rows, hk, N] mass into the
-    request group's fixed [rows, hk_total, N] buffer `gathered`, which the
-    selection then reads; it is inserted between scoring and selection.
+    `exchange` (multi-GPU) all-gathers the local [rows, hk, N] mass into the
+    request group's fixed rank-major [ranks, rows, hk, N] buffer `gathered`,
+    which the selection then reads in place; it is inserted between scoring
+    and selection.  `window` is the rolling recent window in tokens.
     """
     dsb, lib = w.dsb, w.dsb._lib
     total_hq = total_hq or w.hq
@@ -216,7 +223,8 @@ def period_launches(w: "Workload", exchange=None, total_hq=None, gathered=None):
     def select(parts_fn=lambda: w.parts):
         dsb.selection.select_rows(parts_fn(), w.r_len, chunk_size=CHUNK, token_budget=HISTORY_BUDGET,
                                   normalize_heads=total_hq, row_slots=w.r_slot,
-                                  sel_chunks=w.sel_chunks, sel_count=w.sel_count)
+                                  sel_chunks=w.sel_chunks, sel_count=w.sel_count,
+                                  recent_window=window)
 
     seq = [("prepare", prepare), ("scores", scores)]
     if exchange is not None:
@@ -230,7 +238,7 @@ def period_launches(w: "Workload", exchange=None, total_hq=None, gathered=None):
                 w.raw_key, w.raw_value, w.working_key, w.working_value, w.active, w.committed[c],
                 w.sel_chunks, w.sel_count, w.cos_sin, chunk_size=CHUNK,
                 history_budget=HISTORY_BUDGET, rotary_dim=D, is_neox_style=True, plan=w.plan,
-                history_lens=w.hist)
+                history_lens=w.hist, recent_window=window)
 
         seq.append(("rebuild", rebuild))
         for j in range(DEPTH):
@@ -402,6 +410,123 @@ def chain_time(torch, device, launches, kind, iters=20):
     return len(fns), start.elapsed_time(end) / (iters * len(fns))
 
 
+def _reference_runtime():
+    """The reference's own runtime module from baseline/_ref (the package
+    installed there from the reference's source, no dependencies), or
+    (None, why) when it is not installed or does not import here."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "diffspec" / "runtime.py").exists():
+        return None, "baseline/_ref is not installed"
+    if str(ref_dir) not in sys.path:
+        sys.path.insert(0, str(ref_dir))
+    try:
+        from diffspec import runtime as ref_rt
+        from vllm.model_executor.layers.rotary_embedding import RotaryEmbedding
+    except Exception as error:  # noqa: BLE001 - reported in the JSON line
+        return None, f"reference import failed: {type(error).__name__}: {error}"
+    return (ref_rt, RotaryEmbedding), None
+
+
+def cpu_reference_sample(budget_s: float, threads: int):
+    """Time the reference's own PyTorch CPU path on config-2 requests.
+
+    One sample unit = one request's retrieval period, run through the
+    reference's functions exactly as its CPU path runs them:
+    chunk_attention_scores over 40,957 tokens x 32 heads (LSE computed,
+    diffspec/runtime.py:281-345), set_chunk_scores / select_context_chunks
+    (:1554-1567, :348-414), then 4 cycles of _rebuild_working_cache (the CPU
+    loop, :1683-1711, RoPE by vLLM's RotaryEmbedding.forward_static) and 4
+    forward_attention steps (the CPU loop, :2040-2077).  fp32 (the
+    reference's CPU attention loop needs fp32 caches); one request at a time
+    (its loops are per request) with torch using `threads` host threads.
+    The reference has no rolling-window mode, so its tail is one chunk.
+    Returns (seconds per request-period, requests done) or None."""
+    import torch
+
+    mod, _ = _reference_runtime()
+    if mod is None:
+        return None
+    torch.set_num_threads(threads)
+    one_request = _REFERENCE_SETUP.get("one_request")
+    if one_request is None:  # built once: the inputs take seconds to draw
+        one_request = _REFERENCE_SETUP["one_request"] = _reference_request(mod)
+    done = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and done < 4 * B_GROUP:
+        one_request()
+        done += 1
+    return (time.perf_counter() - t0) / max(done, 1), done
+
+
+_REFERENCE_SETUP: dict = {}
+
+
+def _reference_request(mod):
+    """One config-2 request's period through the reference's functions
+    (see cpu_reference_sample), as a closure over its inputs."""
+    import torch
+
+    ref_rt, rope = mod
+    g = torch.Generator().manual_seed(7)
+    L = CTX - REJECTED
+
+    def bf16_exact(*shape):
+        return torch.randn(shape, generator=g).bfloat16().float()
+
+    keys = bf16_exact(L, HK, D)
+    q = bf16_exact(HQ, D)
+    inv = 1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float64) / D))
+    fr = torch.arange(TOKEN_BUDGET, dtype=torch.float64)[:, None] * inv[None]
+    table = torch.cat((fr.cos(), fr.sin()), -1).float()
+
+    class Rotary:  # the attributes DiffSpecDraftCache reads; vLLM's own CPU rotation
+        rotary_dim, head_size, is_neox_style, cos_sin_cache = D, D, True, table
+
+        def forward_native(self, positions, query, key=None):
+            return rope.forward_static(positions, query, key, D, D, table, True)
+
+    cache = ref_rt.DiffSpecDraftCache(
+        ref_rt.DiffSpecSettings(CHUNK, TOKEN_BUDGET, INTERVAL, 4, DEPTH, 0.7, False),
+        max_num_reqs=1, max_model_len=CTX + 64, num_kv_heads=HK, head_dim=D, target_num_layers=2,
+        dtype=torch.float32, device=torch.device("cpu"), rotary_embedding=Rotary())
+    cache.raw_key[0] = bf16_exact(CTX + 64, HK, D)
+    cache.raw_value[0] = bf16_exact(CTX + 64, HK, D)
+    dq, dk = bf16_exact(1, HQ, D), bf16_exact(1, HK, D)
+    out = torch.empty_like(dq)
+
+    def one_request():
+        scores = ref_rt.chunk_attention_scores(q, keys, CHUNK, None, D ** -0.5)
+        cache.begin_cycle(["r"])
+        cache.set_chunk_scores(0, scores, L)
+        for c in range(INTERVAL):
+            local = cache._rebuild_working_cache([0], [CTX - REJECTED + ACCEPT_PER_CYCLE * c])
+            for j in range(DEPTH):
+                cache._pending_request_indices = [0]
+                cache._pending_local_positions = [local[0] + j]
+                cache.forward_attention(dq, dk, dk, D ** -0.5, out)
+        cache.end_cycle()
+
+    return one_request
+
+
+def cpu_baseline_sample(budget_s: float, threads: int):
+    """The reference's own CPU path when baseline/_ref imports (kind
+    "reference"), else the oracle port (kind "port", with the reason)."""
+    got = cpu_reference_sample(budget_s, threads)
+    if got is not None:
+        t_req, done = got
+        return t_req, done, threads, "reference", (
+            f"{done} request-periods of config 2 through the reference's own PyTorch CPU path "
+            f"(baseline/_ref: chunk_attention_scores, select_context_chunks, "
+            f"_rebuild_working_cache, forward_attention; fp32, window = one chunk), "
+            f"{threads} torch threads")
+    why = _reference_runtime()[1]
+    t_req, done, used = cpu_oracle_sample(budget_s, threads)
+    return t_req, done, used, "port", (
+        f"{done} request-periods of config 2 (oracle port, numpy fp32 scores, one worker per "
+        f"core; the reference's own code is unavailable: {why})")
+
+
 def cpu_oracle_sample(budget_s: float, threads: int, acc="float32"):
     """Time the oracle port of the reference's CPU path on config-2 requests.
 
@@ -438,13 +563,15 @@ def cpu_oracle_sample(budget_s: float, threads: int, acc="float32"):
         scores = O.paged_chunk_attention_scores(q[None], kc, None, table, np.array([L]), CHUNK, L,
                                                 D ** -0.5, acc=dtype)[0]
         n = (L + CHUNK - 1) // CHUNK
-        chunks = O.select_context_chunks(scores[:n], L, CHUNK, HISTORY_BUDGET)[0].tolist()
+        chunks = O.select_context_chunks(scores[:n], L, CHUNK, HISTORY_BUDGET,
+                                         recent_window=RECENT_WINDOW)[0].tolist()
         wk = np.zeros((1, HK, TOKEN_BUDGET, D), np.float32)
         wv = np.zeros_like(wk)
         for c in range(INTERVAL):
             committed = CTX - REJECTED + ACCEPT_PER_CYCLE * c
             plan = np.zeros((1, 5 + TOKEN_BUDGET // CHUNK), np.int64)
-            row = O.history_plan(0, chunks, committed - 1, CHUNK, HISTORY_BUDGET)
+            row = O.history_plan(0, chunks, committed - 1, CHUNK, HISTORY_BUDGET,
+                                 recent_window=RECENT_WINDOW)
             plan[0, : len(row)] = row
             O.rebuild_compact_kv_from_plan(raw_k[None], raw_v[None], wk, wv, plan, cos_sin, CHUNK,
                                            HISTORY_BUDGET, D, True, "bf16")
@@ -487,7 +614,10 @@ def run_ours(args):
     w = Workload(torch, dsb, device, rows, hk_local, hq_local, seed=1234 + rank // hg)
     exchange = None
     if hg > 1:
-        gathered = torch.empty((rows, HK, w.max_chunks), dtype=torch.float32, device=device)
+        # rank-major [hg, rows, hk_local, N]: the all-gather writes it and the
+        # selection reads it in place
+        gathered = torch.empty((hg, rows, hk_local, w.max_chunks), dtype=torch.float32,
+                               device=device)
         exchange = lambda parts: dsb.parallel.gather_head_scores(parts, group, out=gathered)  # noqa: E731
     launches = period_launches(w, exchange, total_hq=HQ,
                                gathered=gathered if exchange is not None else None)
@@ -588,7 +718,7 @@ def run_e2e(res, args):
         settings, max_num_reqs=rows, max_model_len=1, num_kv_heads=w.hk, head_dim=D,
         target_num_layers=2, dtype=torch.bfloat16, device=device, cos_sin_cache=w.cos_sin,
         rotary_dim=D, is_neox_style=True, target_tensor_parallel_size=hg,
-        process_group=res["group"])
+        process_group=res["group"], recent_window=RECENT_WINDOW)
     cache.raw_key, cache.raw_value = w.raw_key, w.raw_value  # share the canonical cache
     cache.max_model_len = w.raw_key.shape[1]
     # Each cycle's verify-pass inputs (query, LSE, accepted counts) and each
@@ -661,7 +791,7 @@ def period_bytes(res):
         w.dsb.selection.build_history_plan(
             w.active, w.committed[c], w.sel_chunks, w.sel_count, chunk_size=CHUNK,
             history_budget=HISTORY_BUDGET, working_budget=TOKEN_BUDGET, plan=w.plan,
-            history_lens=w.hist)
+            history_lens=w.hist, recent_window=RECENT_WINDOW)
         hls.append(w.hist[: res["rows"]].cpu().tolist())
     b = algorithmic_bytes([CTX - REJECTED] * res["rows"], hls, w.hk, res["rows"])
     per_launch = dict(scores=b["retrieval"], rebuild=b["rebuild"] / INTERVAL,
@@ -698,10 +828,8 @@ def emit_ours(args):
     e2e = None if args.no_e2e else run_e2e(res, args)
     cpu = None
     if world == 1 and not args.no_cpu:
-        threads = os.cpu_count() or 1
-        t_req, done, threads = cpu_oracle_sample(args.cpu_seconds, threads)
-        cpu = dict(value=round(1.0 / t_req, 4), unit=UNIT, cores=threads, kind="port",
-                   sample=f"{done} request-periods of config 2 (oracle port, numpy fp32 scores)")
+        t_req, done, threads, kind, sample = cpu_baseline_sample(args.cpu_seconds, os.cpu_count() or 1)
+        cpu = dict(value=round(1.0 / t_req, 4), unit=UNIT, cores=threads, kind=kind, sample=sample)
     period_ms = res["ms"]
     line = dict(
         metric=METRIC, value=round(res["value"], 2), unit=UNIT, n_gpus=world, steps=args.steps,
@@ -710,7 +838,8 @@ def emit_ours(args):
         config=dict(workload="config 2: retrieval period (1 retrieval + 4 cycles x (plan + "
                     "rebuild, 4 draft attention steps)) over 16 requests x 40960 ctx per "
                     "request group", requests=B_GROUP * world, context=CTX, chunk=CHUNK,
-                    token_budget=TOKEN_BUDGET, history_budget=HISTORY_BUDGET, q_heads=HQ,
+                    token_budget=TOKEN_BUDGET, history_budget=HISTORY_BUDGET,
+                    recent_window=RECENT_WINDOW, q_heads=HQ,
                     kv_heads=HK, head_dim=D, draft_steps_per_bench_step=STEPS_PER_PERIOD,
                     retrieval_interval=INTERVAL, page_size=PAGE,
                     parallelism=f"kv-head shards {res['hg']} x request groups {world // res['hg']}",
@@ -729,6 +858,9 @@ def emit_ours(args):
 
 
 def emit_reference(args):
+    """The reference arm: the reference's own CPU path (baseline/_ref) timed
+    on the host cores over bounded samples of the config-2 workload, on rank
+    0 only; the oracle port stands in when the reference does not import."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
@@ -736,23 +868,29 @@ def emit_reference(args):
     threads = os.cpu_count() or 1
     per_step = max(2.0, min(10.0, 150.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
-        cpu_oracle_sample(per_step / 4, threads)
-    times, done_total = [], 0
+        cpu_baseline_sample(per_step / 4, threads)
+    times, done_total, kind, sample = [], 0, "port", ""
     for _ in range(args.steps):
-        t_req, done, _ = cpu_oracle_sample(per_step, threads)
+        t_req, done, used, kind, sample = cpu_baseline_sample(per_step, threads)
         times.append(t_req)
         done_total += done
     t_req = sum(times) / len(times)
     value = 1.0 / t_req
-    sample = (f"{done_total} request-periods of config 2 over {args.steps} steps "
-              f"(about {per_step:.0f} s of CPU work each)")
+    sample = (f"{done_total} request-periods over {args.steps} steps (about {per_step:.0f} s of "
+              f"CPU work each); " + sample.split(" ", 1)[1])
     line = dict(
         metric=METRIC, value=round(value, 4), unit=UNIT, n_gpus=world, steps=args.steps,
         warmup=args.warmup, ms_per_step=round(t_req * B_GROUP * 1e3, 3), higher_is_better=True,
         scaling="weak", vs_baseline=None, dtype="f32", data="synthetic", impl="reference",
-        config=dict(workload="config 2 retrieval period, reference CPU algorithm (oracle port)",
-                    requests=B_GROUP, context=CTX),
-        cpu_baseline=dict(value=round(value, 4), unit=UNIT, cores=threads, kind="port", sample=sample),
+        config=dict(workload="config 2: retrieval period (1 retrieval + 4 cycles x (plan + "
+                    "rebuild, 4 draft attention steps)) over 16 requests x 40960 ctx per "
+                    "request group", requests=B_GROUP, context=CTX, chunk=CHUNK,
+                    token_budget=TOKEN_BUDGET, history_budget=HISTORY_BUDGET, q_heads=HQ,
+                    kv_heads=HK, head_dim=D, retrieval_interval=INTERVAL,
+                    implementation=("the reference's own PyTorch CPU path (baseline/_ref)"
+                                    if kind == "reference" else "oracle port of the reference's "
+                                    "CPU path")),
+        cpu_baseline=dict(value=round(value, 4), unit=UNIT, cores=threads, kind=kind, sample=sample),
         e2e=dict(value=round(value, 4), unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
 
@@ -803,7 +941,7 @@ def run_draft_step(args):
     bf = torch.bfloat16
     x_in = torch.randn((B_GROUP, 4096), generator=g, device=device).to(bf)
     residual = torch.randn((B_GROUP, 2048), generator=g, device=device).to(bf)
-    launches = period_launches(w)
+    launches = period_launches(w, window=CHUNK)  # config 5 names no window: the reference's tail
     retrieval = [(k, fn) for k, fn in launches if k in ("prepare", "scores", "select")]
     rebuilds = [fn for k, fn in launches if k == "rebuild"]
     abs_pos = [[(w.committed[c] + j).to(torch.int64) for j in range(DEPTH)] for c in range(INTERVAL)]
@@ -1050,6 +1188,122 @@ def run_target_attention(args):
                           l2="K/V 1.34 GB per launch, larger than L2")))
 
 
+def run_reference_triton(args):
+    """A secondary comparison arm on the GPU: the reference's two Triton
+    kernels (diffspec/kernels.py:11-150 chunk scores, diffspec/compact_kv.py:
+    8-242 plan-driven rebuild), imported from baseline/_ref and compiled by
+    Triton for this B200, against this library's kernels on the same config-2
+    inputs (16 requests x 40960 tokens, 32 / 4 heads of 128, chunk 64, budget
+    2048).  Both sides run back to back in CUDA graphs (eager when a Triton
+    launch cannot be captured); outputs are compared.  The product has no
+    Triton: this only times the reference's own device code."""
+    import torch
+
+    ref_dir = ROOT / "baseline" / "_ref"
+    stubs = ROOT / "tests" / "golden" / "ref_stubs"  # vllm_ascend import stand-ins
+    for path in (str(stubs), str(ref_dir)):
+        if path not in sys.path:
+            sys.path.insert(0, path)
+    try:
+        from diffspec import compact_kv as ref_compact
+        from diffspec import kernels as ref_kernels
+    except Exception as error:  # noqa: BLE001
+        print(json.dumps(dict(mode="reference_triton",
+                              unavailable=f"reference import failed: {error}")))
+        return
+    dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    w = Workload(torch, dsb, device, B_GROUP, HK, HQ, seed=1234)
+    launches = period_launches(w, window=CHUNK)
+    for _, fn in launches:  # selection state and plans of a real period
+        fn()
+    dsb.selection.build_history_plan(
+        w.active, w.committed[0], w.sel_chunks, w.sel_count, chunk_size=CHUNK,
+        history_budget=HISTORY_BUDGET, working_budget=TOKEN_BUDGET, plan=w.plan, history_lens=w.hist)
+    torch.cuda.synchronize(device)
+    q_rows = (torch.arange(B_GROUP, device=device) * 5 + (5 - REJECTED) - 1)
+    query = w.query[q_rows].contiguous()
+    lse = w.lse[q_rows].contiguous()
+    seq = w.r_len.clone()
+    wk_t, wv_t = torch.zeros_like(w.working_key), torch.zeros_like(w.working_value)
+
+    def triton_scores():
+        return ref_kernels.paged_chunk_attention_scores(
+            query, w.key_cache, lse, w.block_table, seq, chunk_size=CHUNK, max_seq_len=CTX,
+            scale=D ** -0.5)
+
+    def ours_scores():
+        return dsb.kernels.paged_chunk_attention_scores(
+            query, w.key_cache, lse, w.block_table, seq, chunk_size=CHUNK, max_seq_len=CTX,
+            scale=D ** -0.5)
+
+    def triton_rebuild():
+        ref_compact.rebuild_compact_kv_from_plan(
+            w.raw_key, w.raw_value, wk_t, wv_t, w.plan, w.cos_sin, chunk_size=CHUNK,
+            max_width=HISTORY_BUDGET, rotary_dim=D, is_neox_style=True)
+
+    def ours_rebuild():
+        dsb.compact_kv.rebuild_compact_kv_from_plan(
+            w.raw_key, w.raw_value, w.working_key, w.working_value, w.plan, w.cos_sin,
+            chunk_size=CHUNK, max_width=HISTORY_BUDGET, rotary_dim=D, is_neox_style=True)
+
+    def timed(fn, n=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        mode = "graph"
+        try:
+            s = torch.cuda.Stream(device)
+            s.wait_stream(torch.cuda.current_stream(device))
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                for _ in range(n):
+                    fn()
+            run = graph.replay
+        except Exception:  # noqa: BLE001 - eager launches instead
+            torch.cuda.synchronize(device)
+            mode = "eager"
+
+            def run():
+                for _ in range(n):
+                    fn()
+        run()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(max(1, args.steps)):
+            run()
+        b.record()
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) * 1e3 / (max(1, args.steps) * n), mode
+
+    s_ref, s_ours = triton_scores(), ours_scores()
+    rel = ((s_ref - s_ours).abs() / s_ref.abs().clamp_min(1e-30)).max().item()
+    triton_rebuild()
+    ours_rebuild()
+    torch.cuda.synchronize(device)
+    hmax = int(w.hist[: B_GROUP].max())
+    same_v = bool(torch.equal(wv_t[:, :, :hmax], w.working_value[:, :, :hmax]))
+    dk = (wk_t[:, :, :hmax].float() - w.working_key[:, :, :hmax].float()).abs().max().item()
+    t_s, m_s = timed(triton_scores, 5)
+    o_s, _ = timed(ours_scores, 5)
+    t_r, m_r = timed(triton_rebuild)
+    o_r, _ = timed(ours_rebuild)
+    assert dsb._lib.read_and_clear_error_flag(device) == 0
+    score_bytes = sum(int(x) for x in seq.tolist()) * HK * D * 2
+    rebuild_bytes = sum(4 * int(h) * HK * D * 2 for h in w.hist[:B_GROUP].tolist())
+    print(json.dumps(dict(
+        mode="reference_triton", config="config 2 (16 x 40960, 32/4 heads, chunk 64, budget 2048)",
+        scores=dict(triton_us=round(t_s, 1), ours_us=round(o_s, 1), speedup=round(t_s / o_s, 2),
+                    triton_gbs=round(score_bytes / t_s / 1e3, 1), ours_gbs=round(score_bytes / o_s / 1e3, 1),
+                    max_rel_diff=rel, triton_timing=m_s),
+        rebuild=dict(triton_us=round(t_r, 2), ours_us=round(o_r, 2), speedup=round(t_r / o_r, 2),
+                     triton_gbs=round(rebuild_bytes / t_r / 1e3, 1),
+                     ours_gbs=round(rebuild_bytes / o_r / 1e3, 1), values_equal=same_v,
+                     key_max_abs_diff=dk, triton_timing=m_r))), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -1069,6 +1323,8 @@ def main():
                    help="time the config-5 draft layer's four linears against cuBLAS")
     p.add_argument("--target-attention", action="store_true",
                    help="time the target paged decode attention with the LSE export")
+    p.add_argument("--reference-triton", action="store_true",
+                   help="time the reference's Triton kernels (compiled for this GPU) against ours")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -1080,6 +1336,8 @@ def main():
         run_draft_linear(args)
     elif args.target_attention:
         run_target_attention(args)
+    elif args.reference_triton:
+        run_reference_triton(args)
     elif args.only:
         run_only(args)
     elif args.impl == "reference":

@@ -5,7 +5,9 @@ given by the DIFFSPEC_REFERENCE environment variable) on seeded inputs:
 
 * its PyTorch CPU path (chunk_attention_scores, select_context_chunks,
   DiffSpecDraftCache._history_indices / _history_plan_host /
-  _rebuild_working_cache / forward_attention / accept_target_queries);
+  _rebuild_working_cache / forward_attention / accept_target_queries /
+  populate_prefill / prepare_compact_prefill / capture_raw_kv), including
+  BASELINE config 1 as one chain;
 * its Triton kernels (paged_chunk_attention_scores,
   rebuild_compact_kv_from_plan, gather_raw_kv_with_local_rope) on the CPU
   under TRITON_INTERPRET=1.
@@ -15,7 +17,8 @@ ref_stubs/vllm_ascend/ops/triton/rope.py for the one with math in it).  The
 outputs are written as compressed .npz files; bf16 tensors are stored as
 uint16 bit patterns (keys ending in "_bf16").
 
-Usage: DIFFSPEC_REFERENCE=<reference checkout> python tests/golden/make_golden.py
+Usage: DIFFSPEC_REFERENCE=<reference checkout> python tests/golden/make_golden.py [names...]
+(no names: every fixture; names: e.g. ``config1 capture``).
 """
 
 from __future__ import annotations
@@ -331,12 +334,109 @@ def make_hook() -> dict:
     return out
 
 
+# --------------------------------------------------------------------- config 1
+def make_config1() -> dict:
+    """BASELINE config 1 as one chain of the reference's CPU path:
+    chunk_attention_scores (LSE computed) -> set_chunk_scores /
+    select_context_chunks -> _rebuild_working_cache -> forward_attention for
+    the K draft steps, in fp32."""
+    c, inp = R.CONFIG1, R.config1_inputs()
+    d, hq, hk = c["d"], c["hq"], c["hk"]
+    scale = d ** -0.5
+    L = inp["retrieval_len"]
+    scores = ref_rt.chunk_attention_scores(T(inp["query"]), T(inp["keys"][:L]), c["chunk"], None, scale)
+    cache = ref_rt.DiffSpecDraftCache(
+        ref_rt.DiffSpecSettings(c["chunk"], c["budget"], 1, 4, c["depth"], 0.7, False),
+        max_num_reqs=1, max_model_len=c["tokens"], num_kv_heads=hk, head_dim=d,
+        target_num_layers=2, dtype=torch.float32, device=torch.device("cpu"),
+        rotary_embedding=Rotary(d, d, True, T(inp["cos_sin"])),
+    )
+    cache.raw_key[0].copy_(T(inp["keys"]))
+    cache.raw_value[0].copy_(T(inp["values"]))
+    cache.begin_cycle(["r"])
+    sel = cache.set_chunk_scores(0, scores, L)
+    plan = cache._history_plan_host(0, inp["committed"] - 1)
+    local = cache._rebuild_working_cache([0], [inp["committed"]])
+    out = {"n": np.array(1), "crc": np.array(R.crc(inp["keys"], inp["values"], inp["query"])),
+           "history_budget": np.array(cache.history_budget), "scores": scores.numpy(),
+           "chunk_indices": sel.chunk_indices.numpy(), "token_indices": sel.token_indices.numpy(),
+           "plan": np.array(plan, np.int64), "local_positions": np.array(local, np.int64),
+           "working_key": cache.working_key[0, :, : local[0]].numpy().copy()}
+    st = inp["steps"]
+    for j in range(c["depth"]):
+        cache._pending_request_indices = [0]
+        cache._pending_local_positions = [local[0] + j]
+        query = T(st["query"][j])
+        o = cache.forward_attention(query, T(st["key"][j]), T(st["value"][j]), scale,
+                                    torch.full_like(query, float("nan")))
+        out[f"step{j}_out"] = o.numpy().copy()
+    out["working_lens"] = np.array([cache._working_lens[0]], np.int64)
+    return out
+
+
+# --------------------------------------------------------------------- KV sink
+def make_capture() -> dict:
+    """populate_prefill -> set_chunk_scores -> prepare_compact_prefill ->
+    (capture_raw_kv -> forward_attention) per draft step, with graph padding
+    rows, on the reference's CPU path (fp32 caches: its CPU attention loop
+    needs them; the inputs are exact in bf16); the forward context's
+    attention metadata is supplied directly."""
+    c, inp = R.CAPTURE, R.capture_inputs()
+    d, hk = c["d"], c["hk"]
+    cache = ref_rt.DiffSpecDraftCache(
+        ref_rt.DiffSpecSettings(c["chunk"], c["budget"], 1, 4, c["depth"], 0.7, False),
+        max_num_reqs=c["slots"], max_model_len=c["max_len"], num_kv_heads=hk, head_dim=d,
+        target_num_layers=2, dtype=torch.float32, device=torch.device("cpu"),
+        rotary_embedding=Rotary(d, d, True, T(inp["cos_sin"])),
+    )
+    cache.raw_key.zero_()
+    cache.raw_value.zero_()
+    ids = ["c", "a", "b"]
+    cache.set_active_requests(["x", "a", "b", "c"])
+    cache.set_active_requests(ids)  # slots [3, 1, 2]: "x" released slot 0
+    prompts = list(c["prompts"])
+    prefill_meta = SimpleNamespace(actual_seq_lengths_q=inp["query_ends"].tolist())
+    cache.populate_prefill(torch.from_numpy(inp["prefill_positions"]), T(inp["prefill_key"]),
+                           T(inp["prefill_value"]), prefill_meta)
+    sel = cache.set_chunk_scores(cache._active_slots[1], torch.from_numpy(inp["mid_scores"]), prompts[1])
+    out = {"n": np.array(1), "active_slots": np.array(cache._active_slots, np.int64),
+           "crc": np.array(R.crc(inp["prefill_key"], inp["prefill_value"], inp["mid_scores"])),
+           "mid_chunks": sel.chunk_indices.numpy()}
+    cache.begin_cycle(ids)
+    committed = [n + 1 for n in prompts]  # the root at position n is the cycle's first token
+    meta = SimpleNamespace(seq_lens_list=committed, actual_seq_lengths_q=[1, 2, 3])
+    cache._first_attention_metadata = lambda: meta
+    cache.prepare_compact_prefill(meta, len(ids), committed_seq_lens=committed)
+    for j, st in enumerate(inp["steps"]):
+        pos = cache.capture_raw_kv(0, torch.from_numpy(st["positions"]), T(st["key"]),
+                                   T(st["value"]))
+        query = T(st["query"])
+        o = cache.forward_attention(query, T(st["key"]), T(st["value"]), d ** -0.5,
+                                    torch.full_like(query, float("nan")))
+        out[f"step{j}_local_positions"] = pos.numpy().copy()
+        arr(o, f"step{j}_out", out)
+    cache.end_cycle()
+    arr(cache.raw_key, "raw_key", out)
+    arr(cache.raw_value, "raw_value", out)
+    arr(cache.working_key, "working_key", out)
+    arr(cache.working_value, "working_value", out)
+    out["working_lens"] = np.array([int(cache._working_lens[s]) for s in range(c["slots"])], np.int64)
+    return out
+
+
+FIXTURES = (("scores", "make_scores"), ("select", "make_select"), ("plans", "make_plans"),
+            ("rebuild", "make_rebuild"), ("gather", "make_gather"), ("attention", "make_attention"),
+            ("hook", "make_hook"), ("config1", "make_config1"), ("capture", "make_capture"))
+
+
 def main() -> None:
+    """Writes every fixture, or only those named on the command line."""
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    for name, fn in (("scores", make_scores), ("select", make_select), ("plans", make_plans),
-                     ("rebuild", make_rebuild), ("gather", make_gather),
-                     ("attention", make_attention), ("hook", make_hook)):
-        data = fn()
+    wanted = set(sys.argv[1:])
+    for name, fn_name in FIXTURES:
+        if wanted and name not in wanted:
+            continue
+        data = globals()[fn_name]()
         path = HERE / f"{name}.npz"
         np.savez_compressed(path, **data)
         print(f"{path.name}: {int(data['n'])} cases, {path.stat().st_size / 1024:.0f} KiB")

@@ -193,3 +193,64 @@ def hook_inputs(i: int) -> dict:
                 key_cache=key_cache, block_tables=tables,
                 seq_lens=np.array([90, 70, 1][:rows], np.int32),
                 query_ends=np.array([4 * (r + 1) for r in range(rows)], np.int32))
+
+
+# ---------------------------------------------------------------- config 1 chain (A2, A4-A6, A8)
+# one request, 4096 tokens, chunk 32, budget 512, 1 kv head
+# + 8 query heads of 128, fp32, RoPE theta 1e6, K = 4 draft tokens with the
+# last 3 rejected (retrieval over 4093 tokens, history ending at 4092).  The
+# keys of 4 planted chunks are the committed query's GQA-group mean + N(0,
+# 0.1).  Values are drawn exact in bf16 so the GPU path (bf16 caches) sees
+# the same numbers as the reference's fp32 run.  The target's keys double as
+# the draft's pre-RoPE raw keys.
+CONFIG1 = dict(tokens=4096, chunk=32, budget=512, window=128, hk=1, hq=8, d=128, theta=1e6,
+               depth=4, rejected=3, planted=(10, 40, 77, 100))
+
+
+def config1_inputs() -> dict:
+    c = CONFIG1
+    g = rng(1001)
+    t, hk, hq, d = c["tokens"], c["hk"], c["hq"], c["d"]
+    keys = normal(g, (t, hk, d), "bf16")
+    values = normal(g, (t, hk, d), "bf16")
+    query = normal(g, (hq, d), "bf16")
+    mean = query.reshape(hk, hq // hk, d).mean(1)
+    for ch in c["planted"]:
+        noise = 0.1 * g.standard_normal((c["chunk"], hk, d)).astype(np.float32)
+        keys[ch * c["chunk"]:(ch + 1) * c["chunk"]] = round_to(mean[None] + noise, "bf16")
+    steps = dict(query=normal(g, (c["depth"], 1, hq, d), "bf16"),
+                 key=normal(g, (c["depth"], 1, hk, d), "bf16"),
+                 value=normal(g, (c["depth"], 1, hk, d), "bf16"))
+    retrieval_len = t - c["rejected"]
+    return dict(keys=keys, values=values, query=query, steps=steps,
+                cos_sin=cos_sin_table(c["budget"], d, c["theta"]), retrieval_len=retrieval_len,
+                committed=retrieval_len)
+
+
+# ---------------------------------------------------------------- KV sink (A9)
+# Three requests in reordered canonical slots [3, 1, 2] (a released slot 0),
+# prefill written through populate_prefill, one retrieval for the middle
+# request, then a draft cycle of 3 steps whose tensors carry 2 graph-padding
+# rows after the 3 requests.
+CAPTURE = dict(chunk=8, budget=64, depth=3, hk=2, hq=4, d=64, slots=5, max_len=200,
+               prompts=(40, 70, 25), padding=2)
+
+
+def capture_inputs() -> dict:
+    c = CAPTURE
+    g = rng(1777)
+    rows, pad, hk, hq, d = len(c["prompts"]), c["padding"], c["hk"], c["hq"], c["d"]
+    total = sum(c["prompts"])
+    prefill_pos = np.concatenate([np.arange(n) for n in c["prompts"]]).astype(np.int64)
+    steps = []
+    for j in range(c["depth"]):
+        pos = np.array([n + j for n in c["prompts"]] + [0] * pad, np.int64)
+        steps.append(dict(positions=pos, key=normal(g, (rows + pad, hk, d), "bf16"),
+                          value=normal(g, (rows + pad, hk, d), "bf16"),
+                          query=normal(g, (rows + pad, hq, d), "bf16")))
+    n_mid = (c["prompts"][1] + c["chunk"] - 1) // c["chunk"]
+    return dict(prefill_positions=prefill_pos, prefill_key=normal(g, (total, hk, d), "bf16"),
+                prefill_value=normal(g, (total, hk, d), "bf16"),
+                query_ends=np.cumsum(c["prompts"]).astype(np.int64), steps=steps,
+                mid_scores=g.random(n_mid, dtype=np.float32),
+                cos_sin=round_to(cos_sin_table(c["budget"], d), "bf16"))

@@ -130,8 +130,15 @@ def test_target_attention_wrapper_rejects_bad_arguments(dsb):
     lens = torch.ones(2, dtype=torch.int32)
     with pytest.raises(ValueError, match="table_rows"):
         f(q, kc, kc, bt, lens, scale=0.1, max_seq_len=32, table_rows=torch.zeros(1, dtype=torch.int32))
-    with pytest.raises(ValueError, match="tokens_per_split"):
+    with pytest.raises(ValueError, match="max_seq_len"):
+        f(q, kc, kc, bt, lens, scale=0.1, max_seq_len=-1)
+    # tokens_per_split <= 0 picks the library's default of 512, in the wrapper
+    # (which then only fails on the CPU tensors) and in the C ABI alike
+    with pytest.raises(ValueError, match="CUDA"):
         f(q, kc, kc, bt, lens, scale=0.1, max_seq_len=32, tokens_per_split=0)
+    lib = dsb._lib.load()
+    assert lib.dsb_paged_decode_scratch_floats(2, 8, 4096, 0) == \
+        lib.dsb_paged_decode_scratch_floats(2, 8, 4096, 512) == 2 * 8 * 8 * 130
     with pytest.raises(ValueError):
         f(q, kc[..., :64], kc[..., :64], bt, lens, scale=0.1, max_seq_len=32)  # head dims differ
     with pytest.raises(ValueError):

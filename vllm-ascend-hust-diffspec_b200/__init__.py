@@ -14,6 +14,8 @@ operator surface:
 * ``runtime``     — ``DiffSpecDraftCache`` retrieval hook / rebuild / attention
 * ``parallel``    — head-sharded score exchange over NCCL
 * ``draft_layer`` — one Eagle3-style draft decoder layer built on the above
+* ``torch_ops``   — the same entry points as ``torch.ops.diffspec_b200.*`` custom
+  ops (fake implementations, declared in-place writes) for compiled graphs
 
 All compute runs in ``libdiffspec_b200.so`` (C ABI: include/diffspec_b200.h).
 The directory name is not a Python identifier; importing it under any name
@@ -23,6 +25,7 @@ also registers it (and its submodules) as ``diffspec_b200``.
 import sys as _sys
 
 from . import _lib, attention, compact_kv, draft_layer, kernels, parallel, runtime, selection  # noqa: F401
+from . import torch_ops  # noqa: F401  (registers torch.ops.diffspec_b200.*)
 from .attention import AttentionWorkspace, draft_decode_attention  # noqa: F401
 from .compact_kv import rebuild_compact_kv_from_plan  # noqa: F401
 from .kernels import (  # noqa: F401
@@ -38,7 +41,8 @@ from .runtime import (  # noqa: F401
 from .selection import DiffSpecSelection, build_history_plan, select_context_chunks, select_rows  # noqa: F401
 
 _sys.modules.setdefault("diffspec_b200", _sys.modules[__name__])
-for _name in ("_lib", "attention", "compact_kv", "draft_layer", "kernels", "parallel", "runtime", "selection"):
+for _name in ("_lib", "attention", "compact_kv", "draft_layer", "kernels", "parallel", "runtime", "selection",
+              "torch_ops"):
     _sys.modules.setdefault(f"diffspec_b200.{_name}", _sys.modules[f"{__name__}.{_name}"])
 
 

@@ -208,8 +208,16 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     if (__syncthreads_and(got) && !s_abort) {
       tc_fence_after();
       tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16), acc);
-    } else if (tid == 0) {
-      flag_error(a.err, DSB_FLAG_TIMEOUT);
+    } else {
+      // `done` is committed after the last product that was issued (a wait
+      // that ran out above stops the issuing, it never leaves a product
+      // half-issued), so it arrives once those few MMAs finish; wait for it
+      // once more (bounded) so no product still writes the tensor memory
+      // freed below.  The partial stays zero and the launch is flagged.
+      if (tid == 0) {
+        flag_error(a.err, DSB_FLAG_TIMEOUT);
+        if (!got) mbar_wait(done, 0);
+      }
     }
   }
   tc_fence_before();

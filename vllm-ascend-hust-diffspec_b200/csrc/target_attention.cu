@@ -87,7 +87,10 @@ __global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const
     L = 0;
   }
   const int64_t cap = a.bt_cols * a.bs;  // tokens the table row can address
-  if ((int64_t)L > cap) L = (int)cap;
+  if ((int64_t)L > cap) {  // seq_lens[r] beyond its block-table row
+    if (threadIdx.x == 0 && split == 0 && h == 0) flag_error(a.err, DSB_FLAG_POSITION);
+    L = (int)cap;
+  }
   if (L < 0) L = 0;
   if ((int64_t)L > (int64_t)a.splits * a.tps) {  // seq_lens[r] above max_seq_len
     if (threadIdx.x == 0 && split == 0 && h == 0) flag_error(a.err, DSB_FLAG_POSITION);
@@ -311,8 +314,8 @@ template <typename T> int launch_typed(const TaArgs &a, int group, cudaStream_t 
   return check_launch("paged_decode_merge_kernel");
 }
 
-int splits_for(int32_t max_seq_len, int32_t tokens_per_split) {
-  return std::max(1, (max_seq_len + tokens_per_split - 1) / tokens_per_split);
+int64_t splits_for(int32_t max_seq_len, int32_t tokens_per_split) {
+  return std::max<int64_t>(1, ((int64_t)max_seq_len + tokens_per_split - 1) / tokens_per_split);
 }
 
 }  // namespace
@@ -322,7 +325,8 @@ using namespace dsb;
 
 extern "C" int64_t dsb_paged_decode_scratch_floats(int32_t query_rows, int32_t num_query_heads,
                                                     int32_t max_seq_len, int32_t tokens_per_split) {
-  if (query_rows <= 0 || num_query_heads <= 0 || max_seq_len < 0 || tokens_per_split <= 0) return 0;
+  if (query_rows <= 0 || num_query_heads <= 0 || max_seq_len < 0) return 0;
+  if (tokens_per_split <= 0) tokens_per_split = 512;  // the launch's default
   return (int64_t)query_rows * num_query_heads * splits_for(max_seq_len, tokens_per_split) *
          (kTaD + 2);
 }
@@ -349,7 +353,7 @@ extern "C" int dsb_paged_decode_attention_lse(
   if (!(scale > 0.f)) return fail(DSB_ERR_INVALID, "scale must be positive");
   if (!query || !key_cache || !value_cache || !block_table || !seq_lens || !out || !lse || !scratch)
     return fail(DSB_ERR_INVALID, "null pointer argument");
-  const int splits = splits_for(max_seq_len, tokens_per_split);
+  const int64_t splits = splits_for(max_seq_len, tokens_per_split);
   if (splits > 65535 || num_kv_heads > 65535 || query_rows > 65535)
     return fail(DSB_ERR_UNSUPPORTED, "grid too large");
   if (scratch_floats < dsb_paged_decode_scratch_floats(query_rows, num_query_heads, max_seq_len,
@@ -373,7 +377,7 @@ extern "C" int dsb_paged_decode_attention_lse(
   a.hq = num_query_heads;
   a.hk = num_kv_heads;
   a.rows = query_rows;
-  a.splits = splits;
+  a.splits = (int)splits;
   a.tps = tokens_per_split;
   a.scale_log2 = scale * kTaLog2e;
   a.part = scratch;

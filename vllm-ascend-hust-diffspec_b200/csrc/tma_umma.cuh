@@ -26,6 +26,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+// 3-D tiled TMA load (coordinates x innermost, then y, then z).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
 // The same load with an L2 cache policy (e.g. l2_evict_first() for weights
 // streamed once per step, so the lines other kernels re-read stay in L2).
 __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap *map, int x, int y,
@@ -157,6 +167,26 @@ bool encode_kv_map(CUtensorMap *map, const void *base, int64_t rows, int head_di
   return r == CUDA_SUCCESS;
 }
 
+
+// 3-D map over a paged cache [num_blocks * block_size token rows, heads, D]:
+// dims (D, heads, token rows), boxes of 64 columns x 1 head x box_rows token
+// rows with the 128-byte swizzle (a box lands as box_rows rows of 128 bytes).
+bool encode_paged_map(CUtensorMap *map, const void *base, int64_t token_rows, int heads,
+                      int head_dim, int dtype, int box_rows) {
+  auto fn = tensor_map_encoder();
+  if (fn == nullptr || reinterpret_cast<uintptr_t>(base) % 16 || token_rows <= 0 ||
+      token_rows > 0x7fffffff || heads <= 0 || head_dim % 64)
+    return false;
+  cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)heads, (cuuint64_t)token_rows};
+  cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, (cuuint64_t)heads * head_dim * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, dtype == DSB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        3, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
 
 }  // namespace
 }  // namespace dsb

@@ -526,8 +526,10 @@ def paged_decode_attention_lse(
         raise ValueError("block_table must be 2-D and seq_lens cover every row")
     if table_rows is not None and table_rows.numel() < rows:
         raise ValueError("table_rows must map every query row")
-    if max_seq_len < 0 or tokens_per_split <= 0:
-        raise ValueError("max_seq_len must be >= 0 and tokens_per_split positive")
+    if max_seq_len < 0:
+        raise ValueError("max_seq_len must be >= 0")
+    if tokens_per_split <= 0:  # the library's default split length
+        tokens_per_split = 512
     device = _lib.require_cuda(query, key_cache, value_cache, block_table, seq_lens, table_rows)
     if out is None:
         out = torch.empty_like(query)
