@@ -20,8 +20,6 @@ test_oracle_chains.py); against the reference's fp32-cache outputs directly
 the mean bound is 4e-3, since the bf16 rounding of every rotated key adds
 about as much error as the bf16 rounding of the output."""
 
-FP32_CACHE_MEAN_REL = 4e-3  # GPU (bf16 working cache) against the reference's fp32 cache
-
 from __future__ import annotations
 
 import numpy as np
@@ -33,6 +31,8 @@ from conftest import close_bf16, golden
 from oracle import diffspec_oracle as O
 
 pytestmark = pytest.mark.gpu
+
+FP32_CACHE_MEAN_REL = 4e-3  # GPU (bf16 working cache) against the reference's fp32 cache
 
 
 def _bf(a, dev):
