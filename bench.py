@@ -72,19 +72,47 @@ UNIT = "draft steps/s"
 STEPS_PER_PERIOD = INTERVAL * DEPTH
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch per
-# kind, from one ncu capture of the current kernels on a B200:
-# `ncu --set full --clock-control none -k regex:<kernel> -s 2 -c 1
-#  python bench.py --only <kind> --steps 3 --warmup 2`.
-PROFILED_TRAFFIC = {"attention": 67_278_592 + 482_816, "rebuild": 65_555_968 + 9_956_096,
-                    "scores": 671_409_920 + 6_066_688}
-# DRAM bytes per launch inside a running period (caches not flushed between
-# kernels), from the one-pass launch list `ncu --metrics gpu__time_duration.sum,
-# dram__bytes_read.sum,dram__bytes_write.sum --cache-control none
-# --clock-control none -s 24 -c 23 python bench.py --steps 3 --warmup 3
-# --no-cpu --no-e2e`, averaged over the period's launches of the kind: the
-# working cache stays in L2 between the rebuild and the four draft steps.
-IN_SITU_TRAFFIC = {"attention": 2_153_520, "rebuild": 88_181_440, "scores": 680_546_560}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# period's kernels come from the committed ncu summary below: one row per
+# launch kind with the kernel's source files, a digest of those sources at
+# capture time, the cold-cache figure and the in-period figure.  A row whose
+# sources have changed since the capture is reported as stale (null).
+TRAFFIC_PROFILE = ROOT / "profiles" / "dram_traffic_config2.md"
+
+
+def source_digest(files: str) -> str:
+    """sha256 (16 hex) of the '+'-joined package source files, in order."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for name in files.split("+"):
+        h.update((ROOT / "vllm-ascend-hust-diffspec_b200" / name.strip()).read_bytes())
+    return h.hexdigest()[:16]
+
+
+def profiled_traffic() -> dict:
+    """{kind: dict(traffic, traffic_in_situ, source)} from TRAFFIC_PROFILE's
+    table rows `| kind | kernel | sources | digest | cold bytes | in-period
+    bytes |`; values are None when the digest no longer matches."""
+    out = {}
+    try:
+        lines = TRAFFIC_PROFILE.read_text().splitlines()
+    except OSError:
+        return out
+    for line in lines:
+        cells = [c.strip().strip("`") for c in line.strip().strip("|").split("|")]
+        if len(cells) != 6 or not cells[4].replace(",", "").isdigit():
+            continue
+        kind, _, files, digest, cold, warm = cells
+        try:
+            fresh = source_digest(files) == digest
+        except OSError:
+            fresh = False
+        out[kind] = dict(traffic=int(cold.replace(",", "")) if fresh else None,
+                         traffic_in_situ=int(warm.replace(",", "")) if fresh else None,
+                         source=f"{TRAFFIC_PROFILE.relative_to(ROOT)}" +
+                         ("" if fresh else f" (stale: {files} changed since the capture)"))
+    return out
 
 
 def _peaks() -> tuple[float, str]:
@@ -813,10 +841,12 @@ def emit_ours(args):
                    for k in per_launch if k in kernel_t}
         n, avg_ms = chained[dominant]
         achieved = per_launch[dominant] / (avg_ms / 1e3) / 1e9
+        traffic = profiled_traffic().get(dominant, {})
         roofline = dict(bound="hbm", kernel=dominant, achieved=round(achieved, 1), peak=peak,
                         peak_kind=peak_kind, unit="GB/s", frac=round(achieved / peak, 4),
-                        traffic=PROFILED_TRAFFIC.get(dominant),
-                        traffic_in_situ=IN_SITU_TRAFFIC.get(dominant),
+                        traffic=traffic.get("traffic"),
+                        traffic_in_situ=traffic.get("traffic_in_situ"),
+                        traffic_source=traffic.get("source", "no ncu capture committed"),
                         algorithmic_bytes_per_launch=int(per_launch[dominant]),
                         avg_launch_us=round(avg_ms * 1e3, 3),
                         timing="avg_launch_us: the kind's launches of one period back to back "
@@ -895,6 +925,200 @@ def emit_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- config 4
+C4_REQUESTS, C4_CTX, C4_HQ, C4_HK, C4_BUDGET = 32, 131072, 64, 8, 4096
+C4_HISTORY_BUDGET = (C4_BUDGET - DEPTH - 1) // CHUNK * CHUNK  # 4032
+
+
+class RetrievalWorkload:
+    """Config 4 on one rank: the target's paged K for 32 requests x 131072
+    tokens and this rank's contiguous kv heads [head_lo, head_hi) of 8 (with
+    their 8 query heads each).  Every global kv head draws its keys, queries
+    and planted-chunk noise from its own generator, and the block table and
+    planted chunks from a shared one, so the data of a kv head is the same at
+    any GPU count and the selection can be compared across counts."""
+
+    def __init__(self, torch, dsb, device, head_lo, head_hi, seed=4242):
+        self.torch, self.dsb, self.device = torch, dsb, device
+        rows, ctx, group = C4_REQUESTS, C4_CTX, C4_HQ // C4_HK
+        self.rows, self.hk, self.hq = rows, head_hi - head_lo, (head_hi - head_lo) * group
+        bf = torch.bfloat16
+        pages = ctx // PAGE
+        nblocks = rows * pages
+        shared = torch.Generator(device=device).manual_seed(seed)
+        self.block_table = torch.randperm(nblocks, generator=shared, device=device).view(
+            rows, pages).to(torch.int32).contiguous()
+        planted = [torch.randperm(ctx // CHUNK - 1, generator=shared, device=device)[:PLANTED]
+                   for _ in range(rows)]
+        self.planted = [sorted(p.tolist()) for p in planted]
+        self.key_cache = torch.empty((nblocks, PAGE, self.hk, D), dtype=bf, device=device)
+        self.query = torch.empty((5 * rows, self.hq, D), dtype=bf, device=device)
+        committed_q = 5 - REJECTED - 1
+        for i, h in enumerate(range(head_lo, head_hi)):
+            gh = torch.Generator(device=device).manual_seed(seed + 1 + h)
+            keys = torch.randn((nblocks, PAGE, D), generator=gh, device=device).to(bf)
+            q = torch.randn((5 * rows, group, D), generator=gh, device=device).to(bf)
+            for r in range(rows):
+                target = q[5 * r + committed_q].float().mean(0)
+                tok = (planted[r][:, None] * CHUNK + torch.arange(CHUNK, device=device)).reshape(-1)
+                noise = 0.1 * torch.randn((tok.numel(), D), generator=gh, device=device)
+                keys[self.block_table[r].long()[tok // PAGE], tok % PAGE] = (target + noise).to(bf)
+            self.key_cache[:, :, i] = keys
+            self.query[:, i * group:(i + 1) * group] = q
+            del keys
+        self.query_ends = torch.arange(1, rows + 1, device=device, dtype=torch.int32) * 5
+        self.target_seq = torch.full((rows,), ctx, dtype=torch.int32, device=device)
+        self.counts = torch.full((rows,), 5 - REJECTED, dtype=torch.int64, device=device)
+        self.active = torch.arange(rows, dtype=torch.int32, device=device)
+        self.q_index = torch.empty(rows, dtype=torch.int32, device=device)
+        self.r_len = torch.empty(rows, dtype=torch.int32, device=device)
+        self.r_slot = torch.empty(rows, dtype=torch.int32, device=device)
+        self.status = torch.zeros(2, dtype=torch.int32, device=device)
+        self.max_chunks = (ctx + CHUNK - 1) // CHUNK
+        self.parts = torch.zeros((rows, self.hk, self.max_chunks), dtype=torch.float32,
+                                 device=device)
+        self.sel_chunks = torch.zeros((rows, C4_HISTORY_BUDGET // CHUNK), dtype=torch.int32,
+                                      device=device)
+        self.sel_count = torch.full((rows,), -1, dtype=torch.int32, device=device)
+        # the target's softmax LSE of the committed queries, per local query head
+        qi = torch.arange(rows, device=device) * 5 + committed_q
+        seq = torch.full((rows,), ctx - REJECTED, dtype=torch.int32, device=device)
+        cmax, csum = dsb.kernels.paged_chunk_stats(
+            self.query[qi].contiguous(), self.key_cache, self.block_table, seq, chunk_size=CHUNK,
+            max_seq_len=ctx, scale=D ** -0.5)
+        lse_rows = torch.empty((rows, self.hq), dtype=torch.float32, device=device)
+        dsb.kernels.stats_to_head_scores(cmax, csum, seq, self.hk, chunk_size=CHUNK,
+                                         lse_out=lse_rows)
+        self.lse = torch.zeros((5 * rows, self.hq), dtype=torch.float32, device=device)
+        self.lse[qi] = lse_rows
+
+
+def retrieval_launches(w, exchange=None, gathered=None):
+    """Config 4's retrieval as (kind, callable): committed-query pick, chunk
+    scores of the local kv heads, the all-gather of their mass (N > 1), and
+    the selection over all 64 query heads (replicated on every rank)."""
+    dsb, lib = w.dsb, w.dsb._lib
+
+    def prepare():
+        lib.call("dsb_prepare_retrieval_rows", w.query_ends.data_ptr(), w.target_seq.data_ptr(),
+                 w.counts.data_ptr(), 1, w.active.data_ptr(), w.rows, w.q_index.data_ptr(),
+                 w.r_len.data_ptr(), w.r_slot.data_ptr(), w.status.data_ptr(),
+                 lib.stream_ptr(w.device))
+
+    def scores():
+        dsb.kernels.paged_chunk_head_scores(
+            w.query, w.key_cache, w.lse, w.block_table, w.r_len, chunk_size=CHUNK,
+            max_seq_len=C4_CTX, scale=D ** -0.5, query_index=w.q_index, out=w.parts)
+
+    def select():
+        dsb.selection.select_rows(gathered if exchange is not None else w.parts, w.r_len,
+                                  chunk_size=CHUNK, token_budget=C4_HISTORY_BUDGET,
+                                  normalize_heads=C4_HQ, row_slots=w.r_slot,
+                                  sel_chunks=w.sel_chunks, sel_count=w.sel_count)
+
+    seq = [("prepare", prepare), ("scores", scores)]
+    if exchange is not None:
+        seq.append(("exchange", lambda: exchange(w.parts)))
+    seq.append(("select", select))
+    return seq
+
+
+def run_config4(args):
+    """head-sharded retrieval at fixed total work (strong
+    scaling).  32 requests x 131072 tokens, 64 query / 8 kv heads, chunk 64,
+    budget 4096 (history budget 4032, 62 ranked chunks + the newest); the 8
+    kv heads are split evenly over the N ranks, each rank scores its heads
+    over every request, the per-kv-head mass is all-gathered over NCCL and
+    every rank runs the same selection.  One step = one retrieval of all 32
+    requests; the line carries a digest of the selected chunk ids, which
+    must be the same at every N."""
+    import hashlib
+
+    import torch
+    import torch.distributed as dist
+
+    dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus or C4_HK % world:
+        raise SystemExit(f"config 4 runs on 1, 2, 4 or 8 ranks (--gpus {args.gpus}, "
+                         f"WORLD_SIZE={world})")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    per = C4_HK // world
+    w = RetrievalWorkload(torch, dsb, device, rank * per, (rank + 1) * per)
+    exchange = gathered = None
+    if world > 1:
+        gathered = torch.empty((world, w.rows, per, w.max_chunks), dtype=torch.float32,
+                               device=device)
+        exchange = lambda parts: dsb.parallel.gather_head_scores(parts, None, out=gathered)  # noqa: E731
+    launches = retrieval_launches(w, exchange, gathered)
+    if exchange is not None:  # one eager collective sets up the communicator
+        exchange(w.parts)
+        torch.cuda.synchronize(device)
+        dist.barrier()
+    graph = Graph(torch, launches, device)
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    assert dsb._lib.read_and_clear_error_flag(device) == 0, "kernel index check tripped"
+    with ClockSampler(local) as clocks:
+        for _ in range(200):  # ~0.3 s of load before the timed region
+            graph.replay()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kinds = [k for k, _ in launches if k != "exchange"]
+    kernel_t = per_kernel_times(torch, device, [x for x in launches if x[0] != "exchange"]) or {}
+    del graph
+    torch.cuda.synchronize(device)
+    sel = torch.cat((w.sel_chunks.flatten(), w.sel_count)).cpu().numpy().tobytes()
+    planted_found = all(set(p) <= set(w.sel_chunks[r, : int(w.sel_count[r])].tolist())
+                        for r, p in enumerate(w.planted))
+    peak, peak_kind = _peaks()
+    k_bytes = C4_REQUESTS * (C4_CTX - REJECTED) * per * D * 2
+    line = dict(
+        mode="config4", metric="config 4 head-sharded retrievals/s (32 x 131072 ctx, 64/8 heads, "
+        "budget 4096)", value=round(1e3 / ms, 2), unit="retrievals/s", n_gpus=world,
+        steps=args.steps, warmup=args.warmup, ms_per_step=round(ms, 4), higher_is_better=True,
+        scaling="strong", dtype="bf16", data="synthetic (seeded Gaussian K/Q per kv head, 8 "
+        "planted chunks per request)",
+        config=dict(requests=C4_REQUESTS, context=C4_CTX, q_heads=C4_HQ, kv_heads=C4_HK,
+                    kv_heads_per_gpu=per, head_dim=D, chunk=CHUNK, token_budget=C4_BUDGET,
+                    history_budget=C4_HISTORY_BUDGET, page_size=PAGE,
+                    l2=f"inputs larger than L2 (K {k_bytes / 1e9:.2f} GB per GPU)",
+                    exchange="NCCL all-gather of per-kv-head mass, read in place by the selection"
+                    if world > 1 else "none"),
+        k_bytes_per_gpu=k_bytes,
+        hbm_frac_per_gpu=round(k_bytes / (ms / 1e3) / 1e9 / peak, 4), peak=peak,
+        peak_kind=peak_kind,
+        per_kind_us={k: round(v[1] / v[0] * 1e3, 3) for k, v in kernel_t.items()},
+        selection_digest=hashlib.sha256(sel).hexdigest()[:16], planted_found=planted_found,
+        gpu_launches=len(kinds) * args.steps, clocks=clocks.summary())
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_only(args):
     """One kernel kind of the config-2 period, launched eagerly `--steps`
     times after `--warmup` launches (the command the ncu captures run)."""
@@ -907,6 +1131,19 @@ def run_only(args):
     launches = period_launches(w)
     for kind, fn in launches:  # one full period so selection/plan state is real
         fn()
+    if args.only == "gather":
+        # the paged gather entry point over the period's selection: the raw
+        # caches viewed as 16-token pages (identity block table), the selected
+        # chunks expanded to token ids and padded with -1 to the token budget
+        pages = w.raw_key.shape[1] // PAGE
+        paged = [t.view(w.rows * pages, PAGE, w.hk, D) for t in (w.raw_key, w.raw_value)]
+        table = torch.arange(w.rows * pages, dtype=torch.int32, device=device).view(w.rows, pages)
+        tok = torch.full((w.rows, TOKEN_BUDGET), -1, dtype=torch.int64, device=device)
+        n_sel = w.sel_chunks.shape[1]
+        tok[:, : n_sel * CHUNK] = (w.sel_chunks.long()[:, :, None] * CHUNK
+                                   + torch.arange(CHUNK, device=device)).view(w.rows, -1)
+        launches = [("gather", lambda: dsb.kernels.gather_raw_kv_with_local_rope(
+            paged[0], paged[1], table, tok, w.cos_sin, rope_dim=D, is_neox_style=True))]
     picked = [fn for kind, fn in launches if kind == args.only]
     if not picked:
         raise SystemExit(f"no launch of kind {args.only}")
@@ -1313,7 +1550,8 @@ def main():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end API leg")
-    p.add_argument("--only", choices=["prepare", "scores", "select", "rebuild", "attention"],
+    p.add_argument("--only", choices=["prepare", "scores", "select", "rebuild", "attention",
+                                      "gather"],
                    help="launch one kernel kind eagerly (for profiler captures)")
     p.add_argument("--kv-projection", action="store_true",
                    help="time the K/V projection + raw-cache write (config 5 decode step)")
@@ -1323,6 +1561,8 @@ def main():
                    help="time the config-5 draft layer's four linears against cuBLAS")
     p.add_argument("--target-attention", action="store_true",
                    help="time the target paged decode attention with the LSE export")
+    p.add_argument("--config4", action="store_true",
+                   help="config 4: head-sharded retrieval at fixed work over --gpus N ranks")
     p.add_argument("--reference-triton", action="store_true",
                    help="time the reference's Triton kernels (compiled for this GPU) against ours")
     args = p.parse_args()
@@ -1338,6 +1578,8 @@ def main():
         run_target_attention(args)
     elif args.reference_triton:
         run_reference_triton(args)
+    elif args.config4:
+        run_config4(args)
     elif args.only:
         run_only(args)
     elif args.impl == "reference":

@@ -22,20 +22,16 @@ def bf16(a, device):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device).bfloat16()
 
 
-KERNELS = ["tma", "tma-ticket", "umma", "umma-ticket", "legacy"]
+KERNELS = ["tma", "tma-ticket", "legacy"]
 
 
 def use_kernel(kernel, monkeypatch):
-    """tma: TMA-fed kernel on mma.sync (the default); umma: the opt-in
-    TMA-fed kernel with both products on tcgen05 (head_dim 128; other head
-    dims fall through to the mma.sync kernel); *-ticket: splits merged
-    through global partials and an atomic ticket instead of inside a
+    """tma: TMA-fed kernel on mma.sync (the default); tma-ticket: splits
+    merged through global partials and an atomic ticket instead of inside a
     thread-block cluster; legacy: the register-fed kernel the library falls
     back to."""
     if kernel == "legacy":
         monkeypatch.setenv("DSB_ATTENTION_LEGACY", "1")
-    if kernel.startswith("umma"):
-        monkeypatch.setenv("DSB_ATTENTION_UMMA", "1")
     if kernel.endswith("-ticket"):
         monkeypatch.setenv("DSB_ATTENTION_TICKET_MERGE", "1")
 

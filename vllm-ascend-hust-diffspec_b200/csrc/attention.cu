@@ -988,394 +988,6 @@ draft_attention_tma_kernel(const __grid_constant__ CUtensorMap tmk,
 }
 
 
-// ===========================================================================
-// tcgen05 variant (opt-in, head_dim 128 and up to 16 query heads per kv
-// head): 128-token K/V stages arrive by TMA exactly as above, but both
-// products run on the 5th-generation tensor cores with fp32 accumulators in
-// tensor memory, issued by one thread:
-//   S^T[128 tokens][16 heads] = K[128][128] . Q^T      (A = K tile, K-major)
-//   O^T[128 dims][16 heads]  += V^T . (P_hi + P_lo)^T   (A = V tile, MN-major)
-// Each of the 128 threads owns one token of S (and one head-dim row of O):
-// it reads its S row from tensor memory, applies the online softmax with a
-// lazily updated per-head reference max (rescaling O in tensor memory only
-// when some score exceeds it by 2^8), and writes its P column to shared
-// memory as the B operand.  S is double-buffered in tensor memory so the
-// next stage's QK^T runs under this stage's softmax; P is double-buffered in
-// shared memory.  All waits are bounded (DSB_FLAG_TIMEOUT), and the CTA
-// frees its tensor memory before any exit that follows the allocation.
-// ===========================================================================
-constexpr int kUmmaThreads = 128;
-constexpr int kUmmaN = 16;  // query heads per kv head, padded (tcgen05 N)
-
-template <int NS> struct UmmaCfg {
-  static constexpr int D = 128, kStageTok = 128, kBoxes = 2;
-  static constexpr int kBoxBytes = 128 * kStageTok;               // [128 rows][64 cols] x 2 B
-  static constexpr int kStageBytes = 2 * kBoxes * kBoxBytes;      // K + V: 64 KB
-  static constexpr int kRingBytes = NS * kStageBytes;
-  static constexpr int kQBytes = kBoxes * 16 * 128;               // Q^T: 2 boxes [16][64]
-  static constexpr int kPBytes = 2 * 16 * 128;                    // P^T of a stage: 2 boxes [16][64]
-  static constexpr int kPOffset = kRingBytes + kQBytes;           // P[parity][hi, lo]
-  static constexpr int kTailOffset = kPOffset + 4 * kPBytes;      // barriers, reductions
-  // barriers: full[NS], s, o[2]; tmem base; per-warp head reductions [4][16]
-  static constexpr int kTailBytes = 8 * (NS + 3) + 16 + 4 * 4 * 16 + 16;
-  static constexpr int kXOffset = (kTailOffset + kTailBytes + 15) / 16 * 16;  // cluster exchange
-};
-
-template <typename T, int NS, int GPF, bool CL>
-__global__ void __launch_bounds__(kUmmaThreads)
-draft_attention_umma_kernel(const __grid_constant__ CUtensorMap tmk,
-                            const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
-  using Cfg = UmmaCfg<NS>;
-  constexpr int D = Cfg::D, GP = kUmmaN, kStageTok = Cfg::kStageTok, kBoxBytes = Cfg::kBoxBytes;
-  if (threadIdx.x == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
-  }
-  pdl_begin();
-  if (CL) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t *ring = smem;
-  uint8_t *qt = smem + Cfg::kRingBytes;
-  uint8_t *pt = smem + Cfg::kPOffset;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kTailOffset);  // full[NS], s, o[2]
-  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(bars + NS + 3);
-  float *s_red = reinterpret_cast<float *>(s_tmem + 4);                   // [4 warps][16]
-  __shared__ int s_last, s_abort;
-
-  const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int group = a.Hq / a.Hk;
-  T *out = static_cast<T *>(a.out);
-  const uint32_t ring_u32 = smem_u32(ring), qt_u32 = smem_u32(qt), pt_u32 = smem_u32(pt);
-  const uint32_t bar_full = smem_u32(bars), bar_s = bar_full + 8 * NS, bar_o = bar_s + 8;
-  if (tid == 0) {
-    for (int s = 0; s < NS + 3; ++s) mbar_init(bar_full + 8 * s);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    s_abort = 0;
-  }
-  if (row >= a.rows) {
-    if (split == 0) zero_heads<T, D>(out, row, a.Hq, kvh * group, group);
-    return;
-  }
-  // Q^T (zero-padded to 16 heads) as the K-major B operand of S^T = K Q^T.
-  {
-    const T *qrow = static_cast<const T *>(a.query) + ((int64_t)row * a.Hq + kvh * group) * D;
-    for (int i = tid; i < GP * (D / 8); i += kUmmaThreads) {  // 16-byte vectors
-      const int h = i / (D / 8), c = i % (D / 8);
-      const uint4 v = h < group ? *reinterpret_cast<const uint4 *>(qrow + (int64_t)h * D + c * 8)
-                                : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4 *>(qt + (c / 8) * 2048 + h * 128 + (((c & 7) ^ (h & 7)) << 4)) = v;
-    }
-  }
-  if constexpr (GPF < GP) {  // P^T rows of the padding heads stay zero for the whole kernel
-    constexpr int kPad = GPF < GP ? GP - GPF : 1;
-    for (int i = tid; i < 4 * 2 * kPad * 8; i += kUmmaThreads) {
-      const int c = i % 8, r = GPF + (i / 8) % kPad, tile = i / (8 * kPad);  // tile: 8 boxes
-      *reinterpret_cast<uint4 *>(pt + tile * 2048 + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
-    }
-  }
-  constexpr int VE = 16 / sizeof(T), kNewVecs = 2 * (D / VE), kNewPerLane = (kNewVecs + 31) / 32;
-  uint4 new_kv[kNewPerLane];
-  if (warp == 0) {
-#pragma unroll
-    for (int j = 0; j < kNewPerLane; ++j) {
-      const int i = lane + 32 * j;
-      const T *src = static_cast<const T *>(i < D / VE ? a.key : a.value) +
-                     ((int64_t)row * a.Hk + kvh) * D + (i % (D / VE)) * VE;
-      new_kv[j] = (i < kNewVecs) ? *reinterpret_cast<const uint4 *>(src) : make_uint4(0, 0, 0, 0);
-    }
-  }
-  const int slot = a.slots[row];
-  const int pos = a.positions[row] + a.position_offset;
-  if (slot < 0 || slot >= a.num_slots || pos < 0 || pos >= a.W) {
-    if (split == 0) {
-      if (tid == 0)
-        flag_error(a.err, (slot < 0 || slot >= a.num_slots) ? DSB_FLAG_SLOT : DSB_FLAG_POSITION);
-      zero_heads<T, D>(out, row, a.Hq, kvh * group, group);
-    }
-    return;
-  }
-  const int len = pos + 1;
-  const int active = (len + a.split_tokens - 1) / a.split_tokens;
-  if (!CL && split >= active) return;
-  const bool live = split < active;
-  const int ts = live ? split * a.split_tokens : 0;
-  const int te = live ? min(len, ts + a.split_tokens) : 0;
-  const int64_t head_row0 = ((int64_t)slot * a.Hk + kvh) * a.W;
-  const int n_stages = (te - ts + kStageTok - 1) / kStageTok;
-
-  auto issue = [&](int k) {  // thread 0: TMA of stage k into slot k % NS
-    const int s = k % NS;
-    const uint32_t kb = ring_u32 + s * Cfg::kStageBytes;
-    const uint32_t vb = kb + Cfg::kBoxes * kBoxBytes;
-    const int y = (int)(head_row0 + ts + k * kStageTok);
-    mbar_expect_tx(bar_full + 8 * s, Cfg::kStageBytes);
-#pragma unroll
-    for (int b = 0; b < Cfg::kBoxes; ++b) {
-      tma_load_2d(kb + b * kBoxBytes, &tmk, 64 * b, y, bar_full + 8 * s);
-      tma_load_2d(vb + b * kBoxBytes, &tmv, 64 * b, y, bar_full + 8 * s);
-    }
-  };
-  if (warp == 0) {
-    const bool owner = pos >= ts && pos < te;
-    const int n_first = min(NS, n_stages);
-    const int k_pos = owner ? (pos - ts) / kStageTok : n_first;
-    if (lane == 0)
-      for (int k = 0; k < min(n_first, k_pos); ++k) issue(k);
-    if (owner) {
-      T *dst = static_cast<T *>(a.wk) + (head_row0 + pos) * D;
-      T *dsv = static_cast<T *>(a.wv) + (head_row0 + pos) * D;
-#pragma unroll
-      for (int j = 0; j < kNewPerLane; ++j) {
-        const int i = lane + 32 * j;
-        if (i < kNewVecs)
-          *reinterpret_cast<uint4 *>((i < D / VE ? dst : dsv) + (i % (D / VE)) * VE) = new_kv[j];
-      }
-      asm volatile("fence.proxy.async.global;" ::: "memory");
-      __syncwarp();
-    }
-    if (lane == 0)
-      for (int k = min(n_first, k_pos); k < n_first; ++k) issue(k);
-    // tensor memory: S[2] (16 columns each) and O (16 columns)
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 64;" ::"r"(
-                     smem_u32(s_tmem))
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // Q^T for the tensor core
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *s_tmem;
-  const uint32_t t_s0 = tmem, t_o = tmem + 32;
-  const uint32_t lane_off = (uint32_t)(32 * warp) << 16;  // this warp's tensor-memory lanes
-  const uint32_t id_k = umma_idesc<T>(false), id_v = umma_idesc<T>(true);
-
-  bool ok = true;
-  int issued = min(NS, n_stages);  // TMA stages issued (thread 0)
-  int pv_issued = 0;                // PV products committed (thread 0)
-  int qk_issued = 0;                // QK^T products committed (thread 0)
-  // thread 0: wait for stage k's copies, then S^T(k) = K(k) Q^T into S[k & 1]
-  auto issue_qk = [&](int k) {
-    if (!mbar_wait(bar_full + 8 * (k % NS), (k / NS) & 1)) {
-      ok = false;
-      s_abort = 1;
-      return;
-    }
-    tc_fence_after();
-    const uint32_t kb = ring_u32 + (k % NS) * Cfg::kStageBytes;
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks)
-      umma(t_s0 + 16 * (k & 1), umma_desc(kb + (ks / 4) * kBoxBytes + (ks % 4) * 32, 16, 1024),
-           umma_desc(qt_u32 + (ks / 4) * 2048 + (ks % 4) * 32, 16, 1024), id_k, ks > 0);
-    umma_commit(bar_s);
-    ++qk_issued;
-  };
-  if (tid == 0 && n_stages > 0) issue_qk(0);
-
-  float m_ref[GP], l_part[GP];
-#pragma unroll
-  for (int h = 0; h < GP; ++h) {
-    m_ref[h] = -INFINITY;
-    l_part[h] = 0.f;
-  }
-  for (int k = 0; k < n_stages; ++k) {
-    const int s = k % NS;
-    const int tok = ts + k * kStageTok + tid;  // this thread's token
-    const bool valid = tok < te;
-    // ---- S row of this token (QK^T of stage k is complete)
-    if (s_abort || !mbar_wait(bar_s, k & 1)) {
-      ok = false;
-      s_abort = 1;
-    }
-    float x[GP];
-#pragma unroll
-    for (int h = 0; h < GP; ++h) x[h] = -INFINITY;
-    if (!s_abort) {
-      tc_fence_after();
-      tmem_ld16(t_s0 + 16 * (k & 1) + lane_off, x);
-    }
-#pragma unroll
-    for (int h = 0; h < GPF; ++h) x[h] = (valid && h < group) ? x[h] * a.scale_log2 : -INFINITY;
-    // ---- lazy reference max: refresh (and rescale O, l) only when some
-    // score exceeds its head's reference by more than 2^8
-    bool over = false;
-#pragma unroll
-    for (int h = 0; h < GPF; ++h) over |= x[h] > m_ref[h] + kLazyRescale;
-    if (__syncthreads_or(over)) {
-      float mx[GPF];
-#pragma unroll
-      for (int h = 0; h < GPF; ++h) {
-        mx[h] = x[h];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], o));
-      }
-      if (lane == 0)
-#pragma unroll
-        for (int h = 0; h < GPF; ++h) s_red[warp * GP + h] = mx[h];
-      // PV(k - 1) must be complete before O is rescaled in tensor memory
-      if (k > 0 && !s_abort && !mbar_wait(bar_o + 8 * ((k - 1) & 1), ((k - 1) / 2) & 1)) {
-        ok = false;
-        s_abort = 1;
-      }
-      __syncthreads();
-      float alpha[GP];
-#pragma unroll
-      for (int h = GPF; h < GP; ++h) alpha[h] = 1.f;  // padding heads: O stays zero
-#pragma unroll
-      for (int h = 0; h < GPF; ++h) {
-        float mn = m_ref[h];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) mn = fmaxf(mn, s_red[w * GP + h]);
-        alpha[h] = (m_ref[h] == -INFINITY) ? 0.f : exp2f(m_ref[h] - mn);
-        m_ref[h] = mn;
-        l_part[h] *= alpha[h];
-      }
-      if (k > 0 && !s_abort) {  // thread t owns O row t (head dim t)
-        tc_fence_after();
-        float ov[GP];
-        tmem_ld16(t_o + lane_off, ov);
-#pragma unroll
-        for (int h = 0; h < GP; ++h) ov[h] *= alpha[h];
-        tmem_st16(t_o + lane_off, ov);
-      }
-      __syncthreads();  // s_red reused at the next refresh
-    }
-    float p[GPF];
-#pragma unroll
-    for (int h = 0; h < GPF; ++h) {
-      p[h] = (x[h] == -INFINITY) ? 0.f : exp2f(x[h] - m_ref[h]);
-      l_part[h] += p[h];
-    }
-    // ---- P^T (hi, lo) of this token into P[k & 1]: PV(k - 2) must be done with it
-    if (k >= 2 && !s_abort && !mbar_wait(bar_o + 8 * (k & 1), ((k - 2) / 2) & 1)) {
-      ok = false;
-      s_abort = 1;
-    }
-    {
-      uint8_t *ph = pt + (k & 1) * 2 * Cfg::kPBytes;
-      uint8_t *pl = ph + Cfg::kPBytes;
-      const int box = tid >> 6, c = tid & 63;  // token column inside the 64-token box
-#pragma unroll
-      for (int h = 0; h < GPF; h += 2) {
-        uint32_t hi, lo;
-        pack2_split<T>(p[h], p[h + 1], hi, lo);
-        const uint32_t o0 = box * 2048 + h * 128 + ((((c >> 3) ^ (h & 7)) << 4) | ((c & 7) << 1));
-        const uint32_t o1 = box * 2048 + (h + 1) * 128 + ((((c >> 3) ^ ((h + 1) & 7)) << 4) | ((c & 7) << 1));
-        *reinterpret_cast<uint16_t *>(ph + o0) = (uint16_t)(hi & 0xffffu);
-        *reinterpret_cast<uint16_t *>(ph + o1) = (uint16_t)(hi >> 16);
-        *reinterpret_cast<uint16_t *>(pl + o0) = (uint16_t)(lo & 0xffffu);
-        *reinterpret_cast<uint16_t *>(pl + o1) = (uint16_t)(lo >> 16);
-      }
-    }
-    // V rows past the split end hold stale data: zero them so 0 * V stays 0
-    if (!valid) {
-      uint8_t *vrow = ring + s * Cfg::kStageBytes + Cfg::kBoxes * kBoxBytes + tid * 128;
-#pragma unroll
-      for (int b = 0; b < Cfg::kBoxes; ++b)
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4 *>(vrow + b * kBoxBytes + c * 16) = make_uint4(0, 0, 0, 0);
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && !s_abort) {
-      tc_fence_after();
-      // ---- O^T += V^T (P_hi + P_lo)^T over the stage's 128 tokens
-      const uint32_t vb = ring_u32 + s * Cfg::kStageBytes + Cfg::kBoxes * kBoxBytes;
-      const uint32_t ph = pt_u32 + (k & 1) * 2 * Cfg::kPBytes, pl = ph + Cfg::kPBytes;
-#pragma unroll
-      for (int ks = 0; ks < kStageTok / 16; ++ks) {
-        const uint64_t da = umma_desc(vb + ks * 2048, kBoxBytes, 1024);
-        const uint32_t bo = (ks / 4) * 2048 + (ks % 4) * 32;
-        umma(t_o, da, umma_desc(ph + bo, 16, 1024), id_v, k > 0 || ks > 0);
-        umma(t_o, da, umma_desc(pl + bo, 16, 1024), id_v, true);
-      }
-      umma_commit(bar_o + 8 * (k & 1));
-      ++pv_issued;
-      // refill the slot of stage k - 1 once its PV(k - 1) has read it
-      if (k >= 1 && k - 1 + NS < n_stages) {
-        if (mbar_wait(bar_o + 8 * ((k - 1) & 1), ((k - 1) / 2) & 1)) {
-          issue(k - 1 + NS);
-          ++issued;
-        } else {
-          ok = false;
-          s_abort = 1;
-        }
-      }
-      if (k + 1 < n_stages && !s_abort) issue_qk(k + 1);
-    }
-  }
-  // ---- drain: the last PV, and on a timeout every copy still in flight
-  if (n_stages > 0 && !s_abort &&
-      !mbar_wait(bar_o + 8 * ((n_stages - 1) & 1), ((n_stages - 1) / 2) & 1)) {
-    ok = false;
-    s_abort = 1;
-  }
-  __syncthreads();
-  if (!ok && lane == 0) flag_error(a.err, DSB_FLAG_TIMEOUT);
-  if (s_abort) {
-    if (tid == 0) {  // every copy and product already issued must land first
-      for (int s = 0; s < NS && s < issued; ++s) {
-        const int last = issued - 1 - ((issued - 1 - s) % NS);
-        mbar_wait(bar_full + 8 * s, (last / NS) & 1);
-      }
-      for (int j = 0; j < 2 && j < pv_issued; ++j) {
-        const int last = pv_issued - 1 - ((pv_issued - 1 - j) % 2);
-        mbar_wait(bar_o + 8 * j, (last / 2) & 1);
-      }
-      if (qk_issued > 0) mbar_wait(bar_s, (qk_issued - 1) & 1);
-    }
-    __syncthreads();
-  }
-  // ---- O row t (head dim t) from tensor memory, l reduced over tokens
-  float ov[GP];
-  if (n_stages > 0 && !s_abort) {
-    tc_fence_after();
-    tmem_ld16(t_o + lane_off, ov);
-  } else {
-#pragma unroll
-    for (int h = 0; h < GP; ++h) ov[h] = 0.f;
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 64;" ::"r"(tmem) : "memory");
-#pragma unroll
-  for (int h = 0; h < GPF; ++h) {
-    float l = l_part[h];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    l_part[h] = l;
-  }
-  // stage O^T as e_o[head][dim] (padded rows) and the per-warp l in the idle ring
-  constexpr int DP = D + 4;
-  float *e_o = reinterpret_cast<float *>(ring);
-  float *e_l = e_o + GP * DP;  // [4 warps][GP]
-#pragma unroll
-  for (int h = 0; h < GPF; ++h) e_o[h * DP + tid] = ov[h];
-  if (lane == 0)
-#pragma unroll
-    for (int h = 0; h < GPF; ++h) e_l[warp * GP + h] = l_part[h];
-  __syncthreads();
-  auto fold = [&](int it, int &h, int &d, float4 &acc, float &M, float &L) {
-    h = it / (D / 4);
-    d = (it % (D / 4)) * 4;
-    M = m_ref[0];
-#pragma unroll
-    for (int hh = 1; hh < GPF; ++hh)
-      if (hh == h) M = m_ref[hh];
-    L = e_l[h] + e_l[GP + h] + e_l[2 * GP + h] + e_l[3 * GP + h];
-    acc = *reinterpret_cast<const float4 *>(e_o + h * DP + d);
-  };
-  finish_split<T, D, GPF, CL>(a, fold, out, row, kvh, split, active, group,
-                              reinterpret_cast<float *>(smem + Cfg::kXOffset),
-                              e_l + 4 * GP, &s_last);
-}
-
 bool legacy_attention_requested() {
   const char *v = getenv("DSB_ATTENTION_LEGACY");
   return v != nullptr && v[0] == '1';
@@ -1424,44 +1036,6 @@ int launch_tma(const AttnArgs &a, int splits, cudaStream_t st) {
   return check_launch("draft_attention_tma_kernel");
 }
 
-// DSB_ATTENTION_UMMA=1 selects the tcgen05 kernel (head_dim 128).  It is
-// parity-tested but not the default: with one 128-thread CTA per SM its
-// per-stage chain (S read, softmax, P store, single-thread MMA issue) runs
-// ~2 us per 128-token stage, against ~1 us for the mma.sync kernel's loop,
-// which already streams at the per-SM share of HBM.
-bool umma_requested() {
-  const char *v = getenv("DSB_ATTENTION_UMMA");
-  return v != nullptr && v[0] == '1';
-}
-
-template <typename T, int GPF>
-int launch_umma(const AttnArgs &a, int splits, cudaStream_t st) {
-  constexpr int D = 128, NS = 3;
-  using Cfg = UmmaCfg<NS>;
-  CUtensorMap tmk, tmv;
-  const int64_t rows_total = (int64_t)a.num_slots * a.Hk * a.W;
-  const int dt = std::is_same<T, __half>::value ? DSB_F16 : DSB_BF16;
-  if (!encode_kv_map(&tmk, a.wk, rows_total, D, dt, Cfg::kStageTok) ||
-      !encode_kv_map(&tmv, a.wv, rows_total, D, dt, Cfg::kStageTok))
-    return -1;
-  constexpr size_t kMaxSmem = 227 * 1024;
-  const size_t smem = 1024 + Cfg::kXOffset;
-  const size_t smem_cl = smem + sizeof(float) * (size_t)splits * GPF * (D + 2);
-  const dim3 grid(splits, a.Hk, a.out_rows);
-  if (splits >= 2 && splits <= 8 && smem_cl <= kMaxSmem && !legacy_merge_requested()) {
-    auto kern = draft_attention_umma_kernel<T, NS, GPF, true>;
-    if (int e = ensure_smem((const void *)kern, smem_cl); e != DSB_OK) return e;
-    if (max_active_clusters((const void *)kern, splits, kUmmaThreads, smem_cl) > 0) {
-      launch_kernel_cluster(kern, grid, dim3(kUmmaThreads), smem_cl, st, splits, tmk, tmv, a);
-      return check_launch("draft_attention_umma_kernel (cluster merge)");
-    }
-  }
-  auto kern = draft_attention_umma_kernel<T, NS, GPF, false>;
-  if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
-  launch_kernel(kern, grid, dim3(kUmmaThreads), smem, st, tmk, tmv, a);
-  return check_launch("draft_attention_umma_kernel");
-}
-
 // Geometry of the TMA kernel: 8 consumer warps and 64-token stages up to
 // head_dim 128 (a 192 KB ring at 128, one CTA per SM), 4 warps and 32-token
 // stages at 256 (128 KB).
@@ -1473,12 +1047,6 @@ template <int D> struct TmaGeom {
 template <typename T, int D, int NT>
 int launch_attention_typed(const AttnArgs &a, int splits, cudaStream_t st) {
   if (!legacy_attention_requested()) {
-    if constexpr (D == 128) {
-      if (umma_requested()) {
-        const int e = launch_umma<T, NT * 8>(a, splits, st);
-        if (e != -1) return e;
-      }
-    }
     const int e = launch_tma<T, D, NT, TmaGeom<D>::NS, TmaGeom<D>::W>(a, splits, st);
     if (e != -1) return e;
   }
