@@ -733,11 +733,14 @@ def run_ours(args):
 
 
 def run_e2e(res, args):
-    """Same workload through DiffSpecDraftCache with host buffers: per cycle
-    the verify pass's query/LSE/accepted counts and per draft step q/k/v go
-    H2D from pinned memory, and each step's attention output goes D2H."""
+    """Same workload through the runtime's public API with host buffers: a
+    DiffSpecDraftCache and its DraftPeriodGraph (one retrieval period
+    captured as a CUDA graph).  Every period copies the verify pass's query,
+    LSE, accepted counts and lengths of each cycle and every draft step's
+    q/k/v from pinned host memory to the device, and every step's attention
+    output back to pinned host memory; the copies are nodes of the graph on
+    side streams, so they overlap the kernels."""
     torch, dsb, w, device = res["torch"], res["dsb"], res["w"], res["device"]
-    from types import SimpleNamespace
 
     rows = res["rows"]
     hg = res["hg"]
@@ -749,46 +752,27 @@ def run_e2e(res, args):
         process_group=res["group"], recent_window=RECENT_WINDOW)
     cache.raw_key, cache.raw_value = w.raw_key, w.raw_value  # share the canonical cache
     cache.max_model_len = w.raw_key.shape[1]
-    # Each cycle's verify-pass inputs (query, LSE, accepted counts) and each
-    # draft step's q/k/v travel as one pinned host buffer and one copy; the
-    # device tensors are views of the copied bytes.
-    def packed(tensors):
-        flat = [t.reshape(-1).view(torch.uint8) for t in tensors]
-        host = torch.cat([f.cpu() for f in flat]).pin_memory()
-        dev = torch.empty_like(host, device=device)
-        views, o = [], 0
-        for t, f in zip(tensors, flat):
-            views.append(dev[o:o + f.numel()].view(t.dtype).view(t.shape))
-            o += f.numel()
-        return host, dev, views
-
-    h_cycle, d_cycle, (d_query, d_lse, d_counts) = packed([w.query, w.lse, w.counts])
-    h_step, d_step, (d_dq, d_dk, d_dv) = packed([w.dq, w.dk, w.dv])
-    h_out = [torch.empty_like(w.out, device="cpu").pin_memory() for _ in range(DEPTH)]
-    out = torch.empty_like(w.out)
     ids = [f"req{i}" for i in range(rows)]
-    meta = SimpleNamespace(actual_seq_lengths_q=[5 * (i + 1) for i in range(rows)],
-                           seq_lens_list=[CTX] * rows, block_tables=w.block_table, num_prefills=0)
-    committed = [[CTX - REJECTED + ACCEPT_PER_CYCLE * c] * rows for c in range(INTERVAL)]
-    h2d = h_cycle.numel() * INTERVAL + h_step.numel() * INTERVAL * DEPTH
-    d2h = out.numel() * 2 * INTERVAL * DEPTH
-
-    def period():
-        for c in range(INTERVAL):
-            d_cycle.copy_(h_cycle, non_blocking=True)
-            cache.begin_target_forward(ids)
-            cache.capture_target_attention(d_query, d_lse, w.key_cache, meta, D ** -0.5)
-            cache.accept_target_queries(d_counts, is_prefill=False)
-            cache.begin_cycle(ids)
-            cache.rebuild(committed[c])
-            for j in range(DEPTH):
-                d_step.copy_(h_step, non_blocking=True)
-                cache.forward_attention(d_dq, d_dk, d_dv, D ** -0.5, out)
-                h_out[j].copy_(out, non_blocking=True)
-            cache.end_cycle()
+    cache.set_active_requests(ids)
+    g = dsb.runtime.DraftPeriodGraph(cache, ids, key_cache=w.key_cache,
+                                     block_tables=w.block_table, query_rows_per_request=5,
+                                     num_query_heads=w.hq, max_seq_len=CTX, scale=D ** -0.5)
+    for c in range(INTERVAL):
+        v = g.inputs["verify"][c]
+        v["query"].copy_(w.query)
+        v["lse"].copy_(w.lse)
+        v["counts"].copy_(w.counts)
+        v["query_ends"].copy_(w.query_ends)
+        v["seq_lens"].copy_(w.target_seq)
+        v["committed"].copy_(w.committed[c])
+        for j in range(DEPTH):
+            st = g.inputs["step"][c][j]
+            st["q"].copy_(w.dq)
+            st["k"].copy_(w.dk)
+            st["v"].copy_(w.dv)
 
     for _ in range(max(args.warmup, 1)):
-        period()
+        g.replay()
     torch.cuda.synchronize(device)
     dist = res["dist"]
     if dist is not None:
@@ -797,7 +781,7 @@ def run_e2e(res, args):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(steps):
-        period()
+        g.replay()
     end.record()
     torch.cuda.synchronize(device)
     ms = start.elapsed_time(end) / steps
@@ -806,8 +790,13 @@ def run_e2e(res, args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     assert dsb._lib.read_and_clear_error_flag(device) == 0
+    h2d, d2h = g.h2d_bytes, g.d2h_bytes
+    del g  # holds NCCL work when N > 1: released before the process group
+    torch.cuda.synchronize(device)
     return dict(value=STEPS_PER_PERIOD * res["world"] / (ms / 1e3), unit=UNIT,
-                ms_per_step=round(ms, 4), h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h))
+                ms_per_step=round(ms, 4), h2d_bytes_per_step=int(h2d),
+                d2h_bytes_per_step=int(d2h),
+                api="DiffSpecDraftCache + DraftPeriodGraph.replay (pinned host inputs and outputs)")
 
 
 def period_bytes(res):
@@ -1402,7 +1391,8 @@ def run_target_attention(args):
 
     def launch():
         dsb.kernels.paged_decode_attention_lse(q, kc, vc, table, lens, scale=D ** -0.5,
-                                               max_seq_len=ctx, out=out, lse=lse)
+                                               max_seq_len=ctx, out=out, lse=lse,
+                                               tokens_per_split=args.tokens_per_split)
 
     for _ in range(max(3, args.warmup)):
         launch()
@@ -1422,6 +1412,7 @@ def run_target_attention(args):
                           head_dim=D, dtype="bf16", bytes_per_launch=nbytes,
                           us_per_launch=round(us, 2), achieved_gbs=round(gbs, 1),
                           frac_of_hbm_peak=round(gbs / peak, 3), peak_kind=peak_kind,
+                          tokens_per_split=args.tokens_per_split,
                           l2="K/V 1.34 GB per launch, larger than L2")))
 
 
@@ -1563,6 +1554,8 @@ def main():
                    help="time the target paged decode attention with the LSE export")
     p.add_argument("--config4", action="store_true",
                    help="config 4: head-sharded retrieval at fixed work over --gpus N ranks")
+    p.add_argument("--tokens-per-split", type=int, default=0,
+                   help="--target-attention: split length (0: the library default)")
     p.add_argument("--reference-triton", action="store_true",
                    help="time the reference's Triton kernels (compiled for this GPU) against ours")
     args = p.parse_args()

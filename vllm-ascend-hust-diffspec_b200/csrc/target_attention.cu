@@ -38,6 +38,7 @@ struct TaArgs {
   const int32_t *bt, *seq, *trows;
   int64_t bt_stride, bt_cols, bt_rows, nblocks;
   int bs, hq, hk, rows, splits, tps;
+  int page_tiles;  // 1: page size and split length multiples of 16 (a tile lies in one page)
   float scale_log2;
   float *part;  // [rows, hq, splits, D + 2]: acc[D], max, sum
   void *out;
@@ -45,37 +46,58 @@ struct TaArgs {
   int32_t *err;
 };
 
-__device__ __forceinline__ uint32_t ta_word(const uint4 &v, int i) {
-  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
-}
-
-constexpr int kTaTile = 16;                // tokens per warp tile
-constexpr int kTaVStride = kTaD * 2 + 16;  // bytes per staged V row (padded: ldmatrix without conflicts)
-constexpr int kTaVBytes = kTaTile * kTaVStride;
+constexpr int kTaTile = 16;                    // tokens per warp tile
+constexpr int kTaStages = 3;                   // tiles in a warp's ring (2 in flight while one computes)
+constexpr int kTaRowBytes = kTaD * 2 + 16;     // staged K/V row, padded: ldmatrix without conflicts
+constexpr int kTaStageBytes = 2 * kTaTile * kTaRowBytes;           // K tile + V tile
+constexpr int kTaRingBytes = kTaWarps * kTaStages * kTaStageBytes;  // 104,448 B: 2 CTAs per SM
 
 template <int G> struct TaSmem {
   static constexpr int kMerge = kTaWarps * G * kTaD * 4 + kTaWarps * 16 * 2 * 4;
-  static constexpr int kStage = kTaWarps * kTaVBytes;
-  static constexpr int kBytes = kMerge > kStage ? kMerge : kStage;
+  static constexpr int kBytes = kMerge > kTaRingBytes ? kMerge : kTaRingBytes;
 };
 
+// 16 bytes of a staged row: a cp.async (L2 only) from `src`, or zeros stored
+// directly when the row has no source.  A zero store never meets a copy in
+// flight to the same bytes: a stage is refilled only after the wait on its
+// previous fill.
+__device__ __forceinline__ void ta_cp16_or_zero(uint32_t dst, const void *src, bool valid) {
+  if (valid)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+  else
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0u) : "memory");
+}
+
+__device__ __forceinline__ void ta_ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ta_ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
 // Split-KV partial of one (split, kv head, row) on the tensor cores
-// (mma.sync m16n8k16, fp32 accumulate).  Per 16-token tile a warp computes
-//   S[16 heads x 16 tokens] = Q . K^T   (A = the group's query heads, rows
-//                                         >= G zero; B = the K rows, loaded
-//                                         straight into fragments with the
-//                                         head dim permuted the same way in
-//                                         A and B)
+// (mma.sync m16n8k16, fp32 accumulate).  The split's 16-token tiles go
+// round-robin to the four warps; each warp streams its tiles through a
+// private 3-stage cp.async ring (K and V rows of a tile staged in padded
+// shared memory, two tiles in flight while the third is computed) and per
+// tile computes
+//   S[16 heads x 16 tokens] = Q . K^T   (A = the group's query heads from
+//                                         registers, rows >= G zero; B = the
+//                                         K rows by ldmatrix)
 // then the base-2 online softmax on S's accumulators, and
 //   O[16 heads x 128] += P . V          (A = P from S's accumulators, split
-//                                         into hi + lo 16-bit terms; B = V
-//                                         rows staged in padded shared memory
-//                                         and read with ldmatrix.trans).
+//                                         into hi + lo 16-bit terms; B = the
+//                                         V rows by ldmatrix.trans).
+// Rows past the split (or past seq_lens) are zero-filled and masked; a page
+// entry outside the cache is flagged and its tokens read as zeros.
 template <typename T, int G>
-__global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const TaArgs a) {
+__global__ void __launch_bounds__(kTaWarps * 32, 2) paged_decode_split_kernel(const TaArgs a) {
   static_assert(G <= 16, "at most 16 query heads per kv head");
-  // V staging during the loop, the warps' states for the merge after it
-  __shared__ __align__(16) uint8_t s_raw[TaSmem<G>::kBytes];
+  extern __shared__ __align__(128) uint8_t s_raw[];  // rings, then the warps' states
   pdl_begin();
   const int split = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,16 +120,18 @@ __global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const
   }
   const int s0 = split * a.tps, s1 = min(L, s0 + a.tps);
 
-  // Q A-fragments: rows g and g + 8 are query heads h * G + g (+ 8) when < G.
-  uint4 qlo[4], qhi[4];
+  // Q A-fragments of the 8 k-steps: rows g and g + 8 are query heads
+  // h * G + g (+ 8) when < G; columns 16 s + 2 t (+ 8).
+  uint32_t qa[8][4];
   {
     const T *qb = static_cast<const T *>(a.q) + ((int64_t)r * a.hq + h * G) * kTaD;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      qlo[j] = g < G ? *reinterpret_cast<const uint4 *>(qb + g * kTaD + 8 * (4 * j + t))
-                     : make_uint4(0, 0, 0, 0);
-      qhi[j] = g + 8 < G ? *reinterpret_cast<const uint4 *>(qb + (g + 8) * kTaD + 8 * (4 * j + t))
-                         : make_uint4(0, 0, 0, 0);
+    for (int s = 0; s < 8; ++s) {
+      const int c = 16 * s + 2 * t;
+      qa[s][0] = g < G ? *reinterpret_cast<const uint32_t *>(qb + g * kTaD + c) : 0u;
+      qa[s][1] = g + 8 < G ? *reinterpret_cast<const uint32_t *>(qb + (g + 8) * kTaD + c) : 0u;
+      qa[s][2] = g < G ? *reinterpret_cast<const uint32_t *>(qb + g * kTaD + c + 8) : 0u;
+      qa[s][3] = g + 8 < G ? *reinterpret_cast<const uint32_t *>(qb + (g + 8) * kTaD + c + 8) : 0u;
     }
   }
   float o[16][4];
@@ -119,63 +143,86 @@ __global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const
 
   const T *kc = static_cast<const T *>(a.k), *vc = static_cast<const T *>(a.v);
   const int32_t *row_bt = a.bt + (int64_t)trow * a.bt_stride;
-  uint8_t *vs = s_raw + warp * kTaVBytes;
+  const uint32_t ring = smem_u32(s_raw) + warp * kTaStages * kTaStageBytes;
+  const int64_t tok_stride = (int64_t)a.hk * kTaD;  // elements between consecutive tokens of a page
   bool bad = false;
-  // element offset of token `tok`'s row for this kv head, or -1
-  auto row_of = [&](int tok) -> int64_t {
-    const int blk = row_bt[tok / a.bs];
-    if (blk < 0 || blk >= a.nblocks) return -1;
-    return (((int64_t)blk * a.bs + tok % a.bs) * a.hk + h) * kTaD;
+
+  // Stage tile k of this split: instruction i moves K and V rows 2 i and
+  // 2 i + 1 (lanes 0-15 and 16-31, 16 bytes each).  When every tile lies in
+  // one page (page size and split length multiples of 16), one table entry
+  // serves the tile; otherwise each row looks up its own.
+  auto issue = [&](int k, int stage) {
+    const int T0 = s0 + kTaTile * k;
+    const uint32_t kd = ring + stage * kTaStageBytes, vd = kd + kTaTile * kTaRowBytes;
+    const int col = lane & 15;
+    int64_t tile_base = -1;
+    if (a.page_tiles) {
+      const int blk = row_bt[T0 / a.bs];
+      if (blk >= 0 && blk < a.nblocks)
+        tile_base = (((int64_t)blk * a.bs + T0 % a.bs) * a.hk + h) * kTaD;
+      else
+        bad = true;
+    }
+#pragma unroll
+    for (int i = 0; i < kTaTile / 2; ++i) {
+      const int row = 2 * i + (lane >> 4), tok = T0 + row;
+      int64_t off = -1;
+      if (tok < s1) {
+        if (a.page_tiles) {
+          if (tile_base >= 0) off = tile_base + row * tok_stride;
+        } else {
+          const int blk = row_bt[tok / a.bs];
+          if (blk >= 0 && blk < a.nblocks)
+            off = (((int64_t)blk * a.bs + tok % a.bs) * a.hk + h) * kTaD;
+          else
+            bad = true;
+        }
+      }
+      const int64_t src = off >= 0 ? off + 8 * col : 0;
+      ta_cp16_or_zero(kd + row * kTaRowBytes + col * 16, kc + src, off >= 0);
+      ta_cp16_or_zero(vd + row * kTaRowBytes + col * 16, vc + src, off >= 0);
+    }
   };
 
-  for (int T0 = s0 + warp * kTaTile; T0 < s1; T0 += kTaWarps * kTaTile) {
-    // ---- loads: K rows of tokens T0 + g and T0 + 8 + g; V chunks to stage
-    uint4 k0[4], k1[4], vv[8];
+  const int ntiles = s1 > s0 ? (s1 - s0 + kTaTile - 1) / kTaTile : 0;
+  const int mine = ntiles > warp ? (ntiles - warp + kTaWarps - 1) / kTaWarps : 0;
+#pragma unroll
+  for (int i = 0; i < kTaStages - 1; ++i) {
+    if (i < mine) issue(warp + kTaWarps * i, i);
+    cp_async_commit();
+  }
+  for (int i = 0; i < mine; ++i) {
     {
-      const int ta = T0 + g, tb = T0 + 8 + g;
-      const int64_t oa = ta < s1 ? row_of(ta) : -2, ob = tb < s1 ? row_of(tb) : -2;
-      bad |= (oa == -1) || (ob == -1);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        k0[j] = oa >= 0 ? *reinterpret_cast<const uint4 *>(kc + oa + 8 * (4 * j + t))
-                        : make_uint4(0, 0, 0, 0);
-        k1[j] = ob >= 0 ? *reinterpret_cast<const uint4 *>(kc + ob + 8 * (4 * j + t))
-                        : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {  // chunk c = lane + 32 i: row c / 16, 16-byte column c % 16
-        const int c = lane + 32 * i, row = c >> 4, col = c & 15;
-        const int tok = T0 + row;
-        const int64_t ov = tok < s1 ? row_of(tok) : -2;
-        vv[i] = ov >= 0 ? *reinterpret_cast<const uint4 *>(vc + ov + 8 * col) : make_uint4(0, 0, 0, 0);
-      }
+      const int nxt = i + kTaStages - 1;  // into the stage computed last iteration
+      if (nxt < mine) issue(warp + kTaWarps * nxt, nxt % kTaStages);
+      cp_async_commit();
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int c = lane + 32 * i;
-      *reinterpret_cast<uint4 *>(vs + (c >> 4) * kTaVStride + (c & 15) * 16) = vv[i];
-    }
+    cp_async_wait<kTaStages - 1>();
+    __syncwarp();
+    const int T0 = s0 + kTaTile * (warp + kTaWarps * i);
+    const uint32_t kb = ring + (i % kTaStages) * kTaStageBytes, vb = kb + kTaTile * kTaRowBytes;
 
-    // ---- S = Q K^T: two n-tiles of 8 tokens, 8 k-steps of 16 head-dim values
+    // ---- S = Q K^T: 8 k-steps, both 8-token n-tiles from one ldmatrix.x4
+    float ce[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    float co[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const uint32_t k_lane = kb + (((lane >> 4) & 1) * 8 + (lane & 7)) * kTaRowBytes +
+                            ((lane >> 3) & 1) * 16;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      uint32_t kf[4];
+      ta_ldsm_x4(kf, k_lane + s * 32);
+      const uint32_t b0[2] = {kf[0], kf[1]}, b1[2] = {kf[2], kf[3]};
+      Mma<T>::run((s & 1) ? co[0] : ce[0], qa[s], b0);
+      Mma<T>::run((s & 1) ? co[1] : ce[1], qa[s], b1);
+    }
     float sc[2][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const int w0 = 2 * s, w1 = 2 * s + 1;
-        const uint32_t af[4] = {ta_word(qlo[w0 / 4], w0 % 4), ta_word(qhi[w0 / 4], w0 % 4),
-                                ta_word(qlo[w1 / 4], w1 % 4), ta_word(qhi[w1 / 4], w1 % 4)};
-        const uint4 *kk = nt == 0 ? k0 : k1;
-        const uint32_t bf[2] = {ta_word(kk[w0 / 4], w0 % 4), ta_word(kk[w1 / 4], w1 % 4)};
-        Mma<T>::run((s & 1) ? co : ce, af, bf);
-      }
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int tok = T0 + 8 * nt + 2 * t + (j & 1);
-        sc[nt][j] = tok < s1 ? (ce[j] + co[j]) * a.scale_log2 : -INFINITY;
+        sc[nt][j] = tok < s1 ? (ce[nt][j] + co[nt][j]) * a.scale_log2 : -INFINITY;
       }
-    }
     // ---- online softmax (rows g: j = 0, 1; rows g + 8: j = 2, 3)
     float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
     float mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
@@ -211,17 +258,21 @@ __global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const
     pack2_split<T>(p[0][2], p[0][3], ph[1], pl[1]);
     pack2_split<T>(p[1][0], p[1][1], ph[2], pl[2]);
     pack2_split<T>(p[1][2], p[1][3], ph[3], pl[3]);
-    __syncwarp();
-    // ---- O += P V over 16 n-tiles of 8 head-dim values
+    // ---- O += P V: two 8-dim n-tiles per ldmatrix.x4.trans
+    const uint32_t v_lane = vb + (lane & 15) * kTaRowBytes + (lane >> 4) * 16;
 #pragma unroll
-    for (int dn = 0; dn < 16; ++dn) {
-      uint32_t bv[2];
-      ldsm_x2_trans(bv, vs + (lane & 15) * kTaVStride + dn * 16);
-      Mma<T>::run(o[dn], ph, bv);
-      Mma<T>::run(o[dn], pl, bv);
+    for (int dn = 0; dn < 16; dn += 2) {
+      uint32_t vf[4];
+      ta_ldsm_x4_trans(vf, v_lane + dn * 16);
+      const uint32_t b0[2] = {vf[0], vf[1]}, b1[2] = {vf[2], vf[3]};
+      Mma<T>::run(o[dn], ph, b0);
+      Mma<T>::run(o[dn], pl, b0);
+      Mma<T>::run(o[dn + 1], ph, b1);
+      Mma<T>::run(o[dn + 1], pl, b1);
     }
-    __syncwarp();  // the next tile overwrites the staged V
+    __syncwarp();  // the stage is refilled next iteration
   }
+  cp_async_wait<0>();
   if (bad) flag_error(a.err, DSB_FLAG_BLOCK);
 
   // Warp state -> shared memory (rows < G), then merge the four warps.
@@ -230,7 +281,7 @@ __global__ void __launch_bounds__(kTaWarps * 32) paged_decode_split_kernel(const
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
   }
-  __syncthreads();  // V staging no longer needed
+  __syncthreads();  // every warp is done with its ring
   float *s_acc = reinterpret_cast<float *>(s_raw);  // [warps][G][D]
   float *s_ml = s_acc + kTaWarps * G * kTaD;        // [warps][16][2]: max, sum
 #pragma unroll
@@ -294,21 +345,26 @@ __global__ void __launch_bounds__(kTaD) paged_decode_merge_kernel(const TaArgs a
   if (d == 0) a.lse[rh] = sum > 0.f ? (M + log2f(sum)) * kTaLn2 : -INFINITY;
 }
 
-template <typename T, int G> void launch_group(const TaArgs &a, cudaStream_t st) {
-  launch_kernel(paged_decode_split_kernel<T, G>, dim3(a.splits, a.hk, a.rows),
-                dim3(kTaWarps * 32), 0, st, a);
+template <typename T, int G> int launch_group(const TaArgs &a, cudaStream_t st) {
+  auto kern = paged_decode_split_kernel<T, G>;
+  constexpr size_t smem = TaSmem<G>::kBytes;
+  if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
+  launch_kernel(kern, dim3(a.splits, a.hk, a.rows), dim3(kTaWarps * 32), smem, st, a);
+  return DSB_OK;
 }
 
 template <typename T> int launch_typed(const TaArgs &a, int group, cudaStream_t st) {
+  int e = DSB_OK;
   switch (group) {
-    case 1: launch_group<T, 1>(a, st); break;
-    case 2: launch_group<T, 2>(a, st); break;
-    case 4: launch_group<T, 4>(a, st); break;
-    case 8: launch_group<T, 8>(a, st); break;
-    case 16: launch_group<T, 16>(a, st); break;
+    case 1: e = launch_group<T, 1>(a, st); break;
+    case 2: e = launch_group<T, 2>(a, st); break;
+    case 4: e = launch_group<T, 4>(a, st); break;
+    case 8: e = launch_group<T, 8>(a, st); break;
+    case 16: e = launch_group<T, 16>(a, st); break;
     default: return fail(DSB_ERR_UNSUPPORTED, "query heads per kv head must be 1, 2, 4, 8 or 16");
   }
-  if (int e = check_launch("paged_decode_split_kernel")) return e;
+  if (e != DSB_OK) return e;
+  if (int e2 = check_launch("paged_decode_split_kernel")) return e2;
   launch_kernel(paged_decode_merge_kernel<T>, dim3((unsigned)(a.rows * a.hq)), dim3(kTaD), 0, st,
                 a);
   return check_launch("paged_decode_merge_kernel");
@@ -379,6 +435,7 @@ extern "C" int dsb_paged_decode_attention_lse(
   a.rows = query_rows;
   a.splits = (int)splits;
   a.tps = tokens_per_split;
+  a.page_tiles = (block_size % kTaTile == 0 && tokens_per_split % kTaTile == 0) ? 1 : 0;
   a.scale_log2 = scale * kTaLog2e;
   a.part = scratch;
   a.out = out;

@@ -45,6 +45,7 @@ from .selection import (
 )
 
 __all__ = [
+    "DraftPeriodGraph",
     "DiffSpecSettings",
     "DiffSpecSelection",
     "DiffSpecRuntimeMetrics",
@@ -455,11 +456,35 @@ class DiffSpecDraftCache:
         scale: float,
     ) -> None:
         """Device retrieval for the active batch: pick -> score -> exchange -> select."""
+        if not self._active_slots:
+            return
+        ends_d, seqs_d = self._staging.upload(query_ends, target_seq_lens)
+        self.retrieve_device(query, softmax_lse, key_cache, block_tables, ends_d, seqs_d,
+                             max(target_seq_lens), counts, scale)
+
+    def retrieve_device(
+        self,
+        query: torch.Tensor,
+        softmax_lse: torch.Tensor,
+        key_cache: torch.Tensor,
+        block_tables: torch.Tensor,
+        query_ends: torch.Tensor,
+        target_seq_lens: torch.Tensor,
+        max_seq_len: int,
+        counts: torch.Tensor,
+        scale: float,
+    ) -> None:
+        """:meth:`retrieve` with the query ends and target lengths already on
+        the device (int32 ``[rows]``) and ``max_seq_len`` bounding the
+        lengths: no host data is read, so the call can be captured in a CUDA
+        graph whose replays see new values in those tensors."""
         started = time.perf_counter()
         rows = len(self._active_slots)
         if rows == 0:
             return
-        ends_d, seqs_d = self._staging.upload(query_ends, target_seq_lens)
+        ends_d, seqs_d = query_ends, target_seq_lens
+        if ends_d.dtype != torch.int32 or seqs_d.dtype != torch.int32:
+            raise ValueError("query_ends and target_seq_lens must be int32 device tensors")
         q_index = torch.empty(rows, dtype=torch.int32, device=self.device)
         r_len = torch.empty_like(q_index)
         r_slot = torch.empty_like(q_index)
@@ -474,7 +499,7 @@ class DiffSpecDraftCache:
             _lib.ptr(q_index), _lib.ptr(r_len), _lib.ptr(r_slot), _lib.ptr(self._status),
             _lib.stream_ptr(self.device),
         )
-        max_len = max(target_seq_lens)
+        max_len = int(max_seq_len)
         parts = paged_chunk_head_scores(
             query, key_cache, softmax_lse, block_tables, r_len,
             chunk_size=self.settings.chunk_size, max_seq_len=max_len, scale=scale,
@@ -794,3 +819,172 @@ class DiffSpecDraftCache:
         if cs.dtype != self.dtype and cs.dtype != torch.float32:
             cs = cs.to(self.dtype)
         return cs
+
+
+class DraftPeriodGraph:
+    """One retrieval period of a :class:`DiffSpecDraftCache`, captured once
+    as a CUDA graph and replayed per period, host copies included.
+
+    A period is what the runtime's methods do between two retrievals: the
+    retrieval hook on the verify pass of the period's first cycle
+    (:meth:`DiffSpecDraftCache.retrieve_device`), then
+    ``retrieval_interval`` draft cycles, each a plan + rebuild at that
+    cycle's committed lengths and ``max_tree_depth`` draft attention steps
+    (:meth:`~DiffSpecDraftCache.rebuild`,
+    :meth:`~DiffSpecDraftCache.forward_attention`).  Replaying the graph
+    replaces those Python calls (about twenty per period), which is the
+    reference's per-cycle host work (diffspec/runtime.py:1170-1334,
+    1683-1765, 2024-2134) reduced to one launch.
+
+    Inputs are written by the caller into pinned host buffers (``inputs``):
+    per cycle the verify pass's query rows, LSE, accepted counts, query ends,
+    target lengths and the committed lengths, and per draft step its q/k/v.
+    The graph copies each block to the device on a side stream just before
+    the kernels that read it (the copies of later cycles run while earlier
+    cycles compute) and copies every step's attention output back into
+    ``outputs`` on a second side stream as soon as that step is done.  After
+    :meth:`replay` returns, the caller synchronizes (or waits on
+    :attr:`done`) before reading ``outputs`` or rewriting ``inputs``.
+
+    The batch (request ids, hence slots), the target's paged K and block
+    table, ``max_seq_len`` and the shapes are fixed at capture; lengths,
+    counts and every tensor's contents may change between replays.  Host-side
+    counters of the cache (``metrics``) do not advance on replay.  Building
+    the graph runs one period eagerly on placeholder inputs (zero queries,
+    nothing accepted, history length 0), which touches only row 0 of the
+    active slots' working caches; the first replay rebuilds them.
+    """
+
+    def __init__(self, cache: "DiffSpecDraftCache", request_ids: list[str], *,
+                 key_cache: torch.Tensor, block_tables: torch.Tensor,
+                 query_rows_per_request: int, num_query_heads: int, max_seq_len: int,
+                 scale: float):
+        self.cache = cache
+        s = cache.settings
+        self.interval, self.depth = s.retrieval_interval, s.max_tree_depth
+        n = len(request_ids)
+        if n == 0:
+            raise ValueError("a period graph needs at least one request")
+        dev, dt = cache.device, cache.dtype
+        hq, hk, d = num_query_heads, cache.num_kv_heads, cache.head_dim
+        rq = n * query_rows_per_request
+        self.request_ids = list(request_ids)
+        self.scale = float(scale)
+        self.max_seq_len = int(max_seq_len)
+        self.key_cache, self.block_tables = key_cache, block_tables
+
+        # One pinned host buffer and its device twin, packed in the order the
+        # period consumes them: [verify block of cycle c][q/k/v of its steps]...
+        verify = [("query", (rq, hq, d), dt), ("lse", (rq, hq), torch.float32),
+                  ("counts", (n,), torch.int64), ("query_ends", (n,), torch.int32),
+                  ("seq_lens", (n,), torch.int32), ("committed", (n,), torch.int32)]
+        step = [("q", (n, hq, d), dt), ("k", (n, hk, d), dt), ("v", (n, hk, d), dt)]
+        layout, off = [], 0
+
+        def place(spec):
+            nonlocal off
+            block, start = [], off
+            for name, shape, dtype in spec:
+                esize = torch.empty((), dtype=dtype).element_size()
+                off = (off + 15) // 16 * 16
+                nbytes = esize * int(torch.Size(shape).numel())
+                block.append((name, shape, dtype, off, nbytes))
+                off += nbytes
+            return block, start, off
+
+        for c in range(self.interval):
+            layout.append(("verify", c, None, *place(verify)))
+            for j in range(self.depth):
+                layout.append(("step", c, j, *place(step)))
+        total = (off + 15) // 16 * 16
+        self._host_in = torch.zeros(total, dtype=torch.uint8).pin_memory()
+        self._dev_in = torch.zeros(total, dtype=torch.uint8, device=dev)
+
+        def views(buf, block):
+            return {name: buf[o:o + nb].view(dtype).view(shape)
+                    for name, shape, dtype, o, nb in block}
+
+        self.inputs = {"verify": [None] * self.interval,
+                       "step": [[None] * self.depth for _ in range(self.interval)]}
+        self._dev = {"verify": [None] * self.interval,
+                     "step": [[None] * self.depth for _ in range(self.interval)]}
+        self._blocks = []  # (kind, c, j, start, end) in copy order
+        for kind, c, j, block, start, end in layout:
+            hv, dv = views(self._host_in, block), views(self._dev_in, block)
+            if kind == "verify":
+                self.inputs["verify"][c], self._dev["verify"][c] = hv, dv
+            else:
+                self.inputs["step"][c][j], self._dev["step"][c][j] = hv, dv
+            self._blocks.append((kind, c, j, start, end))
+        self.outputs = torch.zeros((self.interval, self.depth, n, hq, d), dtype=dt).pin_memory()
+        self._dev_out = torch.zeros((self.interval, self.depth, n, hq, d), dtype=dt, device=dev)
+        self.h2d_bytes = int(total)
+        self.d2h_bytes = int(self.outputs.numel() * self.outputs.element_size())
+        for c in range(self.interval):  # placeholders that keep the first (eager) run in range
+            v = self.inputs["verify"][c]
+            ends = torch.arange(1, n + 1, dtype=torch.int32) * query_rows_per_request
+            v["query_ends"].copy_(ends)
+            v["seq_lens"].fill_(min(self.max_seq_len, cache.max_model_len))
+            v["committed"].fill_(1)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.done: torch.cuda.Event | None = None
+        self._capture()
+
+    def _period(self, main, h2d, d2h) -> None:
+        """Enqueue one period: copies on ``h2d`` / ``d2h``, kernels on ``main``."""
+        cache = self.cache
+        ready = {}
+        h2d.wait_stream(main)
+        with torch.cuda.stream(h2d):
+            for kind, c, j, start, end in self._blocks:
+                self._dev_in[start:end].copy_(self._host_in[start:end], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+                ready[(kind, c, j)] = ev
+        d2h.wait_stream(main)
+        with torch.cuda.stream(main):
+            v0 = self._dev["verify"][0]
+            main.wait_event(ready[("verify", 0, None)])
+            cache.set_active_requests(self.request_ids)
+            cache.retrieve_device(v0["query"], v0["lse"], self.key_cache, self.block_tables,
+                                  v0["query_ends"], v0["seq_lens"], self.max_seq_len,
+                                  v0["counts"], self.scale)
+            for c in range(self.interval):
+                if c:
+                    main.wait_event(ready[("verify", c, None)])
+                cache.begin_cycle(self.request_ids)
+                cache.rebuild(self._dev["verify"][c]["committed"])
+                for j in range(self.depth):
+                    st = self._dev["step"][c][j]
+                    main.wait_event(ready[("step", c, j)])
+                    cache.forward_attention(st["q"], st["k"], st["v"], self.scale,
+                                            self._dev_out[c, j])
+                    out_ready = torch.cuda.Event()
+                    out_ready.record(main)
+                    d2h.wait_event(out_ready)
+                    with torch.cuda.stream(d2h):
+                        self.outputs[c, j].copy_(self._dev_out[c, j], non_blocking=True)
+                cache.end_cycle()
+        main.wait_stream(h2d)
+        main.wait_stream(d2h)
+
+    def _capture(self) -> None:
+        dev = self.cache.device
+        main, h2d, d2h = (torch.cuda.Stream(dev) for _ in range(3))
+        main.wait_stream(torch.cuda.current_stream(dev))
+        self._period(main, h2d, d2h)  # eager run: workspaces, prepared calls
+        torch.cuda.current_stream(dev).wait_stream(main)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=main):
+            self._period(main, h2d, d2h)
+        torch.cuda.synchronize(dev)
+        self.done = torch.cuda.Event()
+
+    def replay(self) -> None:
+        """Run one period on the current stream (asynchronous): copy the
+        pinned inputs in, retrieve, rebuild and attend, copy the outputs
+        out.  :attr:`done` is recorded after it."""
+        self.graph.replay()
+        self.done.record(torch.cuda.current_stream(self.cache.device))
+
