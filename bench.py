@@ -1285,7 +1285,9 @@ def run_kv_projection(args):
 
 def run_draft_linear(args):
     """Time the config-5 draft layer's four linears at a 16-token decode step
-    on the tcgen05 weight-streaming kernel (qkv with the raw-cache write,
+    on the tcgen05 weight-streaming kernel (`us`: tile-packed weights, as the
+    draft layer streams them; `us_row_major_weight`: the same launches on
+    row-major weights) (qkv with the raw-cache write,
     o_proj + residual, gate_up + SwiGLU, down_proj + residual) against cuBLAS
     for the same products (torch.mm; the K/V raw write, the residual add and
     SwiGLU not included on that side).  Each shape cycles enough weight copies
@@ -1318,14 +1320,16 @@ def run_draft_linear(args):
         q_out = torch.empty((tokens, HQ * D), dtype=bf, device=device)
         kv_out = torch.empty((tokens, 2 * HK * D), dtype=bf, device=device)
 
-        def ours(w, name=name, x=x, res=res, out=out, half=half, q_out=q_out, kv_out=kv_out):
+        def ours(w, name=name, x=x, res=res, out=out, half=half, q_out=q_out, kv_out=kv_out,
+                 packed=False):
             if name == "qkv":
                 dsb.kernels.qkv_projection_write_raw(x, w, HQ * D, slots, pos, rk, rv, q_out=q_out,
-                                                     kv_out=kv_out, prefetch_weight=True)
+                                                     kv_out=kv_out, prefetch_weight=True,
+                                                     packed_weight=packed)
             elif name == "gate_up":  # the weight's tile order does not change the time
-                dl.draft_linear(x, w, "swiglu", out=half)
+                dl.draft_linear(x, w, "swiglu", out=half, packed=packed)
             else:
-                dl.draft_linear(x, w, "residual", residual=res, out=out)
+                dl.draft_linear(x, w, "residual", residual=res, out=out, packed=packed)
 
         def cublas(w, x=x, out=out):
             torch.mm(x, w.t(), out=out)
@@ -1353,13 +1357,18 @@ def run_draft_linear(args):
             torch.cuda.synchronize(device)
             return a.elapsed_time(b) * 1e3 / (args.steps * len(ws))
 
-        us = time_graph(ours)
+        us_rowmajor = time_graph(ours)
+        ws = [dl.pack_linear_weight(w) for w in ws]  # the layout Eagle3DraftLayer streams
+        us = time_graph(lambda w: ours(w, packed=True))
         assert dsb._lib.read_and_clear_error_flag(device) == 0
+        del ws  # cuBLAS streams its own row-major copies
+        ws = [(torch.randn((rows, k), generator=g, device=device) / k ** 0.5).to(bf)
+              for _ in range(copies)]
         ref = time_graph(cublas)
         wbytes = rows * k * 2
         result[name] = dict(weight_rows=rows, k=k, us=round(us, 2), weight_gbs=round(wbytes / us / 1e3, 1),
                             frac_of_hbm_peak=round(wbytes / us / 1e3 / peak, 3),
-                            cublas_mm_us=round(ref, 2))
+                            us_row_major_weight=round(us_rowmajor, 2), cublas_mm_us=round(ref, 2))
         del ws
         torch.cuda.empty_cache()
     print(json.dumps(dict(mode="draft_linear", tokens=tokens, dtype="bf16", peak_gbs=peak,

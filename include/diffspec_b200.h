@@ -282,7 +282,8 @@ int dsb_kv_projection_write_raw(
  * block_size, num_kv_heads, 128]; block_table [block_table_rows,
  * block_table_cols] with row stride block_table_stride.  max_seq_len bounds
  * seq_lens and sets the split count (ceil(max_seq_len / tokens_per_split);
- * tokens_per_split <= 0 picks 512); scratch holds
+ * tokens_per_split <= 0 picks 1024 when max_seq_len >= 16384, else 512, in
+ * this call and in dsb_paged_decode_scratch_floats alike); scratch holds
  * dsb_paged_decode_scratch_floats floats.  Bad table rows set DSB_FLAG_SLOT,
  * bad page entries DSB_FLAG_BLOCK (the token is skipped), a seq_lens entry
  * above the split count's reach (max_seq_len too small) DSB_FLAG_POSITION
@@ -302,10 +303,28 @@ int dsb_paged_decode_attention_lse(
 #define DSB_LINEAR_PLAIN 0    /* out = x . W^T                                 */
 #define DSB_LINEAR_RESIDUAL 1 /* out = x . W^T + residual (one rounding)       */
 #define DSB_LINEAR_SWIGLU 2   /* out = silu(gate) * up of a gate/up-interleaved W */
+#define DSB_LINEAR_PARTIAL_F32 3 /* out (float) = x . W^T unrounded: one rank's share
+                                    of a row-split linear, for an fp32 all-reduce */
 /* Request the weight before the previous kernel in the stream has finished
  * (programmatic dependent launch): the weight must not be written by that
  * kernel.  Activations, residuals and outputs are touched only after it. */
 #define DSB_LINEAR_PREFETCH_WEIGHT 1
+/* The weight is in the tile-packed layout [rows / 128][in_features / 64][128]
+ * [64] (row-major [rows, in_features] regrouped so that every 128-row x
+ * 64-column block the kernel streams is one contiguous 16 KB run; see
+ * dsb_pack_linear_weight), instead of row-major [rows, in_features]. */
+#define DSB_LINEAR_PACKED_WEIGHT 2
+
+/* Copy a row-major [rows, cols] weight (rows a multiple of 128, cols of 64;
+ * BF16 or FP16, 16-byte aligned) into the tile-packed layout the linear
+ * entry points read with DSB_LINEAR_PACKED_WEIGHT: out[m][kb][r][c] =
+ * weight[128 m + r][64 kb + c].  A one-time, load-time step (no counterpart
+ * in the reference, whose projections are vLLM linear layers); out must not
+ * alias weight.  The copy completes before the next kernel in the stream
+ * starts, so a linear launch with DSB_LINEAR_PREFETCH_WEIGHT may follow it
+ * directly. */
+int dsb_pack_linear_weight(const void *weight, int64_t rows, int32_t cols, int32_t dtype,
+                           void *out, void *stream);
 
 /* The draft layer's query + K/V projection in one launch (vLLM
  * QKVParallelLinear of the Eagle3 layer, qkv input built at
@@ -354,6 +373,18 @@ int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_features, const v
 int dsb_rms_norm(const void *x, int64_t x_row_stride, const void *weight, void *out,
                  int64_t out_row_stride, int32_t rows, int32_t cols, float eps, int32_t dtype,
                  void *stream);
+
+/* dsb_add_rms_norm: the step after an all-reduced row-split linear.
+ * x_out[r] = round(partial[r] + residual[r]) (fp32 partial, one rounding, as
+ * the DSB_LINEAR_RESIDUAL epilogue of the whole linear rounds) and, when
+ * weight is set, out[r] = rms_norm(x_out[r]) with dsb_rms_norm's arithmetic
+ * bit for bit.  Row strides in elements (multiples of 8, >= cols), cols a
+ * multiple of 8, 16-byte aligned rows; no counterpart in the reference
+ * (vLLM's fused_add_rms_norm after a tensor-parallel all-reduce). */
+int dsb_add_rms_norm(const float *partial, int64_t partial_row_stride, const void *residual,
+                     int64_t residual_row_stride, const void *weight, void *x_out,
+                     int64_t x_row_stride, void *out, int64_t out_row_stride, int32_t rows,
+                     int32_t cols, float eps, int32_t dtype, void *stream);
 
 /* dsb_rope_qk: NeoX rotation at positions[t] of a [cos | sin] table with
  * rotary_rows rows (products rounded before the add, as in the working-cache

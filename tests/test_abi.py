@@ -101,6 +101,10 @@ def test_draft_layer_entry_points_reject_bad_arguments(dsb):
     assert L.dsb_qkv_projection_write_raw(*args) == P.DSB_ERR_UNSUPPORTED
     args[4], args[14] = 128, None
     assert L.dsb_qkv_projection_write_raw(*args) == P.DSB_ERR_INVALID
+    # weight packing: rows not a multiple of 128, cols not of 64, aliased buffers
+    assert L.dsb_pack_linear_weight(fake, 100, 64, 0, ctypes.c_void_p(512), None) == P.DSB_ERR_UNSUPPORTED
+    assert L.dsb_pack_linear_weight(fake, 128, 96, 0, ctypes.c_void_p(512), None) == P.DSB_ERR_UNSUPPORTED
+    assert L.dsb_pack_linear_weight(fake, 128, 64, 0, fake, None) == P.DSB_ERR_INVALID
     # elementwise stages
     assert L.dsb_rms_norm(fake, 12, fake, fake, 12, 2, 12, 1e-6, 0, None) == P.DSB_ERR_UNSUPPORTED
     assert L.dsb_rms_norm(fake, 16, fake, fake, 16, 2, 16, -1.0, 0, None) == P.DSB_ERR_INVALID
@@ -133,3 +137,6 @@ def test_target_attention_rejects_bad_arguments(dsb):
     assert call(a17=2) == P.DSB_ERR_INVALID              # fp32 caches
     assert call(a1=0) == P.DSB_OK                        # no rows
     assert lib.dsb_paged_decode_scratch_floats(4, 32, 1000, 512) == 4 * 32 * 2 * 130
+    # default split length: 512 tokens below 16384, 1024 from there on
+    assert lib.dsb_paged_decode_scratch_floats(4, 32, 1000, 0) == 4 * 32 * 2 * 130
+    assert lib.dsb_paged_decode_scratch_floats(4, 32, 40960, 0) == 4 * 32 * 40 * 130

@@ -206,3 +206,41 @@ def test_draft_linear_epilogues_match_oracle(dsb, cuda, epilogue, dtype, tokens,
         same = (got == O.linear(x, w, res if epilogue == "residual" else None, dtype)).mean()
         assert same > 0.97
     assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+
+
+@pytest.mark.parametrize("rows,k", [(5120, 4096), (2048, 4096), (12288, 2048), (2048, 6144),
+                                    (256, 128)])
+def test_packed_weight_is_bit_identical(dsb, cuda, rows, k):
+    """Tile-packed weights (pack_linear_weight) give the same bits as the
+    row-major weight in every epilogue and in the q / K-V routing with the
+    raw-cache write: the kernel reads the same 128 x 64 blocks in the same
+    order, only from contiguous runs."""
+    g = torch.Generator(device=cuda).manual_seed(rows + k)
+    dl = dsb.draft_layer
+    w = (torch.randn((rows, k), generator=g, device=cuda) / k ** 0.5).bfloat16()
+    x = torch.randn((16, k), generator=g, device=cuda).bfloat16()
+    res = torch.randn((16, rows), generator=g, device=cuda).bfloat16()
+    wp = dl.pack_linear_weight(w)
+    assert torch.equal(wp.view(rows // 128, k // 64, 128, 64),
+                       w.view(rows // 128, 128, k // 64, 64).permute(0, 2, 1, 3))
+    for epi in ("plain", "residual"):
+        r = res if epi == "residual" else None
+        assert torch.equal(dl.draft_linear(x, w, epi, residual=r),
+                           dl.draft_linear(x, wp, epi, residual=r, packed=True))
+    if rows % 256 == 0:
+        wt = dl.interleave_gate_up(w)
+        assert torch.equal(dl.draft_linear(x, wt, "swiglu"),
+                           dl.draft_linear(x, dl.pack_linear_weight(wt), "swiglu", packed=True))
+    if rows == 5120:  # the config-5 qkv projection: 32 query heads + 4 kv heads of 128
+        rk = torch.zeros((16, 64, 4, 128), dtype=torch.bfloat16, device=cuda)
+        outs = []
+        for weight, packed in ((w, False), (wp, True)):
+            rk_, rv_ = rk.clone(), rk.clone()
+            q, kv = dsb.kernels.qkv_projection_write_raw(
+                x, weight, 4096, torch.arange(16, dtype=torch.int32, device=cuda),
+                torch.arange(16, dtype=torch.int64, device=cuda), rk_, rv_, packed_weight=packed)
+            outs.append((q, kv, rk_, rv_))
+        for a, b in zip(*outs):
+            assert torch.equal(a, b)
+    torch.cuda.synchronize()
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0

@@ -46,6 +46,7 @@ def _run(dsb, cuda, dtype, q, kc, vc, bt, lens, table_rows=None, tps=512):
     ("f16", 8, 8, [5, 300, 64], 64),               # one query head per kv head
     ("bf16", 16, 1, [513, 2, 700], 512),           # 16 query heads per kv head
     ("bf16", 4, 2, [4096], 256),                   # one long row, 16 splits
+    ("bf16", 8, 2, [20000, 16384, 3], 0),          # library default split: 1024 from 16384 on
 ])
 def test_decode_attention_and_lse_match_oracle(dsb, cuda, dtype, hq, hk, lens, tps):
     rng = np.random.default_rng(len(lens) * 97 + hq)

@@ -101,10 +101,13 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I32, _I32, _P, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _I64, _I32, _P, _P, _I32,
          _P, _P],
     ),
+    "dsb_pack_linear_weight": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P]),
     "dsb_draft_linear": (
         ctypes.c_int,
         [_P, _I32, _I32, _P, _I32, _I32, _P, _I64, _P, _I64, _I32, _I32, _P, _P],
     ),
+    "dsb_add_rms_norm": (
+        ctypes.c_int, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _I64, _I32, _I32, _F32, _I32, _P]),
     "dsb_rms_norm": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _I32, _I32, _F32, _I32, _P]),
     "dsb_rope_qk": (
         ctypes.c_int,

@@ -51,7 +51,7 @@ constexpr int kLnABytes = 128 * 64 * 2;     // weight box [128 rows][64 cols]
 constexpr int kLnBBytes = kLnTok * 64 * 2;  // activation box [16 rows][64 cols]
 constexpr int kLnMaxK = 1 << 16;
 
-enum Epilogue : int { kPlain = 0, kResidual = 1, kSwiglu = 2 };
+enum Epilogue : int { kPlain = 0, kResidual = 1, kSwiglu = 2, kPartialF32 = 3 };
 
 template <int RANKS> struct LnCfg {
   static constexpr int kTpr = kLnTok / RANKS;  // tokens each rank sums
@@ -73,6 +73,7 @@ struct LnArgs {
   int64_t ldr;
   int mode;
   int prefetch;
+  int packed;  // weight in the tile-packed layout (DSB_LINEAR_PACKED_WEIGHT)
   const int32_t *slots;
   const int64_t *positions;
   void *raw_k, *raw_v;
@@ -119,6 +120,11 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   const int per = (nkb_all + RANKS - 1) / RANKS;
   const int kb0 = rank * per;
   const int nkb = max(0, min(per, nkb_all - kb0));
+  // Weight box of k-block kb: row-major [N, K] -> (x = 64 kb, y = f0); tile-
+  // packed [N/128][K/64][128][64] -> the contiguous 16 KB block
+  // (x = 0, y = 128 * (tile * K/64 + kb)).
+  auto wx = [&](int kb) { return a.packed ? 0 : kb * 64; };
+  auto wy = [&](int kb) { return a.packed ? (blockIdx.y * nkb_all + kb) * 128 : f0; };
   const int first = min(nkb, S);
   // weights are streamed once per step: evicted first, so the working cache
   // the draft attention re-reads keeps its L2 lines
@@ -137,7 +143,8 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     if (a.prefetch)
       for (int kb = 0; kb < first; ++kb) {
         mbar_expect_tx(full0 + 8 * kb, kLnABytes + kLnBBytes);
-        tma_load_2d_hint(s_a + kb * kLnABytes, &tw, (kb0 + kb) * 64, f0, full0 + 8 * kb, wpol);
+        tma_load_2d_hint(s_a + kb * kLnABytes, &tw, wx(kb0 + kb), wy(kb0 + kb), full0 + 8 * kb,
+                         wpol);
       }
   }
   if (warp == 0) {
@@ -166,7 +173,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
       }
       if (!(a.prefetch && kb < first)) {
         mbar_expect_tx(full0 + 8 * s, kLnABytes + kLnBBytes);
-        tma_load_2d_hint(s_a + s * kLnABytes, &tw, (kb0 + kb) * 64, f0, full0 + 8 * s, wpol);
+        tma_load_2d_hint(s_a + s * kLnABytes, &tw, wx(kb0 + kb), wy(kb0 + kb), full0 + 8 * s, wpol);
       }
       tma_load_2d(s_b + s * kLnBBytes, &tx, (kb0 + kb) * 64, t0, full0 + 8 * s);
     }
@@ -275,6 +282,10 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     const int t = t0 + kTpr * rank + j;
     if (t >= a.T) continue;
     if (g < a.split) {
+      if (a.mode == kPartialF32) {  // the fp32 sums themselves (no rounding)
+        static_cast<float *>(a.out)[(int64_t)t * a.ldo + g] = v[j];
+        continue;
+      }
       float y = v[j];
       if (a.mode == kResidual)
         y = __fadd_rn(y, Elem<T>::to_f(static_cast<const T *>(a.residual)[(int64_t)t * a.ldr + g]));
@@ -369,7 +380,10 @@ template <typename T> int pick_ranks(const LnArgs &a) {
 template <typename T>
 int launch_linear(const void *x, const void *weight, const LnArgs &a, int dtype, cudaStream_t st) {
   CUtensorMap tw, tx;
-  if (!encode_kv_map(&tw, weight, a.N, a.K, dtype, 128) ||
+  // packed: the weight viewed as [N * K / 64, 64] rows of 128 bytes
+  const bool wmap = a.packed ? encode_kv_map(&tw, weight, (int64_t)a.N * (a.K / 64), 64, dtype, 128)
+                             : encode_kv_map(&tw, weight, a.N, a.K, dtype, 128);
+  if (!wmap ||
       !encode_kv_map(&tx, x, a.T, a.K, dtype, kLnTok))
     return fail(DSB_ERR_UNSUPPORTED, "no tensor map for the weight or activation rows");
   switch (pick_ranks<T>(a)) {
@@ -390,7 +404,8 @@ int check_common(const void *x, int32_t tokens, int32_t in_features, const void 
     return fail(DSB_ERR_UNSUPPORTED, "in_features must be a multiple of 64 and at most 65536");
   if (out_features <= 0 || out_features % 128)
     return fail(DSB_ERR_UNSUPPORTED, "the weight's row count must be a multiple of 128");
-  if ((tokens + kLnTok - 1) / kLnTok > 65535 || out_features / 128 > 65535)
+  if ((tokens + kLnTok - 1) / kLnTok > 65535 || out_features / 128 > 65535 ||
+      out_features * (in_features / 64) > INT_MAX)
     return fail(DSB_ERR_UNSUPPORTED, "grid too large");
   if (!x || !weight) return fail(DSB_ERR_INVALID, "null pointer argument");
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(weight) % 16)
@@ -402,6 +417,27 @@ int dispatch(const void *x, const void *weight, const LnArgs &a, int32_t dtype, 
   cudaStream_t st = as_stream(stream);
   return dtype == DSB_BF16 ? launch_linear<__nv_bfloat16>(x, weight, a, dtype, st)
                            : launch_linear<__half>(x, weight, a, dtype, st);
+}
+
+// out[m][kb][r][0..63] = weight[128 m + r][64 kb .. 64 kb + 63]: one thread
+// per 16-byte piece (8 elements), reads and writes coalesced along kb / r.
+// Launched without programmatic dependent launch and never releasing its
+// dependents early: the next kernel in the stream may be a linear that
+// requests this very weight before its own dependency wait, so it must not
+// start before these writes are complete.
+template <typename T>
+__global__ void pack_weight_kernel(const T *__restrict__ w, int64_t rows, int cols,
+                                   T *__restrict__ out) {
+  const int64_t pieces = rows * (cols / 8);
+  const int nkb = cols / 64;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < pieces;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t blk = i / (128 * 8);  // m * nkb + kb
+    const int rem = (int)(i % (128 * 8)), r = rem / 8, p = rem % 8;
+    const int64_t m = blk / nkb, kb = blk % nkb;
+    const int64_t src = (m * 128 + r) * cols + kb * 64 + p * 8;
+    *reinterpret_cast<uint4 *>(out + i * 8) = *reinterpret_cast<const uint4 *>(w + src);
+  }
 }
 
 }  // namespace
@@ -436,6 +472,7 @@ extern "C" int dsb_qkv_projection_write_raw(
   a.split = q_features;
   a.mode = kPlain;
   a.prefetch = (flags & DSB_LINEAR_PREFETCH_WEIGHT) != 0;
+  a.packed = (flags & DSB_LINEAR_PACKED_WEIGHT) != 0;
   a.slots = slots;
   a.positions = positions;
   a.raw_k = raw_key;
@@ -470,7 +507,7 @@ extern "C" int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_featur
   if (tokens < 0) return fail(DSB_ERR_INVALID, "negative token count");
   if (tokens == 0) return DSB_OK;
   if (epilogue != DSB_LINEAR_PLAIN && epilogue != DSB_LINEAR_RESIDUAL &&
-      epilogue != DSB_LINEAR_SWIGLU)
+      epilogue != DSB_LINEAR_SWIGLU && epilogue != DSB_LINEAR_PARTIAL_F32)
     return fail(DSB_ERR_INVALID, "unknown epilogue");
   if (int e = check_common(x, tokens, in_features, weight, weight_rows, dtype)) return e;
   const int64_t out_cols = epilogue == DSB_LINEAR_SWIGLU ? weight_rows / 2 : weight_rows;
@@ -484,11 +521,38 @@ extern "C" int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_featur
   a.split = weight_rows;  // every feature goes to `out`
   a.residual = residual;
   a.ldr = residual_row_stride;
-  a.mode = epilogue == DSB_LINEAR_PLAIN ? kPlain : epilogue == DSB_LINEAR_RESIDUAL ? kResidual : kSwiglu;
+  a.mode = epilogue == DSB_LINEAR_PLAIN      ? kPlain
+           : epilogue == DSB_LINEAR_RESIDUAL ? kResidual
+           : epilogue == DSB_LINEAR_SWIGLU   ? kSwiglu
+                                             : kPartialF32;
   a.prefetch = (flags & DSB_LINEAR_PREFETCH_WEIGHT) != 0;
+  a.packed = (flags & DSB_LINEAR_PACKED_WEIGHT) != 0;
   a.T = tokens;
   a.K = in_features;
   a.N = weight_rows;
   a.err = error_flag;
   return dispatch(x, weight, a, dtype, stream);
+}
+
+extern "C" int dsb_pack_linear_weight(const void *weight, int64_t rows, int32_t cols,
+                                      int32_t dtype, void *out, void *stream) {
+  if (dtype != DSB_BF16 && dtype != DSB_F16)
+    return fail(DSB_ERR_INVALID, "the weight must be BF16 or FP16");
+  if (rows <= 0 || rows % 128 || cols <= 0 || cols % 64)
+    return fail(DSB_ERR_UNSUPPORTED, "rows must be a multiple of 128 and cols of 64");
+  if (!weight || !out || weight == out) return fail(DSB_ERR_INVALID, "null or aliased buffers");
+  if (reinterpret_cast<uintptr_t>(weight) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(DSB_ERR_UNSUPPORTED, "weight and out must be 16-byte aligned");
+  const int64_t pieces = rows * (cols / 8);
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((pieces + threads - 1) / threads, 8 * sm_count());
+  cudaStream_t st = as_stream(stream);
+  if (dtype == DSB_BF16)
+    pack_weight_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, st>>>(
+        static_cast<const __nv_bfloat16 *>(weight), rows, (int)cols,
+        static_cast<__nv_bfloat16 *>(out));
+  else
+    pack_weight_kernel<__half><<<(unsigned)blocks, threads, 0, st>>>(
+        static_cast<const __half *>(weight), rows, (int)cols, static_cast<__half *>(out));
+  return check_launch("pack_weight_kernel");
 }

@@ -90,6 +90,63 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
+// x = round(partial + residual) per element (fp32 add, one rounding: what a
+// residual epilogue of one whole linear gives), stored to x_out; then, when
+// w is set, norm_out = rms_norm(x) with exactly rms_norm_kernel's arithmetic
+// (same per-thread vectors, reduction tree and rounding points), so a
+// tensor-parallel layer whose linears all-reduce fp32 partials reaches the
+// same values as the single-GPU layer up to the partials' summation order.
+// One CTA per row; cols a multiple of 8.
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
+    add_rms_norm_kernel(const float *__restrict__ part, int64_t p_stride,
+                        const T *__restrict__ res, int64_t r_stride, const T *__restrict__ w,
+                        T *__restrict__ x_out, int64_t x_stride, T *__restrict__ out,
+                        int64_t out_stride, int cols, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  pdl_begin();
+  const float *prow = part + blockIdx.x * p_stride;
+  const T *rrow = res + blockIdx.x * r_stride;
+  T *xrow = x_out + blockIdx.x * x_stride;
+  const int vecs = cols / 8;
+  float ss = 0.f;
+  auto sum8 = [&](int v, float (&f)[8]) {
+    const float4 a = *reinterpret_cast<const float4 *>(prow + 8 * v);
+    const float4 b = *reinterpret_cast<const float4 *>(prow + 8 * v + 4);
+    const float pv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float r[8];
+    load8(rrow + 8 * v, r);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = Elem<T>::to_f(Elem<T>::from_f(__fadd_rn(pv[i], r[i])));
+  };
+  for (int v = threadIdx.x; v < vecs; v += kNormThreads) {
+    float f[8];
+    sum8(v, f);
+    store8(xrow + 8 * v, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+  }
+  if (w == nullptr) return;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) total += red[i];
+  const float inv = rsqrtf(total / static_cast<float>(cols) + eps);
+  T *orow = out + blockIdx.x * out_stride;
+  for (int v = threadIdx.x; v < vecs; v += kNormThreads) {
+    float f[8], g[8];
+    sum8(v, f);
+    load8(w + 8 * v, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      f[i] = __fmul_rn(Elem<T>::to_f(Elem<T>::from_f(__fmul_rn(f[i], inv))), g[i]);
+    store8(orow + 8 * v, f);
+  }
+}
+
 struct RopeArgs {
   void *q;
   const void *k, *v;
@@ -197,6 +254,43 @@ extern "C" int dsb_rms_norm(const void *x, int64_t x_row_stride, const void *wei
                   static_cast<const __half *>(x), x_row_stride, static_cast<const __half *>(weight),
                   static_cast<__half *>(out), out_row_stride, (int)cols, eps);
   return check_launch("rms_norm_kernel");
+}
+
+extern "C" int dsb_add_rms_norm(const float *partial, int64_t partial_row_stride,
+                                const void *residual, int64_t residual_row_stride,
+                                const void *weight, void *x_out, int64_t x_row_stride, void *out,
+                                int64_t out_row_stride, int32_t rows, int32_t cols, float eps,
+                                int32_t dtype, void *stream) {
+  if (rows < 0 || cols <= 0) return fail(DSB_ERR_INVALID, "rows must be >= 0 and cols > 0");
+  if (rows == 0) return DSB_OK;
+  if (dtype != DSB_BF16 && dtype != DSB_F16)
+    return fail(DSB_ERR_INVALID, "add_rms_norm rows and weight must be BF16 or FP16");
+  if (!partial || !residual || !x_out || (weight && !out))
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (!(eps >= 0.f)) return fail(DSB_ERR_INVALID, "eps must be >= 0");
+  const bool strides_ok = cols % 8 == 0 && partial_row_stride % 8 == 0 &&
+                          residual_row_stride % 8 == 0 && x_row_stride % 8 == 0 &&
+                          partial_row_stride >= cols && residual_row_stride >= cols &&
+                          x_row_stride >= cols &&
+                          (!weight || (out_row_stride % 8 == 0 && out_row_stride >= cols));
+  if (!strides_ok || !aligned16(partial) || !aligned16(residual) || !aligned16(x_out) ||
+      (weight && (!aligned16(weight) || !aligned16(out))))
+    return fail(DSB_ERR_UNSUPPORTED,
+                "add_rms_norm needs cols and row strides that are multiples of 8 (>= cols) and "
+                "16-byte aligned rows");
+  const cudaStream_t st = as_stream(stream);
+  if (dtype == DSB_BF16)
+    launch_kernel(add_rms_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), 0, st,
+                  partial, partial_row_stride, static_cast<const __nv_bfloat16 *>(residual),
+                  residual_row_stride, static_cast<const __nv_bfloat16 *>(weight),
+                  static_cast<__nv_bfloat16 *>(x_out), x_row_stride,
+                  static_cast<__nv_bfloat16 *>(out), out_row_stride, (int)cols, eps);
+  else
+    launch_kernel(add_rms_norm_kernel<__half>, dim3(rows), dim3(kNormThreads), 0, st, partial,
+                  partial_row_stride, static_cast<const __half *>(residual), residual_row_stride,
+                  static_cast<const __half *>(weight), static_cast<__half *>(x_out), x_row_stride,
+                  static_cast<__half *>(out), out_row_stride, (int)cols, eps);
+  return check_launch("add_rms_norm_kernel");
 }
 
 extern "C" int dsb_rope_qk(void *query, int64_t query_row_stride, int32_t num_query_heads,

@@ -99,7 +99,9 @@ __global__ void __launch_bounds__(kTaWarps * 32, 2) paged_decode_split_kernel(co
   static_assert(G <= 16, "at most 16 query heads per kv head");
   extern __shared__ __align__(128) uint8_t s_raw[];  // rings, then the warps' states
   pdl_begin();
-  const int split = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
+  // kv head fastest: the Hk CTAs of one (split, row) read the quarters of
+  // the same token rows, and run side by side (DRAM row locality)
+  const int h = blockIdx.x, split = blockIdx.y, r = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   int L = a.seq[r];
@@ -349,7 +351,7 @@ template <typename T, int G> int launch_group(const TaArgs &a, cudaStream_t st) 
   auto kern = paged_decode_split_kernel<T, G>;
   constexpr size_t smem = TaSmem<G>::kBytes;
   if (int e = ensure_smem((const void *)kern, smem); e != DSB_OK) return e;
-  launch_kernel(kern, dim3(a.splits, a.hk, a.rows), dim3(kTaWarps * 32), smem, st, a);
+  launch_kernel(kern, dim3(a.hk, a.splits, a.rows), dim3(kTaWarps * 32), smem, st, a);
   return DSB_OK;
 }
 
@@ -370,6 +372,14 @@ template <typename T> int launch_typed(const TaArgs &a, int group, cudaStream_t 
   return check_launch("paged_decode_merge_kernel");
 }
 
+// The split length when the caller passes <= 0: 1024 tokens for long
+// contexts (max_seq_len >= 16384: fewer CTA ramp-ups and a smaller merge;
+// 266 us against 313 us at 16 rows x 40960 tokens), 512 otherwise (more
+// splits to fill the GPU when the rows are short).
+int32_t default_tokens_per_split(int32_t max_seq_len) {
+  return max_seq_len >= 16384 ? 1024 : 512;
+}
+
 int64_t splits_for(int32_t max_seq_len, int32_t tokens_per_split) {
   return std::max<int64_t>(1, ((int64_t)max_seq_len + tokens_per_split - 1) / tokens_per_split);
 }
@@ -382,7 +392,7 @@ using namespace dsb;
 extern "C" int64_t dsb_paged_decode_scratch_floats(int32_t query_rows, int32_t num_query_heads,
                                                     int32_t max_seq_len, int32_t tokens_per_split) {
   if (query_rows <= 0 || num_query_heads <= 0 || max_seq_len < 0) return 0;
-  if (tokens_per_split <= 0) tokens_per_split = 512;  // the launch's default
+  if (tokens_per_split <= 0) tokens_per_split = default_tokens_per_split(max_seq_len);
   return (int64_t)query_rows * num_query_heads * splits_for(max_seq_len, tokens_per_split) *
          (kTaD + 2);
 }
@@ -405,7 +415,7 @@ extern "C" int dsb_paged_decode_attention_lse(
   if (num_blocks <= 0 || block_size <= 0 || block_table_rows <= 0 || block_table_cols <= 0 ||
       block_table_stride < block_table_cols || max_seq_len < 0)
     return fail(DSB_ERR_INVALID, "bad cache or block-table geometry");
-  if (tokens_per_split <= 0) tokens_per_split = 512;
+  if (tokens_per_split <= 0) tokens_per_split = default_tokens_per_split(max_seq_len);
   if (!(scale > 0.f)) return fail(DSB_ERR_INVALID, "scale must be positive");
   if (!query || !key_cache || !value_cache || !block_table || !seq_lens || !out || !lse || !scratch)
     return fail(DSB_ERR_INVALID, "null pointer argument");

@@ -26,8 +26,8 @@ from . import _lib
 from .attention import AttentionWorkspace, draft_decode_attention
 from .kernels import qkv_projection_write_raw
 
-__all__ = ["Eagle3DraftLayer", "draft_linear", "interleave_gate_up", "rms_norm", "rope_qk",
-           "silu_mul"]
+__all__ = ["Eagle3DraftLayer", "Eagle3DraftLayerTP", "add_rms_norm", "draft_linear",
+           "interleave_gate_up", "pack_linear_weight", "rms_norm", "rope_qk", "silu_mul"]
 
 
 def _rows(t: torch.Tensor, what: str) -> int:
@@ -37,7 +37,7 @@ def _rows(t: torch.Tensor, what: str) -> int:
     return t.stride(0)
 
 
-_EPILOGUES = {"plain": 0, "residual": 1, "swiglu": 2}
+_EPILOGUES = {"plain": 0, "residual": 1, "swiglu": 2, "partial": 3}
 
 
 def interleave_gate_up(weight: torch.Tensor) -> torch.Tensor:
@@ -52,16 +52,36 @@ def interleave_gate_up(weight: torch.Tensor) -> torch.Tensor:
     return torch.stack((gate, up), 1).reshape(2 * inter, -1).contiguous()
 
 
+def pack_linear_weight(weight: torch.Tensor) -> torch.Tensor:
+    """A ``[rows, K]`` weight (rows a multiple of 128, K of 64) in the
+    tile-packed layout ``[rows / 128][K / 64][128][64]`` that
+    ``draft_linear(..., packed=True)`` streams: every 128-row x 64-column
+    block the kernel loads becomes one contiguous 16 KB run, so the weight
+    stream reads whole DRAM pages instead of 128-byte pieces of 128 rows.
+    One launch (``dsb_pack_linear_weight``), done once at load time; the
+    result has the same bytes, reordered."""
+    if weight.ndim != 2 or weight.shape[0] % 128 or weight.shape[1] % 64:
+        raise ValueError("weight must be [rows, K] with rows % 128 == 0 and K % 64 == 0")
+    device = _lib.require_cuda(weight)
+    weight = weight.contiguous()
+    out = torch.empty_like(weight)
+    _lib.call("dsb_pack_linear_weight", _lib.ptr(weight), weight.shape[0], weight.shape[1],
+              _lib.dtype_code(weight.dtype), _lib.ptr(out), _lib.stream_ptr(device))
+    return out
+
+
 def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
                  residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                 prefetch_weight: bool = True) -> torch.Tensor:
+                 prefetch_weight: bool = True, packed: bool = False) -> torch.Tensor:
     """``x [T, K] @ weight.T`` on the tensor cores (``dsb_draft_linear``),
     with ``epilogue`` "plain", "residual" (``+ residual`` before the one
-    rounding) or "swiglu" (``weight`` from :func:`interleave_gate_up`; out
+    rounding), "partial" (the fp32 sums unrounded, ``out`` float32: one
+    rank's share of a row-split linear) or "swiglu" (``weight`` from :func:`interleave_gate_up`; out
     ``[T, rows / 2] = round(round(silu(gate)) * up)`` with gate and up
     rounded first, as vLLM's gate_up output and SiluAndMul round them).  ``prefetch_weight`` starts the
     weight stream before the previous kernel has finished (the weight must
-    not be written by that kernel)."""
+    not be written by that kernel).  ``packed``: ``weight`` comes from
+    :func:`pack_linear_weight` (same shape, tile-packed bytes)."""
     if epilogue not in _EPILOGUES:
         raise ValueError(f"epilogue must be one of {sorted(_EPILOGUES)}")
     if x.ndim != 2 or weight.ndim != 2 or weight.shape[1] != x.shape[1] or x.dtype != weight.dtype:
@@ -76,13 +96,15 @@ def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
         res_stride = _rows(residual, "residual")
     else:
         res_stride = 0
+    out_dtype = torch.float32 if epilogue == "partial" else x.dtype
     if out is None:
-        out = torch.empty((x.shape[0], cols), dtype=x.dtype, device=device)
-    elif out.shape != (x.shape[0], cols) or out.dtype != x.dtype:
+        out = torch.empty((x.shape[0], cols), dtype=out_dtype, device=device)
+    elif out.shape != (x.shape[0], cols) or out.dtype != out_dtype:
         raise ValueError("out has the wrong shape or dtype")
     _lib.call("dsb_draft_linear", _lib.ptr(x), x.shape[0], x.shape[1], _lib.ptr(weight),
               weight.shape[0], _EPILOGUES[epilogue], _lib.ptr(residual), res_stride, _lib.ptr(out),
-              _rows(out, "out"), _lib.dtype_code(x.dtype), 1 if prefetch_weight else 0,
+              _rows(out, "out"), _lib.dtype_code(x.dtype),
+              (1 if prefetch_weight else 0) | (2 if packed else 0),
               _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device))
     return out
 
@@ -103,6 +125,31 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
               _lib.ptr(out), _rows(out, "out"), x.shape[0], x.shape[1], float(eps),
               _lib.dtype_code(x.dtype), _lib.stream_ptr(device))
     return out
+
+
+def add_rms_norm(partial: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor | None,
+                 eps: float, x_out: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None):
+    """``x = round(partial + residual)`` (fp32 ``partial [rows, cols]``, e.g.
+    an all-reduced "partial" linear, one rounding) and, when ``weight`` is
+    given, ``rms_norm(x)`` with :func:`rms_norm`'s arithmetic bit for bit;
+    one launch (``dsb_add_rms_norm``).  Returns ``(x, normed)`` (``normed``
+    None without a weight)."""
+    if partial.dtype != torch.float32 or partial.shape != residual.shape:
+        raise ValueError("partial must be fp32 and shaped like residual")
+    if weight is not None and (weight.shape != (residual.shape[-1],) or weight.dtype != residual.dtype):
+        raise ValueError("weight must be [cols] in the residual's dtype")
+    device = _lib.require_cuda(partial, residual, weight, x_out, out)
+    if x_out is None:
+        x_out = torch.empty_like(residual)
+    if weight is not None and out is None:
+        out = torch.empty_like(residual)
+    _lib.call("dsb_add_rms_norm", _lib.ptr(partial), _rows(partial, "partial"), _lib.ptr(residual),
+              _rows(residual, "residual"), _lib.ptr(weight), _lib.ptr(x_out), _rows(x_out, "x_out"),
+              _lib.ptr(out), _rows(out, "out") if out is not None else 0, residual.shape[0],
+              residual.shape[1], float(eps), _lib.dtype_code(residual.dtype),
+              _lib.stream_ptr(device))
+    return x_out, out
 
 
 def rope_qk(query: torch.Tensor, kv: torch.Tensor, positions: torch.Tensor,
@@ -184,6 +231,12 @@ class Eagle3DraftLayer:
         # the gate/up weight in the tile order of the SwiGLU epilogue (a
         # one-time permutation; w_gate_up keeps the [gate | up] order)
         self.w_gate_up_tiles = interleave_gate_up(self.w_gate_up)
+        # what step() streams: every weight tile-packed once (same bytes,
+        # reordered so each 128 x 64 block the kernel loads is contiguous)
+        self.p_qkv = pack_linear_weight(self.w_qkv)
+        self.p_o = pack_linear_weight(self.w_o)
+        self.p_gate_up = pack_linear_weight(self.w_gate_up_tiles)
+        self.p_down = pack_linear_weight(self.w_down)
         self.in_norm = torch.ones(qkv_in, dtype=dtype, device=device)
         self.post_norm = torch.ones(hidden, dtype=dtype, device=device)
         self.workspace = AttentionWorkspace(device)
@@ -202,12 +255,126 @@ class Eagle3DraftLayer:
         layer output ``[n, hidden]``."""
         n = x_in.shape[0]
         h = rms_norm(x_in, self.in_norm, self.eps)
-        q, kv = qkv_projection_write_raw(h, self.w_qkv, self.hq * self.d, slots, abs_positions,
-                                         raw_key, raw_value, prefetch_weight=True)
+        q, kv = qkv_projection_write_raw(h, self.p_qkv, self.hq * self.d, slots, abs_positions,
+                                         raw_key, raw_value, prefetch_weight=True,
+                                         packed_weight=True)
         k, v = rope_qk(q, kv, local_positions, cos_sin, self.hk, position_offset=position_offset)
         attn = draft_decode_attention(q.view(n, self.hq, self.d), k, v, working_key, working_value,
                                       slots, local_positions, self.d ** -0.5,
                                       position_offset=position_offset, workspace=self.workspace)
-        x = draft_linear(attn.view(n, self.hq * self.d), self.w_o, "residual", residual)
-        act = draft_linear(rms_norm(x, self.post_norm, self.eps), self.w_gate_up_tiles, "swiglu")
-        return draft_linear(act, self.w_down, "residual", x, out=out)
+        x = draft_linear(attn.view(n, self.hq * self.d), self.p_o, "residual", residual,
+                         packed=True)
+        act = draft_linear(rms_norm(x, self.post_norm, self.eps), self.p_gate_up, "swiglu",
+                           packed=True)
+        return draft_linear(act, self.p_down, "residual", x, out=out, packed=True)
+
+
+class Eagle3DraftLayerTP:
+    """One tensor-parallel shard of an :class:`Eagle3DraftLayer` on rank
+    ``rank`` of ``world`` (vLLM's tensor-parallel split of the Eagle3 layer:
+    QKVParallelLinear / MergedColumnParallelLinear column-split,
+    RowParallelLinear row-split):
+
+    * query heads ``[rank * Hq / world, (rank + 1) * Hq / world)`` and the kv
+      heads they read: ``Hk / world`` of them when ``world <= Hk``, else one
+      kv head replicated on ``world / Hk`` ranks;
+    * qkv and gate_up column-split (this rank's heads and ``inter / world``
+      SwiGLU features), o_proj and down_proj row-split;
+    * the row-split linears write fp32 partials ("partial" epilogue), which
+      are all-reduced (``all_reduce``, NCCL by default) and then added to the
+      residual in one rounding with the next RMSNorm fused
+      (:func:`add_rms_norm`), so the rounding points are the single-GPU
+      layer's; only the fp32 summation order of the split differs.
+
+    The shard is cut from ``full``'s weights (so any world size computes the
+    same layer) and packed once.  ``step`` takes the same arguments as
+    :meth:`Eagle3DraftLayer.step` with the raw / working caches holding this
+    rank's kv heads; :meth:`attention_partial`, :meth:`mlp_partial` and
+    :meth:`finish` are its three stages between the two all-reduces."""
+
+    def __init__(self, full: "Eagle3DraftLayer", rank: int, world: int, group=None,
+                 all_reduce=None):
+        hq, hk, d, inter = full.hq, full.hk, full.d, full.inter
+        if world < 1 or hq % world or (inter // world) % 64 or inter % world:
+            raise ValueError("world must divide the query heads and leave the SwiGLU features "
+                             "a multiple of 64 per rank")
+        if world > hk and world % hk:
+            raise ValueError("world must divide, or be a multiple of, the kv heads")
+        self.rank, self.world, self.group = rank, world, group
+        self.hq, self.d, self.eps = hq // world, d, full.eps
+        self.hidden = full.w_o.shape[0]
+        if world <= hk:
+            self.hk = hk // world
+            kv_heads = list(range(rank * self.hk, (rank + 1) * self.hk))
+        else:
+            self.hk = 1
+            kv_heads = [rank // (world // hk)]
+        self.kv_heads = kv_heads
+        q0 = rank * self.hq * d
+        rows_q = full.w_qkv[q0:q0 + self.hq * d]
+        rows_k = torch.cat([full.w_qkv[hq * d + h * d: hq * d + (h + 1) * d] for h in kv_heads])
+        rows_v = torch.cat([full.w_qkv[(hq + hk) * d + h * d: (hq + hk) * d + (h + 1) * d]
+                            for h in kv_heads])
+        self.w_qkv = torch.cat((rows_q, rows_k, rows_v)).contiguous()
+        self.w_o = full.w_o[:, q0:q0 + self.hq * d].contiguous()
+        il = inter // world
+        self.inter = il
+        gate = full.w_gate_up[rank * il:(rank + 1) * il]
+        up = full.w_gate_up[inter + rank * il: inter + (rank + 1) * il]
+        self.w_gate_up = torch.cat((gate, up)).contiguous()
+        self.w_down = full.w_down[:, rank * il:(rank + 1) * il].contiguous()
+        self.p_qkv = pack_linear_weight(self.w_qkv)
+        self.p_o = pack_linear_weight(self.w_o)
+        self.p_gate_up = pack_linear_weight(interleave_gate_up(self.w_gate_up))
+        self.p_down = pack_linear_weight(self.w_down)
+        self.in_norm, self.post_norm = full.in_norm, full.post_norm
+        self.workspace = AttentionWorkspace(full.w_o.device)
+        if all_reduce is None:
+            def all_reduce(t):
+                if world > 1:
+                    torch.distributed.all_reduce(t, group=group)
+        self.all_reduce = all_reduce
+
+    def weight_bytes(self) -> int:
+        return sum(t.numel() * t.element_size()
+                   for t in (self.w_qkv, self.w_o, self.w_gate_up, self.w_down))
+
+    def attention_partial(self, x_in, *, slots, abs_positions, local_positions, raw_key,
+                          raw_value, working_key, working_value, cos_sin, position_offset=0,
+                          partial=None):
+        """RMSNorm, this rank's q/K/V projection with the raw-cache write, RoPE,
+        the draft attention over its heads and its fp32 o_proj partial."""
+        n = x_in.shape[0]
+        h = rms_norm(x_in, self.in_norm, self.eps)
+        q, kv = qkv_projection_write_raw(h, self.p_qkv, self.hq * self.d, slots, abs_positions,
+                                         raw_key, raw_value, prefetch_weight=True,
+                                         packed_weight=True)
+        k, v = rope_qk(q, kv, local_positions, cos_sin, self.hk, position_offset=position_offset)
+        attn = draft_decode_attention(q.view(n, self.hq, self.d), k, v, working_key, working_value,
+                                      slots, local_positions, self.d ** -0.5,
+                                      position_offset=position_offset, workspace=self.workspace)
+        return draft_linear(attn.view(n, self.hq * self.d), self.p_o, "partial", out=partial,
+                            packed=True)
+
+    def mlp_partial(self, o_sum, residual, partial=None):
+        """``x = round(o_sum + residual)``, RMSNorm, this rank's gate_up +
+        SwiGLU and its fp32 down_proj partial; returns ``(x, partial)``."""
+        x, h2 = add_rms_norm(o_sum, residual, self.post_norm, self.eps)
+        act = draft_linear(h2, self.p_gate_up, "swiglu", packed=True)
+        return x, draft_linear(act, self.p_down, "partial", out=partial, packed=True)
+
+    def finish(self, down_sum, x, out=None):
+        """The layer output ``round(down_sum + x)``."""
+        return add_rms_norm(down_sum, x, None, self.eps, x_out=out)[0]
+
+    def step(self, x_in, residual, *, slots, abs_positions, local_positions, raw_key, raw_value,
+             working_key, working_value, cos_sin, out=None, position_offset=0):
+        """One draft step of this shard: two all-reduces of fp32 partials."""
+        po = self.attention_partial(
+            x_in, slots=slots, abs_positions=abs_positions, local_positions=local_positions,
+            raw_key=raw_key, raw_value=raw_value, working_key=working_key,
+            working_value=working_value, cos_sin=cos_sin, position_offset=position_offset)
+        self.all_reduce(po)
+        x, pd = self.mlp_partial(po, residual)
+        self.all_reduce(pd)
+        return self.finish(pd, x, out=out)

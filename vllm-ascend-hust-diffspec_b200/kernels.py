@@ -440,6 +440,7 @@ def qkv_projection_write_raw(
     q_out: torch.Tensor | None = None,
     kv_out: torch.Tensor | None = None,
     prefetch_weight: bool = False,
+    packed_weight: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """The draft layer's query + K/V projection in one launch.
 
@@ -449,7 +450,8 @@ def qkv_projection_write_raw(
     written, pre-RoPE, to the raw caches at ``[slots[t], positions[t]]`` as
     in :func:`kv_projection_write_raw`.  ``prefetch_weight`` lets the weight
     stream start before the previous kernel in the stream has finished (the
-    weight must not be written by that kernel).
+    weight must not be written by that kernel); ``packed_weight``: ``weight``
+    is in the tile-packed layout of ``draft_layer.pack_linear_weight``.
     """
     if hidden.ndim != 2 or weight.ndim != 2 or weight.shape[1] != hidden.shape[1]:
         raise ValueError("hidden must be [T, hidden] and weight [q + 2 * Hk * D, hidden]")
@@ -483,7 +485,8 @@ def qkv_projection_write_raw(
         _lib.ptr(hidden), tokens, hidden.shape[1], _lib.ptr(weight), q_features, hk, d,
         _lib.ptr(slots), _lib.ptr(positions), _lib.ptr(raw_key), _lib.ptr(raw_value), num_slots,
         max_model_len, _lib.dtype_code(hidden.dtype), _lib.ptr(q_out), _lib.ptr(kv_out),
-        1 if prefetch_weight else 0, _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device),
+        (1 if prefetch_weight else 0) | (2 if packed_weight else 0),
+        _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device),
     )
     return q_out, kv_out
 
@@ -498,7 +501,7 @@ def paged_decode_attention_lse(
     scale: float,
     max_seq_len: int,
     table_rows: torch.Tensor | None = None,
-    tokens_per_split: int = 512,
+    tokens_per_split: int = 0,
     out: torch.Tensor | None = None,
     lse: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
@@ -512,7 +515,9 @@ def paged_decode_attention_lse(
     ``table_rows[r]`` (default ``r``).  Returns ``(out [rows, Hq, 128],
     lse [rows, Hq] fp32)``, ``lse`` the natural log of the softmax
     denominator of ``scale * q . k`` — the ``softmax_lse`` that
-    :func:`paged_chunk_attention_scores` takes.
+    :func:`paged_chunk_attention_scores` takes.  ``tokens_per_split`` sets
+    the split-KV length; 0 picks the library's default (1024 tokens when
+    ``max_seq_len >= 16384``, else 512).
     """
     if query.ndim != 3 or key_cache.ndim != 4 or key_cache.shape != value_cache.shape:
         raise ValueError("query must be [rows, Hq, D] and the caches matching [blocks, bs, Hk, D]")
@@ -528,8 +533,8 @@ def paged_decode_attention_lse(
         raise ValueError("table_rows must map every query row")
     if max_seq_len < 0:
         raise ValueError("max_seq_len must be >= 0")
-    if tokens_per_split <= 0:  # the library's default split length
-        tokens_per_split = 512
+    if tokens_per_split <= 0:  # the library's default split length (see the C ABI)
+        tokens_per_split = 0
     device = _lib.require_cuda(query, key_cache, value_cache, block_table, seq_lens, table_rows)
     if out is None:
         out = torch.empty_like(query)
