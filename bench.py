@@ -1152,23 +1152,49 @@ def run_draft_step(args):
     pick, chunk scores over the paged target K, selection) + 4 cycles x (plan +
     rebuild, 4 draft steps through the layer: RMSNorm, query GEMM, K/V
     projection with the raw-cache write, RoPE, draft attention, output GEMM,
-    RMSNorm, SwiGLU MLP).  The
-    LM head is excluded (its vocabulary is unspecified).  Captured as one CUDA
-    graph; prints draft tokens/s."""
+    RMSNorm, SwiGLU MLP).  The LM head is excluded (its vocabulary is
+    unspecified).  Captured as one CUDA graph; prints draft tokens/s.
+
+    Under torchrun (N ranks) the layer is tensor-parallel
+    (Eagle3DraftLayerTP: qkv / gate_up column-split, o_proj / down_proj
+    row-split with two fp32 NCCL all-reduces per step, kv heads replicated
+    when N > 4) and the DiffSpec cache is sharded by kv head (retrieval mass
+    all-gathered before the selection); every rank drafts the same 16
+    requests, so the total work is fixed (strong scaling)."""
     import torch
+    import torch.distributed as dist
 
     dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
-    device = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     ctx = 65536
-    w = Workload(torch, dsb, device, B_GROUP, HK, HQ, seed=555, ctx=ctx)
-    layer = dsb.draft_layer.Eagle3DraftLayer(device, seed=5)
+    hk_local = HK // world if world <= HK else 1
+    rep = 1 if world <= HK else world // HK  # ranks holding each kv head
+    hq_local = HQ // world
+    kv_group = rank // rep  # this rank's kv-head shard
+    w = Workload(torch, dsb, device, B_GROUP, hk_local, hq_local, seed=555 + kv_group, ctx=ctx)
+    full = dsb.draft_layer.Eagle3DraftLayer(device, seed=5)
+    layer = full if world == 1 else dsb.draft_layer.Eagle3DraftLayerTP(full, rank, world)
     g = torch.Generator(device=device).manual_seed(17)
     bf = torch.bfloat16
     x_in = torch.randn((B_GROUP, 4096), generator=g, device=device).to(bf)
     residual = torch.randn((B_GROUP, 2048), generator=g, device=device).to(bf)
-    launches = period_launches(w, window=CHUNK)  # config 5 names no window: the reference's tail
-    retrieval = [(k, fn) for k, fn in launches if k in ("prepare", "scores", "select")]
+    exchange = gathered = None
+    if world > 1:
+        full_gather = torch.empty((world, B_GROUP, hk_local, w.max_chunks), dtype=torch.float32,
+                                  device=device)
+        gathered = full_gather[::rep]  # one replica of every kv head, read in place
+        exchange = lambda parts: dsb.parallel.gather_head_scores(parts, None, out=full_gather)  # noqa: E731
+    launches = period_launches(w, exchange, total_hq=HQ, gathered=gathered, window=CHUNK)
+    retrieval = [(k, fn) for k, fn in launches if k in ("prepare", "scores", "exchange", "select")]
     rebuilds = [fn for k, fn in launches if k == "rebuild"]
     abs_pos = [[(w.committed[c] + j).to(torch.int64) for j in range(DEPTH)] for c in range(INTERVAL)]
     outs = [torch.empty_like(residual) for _ in range(DEPTH)]
@@ -1184,36 +1210,61 @@ def run_draft_step(args):
         seq.append(("rebuild", rebuilds[c]))
         for j in range(DEPTH):
             seq.append(("layer", lambda c=c, j=j: step(c, j)))
+    if world > 1:  # one eager pass sets up the communicators before capture
+        for _, fn in seq:
+            fn()
+        torch.cuda.synchronize(device)
+        dist.barrier()
     graph = Graph(torch, seq, device)
     for _ in range(max(3, args.warmup)):
         graph.replay()
     torch.cuda.synchronize(device)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(args.steps):
-        graph.replay()
-    b.record()
-    torch.cuda.synchronize(device)
-    ms = a.elapsed_time(b) / args.steps
+    if world > 1:
+        dist.barrier()
+
+    def timed(gr):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        a.record()
+        for _ in range(args.steps):
+            gr.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        ms = a.elapsed_time(b) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    ms = timed(graph)
     assert dsb._lib.read_and_clear_error_flag(device) == 0
     steps_only = Graph(torch, [("layer", lambda j=j: step(0, j)) for j in range(DEPTH)], device)
     for _ in range(3):
         steps_only.replay()
+    step_us = timed(steps_only) * 1e3 / DEPTH
+    del graph, steps_only  # graphs holding NCCL work go before the process group
     torch.cuda.synchronize(device)
-    a.record()
-    for _ in range(args.steps):
-        steps_only.replay()
-    b.record()
-    torch.cuda.synchronize(device)
-    step_us = a.elapsed_time(b) * 1e3 / (args.steps * DEPTH)
     tokens = B_GROUP * INTERVAL * DEPTH
-    print(json.dumps(dict(
-        mode="draft_step", metric="draft tokens/s (config 5, one draft layer, LM head excluded)",
-        value=round(tokens / (ms / 1e3), 1), unit="draft tokens/s", ms_per_period=round(ms, 4),
-        draft_tokens_per_period=tokens, layer_step_us=round(step_us, 2),
-        layer_weight_bytes=layer.weight_bytes(), requests=B_GROUP, context=ctx,
-        token_budget=TOKEN_BUDGET, chunk=CHUNK, retrieval_interval=INTERVAL, draft_depth=DEPTH,
-        dtype="bf16", data="synthetic (random weights and KV)")))
+    if rank == 0:
+        print(json.dumps(dict(
+            mode="draft_step", metric="draft tokens/s (config 5, one draft layer, LM head excluded)",
+            value=round(tokens / (ms / 1e3), 1), unit="draft tokens/s", n_gpus=world,
+            scaling="strong" if world > 1 else None, ms_per_period=round(ms, 4),
+            draft_tokens_per_period=tokens, layer_step_us=round(step_us, 2),
+            layer_weight_bytes_per_gpu=layer.weight_bytes(),
+            parallelism=("one GPU" if world == 1 else
+                         f"tensor parallel over {world} GPUs: {hq_local} query heads and "
+                         f"{hk_local} kv head(s) per GPU (each kv head on {rep} GPU(s)), "
+                         "2 fp32 NCCL all-reduces per layer step"),
+            requests=B_GROUP, context=ctx, token_budget=TOKEN_BUDGET, chunk=CHUNK,
+            retrieval_interval=INTERVAL, draft_depth=DEPTH, dtype="bf16",
+            data="synthetic (random weights and KV)")), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_kv_projection(args):

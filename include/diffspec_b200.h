@@ -309,16 +309,20 @@ int dsb_paged_decode_attention_lse(
  * (programmatic dependent launch): the weight must not be written by that
  * kernel.  Activations, residuals and outputs are touched only after it. */
 #define DSB_LINEAR_PREFETCH_WEIGHT 1
-/* The weight is in the tile-packed layout [rows / 128][in_features / 64][128]
- * [64] (row-major [rows, in_features] regrouped so that every 128-row x
- * 64-column block the kernel streams is one contiguous 16 KB run; see
- * dsb_pack_linear_weight), instead of row-major [rows, in_features]. */
+/* The weight is in the tile-packed layout of dsb_pack_linear_weight (every
+ * 128-row x 64-column block the kernel streams is one contiguous 16 KB run,
+ * already in its shared-memory image, staged by one bulk copy) instead of
+ * row-major [rows, in_features]. */
 #define DSB_LINEAR_PACKED_WEIGHT 2
 
 /* Copy a row-major [rows, cols] weight (rows a multiple of 128, cols of 64;
  * BF16 or FP16, 16-byte aligned) into the tile-packed layout the linear
- * entry points read with DSB_LINEAR_PACKED_WEIGHT: out[m][kb][r][c] =
- * weight[128 m + r][64 kb + c].  A one-time, load-time step (no counterpart
+ * entry points read with DSB_LINEAR_PACKED_WEIGHT: block (m, kb) of 128 x 64
+ * elements is stored contiguously at block index m * (cols / 64) + kb, row r
+ * of it at 128 r bytes, its 16-byte piece p (elements 8 p .. 8 p + 7 of
+ * weight[128 m + r][64 kb ..]) at piece position p ^ (r % 8) (the 128-byte
+ * swizzle of the tensor cores' shared-memory operand layout).  A one-time,
+ * load-time step (no counterpart
  * in the reference, whose projections are vLLM linear layers); out must not
  * alias weight.  The copy completes before the next kernel in the stream
  * starts, so a linear launch with DSB_LINEAR_PREFETCH_WEIGHT may follow it

@@ -1,4 +1,4 @@
-"""BASELINE configs 3 and 4 at their full sizes (rows A1-A8, e).
+"""BASELINE config 2's retrieval batch and configs 3 and 4 at their full sizes (rows A1-A8, e).
 
 At these sizes the oracle cannot score every row, so the tests combine
 size-independent properties over all rows with oracle checks of sampled
@@ -100,6 +100,72 @@ def test_config4_retrieval_identical_at_any_head_shard_count(dsb, cuda):
                                          t_row, np.array([length - 2]), c, length, d ** -0.5)
     got = dsb.kernels.finalize_chunk_scores(full[:1], seq[:1], chunk_size=c, total_query_heads=hq)
     np.testing.assert_allclose(got.cpu().numpy(), ref, rtol=1e-3, atol=1e-9)
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+
+
+def test_config2_batch_selection_and_plans(dsb, cuda):
+    """Config 2's whole retrieval batch as the bench runs it: 16 requests x
+    40960 tokens (3 rejected, 40957 scored), 32 / 4 heads, chunk 64, budget
+    2048 (history 1984), rolling window 256, 8 planted chunks per request,
+    the LSE computed on the device (softmax_lse=None).  Every row is scored
+    by the fp64 oracle: the GPU scores match it, the selection equals the
+    oracle's selection of the GPU's own scores on every row and the oracle's
+    selection of its fp64 scores wherever the boundary gap exceeds fp32
+    rounding, the planted chunks are selected, and the plans of four cycles
+    (two accepted tokens each) equal the oracle's plan rows bit for bit."""
+    b, length, hq, hk, d, bs, c, hb, win = 16, 40960, 32, 4, 128, 16, 64, 1984, 256
+    seq_len = length - 3
+    n = (seq_len + c - 1) // c
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(22)
+    kc, table = _paged_keys(gen, [length] * b, hk, d, bs, cuda)
+    q = torch.randn((b, hq, d), generator=gen, device=cuda).to(torch.bfloat16)
+    planted = []
+    for r in range(b):  # keys = group-mean query + noise
+        chunks = torch.randperm(n - win // c, generator=gen, device=cuda)[:8]
+        planted.append(sorted(chunks.tolist()))
+        tok = (chunks[:, None] * c + torch.arange(c, device=cuda)).reshape(-1)
+        target = q[r].float().view(hk, hq // hk, d).mean(1)
+        noise = 0.1 * torch.randn((tok.numel(), hk, d), generator=gen, device=cuda)
+        kc[table[r, tok // bs].long(), tok % bs] = (target + noise).to(torch.bfloat16)
+    seq = torch.full((b,), seq_len, dtype=torch.int32, device=cuda)
+    kw = dict(chunk_size=c, max_seq_len=length, scale=d ** -0.5)
+    parts = dsb.kernels.paged_chunk_head_scores(q, kc, None, table, seq, **kw)
+    scores = dsb.kernels.finalize_chunk_scores(parts, seq, chunk_size=c,
+                                               total_query_heads=hq).cpu().numpy()
+    slots = torch.arange(b, dtype=torch.int32, device=cuda)
+    sel_chunks = torch.zeros((b, hb // c), dtype=torch.int32, device=cuda)
+    sel_count = torch.full((b,), -1, dtype=torch.int32, device=cuda)
+    ci = dsb.selection.select_rows(parts, seq, chunk_size=c, token_budget=hb, normalize_heads=hq,
+                                   row_slots=slots, sel_chunks=sel_chunks, sel_count=sel_count,
+                                   with_outputs=True, recent_window=win)[0].cpu().numpy()
+    certified = 0
+    for r in range(b):
+        keys, t_row = _row_to_host(kc, table, r, length, bs)
+        oracle = O.paged_chunk_attention_scores(q[r:r + 1].float().cpu().numpy(), keys, None, t_row,
+                                                np.array([seq_len]), c, length, d ** -0.5)[0]
+        np.testing.assert_allclose(scores[r, :n], oracle[:n], rtol=1e-3, atol=1e-9)
+        own = O.select_context_chunks(scores[r, :n], seq_len, c, hb, recent_window=win)[0]
+        got = ci[r][ci[r] >= 0]
+        np.testing.assert_array_equal(got, own)
+        if O.selection_margin(oracle[:n], seq_len, c, hb, recent_window=win) > 1e-5:
+            certified += 1
+            np.testing.assert_array_equal(
+                got, O.select_context_chunks(oracle[:n], seq_len, c, hb, recent_window=win)[0])
+        assert set(planted[r]) <= set(got.tolist())
+    assert certified >= b // 2  # most rows have a clear top-k boundary
+    chosen = [sel_chunks[r, : int(sel_count[r])].cpu().tolist() for r in range(b)]
+    for cycle in range(4):
+        committed = torch.full((b,), seq_len + 1 + 2 * cycle, dtype=torch.int32, device=cuda)
+        plan, hl = dsb.selection.build_history_plan(
+            slots, committed, sel_chunks, sel_count, chunk_size=c, history_budget=hb,
+            working_budget=2048, recent_window=win)
+        plan = plan.cpu().numpy()
+        for r in range(b):
+            expect = O.history_plan(r, chosen[r], int(committed[r]) - 1, c, hb, recent_window=win)
+            assert plan[r, : len(expect)].tolist() == expect
+            assert (plan[r, len(expect):] == 0).all()
+            assert int(hl[r]) == expect[1]
     assert dsb._lib.read_and_clear_error_flag(cuda) == 0
 
 

@@ -221,8 +221,11 @@ def test_packed_weight_is_bit_identical(dsb, cuda, rows, k):
     x = torch.randn((16, k), generator=g, device=cuda).bfloat16()
     res = torch.randn((16, rows), generator=g, device=cuda).bfloat16()
     wp = dl.pack_linear_weight(w)
-    assert torch.equal(wp.view(rows // 128, k // 64, 128, 64),
-                       w.view(rows // 128, 128, k // 64, 64).permute(0, 2, 1, 3))
+    blocks = w.view(rows // 128, 128, k // 64, 8, 8).permute(0, 2, 1, 3, 4)  # [m, kb, r, p, 8]
+    swz = (torch.arange(8, device=cuda)[None, :] ^ torch.arange(128, device=cuda)[:, None] % 8)
+    expect = torch.empty_like(blocks)
+    expect[:, :, torch.arange(128, device=cuda)[:, None], swz] = blocks  # piece p at p ^ (r % 8)
+    assert torch.equal(wp.view(rows // 128, k // 64, 128, 8, 8), expect)
     for epi in ("plain", "residual"):
         r = res if epi == "residual" else None
         assert torch.equal(dl.draft_linear(x, w, epi, residual=r),

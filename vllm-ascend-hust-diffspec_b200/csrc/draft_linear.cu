@@ -74,6 +74,7 @@ struct LnArgs {
   int mode;
   int prefetch;
   int packed;  // weight in the tile-packed layout (DSB_LINEAR_PACKED_WEIGHT)
+  const void *wpacked;  // that weight's base (bulk-copied block by block)
   const int32_t *slots;
   const int64_t *positions;
   void *raw_k, *raw_v;
@@ -120,15 +121,22 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   const int per = (nkb_all + RANKS - 1) / RANKS;
   const int kb0 = rank * per;
   const int nkb = max(0, min(per, nkb_all - kb0));
-  // Weight box of k-block kb: row-major [N, K] -> (x = 64 kb, y = f0); tile-
-  // packed [N/128][K/64][128][64] -> the contiguous 16 KB block
-  // (x = 0, y = 128 * (tile * K/64 + kb)).
-  auto wx = [&](int kb) { return a.packed ? 0 : kb * 64; };
-  auto wy = [&](int kb) { return a.packed ? (blockIdx.y * nkb_all + kb) * 128 : f0; };
   const int first = min(nkb, S);
   // weights are streamed once per step: evicted first, so the working cache
   // the draft attention re-reads keeps its L2 lines
   const uint64_t wpol = l2_evict_first();
+  // Weight block of k-block kb into slot `dst`: row-major [N, K] by a 2-D
+  // TMA box (x = 64 kb, y = f0, swizzled on the way in); tile-packed (the
+  // block already in its swizzled shared-memory image, contiguous) by one
+  // 1-D bulk copy of 16 KB.
+  const uint8_t *wpacked = static_cast<const uint8_t *>(a.wpacked);
+  auto load_w = [&](uint32_t dst, int kb, uint32_t bar) {
+    if (a.packed)
+      bulk_load(dst, wpacked + ((int64_t)blockIdx.y * nkb_all + kb) * kLnABytes, kLnABytes, bar,
+                wpol);
+    else
+      tma_load_2d_hint(dst, &tw, kb * 64, f0, bar, wpol);
+  };
 
   // No activations yet: descriptor prefetch, barriers, tensor memory and
   // (when allowed) the first weight tiles overlap the previous kernel.
@@ -143,8 +151,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     if (a.prefetch)
       for (int kb = 0; kb < first; ++kb) {
         mbar_expect_tx(full0 + 8 * kb, kLnABytes + kLnBBytes);
-        tma_load_2d_hint(s_a + kb * kLnABytes, &tw, wx(kb0 + kb), wy(kb0 + kb), full0 + 8 * kb,
-                         wpol);
+        load_w(s_a + kb * kLnABytes, kb0 + kb, full0 + 8 * kb);
       }
   }
   if (warp == 0) {
@@ -173,7 +180,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
       }
       if (!(a.prefetch && kb < first)) {
         mbar_expect_tx(full0 + 8 * s, kLnABytes + kLnBBytes);
-        tma_load_2d_hint(s_a + s * kLnABytes, &tw, wx(kb0 + kb), wy(kb0 + kb), full0 + 8 * s, wpol);
+        load_w(s_a + s * kLnABytes, kb0 + kb, full0 + 8 * s);
       }
       tma_load_2d(s_b + s * kLnBBytes, &tx, (kb0 + kb) * 64, t0, full0 + 8 * s);
     }
@@ -380,8 +387,9 @@ template <typename T> int pick_ranks(const LnArgs &a) {
 template <typename T>
 int launch_linear(const void *x, const void *weight, const LnArgs &a, int dtype, cudaStream_t st) {
   CUtensorMap tw, tx;
-  // packed: the weight viewed as [N * K / 64, 64] rows of 128 bytes
-  const bool wmap = a.packed ? encode_kv_map(&tw, weight, (int64_t)a.N * (a.K / 64), 64, dtype, 128)
+  // packed weights are bulk-copied (the map is unused; encoded over the
+  // first block so the launch argument stays valid)
+  const bool wmap = a.packed ? encode_kv_map(&tw, weight, 128, 64, dtype, 128)
                              : encode_kv_map(&tw, weight, a.N, a.K, dtype, 128);
   if (!wmap ||
       !encode_kv_map(&tx, x, a.T, a.K, dtype, kLnTok))
@@ -419,8 +427,11 @@ int dispatch(const void *x, const void *weight, const LnArgs &a, int32_t dtype, 
                            : launch_linear<__half>(x, weight, a, dtype, st);
 }
 
-// out[m][kb][r][0..63] = weight[128 m + r][64 kb .. 64 kb + 63]: one thread
-// per 16-byte piece (8 elements), reads and writes coalesced along kb / r.
+// out[m][kb][r][...] = weight[128 m + r][64 kb .. 64 kb + 63] with the
+// 16-byte pieces of row r in the 128-byte-swizzle order (piece p stored at
+// p ^ (r % 8)), i.e. each 16 KB block is byte for byte the shared-memory
+// image a 2-D TMA load with CU_TENSOR_MAP_SWIZZLE_128B would produce, so one
+// 1-D bulk copy stages it.  One thread per 16-byte piece.
 // Launched without programmatic dependent launch and never releasing its
 // dependents early: the next kernel in the stream may be a linear that
 // requests this very weight before its own dependency wait, so it must not
@@ -436,7 +447,8 @@ __global__ void pack_weight_kernel(const T *__restrict__ w, int64_t rows, int co
     const int rem = (int)(i % (128 * 8)), r = rem / 8, p = rem % 8;
     const int64_t m = blk / nkb, kb = blk % nkb;
     const int64_t src = (m * 128 + r) * cols + kb * 64 + p * 8;
-    *reinterpret_cast<uint4 *>(out + i * 8) = *reinterpret_cast<const uint4 *>(w + src);
+    const int64_t dst = (blk * 128 + r) * 64 + (int64_t)(p ^ (r & 7)) * 8;
+    *reinterpret_cast<uint4 *>(out + dst) = *reinterpret_cast<const uint4 *>(w + src);
   }
 }
 
@@ -473,6 +485,7 @@ extern "C" int dsb_qkv_projection_write_raw(
   a.mode = kPlain;
   a.prefetch = (flags & DSB_LINEAR_PREFETCH_WEIGHT) != 0;
   a.packed = (flags & DSB_LINEAR_PACKED_WEIGHT) != 0;
+  a.wpacked = weight;
   a.slots = slots;
   a.positions = positions;
   a.raw_k = raw_key;
@@ -527,6 +540,7 @@ extern "C" int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_featur
                                              : kPartialF32;
   a.prefetch = (flags & DSB_LINEAR_PREFETCH_WEIGHT) != 0;
   a.packed = (flags & DSB_LINEAR_PACKED_WEIGHT) != 0;
+  a.wpacked = weight;
   a.T = tokens;
   a.K = in_features;
   a.N = weight_rows;

@@ -54,12 +54,12 @@ def interleave_gate_up(weight: torch.Tensor) -> torch.Tensor:
 
 def pack_linear_weight(weight: torch.Tensor) -> torch.Tensor:
     """A ``[rows, K]`` weight (rows a multiple of 128, K of 64) in the
-    tile-packed layout ``[rows / 128][K / 64][128][64]`` that
-    ``draft_linear(..., packed=True)`` streams: every 128-row x 64-column
-    block the kernel loads becomes one contiguous 16 KB run, so the weight
-    stream reads whole DRAM pages instead of 128-byte pieces of 128 rows.
-    One launch (``dsb_pack_linear_weight``), done once at load time; the
-    result has the same bytes, reordered."""
+    tile-packed layout that ``draft_linear(..., packed=True)`` streams: every
+    128-row x 64-column block the kernel loads becomes one contiguous 16 KB
+    run in the 128-byte-swizzled order of the tensor cores' shared-memory
+    operand (row r's 16-byte piece p at position p ^ (r % 8)), so the kernel
+    stages it with one bulk copy.  One launch (``dsb_pack_linear_weight``),
+    done once at load time; the result has the same bytes, reordered."""
     if weight.ndim != 2 or weight.shape[0] % 128 or weight.shape[1] % 64:
         raise ValueError("weight must be [rows, K] with rows % 128 == 0 and K % 64 == 0")
     device = _lib.require_cuda(weight)
