@@ -1155,12 +1155,14 @@ def run_draft_step(args):
     RMSNorm, SwiGLU MLP).  The LM head is excluded (its vocabulary is
     unspecified).  Captured as one CUDA graph; prints draft tokens/s.
 
-    Under torchrun (N ranks) the layer is tensor-parallel
-    (Eagle3DraftLayerTP: qkv / gate_up column-split, o_proj / down_proj
-    row-split with two fp32 NCCL all-reduces per step, kv heads replicated
-    when N > 4) and the DiffSpec cache is sharded by kv head (retrieval mass
-    all-gathered before the selection); every rank drafts the same 16
-    requests, so the total work is fixed (strong scaling)."""
+    Under torchrun (N ranks), --draft-parallel tp (default): the layer is
+    tensor-parallel (Eagle3DraftLayerTP: qkv / gate_up column-split, o_proj /
+    down_proj row-split with two fp32 NCCL all-reduces per step, kv heads
+    replicated when N > 4) and the DiffSpec cache is sharded by kv head
+    (retrieval mass all-gathered before the selection); every rank drafts
+    the same 16 requests, so the total work is fixed (strong scaling).
+    --draft-parallel dp: every rank drafts its own 16 requests with the
+    whole layer and the whole cache (weak scaling, no collective)."""
     import torch
     import torch.distributed as dist
 
@@ -1176,19 +1178,23 @@ def run_draft_step(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     ctx = 65536
-    hk_local = HK // world if world <= HK else 1
-    rep = 1 if world <= HK else world // HK  # ranks holding each kv head
-    hq_local = HQ // world
-    kv_group = rank // rep  # this rank's kv-head shard
+    tp = world > 1 and args.draft_parallel == "tp"
+    if tp:
+        hk_local = HK // world if world <= HK else 1
+        rep = 1 if world <= HK else world // HK  # ranks holding each kv head
+        hq_local = HQ // world
+        kv_group = rank // rep  # this rank's kv-head shard
+    else:  # one GPU, or data parallel: every rank drafts its own 16 requests
+        hk_local, rep, hq_local, kv_group = HK, 1, HQ, rank
     w = Workload(torch, dsb, device, B_GROUP, hk_local, hq_local, seed=555 + kv_group, ctx=ctx)
     full = dsb.draft_layer.Eagle3DraftLayer(device, seed=5)
-    layer = full if world == 1 else dsb.draft_layer.Eagle3DraftLayerTP(full, rank, world)
+    layer = dsb.draft_layer.Eagle3DraftLayerTP(full, rank, world) if tp else full
     g = torch.Generator(device=device).manual_seed(17)
     bf = torch.bfloat16
     x_in = torch.randn((B_GROUP, 4096), generator=g, device=device).to(bf)
     residual = torch.randn((B_GROUP, 2048), generator=g, device=device).to(bf)
     exchange = gathered = None
-    if world > 1:
+    if tp:
         full_gather = torch.empty((world, B_GROUP, hk_local, w.max_chunks), dtype=torch.float32,
                                   device=device)
         gathered = full_gather[::rep]  # one replica of every kv head, read in place
@@ -1247,19 +1253,22 @@ def run_draft_step(args):
     step_us = timed(steps_only) * 1e3 / DEPTH
     del graph, steps_only  # graphs holding NCCL work go before the process group
     torch.cuda.synchronize(device)
-    tokens = B_GROUP * INTERVAL * DEPTH
+    tokens = B_GROUP * INTERVAL * DEPTH * (1 if tp else world)  # whole job, per period
     if rank == 0:
         print(json.dumps(dict(
             mode="draft_step", metric="draft tokens/s (config 5, one draft layer, LM head excluded)",
             value=round(tokens / (ms / 1e3), 1), unit="draft tokens/s", n_gpus=world,
-            scaling="strong" if world > 1 else None, ms_per_period=round(ms, 4),
+            scaling=("strong" if tp else "weak") if world > 1 else None,
+            ms_per_period=round(ms, 4),
             draft_tokens_per_period=tokens, layer_step_us=round(step_us, 2),
             layer_weight_bytes_per_gpu=layer.weight_bytes(),
             parallelism=("one GPU" if world == 1 else
                          f"tensor parallel over {world} GPUs: {hq_local} query heads and "
                          f"{hk_local} kv head(s) per GPU (each kv head on {rep} GPU(s)), "
-                         "2 fp32 NCCL all-reduces per layer step"),
-            requests=B_GROUP, context=ctx, token_budget=TOKEN_BUDGET, chunk=CHUNK,
+                         "2 fp32 NCCL all-reduces per layer step" if tp else
+                         f"data parallel over {world} GPUs: every GPU drafts its own 16 "
+                         "requests with the whole layer (no per-step collective)"),
+            requests=B_GROUP * (1 if tp else world), context=ctx, token_budget=TOKEN_BUDGET, chunk=CHUNK,
             retrieval_interval=INTERVAL, draft_depth=DEPTH, dtype="bf16",
             data="synthetic (random weights and KV)")), flush=True)
     if world > 1:
@@ -1608,6 +1617,9 @@ def main():
                    help="time the K/V projection + raw-cache write (config 5 decode step)")
     p.add_argument("--draft-step", action="store_true",
                    help="config 5: draft tokens/s of a draft layer over the DiffSpec cache")
+    p.add_argument("--draft-parallel", choices=["tp", "dp"], default="tp",
+                   help="--draft-step under torchrun: tensor parallel (one 16-request batch "
+                        "over all GPUs) or data parallel (16 requests per GPU)")
     p.add_argument("--draft-linear", action="store_true",
                    help="time the config-5 draft layer's four linears against cuBLAS")
     p.add_argument("--target-attention", action="store_true",
