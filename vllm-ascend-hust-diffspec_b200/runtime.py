@@ -839,9 +839,11 @@ class DraftPeriodGraph:
     Inputs are written by the caller into pinned host buffers (``inputs``):
     per cycle the verify pass's query rows, LSE, accepted counts, query ends,
     target lengths and the committed lengths, and per draft step its q/k/v.
-    The graph copies each block to the device on a side stream just before
-    the kernels that read it (the copies of later cycles run while earlier
-    cycles compute) and copies every step's attention output back into
+    The graph copies the inputs to the device on a side stream in the order
+    the period consumes them, as one copy for the first verify block (it
+    gates the retrieval) and one per cycle for the rest (the copies of later
+    cycles run while earlier cycles compute), and copies every step's
+    attention output back into
     ``outputs`` on a second side stream as soon as that step is done.  After
     :meth:`replay` returns, the caller synchronizes (or waits on
     :attr:`done`) before reading ``outputs`` or rewriting ``inputs``.
@@ -908,14 +910,22 @@ class DraftPeriodGraph:
                        "step": [[None] * self.depth for _ in range(self.interval)]}
         self._dev = {"verify": [None] * self.interval,
                      "step": [[None] * self.depth for _ in range(self.interval)]}
-        self._blocks = []  # (kind, c, j, start, end) in copy order
+        # Copies, in order: the first verify block (it gates the retrieval),
+        # then one contiguous range per cycle ending with its last step block.
+        self._copies = []  # (key, start, end)
         for kind, c, j, block, start, end in layout:
             hv, dv = views(self._host_in, block), views(self._dev_in, block)
             if kind == "verify":
                 self.inputs["verify"][c], self._dev["verify"][c] = hv, dv
+                if c == 0:
+                    self._copies.append(("retrieve", start, end))
+                    cycle_start = end
+                else:
+                    cycle_start = start
             else:
                 self.inputs["step"][c][j], self._dev["step"][c][j] = hv, dv
-            self._blocks.append((kind, c, j, start, end))
+                if j == self.depth - 1:
+                    self._copies.append((c, cycle_start, end))
         self.outputs = torch.zeros((self.interval, self.depth, n, hq, d), dtype=dt).pin_memory()
         self._dev_out = torch.zeros((self.interval, self.depth, n, hq, d), dtype=dt, device=dev)
         self.h2d_bytes = int(total)
@@ -936,27 +946,30 @@ class DraftPeriodGraph:
         ready = {}
         h2d.wait_stream(main)
         with torch.cuda.stream(h2d):
-            for kind, c, j, start, end in self._blocks:
+            for key, start, end in self._copies:
                 self._dev_in[start:end].copy_(self._host_in[start:end], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(h2d)
-                ready[(kind, c, j)] = ev
+                ready[key] = ev
         d2h.wait_stream(main)
         with torch.cuda.stream(main):
             v0 = self._dev["verify"][0]
-            main.wait_event(ready[("verify", 0, None)])
+            main.wait_event(ready["retrieve"])
             cache.set_active_requests(self.request_ids)
             cache.retrieve_device(v0["query"], v0["lse"], self.key_cache, self.block_tables,
                                   v0["query_ends"], v0["seq_lens"], self.max_seq_len,
                                   v0["counts"], self.scale)
             for c in range(self.interval):
-                if c:
-                    main.wait_event(ready[("verify", c, None)])
+                # One wait per cycle, for the copy that holds its verify
+                # block and every step's q/k/v: the kernels of the cycle then
+                # follow one another with no copy dependency in between
+                # (which would also cut the programmatic launch overlap
+                # between them).
+                main.wait_event(ready[c])
                 cache.begin_cycle(self.request_ids)
                 cache.rebuild(self._dev["verify"][c]["committed"])
                 for j in range(self.depth):
                     st = self._dev["step"][c][j]
-                    main.wait_event(ready[("step", c, j)])
                     cache.forward_attention(st["q"], st["k"], st["v"], self.scale,
                                             self._dev_out[c, j])
                     out_ready = torch.cuda.Event()
