@@ -463,6 +463,37 @@ int dsb_capture_raw_kv(
     int32_t working_budget, void *local_positions, int32_t *working_lens, int32_t *error_flag,
     void *stream);
 
+/* Request slots on the device (set_active_requests, diffspec/runtime.py:
+ * 755-778).  slot_keys[num_slots] is the slot table, kept on the device
+ * between calls: the key of the request owning each slot, negative when the
+ * slot is free (initialise it to -1).  request_keys[num_requests] are the
+ * batch's requests in batch order, as non-negative keys that identify a
+ * request for as long as it lives (the host interns its request ids).  One
+ * launch (one CTA):
+ *   1. releases every slot whose key is not in the batch: the key becomes -1,
+ *      sel_count[slot] = -1 and working_lens[slot] = 0 (either may be NULL);
+ *   2. gives every key new to the table the lowest free slot, in batch order
+ *      of its first occurrence (a duplicated key shares its slot);
+ *   3. writes active_slots[i], the slot of request i (-1 for a request left
+ *      without one).
+ * A key already in the table keeps its slot.  If more new keys arrive than
+ * there are free slots, those that fit in batch order are assigned and
+ * status[0] = how many were left without one (the reference raises at the
+ * first, after the same releases and assignments); status[1] = free slots
+ * after the call (status may be NULL).  A negative request key sets
+ * DSB_FLAG_SLOT and gets slot -1.  num_slots and num_requests at most 4096. */
+int dsb_assign_request_slots(int64_t *slot_keys, int32_t num_slots,
+                             const int64_t *request_keys, int32_t num_requests,
+                             int32_t *active_slots, int32_t *sel_count, int32_t *working_lens,
+                             int32_t *status, int32_t *error_flag, void *stream);
+
+/* slots[i] = active_slots[rows[i]] for i < n: the canonical slot of each
+ * token of a pass from its batch row (the token -> slot map of
+ * populate_prefill, diffspec/runtime.py:1336-1347).  A row outside
+ * [0, num_active) gives slot -1 (no cache row) and sets DSB_FLAG_SLOT. */
+int dsb_rows_to_slots(const int32_t *active_slots, int32_t num_active, const int32_t *rows,
+                      int32_t n, int32_t *slots, int32_t *error_flag, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -45,6 +45,7 @@ __all__ = [
     "request_rows",
     "capture_raw_kv",
     "selection_margin",
+    "SlotTable",
 ]
 
 
@@ -432,6 +433,41 @@ def prepare_retrieval_rows(query_ends, target_seq_lens, counts, active_slots):
             r_slot.append(-1)
         start = end
     return q_index, r_len, r_slot
+
+
+# ------------------------------------------------------- (f) request slots
+class SlotTable:
+    """Canonical request slots (set_active_requests, diffspec/runtime.py:
+    755-778): a request keeps its slot while it stays in the batch; the slots
+    of requests that left are released first (their working length becomes
+    0 and their selection is dropped); each request new to the table then
+    takes the lowest free slot, in batch order; when none is left the call
+    raises RuntimeError, after those releases and the assignments before it,
+    leaving ``active`` as it was."""
+
+    def __init__(self, num_slots: int):
+        self.num_slots = num_slots
+        self.slots: dict[str, int] = {}
+        self.active: list[int] = []
+        self.working_lens = [0] * num_slots
+        self.selected: set[int] = set()
+
+    def set_active_requests(self, request_ids) -> None:
+        keep = set(request_ids)
+        for rid in list(self.slots):
+            if rid not in keep:
+                slot = self.slots.pop(rid)
+                self.selected.discard(slot)
+                self.working_lens[slot] = 0
+        used = set(self.slots.values())
+        free = iter(sorted(set(range(self.num_slots)) - used))
+        for rid in request_ids:
+            if rid not in self.slots:
+                nxt = next(free, None)
+                if nxt is None:
+                    raise RuntimeError("DiffSpec canonical request slots are exhausted")
+                self.slots[rid] = nxt
+        self.active = [self.slots[r] for r in request_ids]
 
 
 # ------------------------------------------------------- A9: raw write

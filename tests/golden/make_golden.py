@@ -424,9 +424,43 @@ def make_capture() -> dict:
     return out
 
 
+# ------------------------------------------------------------- request slots
+def make_slots() -> dict:
+    """set_active_requests over recipes.SLOT_STEPS on the reference's cache:
+    before each call every slot in use gets a working length and a
+    selection; after it, the active slots (unchanged when the call raised),
+    whether it raised, the working lengths and which slots keep a
+    selection."""
+    cache = ref_rt.DiffSpecDraftCache(
+        ref_rt.DiffSpecSettings(8, 64, 1, 4, 3, 0.7, False), max_num_reqs=R.SLOT_COUNT,
+        max_model_len=32, num_kv_heads=1, head_dim=64, target_num_layers=2,
+        dtype=torch.float32, device=torch.device("cpu"),
+        rotary_embedding=Rotary(64, 64, True, torch.zeros((64, 64))),
+    )
+    out = {"n": np.array(len(R.SLOT_STEPS))}
+    for i, batch in enumerate(R.SLOT_STEPS):
+        for slot in cache._request_slots.values():
+            cache._working_lens[slot] = 100 + 10 * i + slot
+            cache._selected_token_indices[slot] = torch.zeros(1, dtype=torch.long)
+        raised = 0
+        try:
+            cache.set_active_requests(list(batch))
+        except RuntimeError as error:
+            assert "exhausted" in str(error)
+            raised = 1
+        out[f"active{i}"] = np.array(cache._active_slots, np.int64)
+        out[f"raised{i}"] = np.array(raised)
+        out[f"working_lens{i}"] = np.array(cache._working_lens, np.int64)
+        sel = np.zeros(R.SLOT_COUNT, np.int64)
+        sel[list(cache._selected_token_indices)] = 1
+        out[f"selected{i}"] = sel
+    return out
+
+
 FIXTURES = (("scores", "make_scores"), ("select", "make_select"), ("plans", "make_plans"),
             ("rebuild", "make_rebuild"), ("gather", "make_gather"), ("attention", "make_attention"),
-            ("hook", "make_hook"), ("config1", "make_config1"), ("capture", "make_capture"))
+            ("hook", "make_hook"), ("config1", "make_config1"), ("capture", "make_capture"),
+            ("slots", "make_slots"))
 
 
 def main() -> None:

@@ -254,3 +254,25 @@ def capture_inputs() -> dict:
                 query_ends=np.cumsum(c["prompts"]).astype(np.int64), steps=steps,
                 mid_scores=g.random(n_mid, dtype=np.float32),
                 cos_sin=round_to(cos_sin_table(c["budget"], d), "bf16"))
+
+
+# ---------------------------------------------------------- request slots (f)
+# Batches passed to set_active_requests one after another on a 6-slot cache:
+# a reorder, cancellations, a released id that comes back (a new request), a
+# duplicated id, a batch of more distinct requests than slots (exhausted:
+# releases and the first assignments happen, then the call raises), the
+# batch after it, an empty batch and a fresh start.  Before every call each
+# slot in use gets working length 100 + 10 * step + slot and a selection, so
+# the fixture shows which slots the call released.
+SLOT_COUNT = 6
+SLOT_STEPS = (
+    ("a", "b", "c"),
+    ("c", "a", "b"),
+    ("c", "d", "b"),
+    ("e", "f", "d", "g"),
+    ("a", "e", "e", "h", "i"),
+    ("j", "k", "l", "m", "n", "o", "p"),
+    ("k", "j"),
+    (),
+    ("q", "r", "q"),
+)

@@ -61,6 +61,17 @@ def test_invalid_arguments_fail_before_any_launch(dsb):
     assert st == dsb._lib.DSB_ERR_UNSUPPORTED
     # empty work is a no-op success
     assert lib.dsb_write_raw_kv(None, None, None, None, None, None, 0, 1, 1, 1, 8, 0, None, None) == 0
+    # request slots: table size in [1, 4096], requests in [0, 4096], a table
+    assert lib.dsb_assign_request_slots(fake, 0, fake, 1, fake, None, None, None, None,
+                                        None) == dsb._lib.DSB_ERR_INVALID
+    assert lib.dsb_assign_request_slots(fake, 4097, fake, 1, fake, None, None, None, None,
+                                        None) == dsb._lib.DSB_ERR_INVALID
+    assert lib.dsb_assign_request_slots(fake, 8, fake, 5000, fake, None, None, None, None,
+                                        None) == dsb._lib.DSB_ERR_INVALID
+    assert lib.dsb_assign_request_slots(None, 8, fake, 1, fake, None, None, None, None,
+                                        None) == dsb._lib.DSB_ERR_INVALID
+    assert lib.dsb_rows_to_slots(fake, 1, fake, -1, fake, None, None) == dsb._lib.DSB_ERR_INVALID
+    assert lib.dsb_rows_to_slots(None, 1, None, 0, None, None, None) == 0
 
 
 def test_split_and_scratch_helpers(dsb):

@@ -146,12 +146,13 @@ def test_capture_cycle_vs_reference(dsb, cuda):
     ids = ["c", "a", "b"]
     cache.set_active_requests(["x", "a", "b", "c"])
     cache.set_active_requests(ids)
-    assert cache._active_slots == d["active_slots"].tolist()
+    slots = cache.active_slots()
+    assert slots == d["active_slots"].tolist()
     cache.populate_prefill(torch.from_numpy(inp["prefill_positions"]).to(cuda),
                            _bf(inp["prefill_key"], cuda), _bf(inp["prefill_value"], cuda),
                            SimpleNamespace(actual_seq_lengths_q=inp["query_ends"].tolist()))
     prompts = list(c["prompts"])
-    sel = cache.set_chunk_scores(cache._active_slots[1], torch.from_numpy(inp["mid_scores"]).to(cuda),
+    sel = cache.set_chunk_scores(slots[1], torch.from_numpy(inp["mid_scores"]).to(cuda),
                                  prompts[1])
     np.testing.assert_array_equal(sel.chunk_indices.cpu().numpy(), d["mid_chunks"])
     cache.begin_cycle(ids)
@@ -162,7 +163,7 @@ def test_capture_cycle_vs_reference(dsb, cuda):
     # the oracle over the GPU's bf16 working cache, rebuilt from the reference's fp32 one
     ok = np.zeros_like(d["working_key"])
     ov = np.zeros_like(ok)
-    for slot in cache._active_slots:
+    for slot in slots:
         h0 = int(d["working_lens"][slot]) - c["depth"]  # the plan's history length
         ok[slot, :, :h0] = O.round_to(d["working_key"][slot, :, :h0], "bf16")
         ov[slot, :, :h0] = d["working_value"][slot, :, :h0]
@@ -180,7 +181,7 @@ def test_capture_cycle_vs_reference(dsb, cuda):
                                 c["d"] ** -0.5, out)
         got = out.float().cpu().numpy()
         ref = O.draft_decode_attention(st["query"], st["key"], st["value"], ok, ov,
-                                       cache._active_slots, local.cpu().numpy()[: len(ids)],
+                                       slots, local.cpu().numpy()[: len(ids)],
                                        c["d"] ** -0.5, dtype=None)
         close_bf16(got[: len(ids)], ref[: len(ids)])
         close_bf16(got[: len(ids)], d[f"step{j}_out"][: len(ids)], mean_rel=FP32_CACHE_MEAN_REL)
@@ -191,7 +192,7 @@ def test_capture_cycle_vs_reference(dsb, cuda):
     cache.end_cycle()
     np.testing.assert_array_equal(cache.raw_key.float().cpu().numpy(), d["raw_key"])
     np.testing.assert_array_equal(cache.raw_value.float().cpu().numpy(), d["raw_value"])
-    for slot in cache._active_slots:
+    for slot in slots:
         h = int(d["working_lens"][slot])
         np.testing.assert_array_equal(cache.working_key[slot, :, :h].float().cpu().numpy(),
                                       O.round_to(d["working_key"][slot, :, :h], "bf16"))

@@ -207,7 +207,7 @@ def test_config3_ragged_draft_cycle(dsb, cuda):
     seq = lengths[order]
     cnt = counts[order]
     cache.begin_target_forward(ids)
-    slots = list(cache._active_slots)
+    slots = cache.active_slots()
     assert slots == order.tolist()
     meta = SimpleNamespace(actual_seq_lengths_q=ends.tolist(), seq_lens_list=seq.tolist(),
                            block_tables=table[torch.from_numpy(order).to(cuda)], num_prefills=0)

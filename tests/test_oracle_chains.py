@@ -9,7 +9,9 @@
 * The draft step's KV sink: populate_prefill, a retrieval, then
   prepare_compact_prefill and capture_raw_kv + forward_attention per draft
   step with graph-padding rows in reordered slots (runtime.py:1336-1371,
-  1602-1618, 1797-1877)."""
+  1602-1618, 1797-1877).
+* Request slots: set_active_requests over a sequence of batches (reorder,
+  cancellation, a returning id, duplicates, exhaustion; runtime.py:755-778)."""
 
 from __future__ import annotations
 
@@ -91,3 +93,27 @@ def test_capture_cycle_matches_reference():
         np.testing.assert_array_equal(wk[slot, :, :h], d["working_key"][slot, :, :h])
         np.testing.assert_array_equal(wv[slot, :, :h], d["working_value"][slot, :, :h])
         assert int(d["working_lens"][slot]) == h
+
+
+def slot_step_state(table: O.SlotTable, d: dict, i: int) -> None:
+    """Compare the oracle's slot table after step i with the reference's."""
+    assert table.active == d[f"active{i}"].tolist()
+    assert table.working_lens == d[f"working_lens{i}"].tolist()
+    assert sorted(table.selected) == np.flatnonzero(d[f"selected{i}"]).tolist()
+
+
+def test_slot_table_matches_reference():
+    d = golden("slots")
+    assert int(d["n"]) == len(R.SLOT_STEPS)
+    table = O.SlotTable(R.SLOT_COUNT)
+    for i, batch in enumerate(R.SLOT_STEPS):
+        for slot in table.slots.values():
+            table.working_lens[slot] = 100 + 10 * i + slot
+            table.selected.add(slot)
+        raised = 0
+        try:
+            table.set_active_requests(list(batch))
+        except RuntimeError:
+            raised = 1
+        assert raised == int(d[f"raised{i}"])
+        slot_step_state(table, d, i)

@@ -25,6 +25,9 @@ DSB_BF16 = 0
 DSB_F16 = 1
 DSB_F32 = 2
 
+DSB_FLAG_SLOT = 1
+DSB_FLAG_POSITION = 2
+
 FLAG_NAMES = {
     1: "slot out of range",
     2: "token position out of range",
@@ -145,6 +148,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I32, _I32, _I32, _P, _I32,
          _I32, _P, _P, _P, _P],
     ),
+    "dsb_assign_request_slots": (
+        ctypes.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _P, _P, _P],
+    ),
+    "dsb_rows_to_slots": (ctypes.c_int, [_P, _I32, _P, _I32, _P, _P, _P]),
 }
 
 _lock = threading.Lock()

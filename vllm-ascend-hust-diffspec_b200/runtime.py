@@ -31,6 +31,7 @@ import time
 from dataclasses import dataclass
 from typing import Any
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -142,7 +143,7 @@ class _Staging:
         self._alloc(max(1, capacity // self.SLOTS))
 
     def _alloc(self, per: int) -> None:
-        self.per = per  # int32 values per slot
+        self.per = (per + 1) // 2 * 2  # int32 values per slot (even: uploads start 8-byte aligned)
         self.dev = torch.empty(self.SLOTS * per, dtype=torch.int32, device=self.device)
         self.host = [torch.empty(per, dtype=torch.int32).pin_memory() for _ in range(self.SLOTS)]
         self.events: list[torch.cuda.Event | None] = [None] * self.SLOTS
@@ -280,8 +281,16 @@ class DiffSpecDraftCache:
         self._attn_workspace = AttentionWorkspace(self.device)
         self.metrics = DiffSpecRuntimeMetrics()
 
-        self._request_slots: dict[str, int] = {}
-        self._active_slots: list[int] = []
+        if max_num_reqs > 4096:
+            raise ValueError("max_num_reqs must be at most 4096 (the device slot table's limit)")
+        # Slot table on the device: the key of the request owning each slot,
+        # -1 when free.  The host only interns request ids as keys that are
+        # never reused (a request that leaves and comes back is a new one, as
+        # in the reference, whose released ids lose their slot).
+        self._slot_keys = torch.full((max_num_reqs,), -1, dtype=torch.int64, device=self.device)
+        self._request_keys: dict[str, int] = {}
+        self._next_key = 0
+        self._num_active = 0
         self._active_slots_dev: torch.Tensor | None = None
         self._retrieval_cycle = 0
         self._cycle_open = False
@@ -298,34 +307,56 @@ class DiffSpecDraftCache:
     # ------------------------------------------------------------ slots
     def set_active_requests(self, request_ids: list[str]) -> None:
         """Keep canonical rows stable across batch reorder and cancellation
-        (diffspec/runtime.py:755-778)."""
+        (diffspec/runtime.py:755-778), with the slot table on the device.
+
+        One ``dsb_assign_request_slots`` launch releases the slots of the
+        requests that left the batch (their selection and working length
+        reset), gives the new requests the lowest free slots in batch order
+        and writes the batch's slot vector; the host reads nothing back.  A
+        batch of more distinct requests than slots raises RuntimeError after
+        the same releases and assignments as the reference's loop (the
+        distinct count alone decides it: every kept request already holds a
+        slot, so the new ones fit exactly when the batch does)."""
         if self._active_ids is not None and request_ids == self._active_ids:
             return  # same batch in the same order: slots unchanged
-        active = set(request_ids)
-        released = []
-        for request_id in list(self._request_slots):
-            if request_id not in active:
-                released.append(self._request_slots.pop(request_id))
-        if released:
-            idx = torch.tensor(released, dtype=torch.long).to(self.device, non_blocking=True)
-            self.sel_count.index_fill_(0, idx, -1)
-            self.working_lens.index_fill_(0, idx, 0)
-        used = set(self._request_slots.values())
-        free = iter(sorted(set(range(self.max_num_reqs)) - used))
-        for request_id in request_ids:
-            if request_id not in self._request_slots:
-                try:
-                    self._request_slots[request_id] = next(free)
-                except StopIteration as error:
-                    raise RuntimeError("DiffSpec canonical request slots are exhausted") from error
-        self._active_ids = list(request_ids)
-        slots = [self._request_slots[r] for r in request_ids]
-        if slots != self._active_slots or self._active_slots_dev is None:
-            self._active_slots = slots
-            self._active_slots_dev = (
-                torch.tensor(slots, dtype=torch.int32).to(self.device, non_blocking=True)
-                if slots else torch.empty(0, dtype=torch.int32, device=self.device)
-            )
+        ids = list(request_ids)
+        keys: dict[str, int] = {}
+        for request_id in ids:
+            if request_id not in keys:
+                key = self._request_keys.get(request_id)
+                if key is None:
+                    key = self._next_key
+                    self._next_key += 1
+                keys[request_id] = key
+        n = len(ids)
+        if n > 4096:
+            raise RuntimeError("DiffSpec canonical request slots are exhausted")
+        exhausted = len(keys) > self.max_num_reqs
+        slots = torch.empty(n, dtype=torch.int32, device=self.device)
+        # int64 keys travel as int32 pairs through the staging ring (every
+        # upload starts 8-byte aligned)
+        batch_keys = np.asarray([keys[r] for r in ids], dtype=np.int64)
+        (pairs,) = self._staging.upload(batch_keys.view(np.int32).tolist())
+        _lib.call(
+            "dsb_assign_request_slots",
+            _lib.ptr(self._slot_keys), self.max_num_reqs, _lib.ptr(pairs.view(torch.int64)), n,
+            _lib.ptr(slots), _lib.ptr(self.sel_count), _lib.ptr(self.working_lens), None,
+            _lib.ptr(_lib.error_flag(self.device)), _lib.stream_ptr(self.device),
+        )
+        # the table now holds keys of this batch only
+        self._request_keys = keys
+        if exhausted:
+            self._active_ids = None
+            raise RuntimeError("DiffSpec canonical request slots are exhausted")
+        self._active_ids = ids
+        self._num_active = n
+        self._active_slots_dev = slots
+
+    def active_slots(self) -> list[int]:
+        """The batch's canonical slots, in batch order (reads the device)."""
+        if self._active_slots_dev is None:
+            return []
+        return [int(x) for x in self._active_slots_dev.tolist()]
 
     def begin_cycle(self, request_ids: list[str]) -> None:
         self.set_active_requests(request_ids)
@@ -428,7 +459,7 @@ class DiffSpecDraftCache:
         if self._retrieval_cycle % self.settings.retrieval_interval:
             self.metrics.retrieval_skipped_interval += 1
             return
-        batch = len(self._active_slots)
+        batch = self._num_active
         t = self._target
         if (
             valid_sampled_token_count.numel() < batch
@@ -456,7 +487,7 @@ class DiffSpecDraftCache:
         scale: float,
     ) -> None:
         """Device retrieval for the active batch: pick -> score -> exchange -> select."""
-        if not self._active_slots:
+        if not self._num_active:
             return
         ends_d, seqs_d = self._staging.upload(query_ends, target_seq_lens)
         self.retrieve_device(query, softmax_lse, key_cache, block_tables, ends_d, seqs_d,
@@ -479,7 +510,7 @@ class DiffSpecDraftCache:
         lengths: no host data is read, so the call can be captured in a CUDA
         graph whose replays see new values in those tensors."""
         started = time.perf_counter()
-        rows = len(self._active_slots)
+        rows = self._num_active
         if rows == 0:
             return
         ends_d, seqs_d = query_ends, target_seq_lens
@@ -588,18 +619,25 @@ class DiffSpecDraftCache:
             rows.append(r)
         return rows
 
-    def _canonical_slots(self, batch_rows: list[int]) -> list[int]:
-        if not self._active_slots:
+    def _canonical_slots(self, batch_rows: list[int]) -> torch.Tensor:
+        """Device slot of each token from its batch row (``dsb_rows_to_slots``)."""
+        if not self._num_active:
             raise RuntimeError("DiffSpec request slots have not been initialized")
-        return [self._active_slots[r] for r in batch_rows]
+        if batch_rows and (min(batch_rows) < 0 or max(batch_rows) >= self._num_active):
+            raise IndexError("list index out of range")
+        (rows_d,) = self._staging.upload(batch_rows)
+        slots = torch.empty(len(batch_rows), dtype=torch.int32, device=self.device)
+        _lib.call("dsb_rows_to_slots", _lib.ptr(self._active_slots_dev), self._num_active,
+                  _lib.ptr(rows_d), len(batch_rows), _lib.ptr(slots),
+                  _lib.ptr(_lib.error_flag(self.device)), _lib.stream_ptr(self.device))
+        return slots
 
     def populate_prefill(self, absolute_positions: torch.Tensor, key: torch.Tensor,
                          value: torch.Tensor, metadata: Any) -> None:
         """Canonical raw KV of a cache-only draft projection (runtime.py:1336-1347):
         token t of the pass belongs to the batch row ``metadata`` gives it and
         is written at ``[slot, absolute_positions[t]]``."""
-        slots = self._canonical_slots(self._request_indices(metadata, key.shape[0]))
-        (slots_d,) = self._staging.upload(slots)
+        slots_d = self._canonical_slots(self._request_indices(metadata, key.shape[0]))
         self.write_raw(slots_d, absolute_positions, key, value)
 
     def capture_raw_kv(self, layer_index: int, absolute_positions: torch.Tensor,
@@ -627,7 +665,7 @@ class DiffSpecDraftCache:
                 return None
             self.populate_prefill(absolute_positions.reshape(-1), key, value, metadata)
             return None
-        rows = len(self._active_slots)
+        rows = self._num_active
         flat = absolute_positions.reshape(-1)
         if key.shape[0] < rows or flat.numel() < rows:
             raise RuntimeError("DiffSpec draft tensors omit active request rows")
@@ -695,7 +733,7 @@ class DiffSpecDraftCache:
         Returns the device int32 ``history_len`` per row, which is also the
         root's local position.
         """
-        rows = len(self._active_slots)
+        rows = self._num_active
         if rows == 0:
             return self._history_lens[:0]
         if isinstance(committed_seq_lens, torch.Tensor):
