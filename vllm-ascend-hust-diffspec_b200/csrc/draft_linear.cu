@@ -57,7 +57,8 @@ template <int RANKS> struct LnCfg {
   static constexpr int kTpr = kLnTok / RANKS;  // tokens each rank sums
   static constexpr int kBarOff = kLnStages * (kLnABytes + kLnBBytes);
   // full[stages], empty[stages], done, then the TMEM address word
-  static constexpr int kXchOff = kBarOff + 8 * (2 * kLnStages + 1) + 16;
+  // 16-byte aligned: the partials arrive as 16-byte (or 8-byte) stores
+  static constexpr int kXchOff = (kBarOff + 8 * (2 * kLnStages + 1) + 16 + 15) / 16 * 16;
   static constexpr int kSwOff = kXchOff + 4 * RANKS * 128 * kTpr;  // [128][kTpr] fp32 (SwiGLU)
   static constexpr size_t kSmem = 1024 + kSwOff + 4 * 128 * kTpr;
 };
@@ -167,6 +168,29 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   pdl_begin();
   asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
 
+  // The epilogue's global operands (written by earlier kernels, valid once
+  // the wait above has returned) are loaded now, so their latency passes
+  // while the weights stream: this thread's residual values, or the slot and
+  // position of each token it stores.
+  const int g = f0 + tid;  // output feature of this thread in the epilogue
+  float res[kTpr];
+  int32_t tslot[kTpr];
+  int64_t tpos[kTpr];
+#pragma unroll
+  for (int j = 0; j < kTpr; ++j) {
+    const int t = t0 + kTpr * rank + j;
+    res[j] = 0.f;
+    tslot[j] = -1;
+    tpos[j] = 0;
+    if (t >= a.T) continue;
+    if (a.mode == kResidual && g < a.split)
+      res[j] = Elem<T>::to_f(static_cast<const T *>(a.residual)[(int64_t)t * a.ldr + g]);
+    if (a.raw_k != nullptr && g >= a.split) {
+      tslot[j] = a.slots[t];
+      tpos[j] = a.positions[t];
+    }
+  }
+
   if (tid == 32) {
     // Producer: fill slot kb % S once the products of its previous fill
     // (k-block kb - S) have completed.
@@ -241,13 +265,23 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
 
   // Rank q sums tokens q * kTpr .. q * kTpr + kTpr - 1 over the ranks: send
   // them there.
+  // (16-byte stores where kTpr allows: the exchange costs per transaction,
+  // and scalar stores made it the largest fixed cost of a launch)
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");  // every rank is running
   const uint32_t x0 = smem_u32(xch);
 #pragma unroll
   for (int q = 0; q < RANKS; ++q) {
     const uint32_t remote = cluster_map(x0, (uint32_t)q) + 4u * (uint32_t)((rank * 128 + tid) * kTpr);
+    if constexpr (kTpr % 4 == 0) {
 #pragma unroll
-    for (int j = 0; j < kTpr; ++j) st_cluster(remote + 4u * j, acc[q * kTpr + j]);
+      for (int j = 0; j < kTpr; j += 4)
+        st_cluster(remote + 4u * j, make_float4(acc[q * kTpr + j], acc[q * kTpr + j + 1],
+                                                acc[q * kTpr + j + 2], acc[q * kTpr + j + 3]));
+    } else if constexpr (kTpr == 2) {
+      st_cluster(remote, make_float2(acc[q * 2], acc[q * 2 + 1]));
+    } else {
+      st_cluster(remote, acc[q]);
+    }
   }
   cluster_sync_all();  // every partial delivered
 
@@ -268,21 +302,19 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
 #pragma unroll
     for (int j = 0; j < kTpr; ++j) sw[tid * kTpr + j] = Elem<T>::to_f(Elem<T>::from_f(v[j]));
     __syncthreads();
-    if (tid < 64) {
-      T *out = static_cast<T *>(a.out);
-#pragma unroll
-      for (int j = 0; j < kTpr; ++j) {
-        const int t = t0 + kTpr * rank + j;
-        if (t >= a.T) continue;
-        const float g = sw[tid * kTpr + j], u = sw[(tid + 64) * kTpr + j];
-        const float sg = Elem<T>::to_f(Elem<T>::from_f(silu_f(g)));  // SiluAndMul rounds silu
-        out[(int64_t)t * a.ldo + f0 / 2 + tid] = Elem<T>::from_f(__fmul_rn(sg, u));
-      }
+    // 64 output features x kTpr tokens over all 128 threads
+    T *out = static_cast<T *>(a.out);
+    const int f = tid & 63;
+    for (int j = tid >> 6; j < kTpr; j += 2) {
+      const int t = t0 + kTpr * rank + j;
+      if (t >= a.T) continue;
+      const float gt = sw[f * kTpr + j], u = sw[(f + 64) * kTpr + j];
+      const float sg = Elem<T>::to_f(Elem<T>::from_f(silu_f(gt)));  // SiluAndMul rounds silu
+      out[(int64_t)t * a.ldo + f0 / 2 + f] = Elem<T>::from_f(__fmul_rn(sg, u));
     }
     return;
   }
 
-  const int g = f0 + tid;  // output feature
   T *raw_k = static_cast<T *>(a.raw_k), *raw_v = static_cast<T *>(a.raw_v);
 #pragma unroll
   for (int j = 0; j < kTpr; ++j) {
@@ -294,8 +326,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
         continue;
       }
       float y = v[j];
-      if (a.mode == kResidual)
-        y = __fadd_rn(y, Elem<T>::to_f(static_cast<const T *>(a.residual)[(int64_t)t * a.ldr + g]));
+      if (a.mode == kResidual) y = __fadd_rn(y, res[j]);
       static_cast<T *>(a.out)[(int64_t)t * a.ldo + g] = Elem<T>::from_f(y);
       continue;
     }
@@ -303,9 +334,9 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     const int gk = g - a.split;
     if (a.out2 != nullptr) static_cast<T *>(a.out2)[(int64_t)t * a.ldo2 + gk] = y;
     if (raw_k == nullptr) continue;
-    const int slot = a.slots[t];
+    const int slot = tslot[j];
     if (slot < 0) continue;  // padding row: no cache row
-    const int64_t pos = a.positions[t];
+    const int64_t pos = tpos[j];
     if (slot >= a.num_slots || pos < 0 || pos >= a.max_len) {
       if (tid == 0) flag_error(a.err, slot >= a.num_slots ? DSB_FLAG_SLOT : DSB_FLAG_POSITION);
       continue;
