@@ -56,10 +56,10 @@ enum Epilogue : int { kPlain = 0, kResidual = 1, kSwiglu = 2, kPartialF32 = 3 };
 template <int RANKS> struct LnCfg {
   static constexpr int kTpr = kLnTok / RANKS;  // tokens each rank sums
   static constexpr int kBarOff = kLnStages * (kLnABytes + kLnBBytes);
-  // full[stages], empty[stages], done, then the TMEM address word
+  // full[stages], empty[stages], done, exchange, then the TMEM address word
   // 16-byte aligned: the partials arrive as 16-byte (or 8-byte) stores
-  static constexpr int kXchOff = (kBarOff + 8 * (2 * kLnStages + 1) + 16 + 15) / 16 * 16;
-  static constexpr int kSwOff = kXchOff + 4 * RANKS * 128 * kTpr;  // [128][kTpr] fp32 (SwiGLU)
+  static constexpr int kXchOff = (kBarOff + 8 * (2 * kLnStages + 2) + 16 + 15) / 16 * 16;
+  static constexpr int kSwOff = kXchOff + 4 * RANKS * 128 * kTpr;  // [kTpr][128] fp32 (SwiGLU)
   static constexpr size_t kSmem = 1024 + kSwOff + 4 * 128 * kTpr;
 };
 
@@ -110,7 +110,8 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   const uint32_t s_a = smem_u32(smem), s_b = s_a + S * kLnABytes;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff);
   const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S, done = full0 + 16 * S;
-  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(bars + 2 * S + 1);
+  const uint32_t xbar = done + 8;  // the partials sent to this rank
+  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(bars + 2 * S + 2);
   float *xch = reinterpret_cast<float *>(smem + Cfg::kXchOff);
   float *sw = reinterpret_cast<float *>(smem + Cfg::kSwOff);
   __shared__ int s_abort, s_consumed, s_issued;
@@ -144,7 +145,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   if (tid == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
-    for (int b = 0; b <= 2 * S; ++b) mbar_init(full0 + 8 * b);
+    for (int b = 0; b <= 2 * S + 1; ++b) mbar_init(full0 + 8 * b);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
     s_consumed = 0;
@@ -264,34 +265,57 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" ::"r"(tmem) : "memory");
 
   // Rank q sums tokens q * kTpr .. q * kTpr + kTpr - 1 over the ranks: send
-  // them there.
-  // (16-byte stores where kTpr allows: the exchange costs per transaction,
-  // and scalar stores made it the largest fixed cost of a launch)
+  // them there, as asynchronous 16-byte stores where kTpr allows (the
+  // exchange costs per transaction) that complete on the receiver's `xbar`.
+  // Each rank then waits only for the bytes addressed to it (thread 0 arms
+  // the barrier with their count; stores that land first are counted all
+  // the same), and leaves only once all of them have landed, so no rank
+  // exits while a peer still writes into its shared memory.
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");  // every rank is running
+  if (tid == 0) mbar_expect_tx(xbar, (uint32_t)(RANKS * 128 * kTpr * 4));
   const uint32_t x0 = smem_u32(xch);
 #pragma unroll
   for (int q = 0; q < RANKS; ++q) {
     const uint32_t remote = cluster_map(x0, (uint32_t)q) + 4u * (uint32_t)((rank * 128 + tid) * kTpr);
+    const uint32_t rbar = cluster_map(xbar, (uint32_t)q);
     if constexpr (kTpr % 4 == 0) {
 #pragma unroll
       for (int j = 0; j < kTpr; j += 4)
-        st_cluster(remote + 4u * j, make_float4(acc[q * kTpr + j], acc[q * kTpr + j + 1],
-                                                acc[q * kTpr + j + 2], acc[q * kTpr + j + 3]));
+        st_async(remote + 4u * j, make_float4(acc[q * kTpr + j], acc[q * kTpr + j + 1],
+                                              acc[q * kTpr + j + 2], acc[q * kTpr + j + 3]),
+                 rbar);
     } else if constexpr (kTpr == 2) {
-      st_cluster(remote, make_float2(acc[q * 2], acc[q * 2 + 1]));
+      st_async(remote, make_float2(acc[q * 2], acc[q * 2 + 1]), rbar);
     } else {
-      st_cluster(remote, acc[q]);
+      st_async(remote, acc[q], rbar);
     }
   }
-  cluster_sync_all();  // every partial delivered
+  if (!mbar_wait_cluster(xbar, 0) && tid == 0) flag_error(a.err, DSB_FLAG_TIMEOUT);
 
+  // (read as the 16- or 8-byte vectors they arrived in; the sum over the
+  // ranks runs in rank order either way)
   float v[kTpr];
 #pragma unroll
-  for (int j = 0; j < kTpr; ++j) {
-    float sum = 0.f;
+  for (int j = 0; j < kTpr; ++j) v[j] = 0.f;
 #pragma unroll
-    for (int r = 0; r < RANKS; ++r) sum += xch[(r * 128 + tid) * kTpr + j];
-    v[j] = sum;
+  for (int r = 0; r < RANKS; ++r) {
+    const float *row = xch + (r * 128 + tid) * kTpr;
+    if constexpr (kTpr % 4 == 0) {
+#pragma unroll
+      for (int j = 0; j < kTpr; j += 4) {
+        const float4 x4 = *reinterpret_cast<const float4 *>(row + j);
+        v[j] += x4.x;
+        v[j + 1] += x4.y;
+        v[j + 2] += x4.z;
+        v[j + 3] += x4.w;
+      }
+    } else if constexpr (kTpr == 2) {
+      const float2 x2 = *reinterpret_cast<const float2 *>(row);
+      v[0] += x2.x;
+      v[1] += x2.y;
+    } else {
+      v[0] += row[0];
+    }
   }
 
   if (a.mode == kSwiglu) {
@@ -300,7 +324,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     // gate_up GEMM output is, then round(round(silu(gate)) * up) as vLLM's
     // SiluAndMul computes it.
 #pragma unroll
-    for (int j = 0; j < kTpr; ++j) sw[tid * kTpr + j] = Elem<T>::to_f(Elem<T>::from_f(v[j]));
+    for (int j = 0; j < kTpr; ++j) sw[j * 128 + tid] = Elem<T>::to_f(Elem<T>::from_f(v[j]));
     __syncthreads();
     // 64 output features x kTpr tokens over all 128 threads
     T *out = static_cast<T *>(a.out);
@@ -308,7 +332,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     for (int j = tid >> 6; j < kTpr; j += 2) {
       const int t = t0 + kTpr * rank + j;
       if (t >= a.T) continue;
-      const float gt = sw[f * kTpr + j], u = sw[(f + 64) * kTpr + j];
+      const float gt = sw[j * 128 + f], u = sw[j * 128 + f + 64];
       const float sg = Elem<T>::to_f(Elem<T>::from_f(silu_f(gt)));  // SiluAndMul rounds silu
       out[(int64_t)t * a.ldo + f0 / 2 + f] = Elem<T>::from_f(__fmul_rn(sg, u));
     }

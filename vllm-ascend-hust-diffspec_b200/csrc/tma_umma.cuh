@@ -133,6 +133,49 @@ __device__ __forceinline__ void st_cluster(uint32_t addr, const float2 &v) {
 __device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
+// Asynchronous stores into a cluster peer's shared memory (cluster addresses
+// from mapa) whose bytes complete on that peer's mbarrier `bar`: the peer
+// learns of the data's arrival from its own barrier, with no cluster-wide
+// barrier round trip.
+__device__ __forceinline__ void st_async(uint32_t addr, const float4 &v, uint32_t bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::
+          "r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void st_async(uint32_t addr, const float2 &v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::
+                   "r"(addr), "f"(v.x), "f"(v.y), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(
+                   addr),
+               "f"(v), "r"(bar)
+               : "memory");
+}
+// Bounded wait on this CTA's mbarrier phase with cluster-scope acquire, for
+// data that peers stored with st_async (their completions release at
+// cluster scope).  False when the bound ran out.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint64_t t0 = 0;
+  for (int i = 0; i < kWaitSpins; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 63) == 0) {
+      const uint64_t now = global_ns();
+      if (i == 0) t0 = now;
+      else if (now - t0 > kWaitNs) return false;
+    }
+  }
+  return false;
+}
 // Every thread of every CTA in the cluster arrives (release) and waits
 // (acquire).  Only called on paths that all CTAs of a cluster take.
 __device__ __forceinline__ void cluster_sync_all() {
