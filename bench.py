@@ -1347,7 +1347,10 @@ def run_draft_linear(args):
     """Time the config-5 draft layer's four linears at a 16-token decode step
     on the tcgen05 weight-streaming kernel (`us`: tile-packed weights, as the
     draft layer streams them; `us_row_major_weight`: the same launches on
-    row-major weights) (qkv with the raw-cache write,
+    row-major weights; `us_prefetch_l2`: tile-packed with the rest of each
+    weight requested into L2 while the previous launch finishes, which the
+    layer leaves off because it evicts the draft attention's working cache)
+    (qkv with the raw-cache write,
     o_proj + residual, gate_up + SwiGLU, down_proj + residual) against cuBLAS
     for the same products (torch.mm; the K/V raw write, the residual add and
     SwiGLU not included on that side).  Each shape cycles enough weight copies
@@ -1381,15 +1384,16 @@ def run_draft_linear(args):
         kv_out = torch.empty((tokens, 2 * HK * D), dtype=bf, device=device)
 
         def ours(w, name=name, x=x, res=res, out=out, half=half, q_out=q_out, kv_out=kv_out,
-                 packed=False):
+                 packed=False, l2=False):
             if name == "qkv":
                 dsb.kernels.qkv_projection_write_raw(x, w, HQ * D, slots, pos, rk, rv, q_out=q_out,
                                                      kv_out=kv_out, prefetch_weight=True,
-                                                     packed_weight=packed)
+                                                     packed_weight=packed, prefetch_l2=l2)
             elif name == "gate_up":  # the weight's tile order does not change the time
-                dl.draft_linear(x, w, "swiglu", out=half, packed=packed)
+                dl.draft_linear(x, w, "swiglu", out=half, packed=packed, prefetch_l2=l2)
             else:
-                dl.draft_linear(x, w, "residual", residual=res, out=out, packed=packed)
+                dl.draft_linear(x, w, "residual", residual=res, out=out, packed=packed,
+                                prefetch_l2=l2)
 
         def cublas(w, x=x, out=out):
             torch.mm(x, w.t(), out=out)
@@ -1420,6 +1424,7 @@ def run_draft_linear(args):
         us_rowmajor = time_graph(ours)
         ws = [dl.pack_linear_weight(w) for w in ws]  # the layout Eagle3DraftLayer streams
         us = time_graph(lambda w: ours(w, packed=True))
+        us_l2 = time_graph(lambda w: ours(w, packed=True, l2=True))
         assert dsb._lib.read_and_clear_error_flag(device) == 0
         del ws  # cuBLAS streams its own row-major copies
         ws = [(torch.randn((rows, k), generator=g, device=device) / k ** 0.5).to(bf)
@@ -1428,7 +1433,8 @@ def run_draft_linear(args):
         wbytes = rows * k * 2
         result[name] = dict(weight_rows=rows, k=k, us=round(us, 2), weight_gbs=round(wbytes / us / 1e3, 1),
                             frac_of_hbm_peak=round(wbytes / us / 1e3 / peak, 3),
-                            us_row_major_weight=round(us_rowmajor, 2), cublas_mm_us=round(ref, 2))
+                            us_row_major_weight=round(us_rowmajor, 2),
+                            us_prefetch_l2=round(us_l2, 2), cublas_mm_us=round(ref, 2))
         del ws
         torch.cuda.empty_cache()
     print(json.dumps(dict(mode="draft_linear", tokens=tokens, dtype="bf16", peak_gbs=peak,

@@ -234,16 +234,24 @@ def test_packed_weight_is_bit_identical(dsb, cuda, rows, k):
         wt = dl.interleave_gate_up(w)
         assert torch.equal(dl.draft_linear(x, wt, "swiglu"),
                            dl.draft_linear(x, dl.pack_linear_weight(wt), "swiglu", packed=True))
+    # the L2 prefetch of the rest of the weight only moves data earlier
+    for weight, packed in ((w, False), (wp, True)):
+        assert torch.equal(dl.draft_linear(x, weight, "residual", residual=res, packed=packed),
+                           dl.draft_linear(x, weight, "residual", residual=res, packed=packed,
+                                           prefetch_l2=True))
     if rows == 5120:  # the config-5 qkv projection: 32 query heads + 4 kv heads of 128
         rk = torch.zeros((16, 64, 4, 128), dtype=torch.bfloat16, device=cuda)
         outs = []
-        for weight, packed in ((w, False), (wp, True)):
+        for weight, packed, l2 in ((w, False, False), (wp, True, False), (wp, True, True),
+                                   (w, False, True)):
             rk_, rv_ = rk.clone(), rk.clone()
             q, kv = dsb.kernels.qkv_projection_write_raw(
                 x, weight, 4096, torch.arange(16, dtype=torch.int32, device=cuda),
-                torch.arange(16, dtype=torch.int64, device=cuda), rk_, rv_, packed_weight=packed)
+                torch.arange(16, dtype=torch.int64, device=cuda), rk_, rv_, packed_weight=packed,
+                prefetch_weight=l2, prefetch_l2=l2)
             outs.append((q, kv, rk_, rv_))
-        for a, b in zip(*outs):
-            assert torch.equal(a, b)
+        for other in outs[1:]:
+            for a, b in zip(outs[0], other):
+                assert torch.equal(a, b)
     torch.cuda.synchronize()
     assert dsb._lib.read_and_clear_error_flag(cuda) == 0

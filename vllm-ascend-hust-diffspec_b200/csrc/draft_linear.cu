@@ -74,6 +74,7 @@ struct LnArgs {
   int64_t ldr;
   int mode;
   int prefetch;
+  int prefetch_l2;  // with prefetch: the rest of the weight into L2 as well
   int packed;  // weight in the tile-packed layout (DSB_LINEAR_PACKED_WEIGHT)
   const void *wpacked;  // that weight's base (bulk-copied block by block)
   const int32_t *slots;
@@ -150,11 +151,22 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
     s_abort = 0;
     s_consumed = 0;
     s_issued = 0;
-    if (a.prefetch)
+    if (a.prefetch) {
       for (int kb = 0; kb < first; ++kb) {
         mbar_expect_tx(full0 + 8 * kb, kLnABytes + kLnBBytes);
         load_w(s_a + kb * kLnABytes, kb0 + kb, full0 + 8 * kb);
       }
+      // the rest of this rank's weight blocks into L2, so that HBM keeps
+      // streaming while the previous kernel finishes and the ring's later
+      // loads hit L2
+      for (int kb = first; kb < nkb && a.prefetch_l2; ++kb) {
+        if (a.packed)
+          bulk_prefetch_l2_hint(wpacked + ((int64_t)blockIdx.y * nkb_all + kb0 + kb) * kLnABytes,
+                                kLnABytes, wpol);
+        else
+          tma_prefetch_2d_hint(&tw, (kb0 + kb) * 64, f0, wpol);
+      }
+    }
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;" ::"r"(
@@ -539,6 +551,7 @@ extern "C" int dsb_qkv_projection_write_raw(
   a.split = q_features;
   a.mode = kPlain;
   a.prefetch = (flags & DSB_LINEAR_PREFETCH_WEIGHT) != 0;
+  a.prefetch_l2 = a.prefetch && (flags & DSB_LINEAR_PREFETCH_L2) != 0;
   a.packed = (flags & DSB_LINEAR_PACKED_WEIGHT) != 0;
   a.wpacked = weight;
   a.slots = slots;
@@ -594,6 +607,7 @@ extern "C" int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_featur
            : epilogue == DSB_LINEAR_SWIGLU   ? kSwiglu
                                              : kPartialF32;
   a.prefetch = (flags & DSB_LINEAR_PREFETCH_WEIGHT) != 0;
+  a.prefetch_l2 = a.prefetch && (flags & DSB_LINEAR_PREFETCH_L2) != 0;
   a.packed = (flags & DSB_LINEAR_PACKED_WEIGHT) != 0;
   a.wpacked = weight;
   a.T = tokens;

@@ -47,6 +47,21 @@ __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+// L2 prefetches (no shared memory, no completion): a 2-D box of a tensor map,
+// or `bytes` contiguous bytes (16-byte aligned, a multiple of 16).
+__device__ __forceinline__ void tma_prefetch_2d_hint(const CUtensorMap *map, int x, int y,
+                                                     uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::
+                   "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "l"(policy)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch_l2_hint(const void *src, uint32_t bytes,
+                                                      uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes),
+               "l"(policy)
+               : "memory");
+}
+
 // UMMA shared-memory descriptor for a 128-byte-swizzled operand.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |

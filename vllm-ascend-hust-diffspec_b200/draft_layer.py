@@ -72,7 +72,8 @@ def pack_linear_weight(weight: torch.Tensor) -> torch.Tensor:
 
 def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
                  residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                 prefetch_weight: bool = True, packed: bool = False) -> torch.Tensor:
+                 prefetch_weight: bool = True, packed: bool = False,
+                 prefetch_l2: bool = False) -> torch.Tensor:
     """``x [T, K] @ weight.T`` on the tensor cores (``dsb_draft_linear``),
     with ``epilogue`` "plain", "residual" (``+ residual`` before the one
     rounding), "partial" (the fp32 sums unrounded, ``out`` float32: one
@@ -80,8 +81,10 @@ def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
     ``[T, rows / 2] = round(round(silu(gate)) * up)`` with gate and up
     rounded first, as vLLM's gate_up output and SiluAndMul round them).  ``prefetch_weight`` starts the
     weight stream before the previous kernel has finished (the weight must
-    not be written by that kernel).  ``packed``: ``weight`` comes from
-    :func:`pack_linear_weight` (same shape, tile-packed bytes)."""
+    not be written by that kernel); ``prefetch_l2`` also requests the rest
+    of it into L2 by then (faster alone; it fills L2 with the weight).
+    ``packed``: ``weight`` comes from :func:`pack_linear_weight` (same shape,
+    tile-packed bytes)."""
     if epilogue not in _EPILOGUES:
         raise ValueError(f"epilogue must be one of {sorted(_EPILOGUES)}")
     if x.ndim != 2 or weight.ndim != 2 or weight.shape[1] != x.shape[1] or x.dtype != weight.dtype:
@@ -104,7 +107,7 @@ def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
     _lib.call("dsb_draft_linear", _lib.ptr(x), x.shape[0], x.shape[1], _lib.ptr(weight),
               weight.shape[0], _EPILOGUES[epilogue], _lib.ptr(residual), res_stride, _lib.ptr(out),
               _rows(out, "out"), _lib.dtype_code(x.dtype),
-              (1 if prefetch_weight else 0) | (2 if packed else 0),
+              (1 if prefetch_weight else 0) | (2 if packed else 0) | (4 if prefetch_l2 else 0),
               _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device))
     return out
 
@@ -240,6 +243,9 @@ class Eagle3DraftLayer:
         self.in_norm = torch.ones(qkv_in, dtype=dtype, device=device)
         self.post_norm = torch.ones(hidden, dtype=dtype, device=device)
         self.workspace = AttentionWorkspace(device)
+        # linears ("qkv", "o_proj", "gate_up", "down_proj") whose whole weight
+        # is requested into L2 while the kernel before them runs
+        self.l2_prefetch: frozenset[str] = frozenset()
 
     def weight_bytes(self) -> int:
         return sum(t.numel() * t.element_size()
@@ -255,18 +261,20 @@ class Eagle3DraftLayer:
         layer output ``[n, hidden]``."""
         n = x_in.shape[0]
         h = rms_norm(x_in, self.in_norm, self.eps)
+        l2 = self.l2_prefetch
         q, kv = qkv_projection_write_raw(h, self.p_qkv, self.hq * self.d, slots, abs_positions,
                                          raw_key, raw_value, prefetch_weight=True,
-                                         packed_weight=True)
+                                         packed_weight=True, prefetch_l2="qkv" in l2)
         k, v = rope_qk(q, kv, local_positions, cos_sin, self.hk, position_offset=position_offset)
         attn = draft_decode_attention(q.view(n, self.hq, self.d), k, v, working_key, working_value,
                                       slots, local_positions, self.d ** -0.5,
                                       position_offset=position_offset, workspace=self.workspace)
         x = draft_linear(attn.view(n, self.hq * self.d), self.p_o, "residual", residual,
-                         packed=True)
+                         packed=True, prefetch_l2="o_proj" in l2)
         act = draft_linear(rms_norm(x, self.post_norm, self.eps), self.p_gate_up, "swiglu",
-                           packed=True)
-        return draft_linear(act, self.p_down, "residual", x, out=out, packed=True)
+                           packed=True, prefetch_l2="gate_up" in l2)
+        return draft_linear(act, self.p_down, "residual", x, out=out, packed=True,
+                            prefetch_l2="down_proj" in l2)
 
 
 class Eagle3DraftLayerTP:

@@ -441,6 +441,7 @@ def qkv_projection_write_raw(
     kv_out: torch.Tensor | None = None,
     prefetch_weight: bool = False,
     packed_weight: bool = False,
+    prefetch_l2: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """The draft layer's query + K/V projection in one launch.
 
@@ -450,8 +451,11 @@ def qkv_projection_write_raw(
     written, pre-RoPE, to the raw caches at ``[slots[t], positions[t]]`` as
     in :func:`kv_projection_write_raw`.  ``prefetch_weight`` lets the weight
     stream start before the previous kernel in the stream has finished (the
-    weight must not be written by that kernel); ``packed_weight``: ``weight``
-    is in the tile-packed layout of ``draft_layer.pack_linear_weight``.
+    weight must not be written by that kernel); ``prefetch_l2`` (with
+    ``prefetch_weight``) also requests the rest of the weight into L2 before
+    that kernel has finished (faster alone; it fills L2 with the weight);
+    ``packed_weight``: ``weight`` is in the tile-packed layout of
+    ``draft_layer.pack_linear_weight``.
     """
     if hidden.ndim != 2 or weight.ndim != 2 or weight.shape[1] != hidden.shape[1]:
         raise ValueError("hidden must be [T, hidden] and weight [q + 2 * Hk * D, hidden]")
@@ -485,7 +489,7 @@ def qkv_projection_write_raw(
         _lib.ptr(hidden), tokens, hidden.shape[1], _lib.ptr(weight), q_features, hk, d,
         _lib.ptr(slots), _lib.ptr(positions), _lib.ptr(raw_key), _lib.ptr(raw_value), num_slots,
         max_model_len, _lib.dtype_code(hidden.dtype), _lib.ptr(q_out), _lib.ptr(kv_out),
-        (1 if prefetch_weight else 0) | (2 if packed_weight else 0),
+        (1 if prefetch_weight else 0) | (2 if packed_weight else 0) | (4 if prefetch_l2 else 0),
         _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device),
     )
     return q_out, kv_out
