@@ -1157,8 +1157,10 @@ def run_draft_step(args):
 
     Under torchrun (N ranks), --draft-parallel tp (default): the layer is
     tensor-parallel (Eagle3DraftLayerTP: qkv / gate_up column-split, o_proj /
-    down_proj row-split with two fp32 NCCL all-reduces per step, kv heads
-    replicated when N > 4) and the DiffSpec cache is sharded by kv head
+    down_proj row-split with two fp32 all-reduces per step, kv heads
+    replicated when N > 4; --tp-exchange peer (default) fuses each all-reduce
+    into its row-split linear over NVLink peer memory, nccl calls
+    torch.distributed.all_reduce) and the DiffSpec cache is sharded by kv head
     (retrieval mass all-gathered before the selection); every rank drafts
     the same 16 requests, so the total work is fixed (strong scaling).
     --draft-parallel dp: every rank drafts its own 16 requests with the
@@ -1188,7 +1190,12 @@ def run_draft_step(args):
         hk_local, rep, hq_local, kv_group = HK, 1, HQ, rank
     w = Workload(torch, dsb, device, B_GROUP, hk_local, hq_local, seed=555 + kv_group, ctx=ctx)
     full = dsb.draft_layer.Eagle3DraftLayer(device, seed=5)
-    layer = dsb.draft_layer.Eagle3DraftLayerTP(full, rank, world) if tp else full
+    sites = None
+    if tp and args.tp_exchange == "peer":
+        hidden = full.w_o.shape[0]
+        sites = tuple(dsb.parallel.PeerExchange.create(B_GROUP, hidden, device) for _ in range(2))
+        dist.barrier()  # every rank's buffers are mapped before the first call
+    layer = dsb.draft_layer.Eagle3DraftLayerTP(full, rank, world, peer=sites) if tp else full
     g = torch.Generator(device=device).manual_seed(17)
     bf = torch.bfloat16
     x_in = torch.randn((B_GROUP, 4096), generator=g, device=device).to(bf)
@@ -1265,13 +1272,19 @@ def run_draft_step(args):
             parallelism=("one GPU" if world == 1 else
                          f"tensor parallel over {world} GPUs: {hq_local} query heads and "
                          f"{hk_local} kv head(s) per GPU (each kv head on {rep} GPU(s)), "
-                         "2 fp32 NCCL all-reduces per layer step" if tp else
+                         + ("2 fp32 all-reduces per layer step fused into the row-split "
+                            "linears over NVLink peer memory" if sites else
+                            "2 fp32 NCCL all-reduces per layer step") if tp else
                          f"data parallel over {world} GPUs: every GPU drafts its own 16 "
                          "requests with the whole layer (no per-step collective)"),
             requests=B_GROUP * (1 if tp else world), context=ctx, token_budget=TOKEN_BUDGET, chunk=CHUNK,
             retrieval_interval=INTERVAL, draft_depth=DEPTH, dtype="bf16",
             data="synthetic (random weights and KV)")), flush=True)
     if world > 1:
+        torch.cuda.synchronize(device)
+        dist.barrier()  # no rank still writes into another's exchange buffer
+        for site in sites or ():
+            site.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -1623,6 +1636,9 @@ def main():
                    help="time the K/V projection + raw-cache write (config 5 decode step)")
     p.add_argument("--draft-step", action="store_true",
                    help="config 5: draft tokens/s of a draft layer over the DiffSpec cache")
+    p.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
+                   help="--draft-step --draft-parallel tp: the all-reduces fused into the "
+                        "row-split linears over NVLink peer memory, or NCCL all-reduces")
     p.add_argument("--draft-parallel", choices=["tp", "dp"], default="tp",
                    help="--draft-step under torchrun: tensor parallel (one 16-request batch "
                         "over all GPUs) or data parallel (16 requests per GPU)")

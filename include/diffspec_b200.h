@@ -468,6 +468,42 @@ int dsb_capture_raw_kv(
     int32_t working_budget, void *local_positions, int32_t *working_lens, int32_t *error_flag,
     void *stream);
 
+/* Fused row-split linear + all-reduce over NVLink peer memory, for a
+ * tensor-parallel draft layer (the all-reduce of vLLM's RowParallelLinear in
+ * the Eagle3 layer the reference drafts through, diffspec/proposer.py:97-119).
+ * Each rank owns one exchange buffer per all-reduce site, of
+ * dsb_peer_buffer_bytes(world, tokens_max, features) bytes, created zeroed by
+ * dsb_peer_buffer_create and mapped into the other ranks' processes with
+ * dsb_ipc_handle / dsb_ipc_open (plain peer mappings; no multicast).
+ * dsb_draft_linear_peer computes x . W^T like dsb_draft_linear and stores the
+ * fp32 sums into this rank's slot of every rank's buffer (peer_bases[q] =
+ * rank q's buffer as mapped in this process, a device array of world
+ * addresses; own_base = this rank's buffer), then marks the call done on
+ * every rank.  dsb_peer_add_rms_norm on each rank waits for all ranks' marks
+ * (bounded by time: DSB_FLAG_TIMEOUT, and the sums are then not meaningful),
+ * sums the partials in rank order and finishes as dsb_add_rms_norm with that
+ * sum as `partial`.  Every rank must issue the same sequence of
+ * dsb_draft_linear_peer / dsb_peer_add_rms_norm calls on a site, alternating,
+ * each on one stream; the call count lives in the buffer, so the sequence can
+ * be captured and replayed as a CUDA graph.  world <= 8, features a multiple
+ * of 8; weight_rows of the linear = features; tokens <= tokens_max. */
+#define DSB_IPC_HANDLE_BYTES 64
+int64_t dsb_peer_buffer_bytes(int32_t world, int32_t tokens_max, int32_t features);
+int dsb_peer_buffer_create(int32_t world, int32_t tokens_max, int32_t features, void **base);
+int dsb_peer_buffer_destroy(void *base);
+int dsb_ipc_handle(void *base, void *handle);
+int dsb_ipc_open(const void *handle, void **base);
+int dsb_ipc_close(void *base);
+int dsb_draft_linear_peer(const void *x, int32_t tokens, int32_t in_features, const void *weight,
+                          int32_t weight_rows, const uint64_t *peer_bases, int32_t world,
+                          int32_t rank, int32_t tokens_max, void *own_base, int32_t dtype,
+                          int32_t flags, int32_t *error_flag, void *stream);
+int dsb_peer_add_rms_norm(void *own_base, int32_t world, int32_t tokens_max, const void *residual,
+                          int64_t residual_row_stride, const void *weight, void *x_out,
+                          int64_t x_row_stride, void *out, int64_t out_row_stride, int32_t rows,
+                          int32_t cols, float eps, int32_t dtype, int32_t *error_flag,
+                          void *stream);
+
 /* Request slots on the device (set_active_requests, diffspec/runtime.py:
  * 755-778).  slot_keys[num_slots] is the slot table, kept on the device
  * between calls: the key of the request owning each slot, negative when the

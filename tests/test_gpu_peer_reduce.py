@@ -1,0 +1,117 @@
+"""Fused row-split linear + all-reduce over peer memory (dsb_draft_linear_peer,
+dsb_peer_add_rms_norm), run on one GPU with virtual ranks whose exchange
+buffers all live on it (PeerExchange.local): every rank's linear runs before
+any rank's add + RMSNorm, so no kernel waits for one that has not been
+launched.  Each rank's result must equal, bit for bit, the rank-ordered fp32
+sum of the ranks' "partial" linears followed by dsb_add_rms_norm, over
+several calls in a row (both buffer parities, ragged token counts); the
+tensor-parallel layer's fused stages must equal its all-reduce stages."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from test_gpu_draft_layer_tp import D, HK, MAX_LEN, SLOTS, _inputs
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("packed", [False, True])
+def test_peer_linear_and_norm_match_rank_ordered_sum(dsb, cuda, world, packed):
+    dl = dsb.draft_layer
+    features, k, tmax = 2048, 1024, 16
+    g = torch.Generator(device=cuda).manual_seed(world * 10 + packed)
+    ws = [(torch.randn((features, k), generator=g, device=cuda) / k ** 0.5).bfloat16()
+          for _ in range(world)]
+    wl = [dl.pack_linear_weight(w) if packed else w for w in ws]
+    norm_w = (torch.rand((features,), generator=g, device=cuda) + 0.5).bfloat16()
+    sites = dsb.parallel.PeerExchange.local(world, tmax, features, cuda)
+    try:
+        for call, tokens in enumerate((16, 16, 5, 16)):  # parities 0, 1, 0, 1
+            xs = [torch.randn((tokens, k), generator=g, device=cuda).bfloat16() for _ in range(world)]
+            res = torch.randn((tokens, features), generator=g, device=cuda).bfloat16()
+            parts = [dl.draft_linear(x, w, "partial", packed=packed) for x, w in zip(xs, wl)]
+            total = parts[0].clone()
+            for p in parts[1:]:
+                total += p  # rank order, fp32
+            want_x, want_n = dl.add_rms_norm(total, res, norm_w, 1e-6)
+            for x, w, site in zip(xs, wl, sites):
+                dl.draft_linear_peer(x, w, site, packed=packed)
+            for site in sites:
+                got_x, got_n = dl.peer_add_rms_norm(site, res, norm_w if call % 2 == 0 else None,
+                                                    1e-6)
+                assert torch.equal(got_x, want_x), (call, site.rank)
+                if call % 2 == 0:
+                    assert torch.equal(got_n, want_n), (call, site.rank)
+            torch.cuda.synchronize()
+            assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+    finally:
+        sites[0].close()
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_tp_layer_peer_stages_match_all_reduce_stages(dsb, cuda, world):
+    """Eagle3DraftLayerTP with peer sites: its three fused stages, run rank
+    after rank, against its all-reduce stages with a rank-ordered sum, twice
+    in a row; world 1 also against the single-GPU layer."""
+    dl = dsb.draft_layer
+    full = dl.Eagle3DraftLayer(cuda, seed=9)
+    inp = _inputs(cuda)
+    offset = 1
+    o_sites = dsb.parallel.PeerExchange.local(world, 16, full.w_o.shape[0], cuda)
+    d_sites = dsb.parallel.PeerExchange.local(world, 16, full.w_o.shape[0], cuda)
+    try:
+        shards = [dl.Eagle3DraftLayerTP(full, r, world, all_reduce=lambda t: None,
+                                        peer=(o_sites[r], d_sites[r])) for r in range(world)]
+
+        def caches():
+            return [dict(raw_k=torch.zeros((SLOTS, MAX_LEN, sh.hk, D), dtype=torch.bfloat16,
+                                           device=cuda),
+                         raw_v=torch.zeros((SLOTS, MAX_LEN, sh.hk, D), dtype=torch.bfloat16,
+                                           device=cuda),
+                         wk=inp["wk"][:, sh.kv_heads].contiguous(),
+                         wv=inp["wv"][:, sh.kv_heads].contiguous()) for sh in shards]
+
+        kw = dict(slots=inp["slots"], abs_positions=inp["abs_pos"],
+                  local_positions=inp["local_pos"] - offset, position_offset=offset,
+                  cos_sin=inp["cos_sin"])
+        for _ in range(2):
+            ca, cb = caches(), caches()
+            parts = [sh.attention_partial(inp["x_in"], raw_key=c["raw_k"], raw_value=c["raw_v"],
+                                          working_key=c["wk"], working_value=c["wv"], **kw)
+                     for sh, c in zip(shards, ca)]
+            o_sum = parts[0].clone()
+            for p in parts[1:]:
+                o_sum += p
+            mlp = [sh.mlp_partial(o_sum, inp["residual"]) for sh in shards]
+            d_sum = mlp[0][1].clone()
+            for _, p in mlp[1:]:
+                d_sum += p
+            want = [sh.finish(d_sum, x) for sh, (x, _) in zip(shards, mlp)]
+            for sh, c in zip(shards, cb):
+                sh.attention_peer(inp["x_in"], raw_key=c["raw_k"], raw_value=c["raw_v"],
+                                  working_key=c["wk"], working_value=c["wv"], **kw)
+            xs = [sh.mlp_peer(inp["residual"]) for sh in shards]
+            got = [sh.finish_peer(x) for sh, x in zip(shards, xs)]
+            torch.cuda.synchronize()
+            assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+            for a, b in zip(got, want):
+                assert torch.equal(a, b)
+            for a, b in zip(cb, ca):
+                for key in a:
+                    assert torch.equal(a[key], b[key])
+        if world == 1:
+            raw_k = torch.zeros((SLOTS, MAX_LEN, HK, D), dtype=torch.bfloat16, device=cuda)
+            ref = full.step(inp["x_in"], inp["residual"], raw_key=raw_k,
+                            raw_value=torch.zeros_like(raw_k), working_key=inp["wk"].clone(),
+                            working_value=inp["wv"].clone(), **kw)
+            out = shards[0].step(inp["x_in"], inp["residual"], raw_key=raw_k.clone(),
+                                 raw_value=torch.zeros_like(raw_k),
+                                 working_key=inp["wk"].clone(), working_value=inp["wv"].clone(),
+                                 **kw)
+            assert torch.equal(out, ref)
+    finally:
+        o_sites[0].close()
+        d_sites[0].close()

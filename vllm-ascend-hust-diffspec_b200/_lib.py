@@ -148,6 +148,17 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I32, _I32, _I32, _P, _I32,
          _I32, _P, _P, _P, _P],
     ),
+    "dsb_peer_buffer_bytes": (_I64, [_I32, _I32, _I32]),
+    "dsb_peer_buffer_create": (ctypes.c_int, [_I32, _I32, _I32, ctypes.POINTER(ctypes.c_void_p)]),
+    "dsb_peer_buffer_destroy": (ctypes.c_int, [_P]),
+    "dsb_ipc_handle": (ctypes.c_int, [_P, _P]),
+    "dsb_ipc_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "dsb_ipc_close": (ctypes.c_int, [_P]),
+    "dsb_draft_linear_peer": (
+        ctypes.c_int, [_P, _I32, _I32, _P, _I32, _P, _I32, _I32, _I32, _P, _I32, _I32, _P, _P]),
+    "dsb_peer_add_rms_norm": (
+        ctypes.c_int,
+        [_P, _I32, _I32, _P, _I64, _P, _P, _I64, _P, _I64, _I32, _I32, _F32, _I32, _P, _P]),
     "dsb_assign_request_slots": (
         ctypes.c_int, [_P, _I32, _P, _I32, _P, _P, _P, _P, _P, _P],
     ),

@@ -39,6 +39,7 @@
 #include <utility>
 
 #include "common.cuh"
+#include "peer.cuh"
 #include "tma_umma.cuh"
 
 namespace dsb {
@@ -51,7 +52,8 @@ constexpr int kLnABytes = 128 * 64 * 2;     // weight box [128 rows][64 cols]
 constexpr int kLnBBytes = kLnTok * 64 * 2;  // activation box [16 rows][64 cols]
 constexpr int kLnMaxK = 1 << 16;
 
-enum Epilogue : int { kPlain = 0, kResidual = 1, kSwiglu = 2, kPartialF32 = 3 };
+// kPeerF32: the fp32 sums go to every rank's peer exchange buffer (peer.cuh)
+enum Epilogue : int { kPlain = 0, kResidual = 1, kSwiglu = 2, kPartialF32 = 3, kPeerF32 = 4 };
 
 template <int RANKS> struct LnCfg {
   static constexpr int kTpr = kLnTok / RANKS;  // tokens each rank sums
@@ -84,6 +86,13 @@ struct LnArgs {
   int64_t max_len;
   int T, K, N;
   int32_t *err;
+  // kPeerF32: base of every rank's exchange buffer as mapped here ([world]),
+  // this rank, the buffers' token capacity, the flags' offset in a buffer,
+  // and this rank's own sync words (epoch, producer ticket)
+  const uint64_t *peers;
+  int pworld, prank, ptmax;
+  int64_t pflags_off;
+  uint32_t *psync;
 };
 
 // Cluster size forced by the environment (0: chosen per launch):
@@ -186,6 +195,7 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
   // while the weights stream: this thread's residual values, or the slot and
   // position of each token it stores.
   const int g = f0 + tid;  // output feature of this thread in the epilogue
+  const uint32_t pepoch = a.mode == kPeerF32 ? *reinterpret_cast<volatile const uint32_t *>(a.psync) : 0u;
   float res[kTpr];
   int32_t tslot[kTpr];
   int64_t tpos[kTpr];
@@ -347,6 +357,36 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
       const float gt = sw[j * 128 + f], u = sw[j * 128 + f + 64];
       const float sg = Elem<T>::to_f(Elem<T>::from_f(silu_f(gt)));  // SiluAndMul rounds silu
       out[(int64_t)t * a.ldo + f0 / 2 + f] = Elem<T>::from_f(__fmul_rn(sg, u));
+    }
+    return;
+  }
+
+  if (a.mode == kPeerF32) {
+    // Fused all-reduce: this rank's fp32 sums into its slot of every rank's
+    // buffer (peer stores over NVLink, own buffer included), then the last
+    // CTA of the launch to take the ticket publishes the call's flag on
+    // every rank, after fences that order every CTA's stores before it.
+    const int par = (int)(pepoch & 1u);
+    const int64_t slot0 = (int64_t)(par * a.pworld + a.prank) * a.ptmax;
+#pragma unroll
+    for (int j = 0; j < kTpr; ++j) {
+      const int t = t0 + kTpr * rank + j;
+      if (t >= a.T) continue;
+      for (int q = 0; q < a.pworld; ++q)
+        reinterpret_cast<float *>(a.peers[q])[(slot0 + t) * a.N + g] = v[j];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+      if (atomicAdd(a.psync + 1, 1u) == total - 1) {
+        a.psync[1] = 0;  // the ticket, reset for the next call
+        __threadfence_system();
+        for (int q = 0; q < a.pworld; ++q)
+          st_release_sys(reinterpret_cast<uint32_t *>(a.peers[q] + a.pflags_off) +
+                             par * a.pworld + a.prank,
+                         pepoch + 1u);
+      }
     }
     return;
   }
@@ -614,6 +654,39 @@ extern "C" int dsb_draft_linear(const void *x, int32_t tokens, int32_t in_featur
   a.K = in_features;
   a.N = weight_rows;
   a.err = error_flag;
+  return dispatch(x, weight, a, dtype, stream);
+}
+
+extern "C" int dsb_draft_linear_peer(const void *x, int32_t tokens, int32_t in_features,
+                                     const void *weight, int32_t weight_rows,
+                                     const uint64_t *peer_bases, int32_t world, int32_t rank,
+                                     int32_t tokens_max, void *own_base, int32_t dtype,
+                                     int32_t flags, int32_t *error_flag, void *stream) {
+  if (tokens < 0) return fail(DSB_ERR_INVALID, "negative token count");
+  if (world < 1 || world > kPeerMaxWorld || rank < 0 || rank >= world)
+    return fail(DSB_ERR_INVALID, "world must be in [1, 8] and rank in [0, world)");
+  if (tokens > tokens_max) return fail(DSB_ERR_INVALID, "more tokens than the exchange buffer holds");
+  if (!peer_bases || !own_base) return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (tokens == 0) return DSB_OK;
+  if (int e = check_common(x, tokens, in_features, weight, weight_rows, dtype)) return e;
+  const PeerLayout L(world, tokens_max, weight_rows);
+  LnArgs a{};
+  a.split = weight_rows;
+  a.mode = kPeerF32;
+  a.prefetch = (flags & DSB_LINEAR_PREFETCH_WEIGHT) != 0;
+  a.prefetch_l2 = a.prefetch && (flags & DSB_LINEAR_PREFETCH_L2) != 0;
+  a.packed = (flags & DSB_LINEAR_PACKED_WEIGHT) != 0;
+  a.wpacked = weight;
+  a.T = tokens;
+  a.K = in_features;
+  a.N = weight_rows;
+  a.err = error_flag;
+  a.peers = peer_bases;
+  a.pworld = world;
+  a.prank = rank;
+  a.ptmax = tokens_max;
+  a.pflags_off = L.flags_off;
+  a.psync = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(own_base) + L.sync_off);
   return dispatch(x, weight, a, dtype, stream);
 }
 

@@ -26,6 +26,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace dsb {
 namespace {
@@ -97,22 +98,53 @@ __global__ void __launch_bounds__(kNormThreads)
 // tensor-parallel layer whose linears all-reduce fp32 partials reaches the
 // same values as the single-GPU layer up to the partials' summation order.
 // One CTA per row; cols a multiple of 8.
-template <typename T>
+// The peer variant's view of this rank's exchange buffer (peer.cuh).
+struct PeerIn {
+  const float *data;      // [2][world][tokens_max][cols]
+  const uint32_t *flags;  // [2][world]
+  uint32_t *sync;         // epoch, producer ticket, consumer ticket
+  int world, tmax;
+};
+
+// PEER: the fp32 partial of (row, c) is the sum, in rank order, of every
+// rank's partial in this rank's exchange buffer, read once all ranks' flags
+// for the call are set (bounded wait); the last CTA advances the epoch.
+template <typename T, bool PEER>
 __global__ void __launch_bounds__(kNormThreads)
     add_rms_norm_kernel(const float *__restrict__ part, int64_t p_stride,
                         const T *__restrict__ res, int64_t r_stride, const T *__restrict__ w,
                         T *__restrict__ x_out, int64_t x_stride, T *__restrict__ out,
-                        int64_t out_stride, int cols, float eps) {
+                        int64_t out_stride, int cols, float eps, PeerIn pin, int32_t *err) {
   __shared__ float red[kNormThreads / 32];
   pdl_begin();
+  uint32_t epoch = 0;
+  if (PEER) {
+    epoch = *reinterpret_cast<volatile const uint32_t *>(pin.sync);
+    part = pin.data + (int64_t)(epoch & 1u) * pin.world * pin.tmax * cols;
+    p_stride = cols;
+    if (threadIdx.x == 0 &&
+        !peer_wait_flags(pin.flags + (epoch & 1u) * pin.world, pin.world, epoch + 1u))
+      flag_error(err, DSB_FLAG_TIMEOUT);
+    __syncthreads();
+  }
   const float *prow = part + blockIdx.x * p_stride;
+  const int64_t rank_stride = PEER ? (int64_t)pin.tmax * cols : 0;
   const T *rrow = res + blockIdx.x * r_stride;
   T *xrow = x_out + blockIdx.x * x_stride;
   const int vecs = cols / 8;
   float ss = 0.f;
   auto sum8 = [&](int v, float (&f)[8]) {
-    const float4 a = *reinterpret_cast<const float4 *>(prow + 8 * v);
-    const float4 b = *reinterpret_cast<const float4 *>(prow + 8 * v + 4);
+    float4 a = *reinterpret_cast<const float4 *>(prow + 8 * v);
+    float4 b = *reinterpret_cast<const float4 *>(prow + 8 * v + 4);
+    if (PEER)
+      for (int q = 1; q < pin.world; ++q) {
+        const float4 a2 = *reinterpret_cast<const float4 *>(prow + q * rank_stride + 8 * v);
+        const float4 b2 = *reinterpret_cast<const float4 *>(prow + q * rank_stride + 8 * v + 4);
+        a = make_float4(__fadd_rn(a.x, a2.x), __fadd_rn(a.y, a2.y), __fadd_rn(a.z, a2.z),
+                        __fadd_rn(a.w, a2.w));
+        b = make_float4(__fadd_rn(b.x, b2.x), __fadd_rn(b.y, b2.y), __fadd_rn(b.z, b2.z),
+                        __fadd_rn(b.w, b2.w));
+      }
     const float pv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     float r[8];
     load8(rrow + 8 * v, r);
@@ -126,24 +158,33 @@ __global__ void __launch_bounds__(kNormThreads)
 #pragma unroll
     for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
   }
-  if (w == nullptr) return;
+  if (w != nullptr) {
 #pragma unroll
-  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  float total = 0.f;
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float total = 0.f;
 #pragma unroll
-  for (int i = 0; i < kNormThreads / 32; ++i) total += red[i];
-  const float inv = rsqrtf(total / static_cast<float>(cols) + eps);
-  T *orow = out + blockIdx.x * out_stride;
-  for (int v = threadIdx.x; v < vecs; v += kNormThreads) {
-    float f[8], g[8];
-    sum8(v, f);
-    load8(w + 8 * v, g);
+    for (int i = 0; i < kNormThreads / 32; ++i) total += red[i];
+    const float inv = rsqrtf(total / static_cast<float>(cols) + eps);
+    T *orow = out + blockIdx.x * out_stride;
+    for (int v = threadIdx.x; v < vecs; v += kNormThreads) {
+      float f[8], g[8];
+      sum8(v, f);
+      load8(w + 8 * v, g);
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      f[i] = __fmul_rn(Elem<T>::to_f(Elem<T>::from_f(__fmul_rn(f[i], inv))), g[i]);
-    store8(orow + 8 * v, f);
+      for (int i = 0; i < 8; ++i)
+        f[i] = __fmul_rn(Elem<T>::to_f(Elem<T>::from_f(__fmul_rn(f[i], inv))), g[i]);
+      store8(orow + 8 * v, f);
+    }
+  }
+  if (PEER) {
+    // every CTA has read the call's epoch and data: the last one advances it
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(pin.sync + 2, 1u) == gridDim.x - 1) {
+      pin.sync[2] = 0;
+      pin.sync[0] = epoch + 1u;
+    }
   }
 }
 
@@ -279,18 +320,65 @@ extern "C" int dsb_add_rms_norm(const float *partial, int64_t partial_row_stride
                 "add_rms_norm needs cols and row strides that are multiples of 8 (>= cols) and "
                 "16-byte aligned rows");
   const cudaStream_t st = as_stream(stream);
+  const PeerIn none{};
   if (dtype == DSB_BF16)
-    launch_kernel(add_rms_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), 0, st,
+    launch_kernel(add_rms_norm_kernel<__nv_bfloat16, false>, dim3(rows), dim3(kNormThreads), 0, st,
                   partial, partial_row_stride, static_cast<const __nv_bfloat16 *>(residual),
                   residual_row_stride, static_cast<const __nv_bfloat16 *>(weight),
                   static_cast<__nv_bfloat16 *>(x_out), x_row_stride,
-                  static_cast<__nv_bfloat16 *>(out), out_row_stride, (int)cols, eps);
+                  static_cast<__nv_bfloat16 *>(out), out_row_stride, (int)cols, eps, none,
+                  (int32_t *)nullptr);
   else
-    launch_kernel(add_rms_norm_kernel<__half>, dim3(rows), dim3(kNormThreads), 0, st, partial,
-                  partial_row_stride, static_cast<const __half *>(residual), residual_row_stride,
-                  static_cast<const __half *>(weight), static_cast<__half *>(x_out), x_row_stride,
-                  static_cast<__half *>(out), out_row_stride, (int)cols, eps);
+    launch_kernel(add_rms_norm_kernel<__half, false>, dim3(rows), dim3(kNormThreads), 0, st,
+                  partial, partial_row_stride, static_cast<const __half *>(residual),
+                  residual_row_stride, static_cast<const __half *>(weight),
+                  static_cast<__half *>(x_out), x_row_stride, static_cast<__half *>(out),
+                  out_row_stride, (int)cols, eps, none, (int32_t *)nullptr);
   return check_launch("add_rms_norm_kernel");
+}
+
+extern "C" int dsb_peer_add_rms_norm(void *own_base, int32_t world, int32_t tokens_max,
+                                     const void *residual, int64_t residual_row_stride,
+                                     const void *weight, void *x_out, int64_t x_row_stride,
+                                     void *out, int64_t out_row_stride, int32_t rows,
+                                     int32_t cols, float eps, int32_t dtype, int32_t *error_flag,
+                                     void *stream) {
+  if (rows < 0 || cols <= 0) return fail(DSB_ERR_INVALID, "rows must be >= 0 and cols > 0");
+  if (world < 1 || world > kPeerMaxWorld || rows > tokens_max)
+    return fail(DSB_ERR_INVALID, "world must be in [1, 8] and rows at most the buffer's tokens");
+  if (rows == 0) return DSB_OK;
+  if (dtype != DSB_BF16 && dtype != DSB_F16)
+    return fail(DSB_ERR_INVALID, "add_rms_norm rows and weight must be BF16 or FP16");
+  if (!own_base || !residual || !x_out || (weight && !out))
+    return fail(DSB_ERR_INVALID, "null pointer argument");
+  if (!(eps >= 0.f)) return fail(DSB_ERR_INVALID, "eps must be >= 0");
+  const bool strides_ok = cols % 8 == 0 && residual_row_stride % 8 == 0 && x_row_stride % 8 == 0 &&
+                          residual_row_stride >= cols && x_row_stride >= cols &&
+                          (!weight || (out_row_stride % 8 == 0 && out_row_stride >= cols));
+  if (!strides_ok || !aligned16(own_base) || !aligned16(residual) || !aligned16(x_out) ||
+      (weight && (!aligned16(weight) || !aligned16(out))))
+    return fail(DSB_ERR_UNSUPPORTED,
+                "add_rms_norm needs cols and row strides that are multiples of 8 (>= cols) and "
+                "16-byte aligned rows");
+  const PeerLayout L(world, tokens_max, cols);
+  uint8_t *b = static_cast<uint8_t *>(own_base);
+  const PeerIn pin{reinterpret_cast<const float *>(b), reinterpret_cast<const uint32_t *>(b + L.flags_off),
+                   reinterpret_cast<uint32_t *>(b + L.sync_off), (int)world, (int)tokens_max};
+  const cudaStream_t st = as_stream(stream);
+  if (dtype == DSB_BF16)
+    launch_kernel(add_rms_norm_kernel<__nv_bfloat16, true>, dim3(rows), dim3(kNormThreads), 0, st,
+                  (const float *)nullptr, (int64_t)0, static_cast<const __nv_bfloat16 *>(residual),
+                  residual_row_stride, static_cast<const __nv_bfloat16 *>(weight),
+                  static_cast<__nv_bfloat16 *>(x_out), x_row_stride,
+                  static_cast<__nv_bfloat16 *>(out), out_row_stride, (int)cols, eps, pin,
+                  error_flag);
+  else
+    launch_kernel(add_rms_norm_kernel<__half, true>, dim3(rows), dim3(kNormThreads), 0, st,
+                  (const float *)nullptr, (int64_t)0, static_cast<const __half *>(residual),
+                  residual_row_stride, static_cast<const __half *>(weight),
+                  static_cast<__half *>(x_out), x_row_stride, static_cast<__half *>(out),
+                  out_row_stride, (int)cols, eps, pin, error_flag);
+  return check_launch("add_rms_norm_kernel (peer)");
 }
 
 extern "C" int dsb_rope_qk(void *query, int64_t query_row_stride, int32_t num_query_heads,

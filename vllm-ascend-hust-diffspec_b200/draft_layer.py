@@ -27,6 +27,7 @@ from .attention import AttentionWorkspace, draft_decode_attention
 from .kernels import qkv_projection_write_raw
 
 __all__ = ["Eagle3DraftLayer", "Eagle3DraftLayerTP", "add_rms_norm", "draft_linear",
+           "draft_linear_peer", "peer_add_rms_norm",
            "interleave_gate_up", "pack_linear_weight", "rms_norm", "rope_qk", "silu_mul"]
 
 
@@ -152,6 +153,52 @@ def add_rms_norm(partial: torch.Tensor, residual: torch.Tensor, weight: torch.Te
               _lib.ptr(out), _rows(out, "out") if out is not None else 0, residual.shape[0],
               residual.shape[1], float(eps), _lib.dtype_code(residual.dtype),
               _lib.stream_ptr(device))
+    return x_out, out
+
+
+def draft_linear_peer(x: torch.Tensor, weight: torch.Tensor, site, packed: bool = False,
+                      prefetch_weight: bool = True) -> None:
+    """This rank's share of a row-split linear, all-reduced over NVLink:
+    ``x [T, K] @ weight.T`` as :func:`draft_linear` computes it, its fp32 sums
+    stored into this rank's slot of every rank's exchange buffer of ``site``
+    (a :class:`parallel.PeerExchange`), one launch
+    (``dsb_draft_linear_peer``).  Read the reduced result with
+    :func:`peer_add_rms_norm`."""
+    if x.ndim != 2 or weight.ndim != 2 or weight.shape[1] != x.shape[1] or x.dtype != weight.dtype:
+        raise ValueError("x must be [T, K] and weight [rows, K] in one dtype")
+    if not (x.is_contiguous() and weight.is_contiguous()):
+        raise ValueError("x and weight must be contiguous")
+    if weight.shape[0] != site.features or x.shape[0] > site.tokens_max:
+        raise ValueError("weight rows must equal the site's features and T its token capacity")
+    device = _lib.require_cuda(x, weight)
+    _lib.call("dsb_draft_linear_peer", _lib.ptr(x), x.shape[0], x.shape[1], _lib.ptr(weight),
+              weight.shape[0], _lib.ptr(site.bases), site.world, site.rank, site.tokens_max,
+              site.own_base, _lib.dtype_code(x.dtype),
+              (1 if prefetch_weight else 0) | (2 if packed else 0),
+              _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device))
+
+
+def peer_add_rms_norm(site, residual: torch.Tensor, weight: torch.Tensor | None, eps: float,
+                      x_out: torch.Tensor | None = None, out: torch.Tensor | None = None):
+    """:func:`add_rms_norm` whose fp32 ``partial`` is the sum, in rank order,
+    of every rank's :func:`draft_linear_peer` partial of ``site``'s current
+    call, once all of them have arrived (``dsb_peer_add_rms_norm``; a wait
+    bounded by time, after which the error word carries
+    DSB_FLAG_TIMEOUT).  Returns ``(x, normed)``."""
+    if residual.ndim != 2 or residual.shape[1] != site.features or residual.shape[0] > site.tokens_max:
+        raise ValueError("residual must be [T <= tokens_max, features]")
+    if weight is not None and (weight.shape != (residual.shape[-1],) or weight.dtype != residual.dtype):
+        raise ValueError("weight must be [cols] in the residual's dtype")
+    device = _lib.require_cuda(residual, weight, x_out, out)
+    if x_out is None:
+        x_out = torch.empty_like(residual)
+    if weight is not None and out is None:
+        out = torch.empty_like(residual)
+    _lib.call("dsb_peer_add_rms_norm", site.own_base, site.world, site.tokens_max,
+              _lib.ptr(residual), _rows(residual, "residual"), _lib.ptr(weight), _lib.ptr(x_out),
+              _rows(x_out, "x_out"), _lib.ptr(out), _rows(out, "out") if out is not None else 0,
+              residual.shape[0], residual.shape[1], float(eps), _lib.dtype_code(residual.dtype),
+              _lib.ptr(_lib.error_flag(device)), _lib.stream_ptr(device))
     return x_out, out
 
 
@@ -292,7 +339,12 @@ class Eagle3DraftLayerTP:
       are all-reduced (``all_reduce``, NCCL by default) and then added to the
       residual in one rounding with the next RMSNorm fused
       (:func:`add_rms_norm`), so the rounding points are the single-GPU
-      layer's; only the fp32 summation order of the split differs.
+      layer's; only the fp32 summation order of the split differs.  With
+      ``peer`` (two :class:`parallel.PeerExchange` sites, o_proj's and
+      down_proj's) the all-reduce is fused instead: each row-split linear
+      stores its partial into every rank's exchange buffer over NVLink
+      (:func:`draft_linear_peer`) and the add + RMSNorm sums them in rank
+      order (:func:`peer_add_rms_norm`); no collective launch.
 
     The shard is cut from ``full``'s weights (so any world size computes the
     same layer) and packed once.  ``step`` takes the same arguments as
@@ -301,7 +353,7 @@ class Eagle3DraftLayerTP:
     :meth:`finish` are its three stages between the two all-reduces."""
 
     def __init__(self, full: "Eagle3DraftLayer", rank: int, world: int, group=None,
-                 all_reduce=None):
+                 all_reduce=None, peer=None):
         hq, hk, d, inter = full.hq, full.hk, full.d, full.inter
         if world < 1 or hq % world or (inter // world) % 64 or inter % world:
             raise ValueError("world must divide the query heads and leave the SwiGLU features "
@@ -342,6 +394,7 @@ class Eagle3DraftLayerTP:
                 if world > 1:
                     torch.distributed.all_reduce(t, group=group)
         self.all_reduce = all_reduce
+        self.peer = peer  # (o_proj site, down_proj site) or None
 
     def weight_bytes(self) -> int:
         return sum(t.numel() * t.element_size()
@@ -377,7 +430,14 @@ class Eagle3DraftLayerTP:
 
     def step(self, x_in, residual, *, slots, abs_positions, local_positions, raw_key, raw_value,
              working_key, working_value, cos_sin, out=None, position_offset=0):
-        """One draft step of this shard: two all-reduces of fp32 partials."""
+        """One draft step of this shard: two all-reduces of fp32 partials
+        (fused into the row-split linears with ``peer``)."""
+        if self.peer is not None:
+            return self._step_peer(x_in, residual, slots=slots, abs_positions=abs_positions,
+                                   local_positions=local_positions, raw_key=raw_key,
+                                   raw_value=raw_value, working_key=working_key,
+                                   working_value=working_value, cos_sin=cos_sin, out=out,
+                                   position_offset=position_offset)
         po = self.attention_partial(
             x_in, slots=slots, abs_positions=abs_positions, local_positions=local_positions,
             raw_key=raw_key, raw_value=raw_value, working_key=working_key,
@@ -386,3 +446,39 @@ class Eagle3DraftLayerTP:
         x, pd = self.mlp_partial(po, residual)
         self.all_reduce(pd)
         return self.finish(pd, x, out=out)
+
+    def attention_peer(self, x_in, *, slots, abs_positions, local_positions, raw_key, raw_value,
+                       working_key, working_value, cos_sin, position_offset=0):
+        """:meth:`attention_partial` with the o_proj partial stored into
+        every rank's buffer of the o_proj site (fused all-reduce)."""
+        n = x_in.shape[0]
+        h = rms_norm(x_in, self.in_norm, self.eps)
+        q, kv = qkv_projection_write_raw(h, self.p_qkv, self.hq * self.d, slots, abs_positions,
+                                         raw_key, raw_value, prefetch_weight=True,
+                                         packed_weight=True)
+        k, v = rope_qk(q, kv, local_positions, cos_sin, self.hk, position_offset=position_offset)
+        attn = draft_decode_attention(q.view(n, self.hq, self.d), k, v, working_key, working_value,
+                                      slots, local_positions, self.d ** -0.5,
+                                      position_offset=position_offset, workspace=self.workspace)
+        draft_linear_peer(attn.view(n, self.hq * self.d), self.p_o, self.peer[0], packed=True)
+
+    def mlp_peer(self, residual):
+        """``x = round(sum of the ranks' o_proj partials + residual)`` once
+        they have all arrived, RMSNorm, gate_up + SwiGLU and the down_proj
+        partial into every rank's buffer of the down_proj site; returns x."""
+        x, h2 = peer_add_rms_norm(self.peer[0], residual, self.post_norm, self.eps)
+        act = draft_linear(h2, self.p_gate_up, "swiglu", packed=True)
+        draft_linear_peer(act, self.p_down, self.peer[1], packed=True)
+        return x
+
+    def finish_peer(self, x, out=None):
+        """The layer output ``round(sum of the ranks' down_proj partials + x)``."""
+        return peer_add_rms_norm(self.peer[1], x, None, self.eps, x_out=out)[0]
+
+    def _step_peer(self, x_in, residual, *, slots, abs_positions, local_positions, raw_key,
+                   raw_value, working_key, working_value, cos_sin, out, position_offset):
+        self.attention_peer(x_in, slots=slots, abs_positions=abs_positions,
+                            local_positions=local_positions, raw_key=raw_key, raw_value=raw_value,
+                            working_key=working_key, working_value=working_value, cos_sin=cos_sin,
+                            position_offset=position_offset)
+        return self.finish_peer(self.mlp_peer(residual), out=out)

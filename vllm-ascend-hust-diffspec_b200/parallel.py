@@ -14,10 +14,14 @@ shards.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-__all__ = ["gather_head_scores", "head_major", "shard_heads"]
+from . import _lib
+
+__all__ = ["PeerExchange", "gather_head_scores", "head_major", "shard_heads"]
 
 
 def shard_heads(num_kv_heads: int, world_size: int, rank: int) -> tuple[int, int]:
@@ -62,3 +66,79 @@ def head_major(gathered: torch.Tensor) -> torch.Tensor:
     order (a copy; the selection does not need it)."""
     world, rows, hk_local, n = gathered.shape
     return gathered.permute(1, 0, 2, 3).reshape(rows, world * hk_local, n)
+
+
+class PeerExchange:
+    """One all-reduce site of the fused row-split linear + all-reduce
+    (``dsb_draft_linear_peer`` then ``dsb_peer_add_rms_norm``): this rank's
+    exchange buffer and every rank's buffer as mapped in this process.
+
+    :meth:`create` (collective over ``group``) allocates the buffer through
+    the library, sends its CUDA IPC handle to the other ranks
+    (``all_gather_object``, any backend) and maps theirs: plain peer mappings
+    over NVLink, no multicast.  :meth:`local` builds ``world`` virtual ranks
+    whose buffers all live on one GPU, so the exchange's layout and sums can
+    be run rank after rank on a single device.  Every rank must then issue
+    the same sequence of calls on the site; the call count lives in the
+    buffers, so the sequence can be captured in a CUDA graph.  :meth:`close`
+    unmaps and frees."""
+
+    def __init__(self, world: int, rank: int, tokens_max: int, features: int,
+                 device: torch.device, own_base: int, bases: list[int], owned: bool,
+                 opened: list[int]):
+        self.world, self.rank = world, rank
+        self.tokens_max, self.features = tokens_max, features
+        self.device = device
+        self.own_base = own_base
+        self.bases = torch.tensor(bases, dtype=torch.int64, device=device)
+        self._owned, self._opened = owned, opened
+
+    @staticmethod
+    def _alloc(world, tokens_max, features) -> int:
+        base = ctypes.c_void_p()
+        _lib.call("dsb_peer_buffer_create", world, tokens_max, features, ctypes.byref(base))
+        return int(base.value)
+
+    @classmethod
+    def create(cls, tokens_max: int, features: int, device: torch.device,
+               group: dist.ProcessGroup | None = None) -> "PeerExchange":
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        with torch.cuda.device(device):
+            own = cls._alloc(world, tokens_max, features)
+            handle = ctypes.create_string_buffer(64)
+            _lib.call("dsb_ipc_handle", ctypes.c_void_p(own), handle)
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle.raw), group=group)
+            bases, opened = [], []
+            for q in range(world):
+                if q == rank:
+                    bases.append(own)
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.call("dsb_ipc_open", ctypes.create_string_buffer(handles[q], 64),
+                          ctypes.byref(peer))
+                bases.append(int(peer.value))
+                opened.append(int(peer.value))
+        return cls(world, rank, tokens_max, features, device, own, bases, True, opened)
+
+    @classmethod
+    def local(cls, world: int, tokens_max: int, features: int,
+              device: torch.device) -> list["PeerExchange"]:
+        with torch.cuda.device(device):
+            bases = [cls._alloc(world, tokens_max, features) for _ in range(world)]
+        sites = [cls(world, r, tokens_max, features, device, bases[r], bases, False, [])
+                 for r in range(world)]
+        sites[0]._local_all = bases  # rank 0 frees every virtual rank's buffer
+        return sites
+
+    def close(self) -> None:
+        with torch.cuda.device(self.device):
+            for base in self._opened:
+                _lib.call("dsb_ipc_close", ctypes.c_void_p(base))
+            self._opened = []
+            if self._owned:
+                _lib.call("dsb_peer_buffer_destroy", ctypes.c_void_p(self.own_base))
+                self._owned = False
+            for base in getattr(self, "_local_all", []):
+                _lib.call("dsb_peer_buffer_destroy", ctypes.c_void_p(base))
+            self._local_all = []
