@@ -475,14 +475,15 @@ int dsb_capture_raw_kv(
  * dsb_peer_buffer_bytes(world, tokens_max, features) bytes, created zeroed by
  * dsb_peer_buffer_create and mapped into the other ranks' processes with
  * dsb_ipc_handle / dsb_ipc_open (plain peer mappings; no multicast).
- * dsb_draft_linear_peer computes x . W^T like dsb_draft_linear and stores the
- * fp32 sums into this rank's slot of every rank's buffer (peer_bases[q] =
- * rank q's buffer as mapped in this process, a device array of world
- * addresses; own_base = this rank's buffer), then marks the call done on
- * every rank.  dsb_peer_add_rms_norm on each rank waits for all ranks' marks
- * (bounded by time: DSB_FLAG_TIMEOUT, and the sums are then not meaningful),
- * sums the partials in rank order and finishes as dsb_add_rms_norm with that
- * sum as `partial`.  Every rank must issue the same sequence of
+ * dsb_draft_linear_peer computes x . W^T like dsb_draft_linear and stores
+ * each fp32 sum, tagged with the call's number in the same 8-byte store, into
+ * this rank's slot of every rank's buffer (peer_bases[q] = rank q's buffer as
+ * mapped in this process, a device array of world addresses; own_base = this
+ * rank's buffer).  dsb_peer_add_rms_norm on each rank reads every rank's
+ * partials from its own buffer as their tags show them arrived (a wait
+ * bounded by time: DSB_FLAG_TIMEOUT, and the sums are then not meaningful),
+ * sums them in rank order and finishes as dsb_add_rms_norm with that sum as
+ * `partial`.  Every rank must issue the same sequence of
  * dsb_draft_linear_peer / dsb_peer_add_rms_norm calls on a site, alternating,
  * each on one stream; the call count lives in the buffer, so the sequence can
  * be captured and replayed as a CUDA graph.  world <= 8, features a multiple

@@ -87,11 +87,9 @@ struct LnArgs {
   int T, K, N;
   int32_t *err;
   // kPeerF32: base of every rank's exchange buffer as mapped here ([world]),
-  // this rank, the buffers' token capacity, the flags' offset in a buffer,
-  // and this rank's own sync words (epoch, producer ticket)
+  // this rank, the buffers' token capacity and this rank's own epoch word
   const uint64_t *peers;
   int pworld, prank, ptmax;
-  int64_t pflags_off;
   uint32_t *psync;
 };
 
@@ -363,30 +361,16 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
 
   if (a.mode == kPeerF32) {
     // Fused all-reduce: this rank's fp32 sums into its slot of every rank's
-    // buffer (peer stores over NVLink, own buffer included), then the last
-    // CTA of the launch to take the ticket publishes the call's flag on
-    // every rank, after fences that order every CTA's stores before it.
-    const int par = (int)(pepoch & 1u);
-    const int64_t slot0 = (int64_t)(par * a.pworld + a.prank) * a.ptmax;
+    // buffer (peer stores over NVLink, own buffer included), each with the
+    // call's tag in the same 8-byte store, so the readers need no flag.
+    const uint32_t tag = pepoch + 1u;
+    const int64_t slot0 = (int64_t)((int)(pepoch & 1u) * a.pworld + a.prank) * a.ptmax;
 #pragma unroll
     for (int j = 0; j < kTpr; ++j) {
       const int t = t0 + kTpr * rank + j;
       if (t >= a.T) continue;
       for (int q = 0; q < a.pworld; ++q)
-        reinterpret_cast<float *>(a.peers[q])[(slot0 + t) * a.N + g] = v[j];
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (tid == 0) {
-      const unsigned total = gridDim.x * gridDim.y * gridDim.z;
-      if (atomicAdd(a.psync + 1, 1u) == total - 1) {
-        a.psync[1] = 0;  // the ticket, reset for the next call
-        __threadfence_system();
-        for (int q = 0; q < a.pworld; ++q)
-          st_release_sys(reinterpret_cast<uint32_t *>(a.peers[q] + a.pflags_off) +
-                             par * a.pworld + a.prank,
-                         pepoch + 1u);
-      }
+        st_tagged(reinterpret_cast<uint8_t *>(a.peers[q]) + ((slot0 + t) * a.N + g) * 8, v[j], tag);
     }
     return;
   }
@@ -685,7 +669,6 @@ extern "C" int dsb_draft_linear_peer(const void *x, int32_t tokens, int32_t in_f
   a.pworld = world;
   a.prank = rank;
   a.ptmax = tokens_max;
-  a.pflags_off = L.flags_off;
   a.psync = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(own_base) + L.sync_off);
   return dispatch(x, weight, a, dtype, stream);
 }

@@ -100,15 +100,14 @@ __global__ void __launch_bounds__(kNormThreads)
 // One CTA per row; cols a multiple of 8.
 // The peer variant's view of this rank's exchange buffer (peer.cuh).
 struct PeerIn {
-  const float *data;      // [2][world][tokens_max][cols]
-  const uint32_t *flags;  // [2][world]
-  uint32_t *sync;         // epoch, producer ticket, consumer ticket
+  const uint8_t *data;  // [2][world][tokens_max][cols] (value, tag) words
+  uint32_t *sync;       // epoch, consumer ticket
   int world, tmax;
 };
 
 // PEER: the fp32 partial of (row, c) is the sum, in rank order, of every
-// rank's partial in this rank's exchange buffer, read once all ranks' flags
-// for the call are set (bounded wait); the last CTA advances the epoch.
+// rank's partial in this rank's exchange buffer, each read once it carries
+// the call's tag (bounded wait); the last CTA advances the epoch.
 template <typename T, bool PEER>
 __global__ void __launch_bounds__(kNormThreads)
     add_rms_norm_kernel(const float *__restrict__ part, int64_t p_stride,
@@ -118,34 +117,35 @@ __global__ void __launch_bounds__(kNormThreads)
   __shared__ float red[kNormThreads / 32];
   pdl_begin();
   uint32_t epoch = 0;
+  const uint8_t *prow8 = nullptr;  // PEER: this row of rank 0's words of the call
   if (PEER) {
     epoch = *reinterpret_cast<volatile const uint32_t *>(pin.sync);
-    part = pin.data + (int64_t)(epoch & 1u) * pin.world * pin.tmax * cols;
-    p_stride = cols;
-    if (threadIdx.x == 0 &&
-        !peer_wait_flags(pin.flags + (epoch & 1u) * pin.world, pin.world, epoch + 1u))
-      flag_error(err, DSB_FLAG_TIMEOUT);
-    __syncthreads();
+    prow8 = pin.data +
+            (((int64_t)(epoch & 1u) * pin.world * pin.tmax + blockIdx.x) * cols) * 8;
   }
-  const float *prow = part + blockIdx.x * p_stride;
-  const int64_t rank_stride = PEER ? (int64_t)pin.tmax * cols : 0;
+  const float *prow = PEER ? nullptr : part + blockIdx.x * p_stride;
+  const int64_t rank_stride = PEER ? (int64_t)pin.tmax * cols * 8 : 0;  // bytes
   const T *rrow = res + blockIdx.x * r_stride;
   T *xrow = x_out + blockIdx.x * x_stride;
   const int vecs = cols / 8;
   float ss = 0.f;
+  bool late = false;
   auto sum8 = [&](int v, float (&f)[8]) {
-    float4 a = *reinterpret_cast<const float4 *>(prow + 8 * v);
-    float4 b = *reinterpret_cast<const float4 *>(prow + 8 * v + 4);
-    if (PEER)
+    float pv[8];
+    if (PEER) {
+      late |= !ld_tagged8(prow8 + (int64_t)v * 64, epoch + 1u, pv);
       for (int q = 1; q < pin.world; ++q) {
-        const float4 a2 = *reinterpret_cast<const float4 *>(prow + q * rank_stride + 8 * v);
-        const float4 b2 = *reinterpret_cast<const float4 *>(prow + q * rank_stride + 8 * v + 4);
-        a = make_float4(__fadd_rn(a.x, a2.x), __fadd_rn(a.y, a2.y), __fadd_rn(a.z, a2.z),
-                        __fadd_rn(a.w, a2.w));
-        b = make_float4(__fadd_rn(b.x, b2.x), __fadd_rn(b.y, b2.y), __fadd_rn(b.z, b2.z),
-                        __fadd_rn(b.w, b2.w));
+        float pq[8];
+        late |= !ld_tagged8(prow8 + q * rank_stride + (int64_t)v * 64, epoch + 1u, pq);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pv[i] = __fadd_rn(pv[i], pq[i]);
       }
-    const float pv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    } else {
+      const float4 a = *reinterpret_cast<const float4 *>(prow + 8 * v);
+      const float4 b = *reinterpret_cast<const float4 *>(prow + 8 * v + 4);
+      pv[0] = a.x, pv[1] = a.y, pv[2] = a.z, pv[3] = a.w;
+      pv[4] = b.x, pv[5] = b.y, pv[6] = b.z, pv[7] = b.w;
+    }
     float r[8];
     load8(rrow + 8 * v, r);
 #pragma unroll
@@ -179,10 +179,11 @@ __global__ void __launch_bounds__(kNormThreads)
     }
   }
   if (PEER) {
+    if (late) flag_error(err, DSB_FLAG_TIMEOUT);
     // every CTA has read the call's epoch and data: the last one advances it
     __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(pin.sync + 2, 1u) == gridDim.x - 1) {
-      pin.sync[2] = 0;
+    if (threadIdx.x == 0 && atomicAdd(pin.sync + 1, 1u) == gridDim.x - 1) {
+      pin.sync[1] = 0;
       pin.sync[0] = epoch + 1u;
     }
   }
@@ -362,8 +363,7 @@ extern "C" int dsb_peer_add_rms_norm(void *own_base, int32_t world, int32_t toke
                 "16-byte aligned rows");
   const PeerLayout L(world, tokens_max, cols);
   uint8_t *b = static_cast<uint8_t *>(own_base);
-  const PeerIn pin{reinterpret_cast<const float *>(b), reinterpret_cast<const uint32_t *>(b + L.flags_off),
-                   reinterpret_cast<uint32_t *>(b + L.sync_off), (int)world, (int)tokens_max};
+  const PeerIn pin{b, reinterpret_cast<uint32_t *>(b + L.sync_off), (int)world, (int)tokens_max};
   const cudaStream_t st = as_stream(stream);
   if (dtype == DSB_BF16)
     launch_kernel(add_rms_norm_kernel<__nv_bfloat16, true>, dim3(rows), dim3(kNormThreads), 0, st,
