@@ -1289,6 +1289,93 @@ def run_draft_step(args):
         dist.destroy_process_group()
 
 
+def run_peer_exchange(args):
+    """Under torchrun (N >= 2 ranks): the cost of one all-reduce of a row-split
+    linear at config 5's shape (16 tokens x 2048 features fp32, a 2048 x 2048
+    weight share), as a CUDA graph of 100 (linear + add + RMSNorm) pairs,
+    max over ranks: fused over NVLink peer memory (dsb_draft_linear_peer +
+    dsb_peer_add_rms_norm), the same kernels on a one-rank site of this GPU
+    (no cross-GPU traffic), the partial linear + NCCL all_reduce +
+    add_rms_norm, and the partial linear + add_rms_norm with no exchange."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    dsb = importlib.import_module("vllm-ascend-hust-diffspec_b200")
+    dl = dsb.draft_layer
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world < 2 or world != args.gpus:
+        raise SystemExit("--peer-exchange runs under torchrun with --gpus N = WORLD_SIZE >= 2")
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    feats, k, tokens = 2048, 2048, B_GROUP
+    g = torch.Generator(device=device).manual_seed(rank)
+    w = dl.pack_linear_weight((torch.randn((feats, k), generator=g, device=device) / k ** 0.5).bfloat16())
+    x = torch.randn((tokens, k), generator=g, device=device).bfloat16()
+    res = torch.randn((tokens, feats), generator=g, device=device).bfloat16()
+    norm_w = torch.ones((feats,), device=device).bfloat16()
+    part = torch.empty((tokens, feats), dtype=torch.float32, device=device)
+    site = dsb.parallel.PeerExchange.create(tokens, feats, device)
+    local = dsb.parallel.PeerExchange.local(1, tokens, feats, device)[0]
+    dist.barrier()
+
+    def fused(s):
+        dl.draft_linear_peer(x, w, s, packed=True)
+        dl.peer_add_rms_norm(s, res, norm_w, 1e-6)
+
+    def nccl():
+        dl.draft_linear(x, w, "partial", out=part, packed=True)
+        dist.all_reduce(part)
+        dl.add_rms_norm(part, res, norm_w, 1e-6)
+
+    def none():
+        dl.draft_linear(x, w, "partial", out=part, packed=True)
+        dl.add_rms_norm(part, res, norm_w, 1e-6)
+
+    out = {}
+    for name, fn in (("peer_fused", lambda: fused(site)), ("fused_one_rank_site", lambda: fused(local)),
+                     ("nccl_all_reduce", nccl), ("no_exchange", none)):
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(max(3, args.warmup)):
+                fn()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(100):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        t = torch.tensor([a.elapsed_time(b) * 1e3 / (100 * args.steps)], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[name] = round(float(t.item()), 2)
+        del graph
+        torch.cuda.synchronize(device)
+        dist.barrier()
+    flag = dsb._lib.read_and_clear_error_flag(device)
+    if rank == 0:
+        print(json.dumps(dict(mode="peer_exchange", n_gpus=world, tokens=tokens, features=feats,
+                              us_per_linear_and_add_rms_norm=out, error_flag=flag)), flush=True)
+    torch.cuda.synchronize(device)
+    dist.barrier()  # no rank still writes into another's exchange buffer
+    site.close()
+    local.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_kv_projection(args):
     """Time the draft-layer K/V projection + raw-cache write (config 5 decode
     step: 16 tokens, Eagle3 qkv input 4096, 4 kv heads x 128) against the
@@ -1636,6 +1723,9 @@ def main():
                    help="time the K/V projection + raw-cache write (config 5 decode step)")
     p.add_argument("--draft-step", action="store_true",
                    help="config 5: draft tokens/s of a draft layer over the DiffSpec cache")
+    p.add_argument("--peer-exchange", action="store_true",
+                   help="under torchrun: time one fused peer all-reduce of a row-split linear "
+                        "against NCCL and against no exchange")
     p.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                    help="--draft-step --draft-parallel tp: the all-reduces fused into the "
                         "row-split linears over NVLink peer memory, or NCCL all-reduces")
@@ -1657,6 +1747,8 @@ def main():
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.kv_projection:
         run_kv_projection(args)
+    elif args.peer_exchange:
+        run_peer_exchange(args)
     elif args.draft_step:
         run_draft_step(args)
     elif args.draft_linear:
