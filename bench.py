@@ -640,13 +640,19 @@ def run_ours(args):
     hq_local = HQ // hg
     rows = B_GROUP * hg
     w = Workload(torch, dsb, device, rows, hk_local, hq_local, seed=1234 + rank // hg)
-    exchange = None
+    exchange = site = None
     if hg > 1:
         # rank-major [hg, rows, hk_local, N]: the all-gather writes it and the
         # selection reads it in place
         gathered = torch.empty((hg, rows, hk_local, w.max_chunks), dtype=torch.float32,
                                device=device)
-        exchange = lambda parts: dsb.parallel.gather_head_scores(parts, group, out=gathered)  # noqa: E731
+        if args.retrieval_exchange == "peer":
+            site = dsb.parallel.PeerExchange.create(1, rows * hk_local * w.max_chunks, device,
+                                                    group=group)
+            dist.barrier()  # every rank's buffer is mapped before the first call
+            exchange = lambda parts: dsb.parallel.peer_all_gather(parts, site, gathered)  # noqa: E731
+        else:
+            exchange = lambda parts: dsb.parallel.gather_head_scores(parts, group, out=gathered)  # noqa: E731
     launches = period_launches(w, exchange, total_hq=HQ,
                                gathered=gathered if exchange is not None else None)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
@@ -668,7 +674,9 @@ def run_ours(args):
         try:
             graphs.append(Graph(torch, launches, device))
             step = graphs[0].replay
-            res_mode = "one CUDA graph per bench step, NCCL exchange captured in it"
+            res_mode = ("one CUDA graph per bench step, peer all-gather (NVLink, two launches) "
+                        "captured in it" if site is not None else
+                        "one CUDA graph per bench step, NCCL exchange captured in it")
         except Exception:  # noqa: BLE001 - fall back to the split graph
             graphs = [Graph(torch, launches[:cut], device), Graph(torch, launches[cut + 1:], device)]
 
@@ -728,7 +736,7 @@ def run_ours(args):
     result = dict(ms=ms, value=value, clocks=clocks.summary(), w=w, launches=launches, rows=rows,
                   graph_mode=res_mode,
                   hk_local=hk_local, world=world, rank=rank, device=device, torch=torch, dsb=dsb,
-                  dist=dist if world > 1 else None, flush=flush, group=group, hg=hg)
+                  dist=dist if world > 1 else None, flush=flush, group=group, hg=hg, site=site)
     return result
 
 
@@ -867,12 +875,18 @@ def emit_ours(args):
                     hbm_frac_whole_step=round(b["total"] / (period_ms / 1e3) / 1e9 / peak, 4),
                     graph=res["graph_mode"]),
         roofline=roofline, cpu_baseline=cpu, e2e=e2e,
-        gpu_launches=sum(1 for k, _ in res["launches"] if k != "exchange") * args.steps,
+        gpu_launches=(sum(1 for k, _ in res["launches"] if k != "exchange") +
+                      (2 if res["site"] is not None else 0)) * args.steps,
         clocks=res["clocks"])
     if rank == 0:
         print(json.dumps(line), flush=True)
     if res["dist"] is not None:
-        res["dist"].barrier()
+        torch = res["torch"]
+        torch.cuda.synchronize(res["device"])
+        res["dist"].barrier()  # no rank still writes into another's exchange buffer
+        if res["site"] is not None:
+            res["site"].close()
+            res["dist"].barrier()
         res["dist"].destroy_process_group()
 
 
@@ -1726,6 +1740,9 @@ def main():
     p.add_argument("--peer-exchange", action="store_true",
                    help="under torchrun: time one fused peer all-reduce of a row-split linear "
                         "against NCCL and against no exchange")
+    p.add_argument("--retrieval-exchange", choices=["peer", "nccl"], default="peer",
+                   help="multi-GPU retrieval: the per-kv-head mass all-gathered over NVLink peer "
+                        "memory (two launches) or by NCCL")
     p.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                    help="--draft-step --draft-parallel tp: the all-reduces fused into the "
                         "row-split linears over NVLink peer memory, or NCCL all-reduces")

@@ -499,6 +499,21 @@ int dsb_draft_linear_peer(const void *x, int32_t tokens, int32_t in_features, co
                           int32_t weight_rows, const uint64_t *peer_bases, int32_t world,
                           int32_t rank, int32_t tokens_max, void *own_base, int32_t dtype,
                           int32_t flags, int32_t *error_flag, void *stream);
+/* All-gather over the same buffers, created with tokens_max 1 and features =
+ * count_max: dsb_peer_all_gather_send stores this rank's `count` floats,
+ * tagged with the call's number, into its slot of every rank's buffer;
+ * dsb_peer_all_gather_recv, after it on each rank, writes out[world][count]
+ * (rank-major, what an NCCL all_gather_into_tensor gives) from its own buffer
+ * once the tags show every rank's values arrived (bounded by time:
+ * DSB_FLAG_TIMEOUT).  Replaces the NCCL all-gather of the per-kv-head chunk
+ * mass of a head-sharded retrieval (the reference's all-reduce of scores,
+ * diffspec/runtime.py:1292-1297).  count and count_max multiples of 8; the
+ * send / receive pairs of a site alternate on every rank, as above. */
+int dsb_peer_all_gather_send(const float *src, int64_t count, const uint64_t *peer_bases,
+                             int32_t world, int32_t rank, int64_t count_max, void *own_base,
+                             void *stream);
+int dsb_peer_all_gather_recv(void *own_base, int32_t world, int64_t count, int64_t count_max,
+                             float *out, int32_t *error_flag, void *stream);
 int dsb_peer_add_rms_norm(void *own_base, int32_t world, int32_t tokens_max, const void *residual,
                           int64_t residual_row_stride, const void *weight, void *x_out,
                           int64_t x_row_stride, void *out, int64_t out_row_stride, int32_t rows,

@@ -115,3 +115,35 @@ def test_tp_layer_peer_stages_match_all_reduce_stages(dsb, cuda, world):
     finally:
         o_sites[0].close()
         d_sites[0].close()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_all_gather_matches_stack(dsb, cuda, world):
+    """peer_all_gather with virtual ranks on one GPU (every send before any
+    receive): each rank's out is the rank-major stack of every rank's local
+    block, bit for bit, over three calls (both parities, a shorter count) and
+    at the retrieval's shape ([rows, Hk_local, chunks])."""
+    rows, hk_local, chunks = 32, 2, 640
+    count = rows * hk_local * chunks
+    g = torch.Generator(device=cuda).manual_seed(world)
+    sites = dsb.parallel.PeerExchange.local(world, 1, count, cuda)
+    try:
+        for call, shape in enumerate(((rows, hk_local, chunks), (rows, hk_local, chunks),
+                                      (rows // 2, hk_local, chunks))):
+            local = [torch.rand(shape, generator=g, device=cuda) for _ in range(world)]
+            outs = [torch.full((world, *shape), float("nan"), device=cuda) for _ in range(world)]
+            for r, site in enumerate(sites):
+                dsb._lib.call("dsb_peer_all_gather_send", local[r].data_ptr(), local[r].numel(),
+                              site.bases.data_ptr(), world, r, site.features, site.own_base,
+                              dsb._lib.stream_ptr(cuda))
+            for r, site in enumerate(sites):
+                dsb._lib.call("dsb_peer_all_gather_recv", site.own_base, world, local[r].numel(),
+                              site.features, outs[r].data_ptr(),
+                              dsb._lib.error_flag(cuda).data_ptr(), dsb._lib.stream_ptr(cuda))
+            want = torch.stack(local)
+            torch.cuda.synchronize()
+            assert dsb._lib.read_and_clear_error_flag(cuda) == 0
+            for out in outs:
+                assert torch.equal(out, want), call
+    finally:
+        sites[0].close()

@@ -3,7 +3,8 @@
 partials stored over NVLink, flags waited on across devices.  Every rank's
 tensor-parallel layer step (Eagle3DraftLayerTP with peer sites) must equal,
 bit for bit, the same layer computed on that rank alone from both shards
-with a rank-ordered fp32 sum, over two steps in a row.  The handles travel
+with a rank-ordered fp32 sum, over two steps in a row; the peer all-gather
+must equal gloo's all_gather of the same blocks, twice.  The handles travel
 over a gloo group on 127.0.0.1."""
 
 from __future__ import annotations
@@ -78,6 +79,20 @@ def _worker(rank, world, port, queue):
         flag = dsb._lib.read_and_clear_error_flag(dev)
         ok = flag == 0 and all(torch.equal(o, want) for o in outs)
         msg = f"flag {flag}, max diff {max((o.float() - want.float()).abs().max().item() for o in outs)}"
+        # the retrieval's all-gather of per-kv-head mass, twice
+        gsite = dsb.parallel.PeerExchange.create(1, 16 * 2 * 640, dev)
+        dist.barrier()
+        for call in range(2):
+            mass = torch.rand((16, 2, 640), generator=torch.Generator(device=dev).manual_seed(
+                10 * call + rank), device=dev)
+            got = dsb.parallel.peer_all_gather(mass, gsite, torch.empty((2, 16, 2, 640), device=dev))
+            every = [torch.empty_like(mass).cpu() for _ in range(world)]
+            dist.all_gather(every, mass.cpu())
+            torch.cuda.synchronize(dev)
+            ok = ok and torch.equal(got.cpu(), torch.stack(every))
+        ok = ok and dsb._lib.read_and_clear_error_flag(dev) == 0
+        dist.barrier()
+        gsite.close()
         dist.barrier()  # no rank still writes into the other's buffers
         for site in sites:
             site.close()

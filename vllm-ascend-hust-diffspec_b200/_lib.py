@@ -156,6 +156,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dsb_ipc_close": (ctypes.c_int, [_P]),
     "dsb_draft_linear_peer": (
         ctypes.c_int, [_P, _I32, _I32, _P, _I32, _P, _I32, _I32, _I32, _P, _I32, _I32, _P, _P]),
+    "dsb_peer_all_gather_send": (ctypes.c_int, [_P, _I64, _P, _I32, _I32, _I64, _P, _P]),
+    "dsb_peer_all_gather_recv": (ctypes.c_int, [_P, _I32, _I64, _I64, _P, _P, _P]),
     "dsb_peer_add_rms_norm": (
         ctypes.c_int,
         [_P, _I32, _I32, _P, _I64, _P, _P, _I64, _P, _I64, _I32, _I32, _F32, _I32, _P, _P]),

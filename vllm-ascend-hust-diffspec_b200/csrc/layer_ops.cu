@@ -133,10 +133,10 @@ __global__ void __launch_bounds__(kNormThreads)
   auto sum8 = [&](int v, float (&f)[8]) {
     float pv[8];
     if (PEER) {
-      late |= !ld_tagged8(prow8 + (int64_t)v * 64, epoch + 1u, pv);
+      late |= !ld_tagged8(prow8 + (int64_t)v * 64, epoch + 1u, pv, !late);
       for (int q = 1; q < pin.world; ++q) {
         float pq[8];
-        late |= !ld_tagged8(prow8 + q * rank_stride + (int64_t)v * 64, epoch + 1u, pq);
+        late |= !ld_tagged8(prow8 + q * rank_stride + (int64_t)v * 64, epoch + 1u, pq, !late);
 #pragma unroll
         for (int i = 0; i < 8; ++i) pv[i] = __fadd_rn(pv[i], pq[i]);
       }

@@ -47,9 +47,11 @@ __device__ __forceinline__ void st_tagged(void *p, float v, uint32_t tag) {
 // Eight consecutive (value, tag) words of this rank's buffer into v[0..7],
 // once all of them carry `tag`: polled (bounded by time, checked every 64
 // polls, with a poll count as a backstop); false when the bound ran out.
-__device__ __forceinline__ bool ld_tagged8(const void *p, uint32_t tag, float (&v)[8]) {
+// With wait false (a wait of this thread already ran out) one poll only.
+__device__ __forceinline__ bool ld_tagged8(const void *p, uint32_t tag, float (&v)[8],
+                                           bool wait = true) {
   uint64_t t0 = 0;
-  for (int i = 0; i < (1 << 24); ++i) {
+  for (int i = 0; i < (wait ? (1 << 24) : 1); ++i) {
     bool all = true;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {

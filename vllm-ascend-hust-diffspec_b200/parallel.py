@@ -21,7 +21,7 @@ import torch.distributed as dist
 
 from . import _lib
 
-__all__ = ["PeerExchange", "gather_head_scores", "head_major", "shard_heads"]
+__all__ = ["PeerExchange", "gather_head_scores", "head_major", "peer_all_gather", "shard_heads"]
 
 
 def shard_heads(num_kv_heads: int, world_size: int, rank: int) -> tuple[int, int]:
@@ -58,6 +58,28 @@ def gather_head_scores(
         dist.all_gather_into_tensor(out, local.contiguous(), group=group)
     else:  # gloo (CPU tests) has no all_gather_into_tensor
         dist.all_gather(list(out.unbind(0)), local.contiguous(), group=group)
+    return out
+
+
+def peer_all_gather(local: torch.Tensor, site: "PeerExchange", out: torch.Tensor) -> torch.Tensor:
+    """All-gather of fp32 ``local`` over NVLink peer memory into ``out``
+    (``[world, *local.shape]``, rank-major, as ``all_gather_into_tensor``
+    writes it): this rank's values, tagged with the call's number, are stored
+    into every rank's buffer of ``site`` (``PeerExchange.create(1, count,
+    ...)``, count = ``local.numel()`` rounded up to 8 or more), then each rank
+    unpacks its own buffer once the tags show every rank's values arrived
+    (``dsb_peer_all_gather_send`` / ``_recv``, two launches, no collective)."""
+    n = local.numel()
+    if local.dtype != torch.float32 or not local.is_contiguous() or n % 8 or n > site.features:
+        raise ValueError("local must be contiguous fp32 with a multiple of 8 elements that fit the site")
+    if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != site.world * n:
+        raise ValueError("out must be contiguous fp32 [world, *local.shape]")
+    device = _lib.require_cuda(local, out)
+    stream = _lib.stream_ptr(device)
+    _lib.call("dsb_peer_all_gather_send", _lib.ptr(local), n, _lib.ptr(site.bases), site.world,
+              site.rank, site.features, site.own_base, stream)
+    _lib.call("dsb_peer_all_gather_recv", site.own_base, site.world, n, site.features,
+              _lib.ptr(out), _lib.ptr(_lib.error_flag(device)), stream)
     return out
 
 
