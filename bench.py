@@ -647,9 +647,21 @@ def run_ours(args):
         gathered = torch.empty((hg, rows, hk_local, w.max_chunks), dtype=torch.float32,
                                device=device)
         if args.retrieval_exchange == "peer":
-            site = dsb.parallel.PeerExchange.create(1, rows * hk_local * w.max_chunks, device,
-                                                    group=group)
+            # every rank must take the same exchange: if any rank cannot map
+            # its peers' buffers, all of them use the NCCL all-gather
+            try:
+                site = dsb.parallel.PeerExchange.create(1, rows * hk_local * w.max_chunks,
+                                                        device, group=group)
+            except Exception as error:  # noqa: BLE001 - reported, then agreed on below
+                print(f"rank {rank}: peer exchange unavailable ({error})", file=sys.stderr)
+                site = None
+            ok = torch.tensor([1 if site is not None else 0], device=device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            if int(ok.item()) == 0 and site is not None:
+                site.close()
+                site = None
             dist.barrier()  # every rank's buffer is mapped before the first call
+        if site is not None:
             exchange = lambda parts: dsb.parallel.peer_all_gather(parts, site, gathered)  # noqa: E731
         else:
             exchange = lambda parts: dsb.parallel.gather_head_scores(parts, group, out=gathered)  # noqa: E731
