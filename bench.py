@@ -646,7 +646,11 @@ def run_ours(args):
         # selection reads it in place
         gathered = torch.empty((hg, rows, hk_local, w.max_chunks), dtype=torch.float32,
                                device=device)
-        if args.retrieval_exchange == "peer":
+        # auto: the peer gather for exchange groups of two ranks, where it has
+        # been run and measured; NCCL for larger groups
+        use_peer = args.retrieval_exchange == "peer" or (args.retrieval_exchange == "auto"
+                                                         and hg == 2)
+        if use_peer:
             # every rank must take the same exchange: if any rank cannot map
             # its peers' buffers, all of them use the NCCL all-gather
             try:
@@ -1752,9 +1756,10 @@ def main():
     p.add_argument("--peer-exchange", action="store_true",
                    help="under torchrun: time one fused peer all-reduce of a row-split linear "
                         "against NCCL and against no exchange")
-    p.add_argument("--retrieval-exchange", choices=["peer", "nccl"], default="peer",
+    p.add_argument("--retrieval-exchange", choices=["auto", "peer", "nccl"], default="auto",
                    help="multi-GPU retrieval: the per-kv-head mass all-gathered over NVLink peer "
-                        "memory (two launches) or by NCCL")
+                        "memory (two launches) or by NCCL; auto: peer for exchange groups of two "
+                        "ranks, NCCL for larger ones")
     p.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                    help="--draft-step --draft-parallel tp: the all-reduces fused into the "
                         "row-split linears over NVLink peer memory, or NCCL all-reduces")
