@@ -1477,9 +1477,9 @@ def run_draft_linear(args):
     """Time the config-5 draft layer's four linears at a 16-token decode step
     on the tcgen05 weight-streaming kernel (`us`: tile-packed weights, as the
     draft layer streams them; `us_row_major_weight`: the same launches on
-    row-major weights; `us_prefetch_l2`: tile-packed with the rest of each
-    weight requested into L2 while the previous launch finishes, which the
-    layer leaves off because it evicts the draft attention's working cache)
+    row-major weights; `us_prefetch_l2`: tile-packed with each CTA's next four weight blocks
+    requested into L2 while the previous launch finishes, which the layer
+    leaves off because it pushes the draft attention's working cache out of L2)
     (qkv with the raw-cache write,
     o_proj + residual, gate_up + SwiGLU, down_proj + residual) against cuBLAS
     for the same products (torch.mm; the K/V raw write, the residual add and

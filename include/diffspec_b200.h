@@ -314,10 +314,11 @@ int dsb_paged_decode_attention_lse(
  * already in its shared-memory image, staged by one bulk copy) instead of
  * row-major [rows, in_features]. */
 #define DSB_LINEAR_PACKED_WEIGHT 2
-/* With DSB_LINEAR_PREFETCH_WEIGHT: also request the rest of the weight into
- * L2 before that wait, so HBM keeps streaming while the previous kernel
- * finishes.  Faster for a linear alone; it fills L2 with a whole weight, so
- * leave it off where another kernel's working set must stay in L2. */
+/* With DSB_LINEAR_PREFETCH_WEIGHT: also request each CTA's next four weight
+ * blocks past its ring into L2 before that wait, so HBM keeps streaming
+ * while the previous kernel finishes.  Faster for a linear alone; it puts
+ * more of the weight in L2, so leave it off where another kernel's working
+ * set must stay in L2. */
 #define DSB_LINEAR_PREFETCH_L2 4
 
 /* Copy a row-major [rows, cols] weight (rows a multiple of 128, cols of 64;

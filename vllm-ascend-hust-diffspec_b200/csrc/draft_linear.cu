@@ -48,6 +48,7 @@ namespace {
 constexpr int kLnThreads = 128;             // 4 warps: one TMEM lane per thread
 constexpr int kLnTok = 16;                  // tokens per tile (the MMA's N)
 constexpr int kLnStages = 4;                // ring slots per CTA (two CTAs fit an SM)
+constexpr int kLnL2Ahead = 4;               // k-blocks past the ring requested into L2
 constexpr int kLnABytes = 128 * 64 * 2;     // weight box [128 rows][64 cols]
 constexpr int kLnBBytes = kLnTok * 64 * 2;  // activation box [16 rows][64 cols]
 constexpr int kLnMaxK = 1 << 16;
@@ -163,10 +164,11 @@ draft_linear_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constan
         mbar_expect_tx(full0 + 8 * kb, kLnABytes + kLnBBytes);
         load_w(s_a + kb * kLnABytes, kb0 + kb, full0 + 8 * kb);
       }
-      // the rest of this rank's weight blocks into L2, so that HBM keeps
-      // streaming while the previous kernel finishes and the ring's later
-      // loads hit L2
-      for (int kb = first; kb < nkb && a.prefetch_l2; ++kb) {
+      // the next kLnL2Ahead of this rank's weight blocks into L2, so that
+      // HBM keeps streaming while the previous kernel finishes and the
+      // ring's next loads hit L2 (a bounded run: the whole weight measured
+      // slower and holds more of L2)
+      for (int kb = first; kb < min(nkb, first + kLnL2Ahead) && a.prefetch_l2; ++kb) {
         if (a.packed)
           bulk_prefetch_l2_hint(wpacked + ((int64_t)blockIdx.y * nkb_all + kb0 + kb) * kLnABytes,
                                 kLnABytes, wpol);

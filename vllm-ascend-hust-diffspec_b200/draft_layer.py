@@ -82,8 +82,9 @@ def draft_linear(x: torch.Tensor, weight: torch.Tensor, epilogue: str = "plain",
     ``[T, rows / 2] = round(round(silu(gate)) * up)`` with gate and up
     rounded first, as vLLM's gate_up output and SiluAndMul round them).  ``prefetch_weight`` starts the
     weight stream before the previous kernel has finished (the weight must
-    not be written by that kernel); ``prefetch_l2`` also requests the rest
-    of it into L2 by then (faster alone; it fills L2 with the weight).
+    not be written by that kernel); ``prefetch_l2`` also requests the next
+    weight blocks of every CTA into L2 by then (faster alone; it puts more
+    of the weight in L2).
     ``packed``: ``weight`` comes from :func:`pack_linear_weight` (same shape,
     tile-packed bytes)."""
     if epilogue not in _EPILOGUES:

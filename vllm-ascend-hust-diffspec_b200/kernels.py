@@ -452,8 +452,9 @@ def qkv_projection_write_raw(
     in :func:`kv_projection_write_raw`.  ``prefetch_weight`` lets the weight
     stream start before the previous kernel in the stream has finished (the
     weight must not be written by that kernel); ``prefetch_l2`` (with
-    ``prefetch_weight``) also requests the rest of the weight into L2 before
-    that kernel has finished (faster alone; it fills L2 with the weight);
+    ``prefetch_weight``) also requests the next weight blocks of every CTA
+    into L2 before that kernel has finished (faster alone; it puts more of
+    the weight in L2);
     ``packed_weight``: ``weight`` is in the tile-packed layout of
     ``draft_layer.pack_linear_weight``.
     """
