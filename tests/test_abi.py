@@ -151,3 +151,34 @@ def test_target_attention_rejects_bad_arguments(dsb):
     # default split length: 512 tokens below 16384, 1024 from there on
     assert lib.dsb_paged_decode_scratch_floats(4, 32, 1000, 0) == 4 * 32 * 2 * 130
     assert lib.dsb_paged_decode_scratch_floats(4, 32, 40960, 0) == 4 * 32 * 40 * 130
+
+
+def test_peer_exchange_entry_points_reject_bad_arguments(dsb):
+    """The fused all-reduce / all-gather entry points and the exchange buffer
+    helpers validate on the host, before any CUDA call."""
+    lib = dsb._lib.load()
+    inv = dsb._lib.DSB_ERR_INVALID
+    fake = ctypes.c_void_p(256)
+    # buffer size: 2 parities x world x tokens x features words of 8 bytes, then
+    # the 128-byte-aligned sync words
+    data = 2 * 2 * 16 * 2048 * 8
+    assert lib.dsb_peer_buffer_bytes(2, 16, 2048) == (data + 127) // 128 * 128 + 128
+    assert lib.dsb_peer_buffer_bytes(0, 16, 2048) == -1
+    assert lib.dsb_peer_buffer_bytes(9, 16, 2048) == -1
+    base = ctypes.c_void_p()
+    assert lib.dsb_peer_buffer_create(9, 16, 2048, ctypes.byref(base)) == inv
+    assert lib.dsb_peer_buffer_create(2, 16, 2047, ctypes.byref(base)) == inv
+    assert lib.dsb_peer_buffer_destroy(None) == 0 and lib.dsb_ipc_close(None) == 0
+    assert lib.dsb_ipc_handle(None, fake) == inv and lib.dsb_ipc_open(None, ctypes.byref(base)) == inv
+    # linear + all-reduce: rank within world, tokens within the buffer
+    assert lib.dsb_draft_linear_peer(fake, 16, 64, fake, 128, fake, 2, 2, 16, fake, 0, 0, None,
+                                     None) == inv
+    assert lib.dsb_draft_linear_peer(fake, 17, 64, fake, 128, fake, 2, 0, 16, fake, 0, 0, None,
+                                     None) == inv
+    assert lib.dsb_peer_add_rms_norm(fake, 2, 16, fake, 128, None, fake, 128, None, 0, 17, 128,
+                                     1e-6, 0, None, None) == inv
+    # all-gather: counts are multiples of 8 within the buffer's row
+    assert lib.dsb_peer_all_gather_send(fake, 12, fake, 2, 0, 64, fake, None) == inv
+    assert lib.dsb_peer_all_gather_send(fake, 72, fake, 2, 0, 64, fake, None) == inv
+    assert lib.dsb_peer_all_gather_recv(fake, 2, 12, 64, fake, None, None) == inv
+    assert lib.dsb_peer_all_gather_send(fake, 0, fake, 2, 0, 64, fake, None) == 0
