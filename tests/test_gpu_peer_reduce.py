@@ -147,3 +147,40 @@ def test_peer_all_gather_matches_stack(dsb, cuda, world):
                 assert torch.equal(out, want), call
     finally:
         sites[0].close()
+
+
+def test_peer_waits_run_out_flag_and_finish(dsb, cuda):
+    """A rank whose peer never sends: the consumer's bounded waits (2 s) run
+    out, the kernels finish with DSB_FLAG_TIMEOUT in the error word, and the
+    context stays usable (a normal call afterwards is exact)."""
+    dl = dsb.draft_layer
+    timeout_bit = 32
+    features, k = 256, 128
+    g = torch.Generator(device=cuda).manual_seed(5)
+    w = (torch.randn((features, k), generator=g, device=cuda) / k ** 0.5).bfloat16()
+    x = torch.randn((16, k), generator=g, device=cuda).bfloat16()
+    res = torch.randn((16, features), generator=g, device=cuda).bfloat16()
+    sites = dsb.parallel.PeerExchange.local(2, 16, features, cuda)
+    gsites = dsb.parallel.PeerExchange.local(2, 1, 64, cuda)
+    try:
+        dl.draft_linear_peer(x, w, sites[0])        # rank 1 never sends
+        dl.peer_add_rms_norm(sites[0], res, None, 1e-6)
+        torch.cuda.synchronize()
+        assert dsb._lib.read_and_clear_error_flag(cuda) & timeout_bit
+        local = torch.rand((64,), generator=g, device=cuda)
+        out = torch.empty((2, 64), device=cuda)
+        dsb._lib.call("dsb_peer_all_gather_send", local.data_ptr(), 64, gsites[0].bases.data_ptr(),
+                      2, 0, 64, gsites[0].own_base, dsb._lib.stream_ptr(cuda))
+        dsb._lib.call("dsb_peer_all_gather_recv", gsites[0].own_base, 2, 64, 64, out.data_ptr(),
+                      dsb._lib.error_flag(cuda).data_ptr(), dsb._lib.stream_ptr(cuda))
+        torch.cuda.synchronize()
+        assert dsb._lib.read_and_clear_error_flag(cuda) & timeout_bit
+        assert torch.equal(out[0], local)  # the slot that did arrive
+    finally:
+        sites[0].close()
+        gsites[0].close()
+    part = dl.draft_linear(x, w, "partial")
+    got, _ = dl.add_rms_norm(part, res, None, 1e-6)
+    assert torch.equal(got, (part + res.float()).bfloat16())
+    torch.cuda.synchronize()
+    assert dsb._lib.read_and_clear_error_flag(cuda) == 0
